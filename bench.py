@@ -1,0 +1,365 @@
+#!/usr/bin/env python3
+"""Decode benchmark of the B200 Gemma-4 26B-A4B path (BASELINE.json metric / config 4).
+
+Workload (config 4): the 26B-A4B-shaped model with seeded random bf16 weights N(0,0.02)
+(seed 3; global head_dim 256 as BASELINE states), batch-1 greedy decode with a
+32,768-token resident KV cache, a 32-token random prompt, then decode steps.  A step
+is one decoded token; the timed steps continue the same sequence (positions
+32+W .. 32+W+K), so the default W=16, K=752 covers exactly config 4's 768 tokens.
+
+value       tokens/s of the captured step graph, K steps between CUDA events on the
+            launching stream (barrier + synchronize on both sides, max over ranks).
+            Inputs are larger than L2 (7.4 GB of weights stream per step).
+e2e         the same metric through the public API: Engine.generate() with the prompt
+            uploaded from host memory and every token read back to the host, wall
+            clock from the call to the last token (includes prefill).
+roofline    the kernel class with the largest time share (per-class CUDA-event timing
+            of event-separated steps): algorithmic bytes per launch / mean duration,
+            against the measured HBM copy peak (MEASURED_PEAKS.json).
+cpu_baseline  the CPU oracle (restatement of the reference forward, oracle/) timing a
+            bounded sample of full-size decode steps on the host cores (rank 0, N=1).
+
+``--impl reference`` times that CPU implementation alone (rank 0; other ranks exit 0).
+Multi-GPU: tensor parallel over N ranks (torchrun, one GPU each); every rank decodes
+the same token, so total work per token is fixed ("scaling": "strong").
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "kaggle-tpu-inference_b200"))
+
+METRIC = "decode tok/s @32K ctx, bs=1"
+FALLBACK_HBM_GBS = 6650.0
+
+# DRAM traffic per launch of the dominant kernel class from an ncu capture; see
+# profiles/ (None until a capture of the current kernels exists).
+NCU_TRAFFIC_BYTES_PER_LAUNCH: dict = {}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser(description=__doc__)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=752)
+    ap.add_argument("--warmup", type=int, default=16)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--max-len", type=int, default=32768)
+    ap.add_argument("--prompt-len", type=int, default=32)
+    ap.add_argument("--global-head-dim", type=int, default=256)
+    ap.add_argument("--seed", type=int, default=3)
+    ap.add_argument("--profile-steps", type=int, default=4)
+    ap.add_argument("--cpu-steps", type=int, default=1)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), "measured"
+    except (OSError, KeyError, ValueError):
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def prompt_ids(cfg, n, seed):
+    import torch
+
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist()
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 100 ms during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, devices):
+        self.devices = devices
+        self.proc = None
+        self.path = tempfile.mktemp(suffix=".csv")
+
+    def start(self):
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(str(d) for d in self.devices), "-lms", "100"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        self.fh.close()
+        sm, smax, reasons = [], [], set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        with open(self.path) as f:
+            for line in f:
+                cols = [c.strip() for c in line.split(",")]
+                if len(cols) < 9:
+                    continue
+                try:
+                    sm.append(float(cols[1]))
+                    smax.append(float(cols[2]))
+                except ValueError:
+                    continue
+                for n, v in zip(names, cols[5:9]):
+                    if v.lower().startswith("active"):
+                        reasons.add(n)
+        os.unlink(self.path)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ----------------------------------------------------------------------------- bytes
+def class_bytes(cfg, world, pos_avg):
+    """Algorithmic HBM bytes per step of each kernel class on one rank (bf16 weights)."""
+    H = cfg.hidden_size
+    I, F, E, K = cfg.intermediate_size // world, cfg.moe_intermediate_size // world, cfg.num_experts, cfg.top_k_experts
+    b = dict.fromkeys(("qkv", "attention", "o_proj", "router_mlp_up", "mlp_down_experts_up",
+                       "experts_down", "lm_head_argmax"), 0.0)
+    for lt in cfg.layer_types:
+        d, kv = cfg.head_dim_for(lt), cfg.kv_heads_for(lt)
+        g = cfg.num_attention_heads // kv
+        if lt == "sliding_attention":
+            n_kv, gl = kv // world, g
+            live = min(pos_avg + 1, cfg.sliding_window)
+        else:
+            n_kv, gl = kv, g // world
+            live = pos_avg + 1
+        rq = n_kv * gl * d
+        rkv = n_kv * d * (1 if cfg.k_eq_v_for(lt) else 2)
+        b["qkv"] += 2 * (rq + rkv) * H
+        b["attention"] += 2 * 2 * live * n_kv * d
+        b["o_proj"] += 2 * H * rq
+        b["router_mlp_up"] += 2 * (E * H + 2 * I * H)
+        b["mlp_down_experts_up"] += 2 * (H * I + K * 2 * F * H)
+        b["experts_down"] += 2 * K * H * F
+    b["lm_head_argmax"] += 2 * (cfg.vocab_size // world) * H
+    return b
+
+
+def step_bytes(cfg, pos_avg):
+    """Algorithmic bytes per token for the whole model (2 x active params + live KV)."""
+    from gemma4_b200.weights import active_params_per_token
+
+    kv = 0
+    for lt in cfg.layer_types:
+        live = min(pos_avg + 1, cfg.sliding_window) if lt == "sliding_attention" else pos_avg + 1
+        kv += 2 * 2 * live * cfg.kv_heads_for(lt) * cfg.head_dim_for(lt)
+    return 2 * active_params_per_token(cfg) + kv
+
+
+# ----------------------------------------------------------------------------- CPU arm
+def cpu_decode_sample(cfg, max_len, n_steps, n_warm=1):
+    """Time full-size decode steps of the CPU oracle (reference algorithm) on all cores.
+
+    Zero-valued weights (torch.zeros is lazily committed, so only the touched pages
+    cost memory); arithmetic time does not depend on the values.  The step attends
+    over the whole max_len cache under the mask, exactly like the reference decode
+    (gemma4_tpu/engine.py:77).
+    """
+    import torch
+
+    from oracle.reference_model import Oracle, param_shapes
+
+    torch.set_num_threads(os.cpu_count() or 1)
+    params = {n: torch.zeros(s, dtype=torch.bfloat16) for n, s in param_shapes(cfg).items()}
+    for n in params:
+        if n.endswith("layer_scalar"):
+            params[n] = torch.ones(1, dtype=torch.bfloat16)
+    o = Oracle(cfg, params, mode="bf16")
+    cache = o.new_cache(1, max_len)
+    pos = 32
+    for _ in range(n_warm):
+        _, cache = o.decode(cache, 1, pos, max_len)
+        pos += 1
+    t0 = time.perf_counter()
+    for _ in range(n_steps):
+        _, cache = o.decode(cache, 1, pos, max_len)
+        pos += 1
+    dt = time.perf_counter() - t0
+    return n_steps / dt, torch.get_num_threads()
+
+
+def run_reference(args, cfg, rank, world, workload):
+    if rank != 0:
+        return 0
+    steps = max(1, min(args.steps, args.cpu_steps))
+    warm = 1 if args.warmup > 0 else 0
+    value, cores = cpu_decode_sample(cfg, args.max_len, steps, warm)
+    sample = (f"{steps} timed full-size decode step(s) after {warm} warm-up at position 32+, "
+              f"max_len {args.max_len}, CPU restatement of the reference forward (oracle/)")
+    line = {
+        "metric": METRIC, "value": value, "unit": "tok/s", "impl": "reference",
+        "n_gpus": world, "steps": steps, "warmup": warm, "ms_per_step": 1000.0 / value,
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic", "config": workload,
+        "cpu_baseline": {"value": value, "unit": "tok/s", "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ----------------------------------------------------------------------------- GPU arm
+def main() -> int:
+    args = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", args.gpus))
+    rank = int(os.environ.get("RANK", 0))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+
+    from gemma4_b200.config import gemma4_26b_a4b
+
+    cfg = gemma4_26b_a4b(args.global_head_dim)
+    workload = {
+        "workload": "BASELINE config 4: 26B-A4B-shaped random model (seed 3), bs=1 greedy decode, "
+                    "32K resident KV cache, 32-token prompt",
+        "model": "gemma-4-26B-A4B-shape (random init)", "global_head_dim": args.global_head_dim,
+        "max_len": args.max_len, "prompt_len": args.prompt_len, "global_batch": 1,
+        "parallelism": f"tp{world}", "l2_policy": "inputs larger than L2 (7.4 GB weights per step)",
+    }
+    if args.impl == "reference":
+        return run_reference(args, cfg, rank, world, workload)
+
+    import torch
+    import torch.distributed as dist
+
+    if world > 1:
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        torch.cuda.set_device(local)
+        from datetime import timedelta
+
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device("cuda", local))
+    from gemma4_b200.engine import Engine
+    from gemma4_b200.model import Mesh
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    mesh = Mesh(rank, world, local)
+    eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh)
+    eng.compile_all()
+    m = eng.model
+    prompt = prompt_ids(cfg, args.prompt_len, args.seed)
+
+    def barrier():
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize(dev)
+
+    # ---- device-timed decode steps (the captured graph)
+    m.reset(prompt)
+    m.step(len(prompt))
+    m.step(args.warmup)
+    barrier()
+    sampler = ClockSampler([local] if world == 1 else list(range(world))) if rank == 0 else None
+    if sampler:
+        sampler.start()
+        time.sleep(0.3)
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    m.step(args.steps)
+    e1.record()
+    barrier()
+    clocks = sampler.stop() if sampler else None
+    ms = e0.elapsed_time(e1)
+    m.check_status()
+    if world > 1:
+        t = torch.tensor([ms], device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    value = args.steps / (ms / 1000.0)
+    pos_avg = len(prompt) + args.warmup + args.steps // 2
+
+    # ---- per-kernel-class timing (event-separated steps, same stream)
+    prof = m.profile(args.profile_steps)
+    barrier()
+    m.check_status()
+    cb = class_bytes(cfg, world, pos_avg)
+    total_ms = sum(prof.values())
+    dom = max(prof, key=prof.get)
+    launches = {"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers) * args.profile_steps
+    dom_ms = prof[dom] / launches
+    dom_bytes = cb[dom] / ({"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers))
+    peak, peak_kind = peaks()
+    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+    traffic = NCU_TRAFFIC_BYTES_PER_LAUNCH.get(dom)
+    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
+                "algorithmic_bytes_per_launch": dom_bytes, "mean_launch_ms": dom_ms,
+                "time_share": prof[dom] / total_ms}
+    sb = step_bytes(cfg, pos_avg)
+    step_roof = {"achieved_aggregate_gbs": sb * value / 1e9, "peak_aggregate_gbs": peak * world,
+                 "frac": sb * value / 1e9 / (peak * world), "bytes_per_token": sb,
+                 "kernel_share": {k: v / total_ms for k, v in prof.items()}}
+
+    # ---- end to end through Engine.generate (host prompt, host token reads)
+    e2e = None
+    if not args.no_e2e:
+        n_new = min(args.steps + args.warmup, args.max_len - len(prompt) - 1)
+        barrier()
+        t0 = time.perf_counter()
+        evs = list(eng.generate(prompt, max_new_tokens=n_new, temperature=0.0, stop_ids=()))
+        wall = time.perf_counter() - t0
+        if world > 1:
+            t = torch.tensor([wall], device=dev, dtype=torch.float64)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            wall = float(t.item())
+        e2e = {"value": len(evs) / wall, "unit": "tok/s", "h2d_bytes_per_step": 4 * len(prompt) / len(evs),
+               "d2h_bytes_per_step": 4, "ttft_ms": 1000 * evs[0]["ttft"], "tokens": len(evs),
+               "path": "Engine.generate (temperature 0), wall clock call -> last token"}
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            v, cores = cpu_decode_sample(cfg, args.max_len, args.cpu_steps, 1)
+            cpu = {"value": v, "unit": "tok/s", "cores": cores, "kind": "port",
+                   "sample": f"{args.cpu_steps} full-size decode step(s) of the CPU oracle "
+                             f"(reference algorithm, masked {args.max_len}-key attention) after 1 warm-up"}
+        except Exception as exc:  # report, never fail the GPU measurement
+            cpu = {"value": None, "unit": "tok/s", "cores": os.cpu_count(), "kind": "port",
+                   "sample": f"failed: {exc!r}"[:200]}
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
+            "step_roofline": step_roof, "cpu_baseline": cpu,
+            "gpu_launches": args.steps * m.kernels_per_step,
+            "load_s": eng.load_seconds,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

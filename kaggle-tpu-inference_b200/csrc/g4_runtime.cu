@@ -1,0 +1,1126 @@
+// Host runtime of g4b200: communicator, model plan, step launcher, graph capture and
+// the C ABI declared in include/g4b200.h.
+//
+// A decode step is 6 kernels per layer + 1 (embedding is fused into layer 0's first
+// kernel, the argmax into the lm_head kernel).  All kernels are launched with the
+// programmatic-stream-serialization attribute so each one is scheduled while its
+// predecessor drains and prefetches its weights before griddepcontrol.wait; the whole
+// step is captured once into a CUDA graph and replayed per token.
+#include <cuda_runtime.h>
+
+#include <cmath>
+#include <cstdarg>
+#include <cstdio>
+#include <cstring>
+#include <map>
+#include <mutex>
+#include <string>
+#include <vector>
+
+#include "g4_attention.cuh"
+#include "g4_ops.cuh"
+
+using namespace g4;
+
+// ------------------------------------------------------------------ errors
+static thread_local std::string g_last_error;
+
+static int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+#define G4_CUDA(call, code)                                                              \
+  do {                                                                                   \
+    cudaError_t e_ = (call);                                                             \
+    if (e_ != cudaSuccess)                                                               \
+      return fail(code, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
+                  __LINE__);                                                             \
+  } while (0)
+
+extern "C" const char* g4_version(void) { return "g4b200 0.1 sm_100a"; }
+
+extern "C" const char* g4_strerror(int code) {
+  switch (code) {
+    case G4_OK: return "ok";
+    case G4_ERR_ARG: return "invalid argument";
+    case G4_ERR_SHAPE: return "unsupported shape";
+    case G4_ERR_LAUNCH: return "kernel launch failed";
+    case G4_ERR_TIMEOUT: return "bounded device wait timed out";
+    case G4_ERR_STATE: return "invalid call order";
+    case G4_ERR_NOMEM: return "device allocation failed";
+    case G4_ERR_CUDA: return "CUDA error";
+    default: return "unknown error";
+  }
+}
+
+extern "C" const char* g4_last_error(void) { return g_last_error.c_str(); }
+
+// ------------------------------------------------------------------ communicator
+struct g4_comm {
+  int device = 0, rank = 0, world = 1, hidden = 0;
+  size_t bytes = 0;
+  char* local = nullptr;
+  char* peer[kMaxWorld] = {};
+  bool mapped[kMaxWorld] = {};
+  bool open = false;
+};
+
+static size_t comm_bytes(int hidden) {
+  return (size_t)kXFlagBytes + (size_t)kSites * 2 * kMaxWorld * (2 * (size_t)hidden) * 4;
+}
+
+extern "C" int g4_comm_create(int device, int rank, int world, int hidden, g4_comm** out) {
+  if (!out || world < 1 || world > kMaxWorld || rank < 0 || rank >= world || hidden <= 0)
+    return fail(G4_ERR_ARG, "g4_comm_create: bad rank/world/hidden (%d/%d/%d)", rank, world, hidden);
+  G4_CUDA(cudaSetDevice(device), G4_ERR_CUDA);
+  g4_comm* c = new g4_comm();
+  c->device = device;
+  c->rank = rank;
+  c->world = world;
+  c->hidden = hidden;
+  c->bytes = comm_bytes(hidden);
+  if (cudaMalloc(&c->local, c->bytes) != cudaSuccess) {
+    delete c;
+    return fail(G4_ERR_NOMEM, "g4_comm_create: cudaMalloc(%zu) failed", comm_bytes(hidden));
+  }
+  cudaMemset(c->local, 0, c->bytes);
+  cudaDeviceSynchronize();
+  c->peer[rank] = c->local;
+  c->open = (world == 1);
+  *out = c;
+  return G4_OK;
+}
+
+extern "C" int g4_comm_get_handle(const g4_comm* c, void* handle_out) {
+  if (!c || !handle_out) return fail(G4_ERR_ARG, "g4_comm_get_handle: null argument");
+  static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle is 64 bytes");
+  G4_CUDA(cudaSetDevice(c->device), G4_ERR_CUDA);
+  cudaIpcMemHandle_t h;
+  G4_CUDA(cudaIpcGetMemHandle(&h, c->local), G4_ERR_CUDA);
+  memcpy(handle_out, &h, 64);
+  return G4_OK;
+}
+
+extern "C" int g4_comm_open(g4_comm* c, const void* handles) {
+  if (!c || (!handles && c->world > 1)) return fail(G4_ERR_ARG, "g4_comm_open: null argument");
+  G4_CUDA(cudaSetDevice(c->device), G4_ERR_CUDA);
+  for (int p = 0; p < c->world; ++p) {
+    if (p == c->rank || c->mapped[p]) continue;
+    cudaIpcMemHandle_t h;
+    memcpy(&h, static_cast<const char*>(handles) + 64 * p, 64);
+    void* ptr = nullptr;
+    G4_CUDA(cudaIpcOpenMemHandle(&ptr, h, cudaIpcMemLazyEnablePeerAccess), G4_ERR_CUDA);
+    c->peer[p] = static_cast<char*>(ptr);
+    c->mapped[p] = true;
+  }
+  c->open = true;
+  return G4_OK;
+}
+
+extern "C" int g4_comm_destroy(g4_comm* c) {
+  if (!c) return G4_OK;
+  cudaSetDevice(c->device);
+  for (int p = 0; p < c->world; ++p)
+    if (c->mapped[p]) cudaIpcCloseMemHandle(c->peer[p]);
+  if (c->local) cudaFree(c->local);
+  delete c;
+  return G4_OK;
+}
+
+// ------------------------------------------------------------------ launch helper
+template <class Kernel, class... Args>
+static cudaError_t launch_pdl(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
+                              Args... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, k, args...);
+}
+
+template <class Op>
+static int prepare_kernel(int smem) {
+  static std::mutex mu;
+  static std::map<int, int> done;  // device -> max smem configured
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev] >= smem) return G4_OK;
+  G4_CUDA(cudaFuncSetAttribute(gemv_kernel<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          G4_ERR_LAUNCH);
+  done[dev] = smem;
+  return G4_OK;
+}
+
+static int prepare_attention(int smem) {
+  static std::mutex mu;
+  static std::map<int, int> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[dev] >= smem) return G4_OK;
+  G4_CUDA(cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          G4_ERR_LAUNCH);
+  G4_CUDA(cudaFuncSetAttribute(attn_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+          G4_ERR_LAUNCH);
+  done[dev] = smem;
+  return G4_OK;
+}
+
+template <class Op>
+static int launch_gemv(const Op& op, int grid, cudaStream_t st) {
+  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1]});
+  int rc = prepare_kernel<Op>(smem);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(gemv_kernel<Op>, dim3(grid), dim3(kGemvThreads), smem, st, op);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "gemv launch: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
+static int launch_attention(const AttnArgs& a, cudaStream_t st) {
+  const int smem = attn_smem_bytes(a.g, a.d);
+  int rc = prepare_attention(smem);
+  if (rc) return rc;
+  cudaError_t e;
+  if (a.d <= 256)
+    e = launch_pdl(attn_decode_kernel<1>, dim3(a.n_kv * a.nsplit), dim3(kAttnThreads), smem, st, a);
+  else
+    e = launch_pdl(attn_decode_kernel<2>, dim3(a.n_kv * a.nsplit), dim3(kAttnThreads), smem, st, a);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
+static void rope_inv_freq(int d, double theta, double partial, float* out) {
+  // model.py:54-61: fp64 inverse frequencies for the rotated pairs, zero (NoPE) tail
+  const int nrot = (int)(partial * d / 2);
+  for (int i = 0; i < d / 2; ++i)
+    out[i] = i < nrot ? (float)(1.0 / std::pow(theta, (double)(2 * i) / (double)d)) : 0.0f;
+}
+
+static float host_bf16_round(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  u += 0x7fffu + ((u >> 16) & 1u);
+  u &= 0xffff0000u;
+  float r;
+  memcpy(&r, &u, 4);
+  return r;
+}
+
+static int pick_nsplit(int n_kv, int max_live, int nsm) {
+  int need = (max_live + kAttnMaxChunk - 1) / kAttnMaxChunk;
+  int want = nsm / n_kv;
+  int ns = want > need ? want : need;
+  if (ns < 1) ns = 1;
+  if (ns > kAttnMaxSplit) ns = kAttnMaxSplit;
+  return ns;
+}
+
+// ------------------------------------------------------------------ model
+struct LayerDev {
+  bool full = false;
+  int d = 0, n_kv = 0, g = 0, rows_q = 0, rows_k = 0, rows_v = 0, k_eq_v = 0, nsplit = 1;
+  bf16_t *qkv = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
+  bf16_t *router = nullptr, *router_scale = nullptr, *pes = nullptr, *exp_gu = nullptr,
+         *exp_down = nullptr;
+  bf16_t *n_in = nullptr, *n_post_attn = nullptr, *n_pre_ff = nullptr, *n_post_ff = nullptr,
+         *n_pre_ff2 = nullptr, *n_post_ff1 = nullptr, *n_post_ff2 = nullptr;
+  bf16_t *q_norm = nullptr, *k_norm = nullptr, *scalar = nullptr;
+  bf16_t *cache_k = nullptr, *cache_v = nullptr;
+};
+
+struct g4_model {
+  g4_config cfg{};
+  std::vector<unsigned char> is_full;
+  int rank = 0, world = 1, max_len = 0, device = 0, nsm = 148;
+  int H = 0, I_local = 0, F_local = 0, V_local = 0, vbegin = 0, E = 0, topk = 0;
+  std::vector<LayerDev> L;
+  bf16_t *embed = nullptr, *final_norm = nullptr;
+  int *ctrl = nullptr, *tokens_in = nullptr, *tokens_out = nullptr;
+  float* logits = nullptr;
+  g4_comm* comm = nullptr;
+  g4_comm* own_comm = nullptr;  // world == 1 without an attached communicator
+  // library scratch
+  char* scratch = nullptr;
+  bf16_t *xres, *resmid, *h2, *qkv_raw, *ctx, *mlp_act, *moe_act, *moe_out;
+  float *o_out, *mlp_out, *router_logits, *top_w, *attn_part, *cand_v;
+  int *top_idx, *attn_cnt, *cand_i, *counters;
+  bool finalized = false;
+  // plans
+  std::vector<QkvOp> k1;
+  std::vector<AttnArgs> k2;
+  std::vector<OProjOp> k3;
+  std::vector<RouterMlpOp> k4;
+  std::vector<MoeUpOp> k5;
+  std::vector<MoeDownOp> k6;
+  LmHeadOp lm{};
+  float* rope_tab = nullptr;
+  int* tokens_host = nullptr;  // mapped pinned mirror of tokens_out (g4_model_host_tokens)
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t gexec = nullptr;
+};
+
+static bool valid_cfg(const g4_config* c) {
+  return c && c->hidden_size > 0 && c->num_hidden_layers > 0 && c->num_attention_heads > 0 &&
+         c->head_dim > 0 && c->global_head_dim > 0 && c->num_key_value_heads > 0 &&
+         c->num_global_key_value_heads > 0 && c->intermediate_size > 0 &&
+         c->moe_intermediate_size > 0 && c->num_experts > 0 && c->top_k_experts > 0 &&
+         c->vocab_size > 0;
+}
+
+extern "C" int g4_model_create(const g4_config* cfg, const unsigned char* layer_is_full, int rank,
+                               int world, int max_len, int device, g4_model** out) {
+  if (!out || !valid_cfg(cfg) || !layer_is_full)
+    return fail(G4_ERR_ARG, "g4_model_create: null or invalid config");
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world || max_len < 1)
+    return fail(G4_ERR_ARG, "g4_model_create: bad rank/world/max_len");
+  const g4_config& c = *cfg;
+  const int G = world;
+  if (!c.enable_moe_block) return fail(G4_ERR_SHAPE, "only MoE (enable_moe_block) models are supported");
+  if (c.hidden_size % 8 != 0) return fail(G4_ERR_SHAPE, "hidden_size must be a multiple of 8");
+  if (c.hidden_size > kMaxPer * kConsumerThreads) return fail(G4_ERR_SHAPE, "hidden_size > 4096");
+  if (c.intermediate_size % (8 * G) || c.moe_intermediate_size % (8 * G) || c.vocab_size % G)
+    return fail(G4_ERR_SHAPE, "intermediate / moe_intermediate / vocab not divisible by 8*world");
+  if (c.top_k_experts > kMaxTopK || c.top_k_experts > c.num_experts)
+    return fail(G4_ERR_SHAPE, "top_k_experts > %d", kMaxTopK);
+  G4_CUDA(cudaSetDevice(device), G4_ERR_CUDA);
+  g4_model* m = new g4_model();
+  m->cfg = c;
+  m->is_full.assign(layer_is_full, layer_is_full + c.num_hidden_layers);
+  m->rank = rank;
+  m->world = world;
+  m->max_len = max_len;
+  m->device = device;
+  cudaDeviceGetAttribute(&m->nsm, cudaDevAttrMultiProcessorCount, device);
+  m->H = c.hidden_size;
+  m->I_local = c.intermediate_size / G;
+  m->F_local = c.moe_intermediate_size / G;
+  m->V_local = c.vocab_size / G;
+  m->vbegin = rank * m->V_local;
+  m->E = c.num_experts;
+  m->topk = c.top_k_experts;
+  m->L.resize(c.num_hidden_layers);
+  for (int i = 0; i < c.num_hidden_layers; ++i) {
+    LayerDev& l = m->L[i];
+    l.full = m->is_full[i] != 0;
+    l.k_eq_v = (c.attention_k_eq_v && l.full) ? 1 : 0;
+    l.d = l.full ? c.global_head_dim : c.head_dim;
+    const int kv = l.k_eq_v ? c.num_global_key_value_heads : c.num_key_value_heads;
+    const int gfull = c.num_attention_heads / kv;
+    if (c.num_attention_heads % kv) { delete m; return fail(G4_ERR_SHAPE, "heads %% kv_heads"); }
+    if (!l.full) {  // sliding: shard KV heads (model.py:141-145)
+      if (kv % G) { delete m; return fail(G4_ERR_SHAPE, "layer %d: kv heads %d %% world %d", i, kv, G); }
+      l.n_kv = kv / G;
+      l.g = gfull;
+    } else {        // full: replicate KV, shard query groups (model.py:146-150)
+      if (gfull % G) { delete m; return fail(G4_ERR_SHAPE, "layer %d: groups %d %% world %d", i, gfull, G); }
+      l.n_kv = kv;
+      l.g = gfull / G;
+    }
+    if (l.g > kAttnMaxG || l.d % 64 || l.d > kAttnMaxD) {
+      delete m;
+      return fail(G4_ERR_SHAPE, "layer %d: head_dim %d / group %d unsupported", i, l.d, l.g);
+    }
+    l.rows_q = l.n_kv * l.g * l.d;
+    l.rows_k = l.n_kv * l.d;
+    l.rows_v = l.k_eq_v ? 0 : l.n_kv * l.d;
+    const int max_live = l.full ? max_len : (c.sliding_window < max_len ? c.sliding_window : max_len);
+    l.nsplit = pick_nsplit(l.n_kv, max_live, m->nsm);
+    if ((max_live + l.nsplit - 1) / l.nsplit > kAttnMaxChunk) {
+      delete m;
+      return fail(G4_ERR_SHAPE, "layer %d: context %d too long for the split-KV limits", i, max_len);
+    }
+  }
+  *out = m;
+  return G4_OK;
+}
+
+static size_t expect_bytes(const g4_model* m, const std::string& name, int* layer, std::string* field) {
+  const g4_config& c = m->cfg;
+  const size_t H = m->H;
+  *layer = -1;
+  if (name == "embed") return (size_t)c.vocab_size * H * 2;
+  if (name == "norm") return H * 2;
+  if (name == "control") return G4_CTRL_WORDS * 4;
+  if (name == "tokens_in") return (size_t)m->max_len * 4;
+  if (name == "tokens_out") return (size_t)(m->max_len + 1) * 4;
+  if (name == "logits") return (size_t)m->V_local * 4;
+  int li = -1, n = 0;
+  if (sscanf(name.c_str(), "layers.%d.%n", &li, &n) != 1 || n <= 0) return 0;
+  if (li < 0 || li >= (int)m->L.size()) return 0;
+  *layer = li;
+  *field = name.substr(n);
+  const LayerDev& l = m->L[li];
+  const std::string& f = *field;
+  if (f == "qkv") return (size_t)(l.rows_q + l.rows_k + l.rows_v) * H * 2;
+  if (f == "o_proj") return H * l.rows_q * 2;
+  if (f == "mlp.gate_proj" || f == "mlp.up_proj" || f == "mlp.down_proj") return (size_t)m->I_local * H * 2;
+  if (f == "router.proj") return (size_t)m->E * H * 2;
+  if (f == "router.per_expert_scale") return (size_t)m->E * 2;
+  if (f == "experts.gate_up_proj") return (size_t)m->E * 2 * m->F_local * H * 2;
+  if (f == "experts.down_proj") return (size_t)m->E * H * m->F_local * 2;
+  if (f == "q_norm" || f == "k_norm") return (size_t)l.d * 2;
+  if (f == "layer_scalar") return 2;
+  if (f == "cache_k" || f == "cache_v") return (size_t)m->max_len * l.n_kv * l.d * 2;
+  if (f == "input_layernorm" || f == "post_attention_layernorm" || f == "pre_feedforward_layernorm" ||
+      f == "post_feedforward_layernorm" || f == "pre_feedforward_layernorm_2" ||
+      f == "post_feedforward_layernorm_1" || f == "post_feedforward_layernorm_2" || f == "router.scale")
+    return H * 2;
+  return 0;
+}
+
+extern "C" int g4_model_set_tensor(g4_model* m, const char* cname, void* ptr, long long nbytes) {
+  if (!m || !cname || !ptr) return fail(G4_ERR_ARG, "g4_model_set_tensor: null argument");
+  if (m->finalized) return fail(G4_ERR_STATE, "g4_model_set_tensor after finalize");
+  if (reinterpret_cast<uintptr_t>(ptr) % 16) return fail(G4_ERR_ARG, "%s: pointer not 16-byte aligned", cname);
+  std::string name(cname), field;
+  int li = -1;
+  const size_t want = expect_bytes(m, name, &li, &field);
+  if (want == 0) return fail(G4_ERR_ARG, "unknown tensor name '%s'", cname);
+  if ((size_t)nbytes != want)
+    return fail(G4_ERR_SHAPE, "%s: %lld bytes, expected %zu", cname, nbytes, want);
+  auto* b = static_cast<bf16_t*>(ptr);
+  if (li < 0) {
+    if (name == "embed") m->embed = b;
+    else if (name == "norm") m->final_norm = b;
+    else if (name == "control") m->ctrl = static_cast<int*>(ptr);
+    else if (name == "tokens_in") m->tokens_in = static_cast<int*>(ptr);
+    else if (name == "tokens_out") m->tokens_out = static_cast<int*>(ptr);
+    else if (name == "logits") m->logits = static_cast<float*>(ptr);
+    return G4_OK;
+  }
+  LayerDev& l = m->L[li];
+  const std::string& f = field;
+  if (f == "qkv") l.qkv = b;
+  else if (f == "o_proj") l.o = b;
+  else if (f == "mlp.gate_proj") l.gate = b;
+  else if (f == "mlp.up_proj") l.up = b;
+  else if (f == "mlp.down_proj") l.down = b;
+  else if (f == "router.proj") l.router = b;
+  else if (f == "router.scale") l.router_scale = b;
+  else if (f == "router.per_expert_scale") l.pes = b;
+  else if (f == "experts.gate_up_proj") l.exp_gu = b;
+  else if (f == "experts.down_proj") l.exp_down = b;
+  else if (f == "input_layernorm") l.n_in = b;
+  else if (f == "post_attention_layernorm") l.n_post_attn = b;
+  else if (f == "pre_feedforward_layernorm") l.n_pre_ff = b;
+  else if (f == "post_feedforward_layernorm") l.n_post_ff = b;
+  else if (f == "pre_feedforward_layernorm_2") l.n_pre_ff2 = b;
+  else if (f == "post_feedforward_layernorm_1") l.n_post_ff1 = b;
+  else if (f == "post_feedforward_layernorm_2") l.n_post_ff2 = b;
+  else if (f == "q_norm") l.q_norm = b;
+  else if (f == "k_norm") l.k_norm = b;
+  else if (f == "layer_scalar") l.scalar = b;
+  else if (f == "cache_k") l.cache_k = b;
+  else if (f == "cache_v") l.cache_v = b;
+  return G4_OK;
+}
+
+extern "C" int g4_model_set_comm(g4_model* m, g4_comm* c) {
+  if (!m || !c) return fail(G4_ERR_ARG, "g4_model_set_comm: null argument");
+  if (c->world != m->world || c->rank != m->rank || c->hidden != m->H)
+    return fail(G4_ERR_ARG, "communicator rank/world/hidden do not match the model");
+  if (!c->open) return fail(G4_ERR_STATE, "communicator not opened (g4_comm_open)");
+  m->comm = c;
+  return G4_OK;
+}
+
+static Common make_common(const g4_model* m, int layer) {
+  Common c{};
+  c.ctrl = m->ctrl;
+  c.counters = m->counters;
+  for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = m->comm ? m->comm->peer[p] : nullptr;
+  c.rank = m->rank;
+  c.world = m->world;
+  c.xpayload = 2 * m->H;
+  c.H = m->H;
+  c.layer = layer;
+  c.nlayers = (int)m->L.size();
+  c.eps = m->cfg.rms_norm_eps;
+  return c;
+}
+
+static Tail make_tail(const g4_model* m, int layer) {
+  const LayerDev& l = m->L[layer];
+  Tail t{};
+  t.resmid = m->resmid;
+  t.mlp = m->mlp_out;
+  t.moe = m->moe_out;
+  t.pf1 = l.n_post_ff1;
+  t.pf2 = l.n_post_ff2;
+  t.pf = l.n_post_ff;
+  t.scalar = l.scalar;
+  t.layer = layer;
+  return t;
+}
+
+extern "C" int g4_model_finalize(g4_model* m) {
+  if (!m) return fail(G4_ERR_ARG, "g4_model_finalize: null model");
+  if (m->finalized) return G4_OK;
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  if (!m->embed || !m->final_norm || !m->ctrl || !m->tokens_in || !m->tokens_out || !m->logits)
+    return fail(G4_ERR_STATE, "missing embed/norm/control/tokens_in/tokens_out/logits");
+  for (size_t i = 0; i < m->L.size(); ++i) {
+    const LayerDev& l = m->L[i];
+    const void* req[] = {l.qkv, l.o, l.gate, l.up, l.down, l.router, l.router_scale, l.pes,
+                         l.exp_gu, l.exp_down, l.n_in, l.n_post_attn, l.n_pre_ff, l.n_post_ff,
+                         l.n_pre_ff2, l.n_post_ff1, l.n_post_ff2, l.q_norm, l.k_norm, l.scalar,
+                         l.cache_k, l.cache_v};
+    for (const void* p : req)
+      if (!p) return fail(G4_ERR_STATE, "layer %zu: missing tensor", i);
+  }
+  if (m->world > 1 && !m->comm) return fail(G4_ERR_STATE, "world > 1 needs g4_model_set_comm");
+  if (!m->comm) {
+    int rc = g4_comm_create(m->device, 0, 1, m->H, &m->own_comm);
+    if (rc) return rc;
+    m->comm = m->own_comm;
+  }
+  // ---- scratch (one allocation, carved)
+  const int H = m->H;
+  size_t max_rows = 0, max_ctx = 0, max_part = 0, max_nkv = 0;
+  for (const LayerDev& l : m->L) {
+    max_rows = std::max(max_rows, (size_t)(l.rows_q + l.rows_k + l.rows_v));
+    max_ctx = std::max(max_ctx, (size_t)l.rows_q);
+    max_part = std::max(max_part, (size_t)l.n_kv * l.nsplit * l.g * (l.d + 2));
+    max_nkv = std::max(max_nkv, (size_t)l.n_kv);
+  }
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off += (bytes + 255) / 256 * 256;
+    return o;
+  };
+  const size_t o_xres = take(H * 2), o_resmid = take(H * 2), o_h2 = take(H * 2);
+  const size_t o_qkv = take(max_rows * 2), o_ctx = take(max_ctx * 2);
+  const size_t o_mlpact = take((size_t)m->I_local * 2), o_moeact = take((size_t)m->topk * m->F_local * 2);
+  const size_t o_moeout = take(H * 2), o_oout = take(H * 4), o_mlpout = take(H * 4);
+  const size_t o_rl = take((size_t)m->E * 4), o_tw = take(kMaxTopK * 4), o_ti = take(kMaxTopK * 4);
+  const size_t o_part = take(max_part * 4), o_acnt = take(max_nkv * 4);
+  const size_t o_cv = take((size_t)m->nsm * 4), o_ci = take((size_t)m->nsm * 4);
+  const size_t o_cnt = take(kNumCounters * 4);
+  if (cudaMalloc(&m->scratch, off) != cudaSuccess)
+    return fail(G4_ERR_NOMEM, "scratch cudaMalloc(%zu) failed", off);
+  cudaMemset(m->scratch, 0, off);
+  char* s = m->scratch;
+  m->xres = (bf16_t*)(s + o_xres);
+  m->resmid = (bf16_t*)(s + o_resmid);
+  m->h2 = (bf16_t*)(s + o_h2);
+  m->qkv_raw = (bf16_t*)(s + o_qkv);
+  m->ctx = (bf16_t*)(s + o_ctx);
+  m->mlp_act = (bf16_t*)(s + o_mlpact);
+  m->moe_act = (bf16_t*)(s + o_moeact);
+  m->moe_out = (bf16_t*)(s + o_moeout);
+  m->o_out = (float*)(s + o_oout);
+  m->mlp_out = (float*)(s + o_mlpout);
+  m->router_logits = (float*)(s + o_rl);
+  m->top_w = (float*)(s + o_tw);
+  m->top_idx = (int*)(s + o_ti);
+  m->attn_part = (float*)(s + o_part);
+  m->attn_cnt = (int*)(s + o_acnt);
+  m->cand_v = (float*)(s + o_cv);
+  m->cand_i = (int*)(s + o_ci);
+  m->counters = (int*)(s + o_cnt);
+
+  // ---- plans
+  const g4_config& c = m->cfg;
+  const int nl = (int)m->L.size();
+  const float hinv = host_bf16_round(std::pow((float)H, -0.5f));
+  m->k1.resize(nl);
+  m->k2.resize(nl);
+  m->k3.resize(nl);
+  m->k4.resize(nl);
+  m->k5.resize(nl);
+  m->k6.resize(nl);
+  for (int i = 0; i < nl; ++i) {
+    const LayerDev& l = m->L[i];
+    const Common cm = make_common(m, i);
+    QkvOp& a = m->k1[i];
+    a = QkvOp{};
+    a.c = cm;
+    a.ctrl = m->ctrl;
+    a.nseg = 1;
+    a.seg[0] = SegDesc{l.rows_q + l.rows_k + l.rows_v, 1, H, 0};
+    a.xbytes[0] = H * 2;
+    a.xbytes[1] = 0;
+    a.w = l.qkv;
+    a.w_in = l.n_in;
+    a.out = m->qkv_raw;
+    a.xres = m->xres;
+    a.embed = m->embed;
+    a.tokens_in = m->tokens_in;
+    a.tokens_out = m->tokens_out;
+    a.vocab = c.vocab_size;
+    a.embed_scale = host_bf16_round(std::sqrt((float)H));
+    if (i > 0) a.tail = make_tail(m, i - 1);
+
+    AttnArgs& t = m->k2[i];
+    t = AttnArgs{};
+    t.qkv = m->qkv_raw;
+    t.q_norm = l.q_norm;
+    t.k_norm = l.k_norm;
+    t.cache_k = l.cache_k;
+    t.cache_v = l.cache_v;
+    t.inv_freq = nullptr;  // set below (per layer type table)
+    t.ctx = m->ctx;
+    t.part = m->attn_part;
+    t.counters = m->attn_cnt;
+    t.ctrl = m->ctrl;
+    t.pos_fixed = -1;
+    t.n_kv = l.n_kv;
+    t.g = l.g;
+    t.d = l.d;
+    t.nsplit = l.nsplit;
+    t.window = l.full ? 0 : c.sliding_window;
+    t.k_eq_v = l.k_eq_v;
+    t.max_len = m->max_len;
+    t.eps = c.rms_norm_eps;
+
+    OProjOp& o = m->k3[i];
+    o = OProjOp{};
+    o.c = cm;
+    o.ctrl = m->ctrl;
+    o.nseg = 1;
+    o.seg[0] = SegDesc{H, 1, l.rows_q, 0};
+    o.xbytes[0] = l.rows_q * 2;
+    o.w = l.o;
+    o.ctx = m->ctx;
+    o.out = m->o_out;
+    o.Kc = l.rows_q;
+
+    RouterMlpOp& r = m->k4[i];
+    r = RouterMlpOp{};
+    r.c = cm;
+    r.ctrl = m->ctrl;
+    r.nseg = 2;
+    r.seg[0] = SegDesc{m->E, 1, H, 0};
+    r.seg[1] = SegDesc{m->I_local, 2, H, 0};
+    r.xbytes[0] = H * 2;
+    r.xbytes[1] = H * 2;
+    r.o_in = m->o_out;
+    r.xres = m->xres;
+    r.n_post_attn = l.n_post_attn;
+    r.n_pre_ff = l.n_pre_ff;
+    r.n_pre_ff2 = l.n_pre_ff2;
+    r.router_scale = l.router_scale;
+    r.resmid = m->resmid;
+    r.h2 = m->h2;
+    r.router_w = l.router;
+    r.pes = l.pes;
+    r.gate = l.gate;
+    r.up = l.up;
+    r.router_logits = m->router_logits;
+    r.top_idx = m->top_idx;
+    r.top_w = m->top_w;
+    r.mlp_act = m->mlp_act;
+    r.E = m->E;
+    r.topk = m->topk;
+    r.hinv = hinv;
+
+    MoeUpOp& u = m->k5[i];
+    u = MoeUpOp{};
+    u.c = cm;
+    u.ctrl = m->ctrl;
+    u.nseg = 2;
+    u.seg[0] = SegDesc{H, 1, m->I_local, 0};
+    u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local};
+    u.xbytes[0] = H * 2;
+    u.xbytes[1] = m->I_local * 2;
+    u.h2 = m->h2;
+    u.mlp_act = m->mlp_act;
+    u.top_idx = m->top_idx;
+    u.top_w = m->top_w;
+    u.mlp_down = l.down;
+    u.gate_up = l.exp_gu;
+    u.mlp_out = m->mlp_out;
+    u.moe_act = m->moe_act;
+    u.I = m->I_local;
+    u.F = m->F_local;
+    u.topk = m->topk;
+
+    MoeDownOp& dn = m->k6[i];
+    dn = MoeDownOp{};
+    dn.c = cm;
+    dn.ctrl = m->ctrl;
+    dn.nseg = 1;
+    dn.seg[0] = SegDesc{H, m->topk, m->F_local, 0};
+    dn.xbytes[0] = m->topk * m->F_local * 2;
+    dn.moe_act = m->moe_act;
+    dn.top_idx = m->top_idx;
+    dn.down = l.exp_down;
+    dn.mlp_out = m->mlp_out;
+    dn.moe_out = m->moe_out;
+    dn.F = m->F_local;
+    dn.topk = m->topk;
+  }
+  {
+    LmHeadOp& lm = m->lm;
+    lm = LmHeadOp{};
+    lm.c = make_common(m, nl - 1);
+    lm.ctrl = m->ctrl;
+    lm.nseg = 1;
+    lm.seg[0] = SegDesc{m->V_local, 1, H, 0};
+    lm.xbytes[0] = H * 2;
+    lm.xbytes[1] = kConsumerThreads * 8;
+    lm.tail = make_tail(m, nl - 1);
+    lm.final_norm = m->final_norm;
+    lm.embed = m->embed;
+    lm.vbegin = m->vbegin;
+    lm.logits = m->logits;
+    lm.cand_v = m->cand_v;
+    lm.cand_i = m->cand_i;
+    lm.tokens_out = m->tokens_out;
+    lm.softcap = c.final_logit_softcapping;
+  }
+  // RoPE tables live in a small device buffer shared by all layers of a type.
+  {
+    const int dsl = c.head_dim, dfu = c.global_head_dim;
+    std::vector<float> tab(dsl / 2 + dfu / 2);
+    rope_inv_freq(dsl, c.rope_theta_sliding, 1.0, tab.data());
+    rope_inv_freq(dfu, c.rope_theta_full, c.rope_partial_rotary_factor_full, tab.data() + dsl / 2);
+    float* dev = nullptr;
+    if (cudaMalloc(&dev, tab.size() * 4) != cudaSuccess) return fail(G4_ERR_NOMEM, "rope table");
+    cudaMemcpy(dev, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
+    m->rope_tab = dev;
+    for (int i = 0; i < nl; ++i) m->k2[i].inv_freq = m->L[i].full ? dev + dsl / 2 : dev;
+  }
+  G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
+  m->finalized = true;
+  return G4_OK;
+}
+
+template <class Op>
+static int prepare_op(const Op& op) {
+  return prepare_kernel<Op>(gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1]}));
+}
+
+static int prepare_all(g4_model* m) {
+  int rc;
+  for (size_t i = 0; i < m->L.size(); ++i) {
+    if ((rc = prepare_op(m->k1[i])) || (rc = prepare_op(m->k3[i])) || (rc = prepare_op(m->k4[i])) ||
+        (rc = prepare_op(m->k5[i])) || (rc = prepare_op(m->k6[i])))
+      return rc;
+    if ((rc = prepare_attention(attn_smem_bytes(m->k2[i].g, m->k2[i].d)))) return rc;
+  }
+  return prepare_op(m->lm);
+}
+
+static int enqueue_step(g4_model* m, cudaStream_t st) {
+  const int nl = (int)m->L.size();
+  int rc;
+  for (int i = 0; i < nl; ++i) {
+    if ((rc = launch_gemv(m->k1[i], m->nsm, st))) return rc;
+    if ((rc = launch_attention(m->k2[i], st))) return rc;
+    if ((rc = launch_gemv(m->k3[i], m->nsm, st))) return rc;
+    if ((rc = launch_gemv(m->k4[i], m->nsm, st))) return rc;
+    if ((rc = launch_gemv(m->k5[i], m->nsm, st))) return rc;
+    if ((rc = launch_gemv(m->k6[i], m->nsm, st))) return rc;
+  }
+  return launch_gemv(m->lm, m->nsm, st);
+}
+
+extern "C" int g4_model_host_tokens(g4_model* m, int** host_ptr) {
+  if (!m || !host_ptr) return fail(G4_ERR_ARG, "g4_model_host_tokens: null argument");
+  if (!m->finalized) return fail(G4_ERR_STATE, "g4_model_host_tokens before finalize");
+  if (m->gexec) return fail(G4_ERR_STATE, "g4_model_host_tokens after graph capture");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  if (!m->tokens_host) {
+    G4_CUDA(cudaHostAlloc(&m->tokens_host, (size_t)(m->max_len + 1) * 4, cudaHostAllocMapped),
+            G4_ERR_NOMEM);
+    memset(m->tokens_host, 0xff, (size_t)(m->max_len + 1) * 4);
+    int* dptr = nullptr;
+    G4_CUDA(cudaHostGetDevicePointer((void**)&dptr, m->tokens_host, 0), G4_ERR_CUDA);
+    m->lm.tokens_host = dptr;
+  }
+  *host_ptr = m->tokens_host;
+  return G4_OK;
+}
+
+// Per-kernel-class timing: `steps` decode steps launched directly (not from the graph)
+// with a CUDA event recorded between consecutive kernels on `stream`; ms_out[c] gets
+// the summed duration of class c = 0 qkv, 1 attention, 2 o_proj, 3 router+MLP up,
+// 4 MLP down+experts up, 5 experts down, 6 lm_head+argmax.  The events serialise the
+// kernels (no programmatic overlap), so per-class times are upper bounds of their
+// share inside the graph.
+extern "C" int g4_model_profile(g4_model* m, void* stream, int steps, float* ms_out, int nclass) {
+  if (!m || !ms_out || nclass < 7 || steps < 1) return fail(G4_ERR_ARG, "g4_model_profile: bad argument");
+  if (!m->finalized) return fail(G4_ERR_STATE, "g4_model_profile before finalize");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int nl = (int)m->L.size();
+  const int per_step = 6 * nl + 1;
+  std::vector<cudaEvent_t> ev((size_t)per_step * steps + 1);
+  for (auto& e : ev) G4_CUDA(cudaEventCreate(&e), G4_ERR_CUDA);
+  int rc = G4_OK;
+  size_t k = 0;
+  G4_CUDA(cudaEventRecord(ev[k++], st), G4_ERR_CUDA);
+  for (int s = 0; s < steps && !rc; ++s) {
+    for (int i = 0; i < nl && !rc; ++i) {
+      if (!rc) rc = launch_gemv(m->k1[i], m->nsm, st);
+      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_attention(m->k2[i], st);
+      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_gemv(m->k3[i], m->nsm, st);
+      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_gemv(m->k4[i], m->nsm, st);
+      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_gemv(m->k5[i], m->nsm, st);
+      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_gemv(m->k6[i], m->nsm, st);
+      cudaEventRecord(ev[k++], st);
+    }
+    if (!rc) rc = launch_gemv(m->lm, m->nsm, st);
+    cudaEventRecord(ev[k++], st);
+  }
+  cudaStreamSynchronize(st);
+  for (int c = 0; c < nclass; ++c) ms_out[c] = 0.f;
+  if (!rc) {
+    for (size_t j = 1; j < k; ++j) {
+      float ms = 0.f;
+      cudaEventElapsedTime(&ms, ev[j - 1], ev[j]);
+      const size_t in_step = (j - 1) % per_step;
+      const int cls = in_step == (size_t)per_step - 1 ? 6 : (int)(in_step % 6);
+      ms_out[cls] += ms;
+    }
+  }
+  for (auto& e : ev) cudaEventDestroy(e);
+  return rc;
+}
+
+extern "C" int g4_model_kernel_count(const g4_model* m) {
+  return m ? 6 * (int)m->L.size() + 1 : 0;
+}
+
+extern "C" int g4_step(g4_model* m, void* stream) {
+  if (!m) return fail(G4_ERR_ARG, "g4_step: null model");
+  if (!m->finalized) return fail(G4_ERR_STATE, "g4_step before g4_model_finalize");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  return enqueue_step(m, static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int g4_graph_capture(g4_model* m, void* stream) {
+  if (!m) return fail(G4_ERR_ARG, "g4_graph_capture: null model");
+  if (!m->finalized) return fail(G4_ERR_STATE, "g4_graph_capture before g4_model_finalize");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (m->gexec) {
+    cudaGraphExecDestroy(m->gexec);
+    m->gexec = nullptr;
+  }
+  if (m->graph) {
+    cudaGraphDestroy(m->graph);
+    m->graph = nullptr;
+  }
+  // kernel attributes are set outside of the capture
+  int rc;
+  if ((rc = prepare_all(m))) return rc;
+  G4_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), G4_ERR_LAUNCH);
+  rc = enqueue_step(m, st);
+  cudaGraph_t g = nullptr;
+  cudaError_t e = cudaStreamEndCapture(st, &g);
+  if (rc) {
+    if (g) cudaGraphDestroy(g);
+    return rc;
+  }
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "EndCapture: %s", cudaGetErrorString(e));
+  m->graph = g;
+  G4_CUDA(cudaGraphInstantiate(&m->gexec, g, 0), G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+extern "C" int g4_graph_launch(g4_model* m, void* stream, int count) {
+  if (!m || !m->gexec) return fail(G4_ERR_STATE, "g4_graph_launch without a captured graph");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  for (int i = 0; i < count; ++i)
+    G4_CUDA(cudaGraphLaunch(m->gexec, static_cast<cudaStream_t>(stream)), G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+extern "C" int g4_model_status(g4_model* m, void* stream, int* status_out) {
+  if (!m || !m->ctrl) return fail(G4_ERR_ARG, "g4_model_status: no model/control block");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  G4_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), G4_ERR_CUDA);
+  int st = 0;
+  G4_CUDA(cudaMemcpy(&st, m->ctrl + G4_CTRL_STATUS, 4, cudaMemcpyDeviceToHost), G4_ERR_CUDA);
+  if (status_out) *status_out = st;
+  if (st) return fail(G4_ERR_TIMEOUT, "device status word 0x%x", st);
+  return G4_OK;
+}
+
+extern "C" int g4_model_destroy(g4_model* m) {
+  if (!m) return G4_OK;
+  cudaSetDevice(m->device);
+  if (m->gexec) cudaGraphExecDestroy(m->gexec);
+  if (m->graph) cudaGraphDestroy(m->graph);
+  if (m->rope_tab) cudaFree(m->rope_tab);
+  if (m->tokens_host) cudaFreeHost(m->tokens_host);
+  if (m->scratch) cudaFree(m->scratch);
+  if (m->own_comm) g4_comm_destroy(m->own_comm);
+  delete m;
+  return G4_OK;
+}
+
+// ------------------------------------------------------------------ block entry points
+namespace {
+struct BlockScratch {
+  char* base = nullptr;
+  size_t bytes = 0;
+};
+std::mutex g_block_mu;
+std::map<int, BlockScratch> g_block_scratch;
+
+// Per-device scratch shared by the block entry points (grown on demand, kept).
+char* block_scratch(size_t bytes) {
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(g_block_mu);
+  BlockScratch& b = g_block_scratch[dev];
+  if (b.bytes < bytes) {
+    if (b.base) {
+      cudaDeviceSynchronize();
+      cudaFree(b.base);
+    }
+    b.base = nullptr;
+    b.bytes = 0;
+    if (cudaMalloc(&b.base, bytes) != cudaSuccess) return nullptr;
+    cudaMemset(b.base, 0, bytes);
+    cudaDeviceSynchronize();
+    b.bytes = bytes;
+  }
+  return b.base;
+}
+}  // namespace
+
+extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, const void* k_norm,
+                                   void* cache_k, void* cache_v, int max_len, int n_q_heads,
+                                   int n_kv_heads, int head_dim, int k_eq_v, int pos, int window,
+                                   float theta, float partial_rotary, float eps, void* ctx,
+                                   void* stream) {
+  if (!qkv_raw || !q_norm || !k_norm || !cache_k || !cache_v || !ctx)
+    return fail(G4_ERR_ARG, "g4_attention_decode: null pointer");
+  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || head_dim % 64 || head_dim > kAttnMaxD ||
+      n_q_heads / n_kv_heads > kAttnMaxG)
+    return fail(G4_ERR_SHAPE, "g4_attention_decode: heads %d/%d dim %d unsupported", n_q_heads,
+                n_kv_heads, head_dim);
+  if (pos < 0 || pos >= max_len) return fail(G4_ERR_ARG, "g4_attention_decode: pos %d out of [0,%d)", pos, max_len);
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int g = n_q_heads / n_kv_heads;
+  const int max_live = window > 0 ? std::min(window, max_len) : max_len;
+  const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
+  if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
+  const size_t part = (size_t)n_kv_heads * nsplit * g * (head_dim + 2) * 4;
+  const size_t need = part + 256 + (size_t)n_kv_heads * 4 + 256 + G4_CTRL_WORDS * 4 + 256 + head_dim * 2;
+  char* s = block_scratch(need);
+  if (!s) return fail(G4_ERR_NOMEM, "g4_attention_decode: scratch allocation failed");
+  AttnArgs a{};
+  a.qkv = static_cast<const bf16_t*>(qkv_raw);
+  a.q_norm = static_cast<const bf16_t*>(q_norm);
+  a.k_norm = static_cast<const bf16_t*>(k_norm);
+  a.cache_k = static_cast<bf16_t*>(cache_k);
+  a.cache_v = static_cast<bf16_t*>(cache_v);
+  a.ctx = static_cast<bf16_t*>(ctx);
+  a.part = reinterpret_cast<float*>(s);
+  size_t off = (part + 255) / 256 * 256;
+  a.counters = reinterpret_cast<int*>(s + off);
+  off += ((size_t)n_kv_heads * 4 + 255) / 256 * 256;
+  a.ctrl = reinterpret_cast<int*>(s + off);
+  off += 256;
+  float* inv = reinterpret_cast<float*>(s + off);
+  std::vector<float> tab(head_dim / 2);
+  rope_inv_freq(head_dim, theta, partial_rotary, tab.data());
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  G4_CUDA(cudaMemcpyAsync(inv, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st), G4_ERR_CUDA);
+  G4_CUDA(cudaStreamSynchronize(st), G4_ERR_CUDA);
+  a.inv_freq = inv;
+  a.pos_fixed = pos;
+  a.n_kv = n_kv_heads;
+  a.g = g;
+  a.d = head_dim;
+  a.nsplit = nsplit;
+  a.window = window;
+  a.k_eq_v = k_eq_v;
+  a.max_len = max_len;
+  a.eps = eps;
+  return launch_attention(a, st);
+}
+
+// A standalone MoE block reuses the layer kernels K4 (router only), K5 (experts
+// gate|up only) and K6 (down + fused all-reduce push), plus a small reduce kernel for
+// world > 1 that plays the role of the next layer's prologue.
+__global__ void moe_block_reduce_kernel(Common c, bf16_t* out) {
+  pdl_wait();
+  __shared__ int ok;
+  const int use = site_use(c, kSiteFfn, c.layer);
+  if (threadIdx.x == 0) {
+    int good = 1;
+    const int tmo = ldcg_i(c.ctrl + G4_CTRL_TIMEOUT_US);
+    for (int src = 0; src < c.world && good; ++src)
+      good = wait_flag_geq(xflag(c, c.rank, kSiteFfn, use & 1, src), use + 1, tmo, c.ctrl + G4_CTRL_STATUS);
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) return;
+  for (int h = threadIdx.x; h < c.H; h += blockDim.x) {
+    float s = 0.f;
+    for (int src = 0; src < c.world; ++src) s += ldcg_f(xslot(c, c.rank, kSiteFfn, use & 1, src) + c.H + h);
+    out[h] = f2bf(s);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) atomicAdd(c.ctrl + G4_CTRL_STEP, 1);  // single block: no reader left
+}
+
+// Router-only prologue: the block input is already the MoE input h2.
+struct RouterOnlyOp : RouterMlpOp {
+  const bf16_t* x_in;
+  __device__ bool prologue(Smem& sm) const {
+    float o[kMaxPer];
+    float s = 0.f;
+    G4_FOR_H(c, i, h) {
+      o[i] = bf2f(x_in[h]);
+      s += o[i] * o[i];
+    }
+    const float r = rms_scale(block_sum(s, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
+    bf16_t* xr = reinterpret_cast<bf16_t*>(sm.x0);
+    G4_FOR_H(c, i, h) {
+      if (blockIdx.x == 0) h2[h] = f2bf(o[i]);
+      xr[h] = f2bf(rbf(rbf(rbf(o[i] * r) * bf2f(router_scale[h])) * hinv));
+    }
+    if (threadIdx.x == 0) sm.ints[kSmemRouterDone] = 0;
+    return true;
+  }
+};
+
+extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* comm, const void* x,
+                            const void* router_proj, const void* router_scale,
+                            const void* per_expert_scale, const void* gate_up, const void* down,
+                            void* out, int* top_idx, float* top_w, int* control, void* stream) {
+  if (!valid_cfg(cfg) || !x || !router_proj || !router_scale || !per_expert_scale || !gate_up ||
+      !down || !out || !control)
+    return fail(G4_ERR_ARG, "g4_moe_block: null argument");
+  if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
+    return fail(G4_ERR_ARG, "g4_moe_block: bad rank/world");
+  if (world > 1 && (!comm || !comm->open || comm->world != world || comm->rank != rank))
+    return fail(G4_ERR_ARG, "g4_moe_block: world > 1 needs an opened communicator");
+  const int H = cfg->hidden_size, E = cfg->num_experts, K = cfg->top_k_experts;
+  if (cfg->moe_intermediate_size % (8 * world) || H % 8 || H > kMaxPer * kConsumerThreads || K > kMaxTopK)
+    return fail(G4_ERR_SHAPE, "g4_moe_block: unsupported shape");
+  const int F = cfg->moe_intermediate_size / world;
+  int dev = 0, nsm = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  // scratch: h2[H] bf16, router logits[E], top (idx,w), act[K*F], counters
+  size_t off = 0;
+  auto take = [&](size_t b) {
+    size_t o = off;
+    off += (b + 255) / 256 * 256;
+    return o;
+  };
+  const size_t o_h2 = take((size_t)H * 2), o_rl = take((size_t)E * 4), o_ti = take(kMaxTopK * 4),
+               o_tw = take(kMaxTopK * 4), o_act = take((size_t)K * F * 2), o_cnt = take(kNumCounters * 4),
+               o_mlp = take((size_t)H * 4);
+  char* s = block_scratch(off);
+  if (!s) return fail(G4_ERR_NOMEM, "g4_moe_block: scratch allocation failed");
+  g4_comm* cm = comm;
+  g4_comm* tmp = nullptr;
+  if (!cm) {
+    int rc = g4_comm_create(dev, 0, 1, H, &tmp);
+    if (rc) return rc;
+    cm = tmp;
+  }
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  Common c{};
+  c.ctrl = control;
+  c.counters = reinterpret_cast<int*>(s + o_cnt);
+  for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = cm->peer[p];
+  c.rank = rank;
+  c.world = world;
+  c.xpayload = 2 * H;
+  c.H = H;
+  c.layer = 0;
+  c.nlayers = 1;
+  c.eps = cfg->rms_norm_eps;
+  int* tidx = top_idx ? top_idx : reinterpret_cast<int*>(s + o_ti);
+  float* tw = top_w ? top_w : reinterpret_cast<float*>(s + o_tw);
+
+  RouterOnlyOp r{};
+  r.c = c;
+  r.ctrl = control;
+  r.nseg = 1;
+  r.seg[0] = SegDesc{E, 1, H, 0};
+  r.xbytes[0] = H * 2;
+  r.xbytes[1] = 0;
+  r.x_in = static_cast<const bf16_t*>(x);
+  r.router_scale = static_cast<const bf16_t*>(router_scale);
+  r.h2 = reinterpret_cast<bf16_t*>(s + o_h2);
+  r.router_w = static_cast<const bf16_t*>(router_proj);
+  r.pes = static_cast<const bf16_t*>(per_expert_scale);
+  r.router_logits = reinterpret_cast<float*>(s + o_rl);
+  r.top_idx = tidx;
+  r.top_w = tw;
+  r.E = E;
+  r.topk = K;
+  r.hinv = host_bf16_round(std::pow((float)H, -0.5f));
+
+  MoeUpOp u{};
+  u.c = c;
+  u.ctrl = control;
+  u.nseg = 2;
+  u.seg[0] = SegDesc{0, 1, 8, 0};
+  u.seg[1] = SegDesc{K * F, 2, H, F};
+  u.xbytes[0] = H * 2;
+  u.xbytes[1] = 16;
+  u.h2 = r.h2;
+  u.mlp_act = r.h2;  // unused (segment 0 is empty)
+  u.top_idx = tidx;
+  u.top_w = tw;
+  u.mlp_down = static_cast<const bf16_t*>(down);
+  u.gate_up = static_cast<const bf16_t*>(gate_up);
+  u.mlp_out = reinterpret_cast<float*>(s + o_mlp);
+  u.moe_act = reinterpret_cast<bf16_t*>(s + o_act);
+  u.I = 8;
+  u.F = F;
+  u.topk = K;
+
+  MoeDownOp dn{};
+  dn.c = c;
+  dn.ctrl = control;
+  dn.nseg = 1;
+  dn.seg[0] = SegDesc{H, K, F, 0};
+  dn.xbytes[0] = K * F * 2;
+  dn.moe_act = u.moe_act;
+  dn.top_idx = tidx;
+  dn.down = static_cast<const bf16_t*>(down);
+  dn.mlp_out = u.mlp_out;
+  dn.moe_out = static_cast<bf16_t*>(out);
+  dn.F = F;
+  dn.topk = K;
+
+  int rc = G4_OK;
+  if (world > 1) cudaMemsetAsync(u.mlp_out, 0, (size_t)H * 4, st);
+  if (!rc) rc = launch_gemv(r, nsm, st);
+  if (!rc) rc = launch_gemv(u, nsm, st);
+  if (!rc) rc = launch_gemv(dn, nsm, st);
+  if (!rc && world > 1) {
+    cudaError_t e = launch_pdl(moe_block_reduce_kernel, dim3(1), dim3(512), 0, st, c,
+                               static_cast<bf16_t*>(out));
+    if (e != cudaSuccess) rc = fail(G4_ERR_LAUNCH, "reduce launch: %s", cudaGetErrorString(e));
+  }
+  if (tmp) {
+    cudaStreamSynchronize(st);
+    g4_comm_destroy(tmp);
+  }
+  return rc;
+}

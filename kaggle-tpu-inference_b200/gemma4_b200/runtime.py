@@ -1,0 +1,164 @@
+"""One rank's native decode model: device buffers, KV cache, communicator, CUDA graph.
+
+``DecodeModel`` owns the per-rank state the C ABI needs (control block, token rings,
+logits shard, KV cache per layer) and forwards the packed weight shards to
+``g4_model_set_tensor``.  A decode step consumes the token at ``control[POS]`` and
+writes the argmax of the next-token logits to ``tokens_out[pos + 1]``; prompts are
+consumed by the same step ("forced" tokens taken from ``tokens_in``).
+
+``Comm`` wraps ``g4_comm``: for world > 1 the 64-byte CUDA IPC handles of every rank's
+exchange buffer are swapped through the torch.distributed process group (host
+plumbing only); the all-reduces themselves are peer stores inside the kernels.
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import numpy as np
+import torch
+
+from . import _native as N
+from .config import TextConfig
+from .model import Mesh, local_cache_shapes
+
+
+class Comm:
+    def __init__(self, mesh: Mesh, hidden: int, group=None):
+        L = N.lib()
+        self.mesh = mesh
+        self.handle = ctypes.c_void_p()
+        N.check(L.g4_comm_create(mesh.device, mesh.rank, mesh.world, hidden, ctypes.byref(self.handle)),
+                "g4_comm_create")
+        if mesh.world > 1:
+            import torch.distributed as dist
+
+            buf = ctypes.create_string_buffer(64)
+            N.check(L.g4_comm_get_handle(self.handle, buf), "g4_comm_get_handle")
+            mine = bytes(buf.raw)
+            allh: list = [None] * mesh.world
+            dist.all_gather_object(allh, mine, group=group)
+            N.check(L.g4_comm_open(self.handle, b"".join(allh)), "g4_comm_open")
+            dist.barrier(group=group)
+
+    def close(self):
+        if self.handle:
+            N.lib().g4_comm_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+
+class DecodeModel:
+    """Per-rank native model.  ``shard``: native tensor name -> CUDA tensor."""
+
+    def __init__(self, cfg: TextConfig, shard: dict, mesh: Mesh, max_len: int,
+                 comm: Comm | None = None, timeout_us: int = 2_000_000):
+        L = N.lib()
+        self.cfg, self.mesh, self.max_len = cfg, mesh, max_len
+        self.device = torch.device("cuda", mesh.device)
+        dev = self.device
+        self.shard = shard  # keep the tensors alive: the library only holds pointers
+        self.ctrl = torch.zeros(N.CTRL_WORDS, dtype=torch.int32, device=dev)
+        self.ctrl[N.CTRL_TIMEOUT_US] = timeout_us
+        self.tokens_in = torch.zeros(max_len, dtype=torch.int32, device=dev)
+        self.tokens_out = torch.zeros(max_len + 1, dtype=torch.int32, device=dev)
+        self.v_local = cfg.vocab_size // mesh.world
+        self.logits = torch.zeros(self.v_local, dtype=torch.float32, device=dev)
+        self.cache_k, self.cache_v = [], []
+        for shape in local_cache_shapes(cfg, 1, max_len, mesh):
+            self.cache_k.append(torch.zeros(shape, dtype=torch.bfloat16, device=dev))
+            self.cache_v.append(torch.zeros(shape, dtype=torch.bfloat16, device=dev))
+
+        ccfg = N.G4Config.from_text_config(cfg)
+        full = bytes(1 if lt == "full_attention" else 0 for lt in cfg.layer_types)
+        self.handle = ctypes.c_void_p()
+        with torch.cuda.device(dev):
+            N.check(L.g4_model_create(ctypes.byref(ccfg), full, mesh.rank, mesh.world, max_len,
+                                      mesh.device, ctypes.byref(self.handle)), "g4_model_create")
+            for name, t in shard.items():
+                self._set(name, t)
+            for i in range(cfg.num_hidden_layers):
+                self._set(f"layers.{i}.cache_k", self.cache_k[i])
+                self._set(f"layers.{i}.cache_v", self.cache_v[i])
+            for name, t in (("control", self.ctrl), ("tokens_in", self.tokens_in),
+                            ("tokens_out", self.tokens_out), ("logits", self.logits)):
+                self._set(name, t)
+            self.comm = comm
+            if comm is not None:
+                N.check(L.g4_model_set_comm(self.handle, comm.handle), "g4_model_set_comm")
+            N.check(L.g4_model_finalize(self.handle), "g4_model_finalize")
+            hp = ctypes.POINTER(ctypes.c_int)()
+            N.check(L.g4_model_host_tokens(self.handle, ctypes.byref(hp)), "g4_model_host_tokens")
+            self.tokens_host = np.ctypeslib.as_array(hp, shape=(max_len + 1,))
+        self.graph_ready = False
+        self.kernels_per_step = L.g4_model_kernel_count(self.handle)
+
+    def _set(self, name: str, t: torch.Tensor):
+        if not t.is_contiguous():
+            raise ValueError(f"{name}: tensor must be contiguous")
+        N.check(N.lib().g4_model_set_tensor(self.handle, name.encode(), N.ptr(t),
+                                            t.numel() * t.element_size()), f"set_tensor({name})")
+
+    # ------------------------------------------------------------------ control
+    def reset(self, prompt_ids, write_logits: bool = False, clear_status: bool = True):
+        """Start a new sequence: position 0, the prompt as forced tokens."""
+        p = len(prompt_ids)
+        if p < 1 or p > self.max_len:
+            raise ValueError(f"prompt length {p} outside [1, {self.max_len}]")
+        self.tokens_in[:p].copy_(torch.as_tensor(list(prompt_ids), dtype=torch.int32))
+        self.ctrl[N.CTRL_POS] = 0
+        self.ctrl[N.CTRL_FORCED_LEN] = p
+        self.ctrl[N.CTRL_WRITE_LOGITS] = 1 if write_logits else 0
+        if clear_status:
+            self.ctrl[N.CTRL_STATUS] = 0
+
+    def set_write_logits(self, on: bool):
+        self.ctrl[N.CTRL_WRITE_LOGITS] = 1 if on else 0
+
+    def step(self, n: int = 1, use_graph: bool = True):
+        """Enqueue ``n`` decode steps on the current stream (asynchronous)."""
+        L = N.lib()
+        st = N.stream_handle()
+        with torch.cuda.device(self.device):
+            if use_graph:
+                if not self.graph_ready:
+                    self.capture()
+                N.check(L.g4_graph_launch(self.handle, st, n), "g4_graph_launch")
+            else:
+                for _ in range(n):
+                    N.check(L.g4_step(self.handle, st), "g4_step")
+
+    def capture(self):
+        with torch.cuda.device(self.device):
+            N.check(N.lib().g4_graph_capture(self.handle, N.stream_handle()), "g4_graph_capture")
+        self.graph_ready = True
+
+    KERNEL_CLASSES = ("qkv", "attention", "o_proj", "router_mlp_up", "mlp_down_experts_up",
+                      "experts_down", "lm_head_argmax")
+
+    def profile(self, steps: int) -> dict:
+        """Summed ms per kernel class over ``steps`` event-separated steps."""
+        out = (ctypes.c_float * 7)()
+        with torch.cuda.device(self.device):
+            N.check(N.lib().g4_model_profile(self.handle, N.stream_handle(), steps, out, 7),
+                    "g4_model_profile")
+        return dict(zip(self.KERNEL_CLASSES, [float(v) for v in out]))
+
+    def check_status(self):
+        """Synchronise and raise if a bounded device wait gave up."""
+        st = ctypes.c_int(0)
+        with torch.cuda.device(self.device):
+            rc = N.lib().g4_model_status(self.handle, N.stream_handle(), ctypes.byref(st))
+        if rc != N.G4_OK:
+            raise N.G4Error(rc, "decode step", f"device status word 0x{st.value:x}")
+
+    def close(self):
+        if self.handle:
+            torch.cuda.synchronize(self.device)
+            N.lib().g4_model_destroy(self.handle)
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):  # pragma: no cover - best effort
+        try:
+            self.close()
+        except Exception:
+            pass
