@@ -46,6 +46,7 @@ extern "C" {
 #define G4_STATUS_PEER_TIMEOUT 0x1  /* a cross-GPU flag never arrived                */
 #define G4_STATUS_MBAR_TIMEOUT 0x2  /* a local TMA/mbarrier wait never completed     */
 #define G4_STATUS_BAD_TOKEN 0x4     /* an input token id was outside [0, vocab)      */
+#define G4_STATUS_POS_OVERFLOW 0x8  /* a step ran at pos >= max_len (nothing written)  */
 
 /* Control block: int32[G4_CTRL_WORDS] in device memory, owned by the caller. */
 #define G4_CTRL_POS 0          /* position consumed by the next step                */
@@ -136,6 +137,10 @@ int g4_model_host_tokens(g4_model* model, int** host_ptr);
  * kernels; ms_out[0..6] = qkv, attention, o_proj, router+MLP up, MLP down+experts up,
  * experts down, lm_head+argmax (summed over steps).  Measurement only. */
 int g4_model_profile(g4_model* model, void* stream, int steps, float* ms_out, int nclass);
+/* Timeline tracer (only in a build with -DG4_TRACE, else G4_ERR_STATE): copies the
+ * device buffer of %globaltimer stamps, uint64[512 launches][4 sample CTAs][8 events]
+ * (launch id = 8*layer + kernel, lm_head = 8*num_layers), to host memory. */
+int g4_trace_read(void* host_dst, long long bytes);
 int g4_model_destroy(g4_model* model);
 
 /* ---------------------------------------------------------------- blocks

@@ -1,23 +1,25 @@
 // Split-KV decode attention for one query token (reference: gemma4_tpu/model.py:195-213).
 //
-// Grid = n_kv (local KV heads) x nsplit.  CTA (h, s) owns a contiguous slice of the
-// live key span of KV head h -- (pos-window, pos] for sliding layers, [0, pos] for
-// full layers -- instead of the reference's masked pass over the whole max_len
-// cache (the masked entries contribute exp(-1e30 - max) = 0 there, so skipping
-// them is exact).  Per CTA:
+// Grid = n_kv (local KV heads) x nsplit.  The live key span of KV head h --
+// (pos-window, pos] for sliding layers, [0, pos] for full layers, instead of the
+// reference's masked pass over the whole max_len cache (masked entries contribute
+// exp(-1e30 - max) = 0 there, so skipping them is exact) -- is cut into
+// n_active <= nsplit slices of at least kAttnMinKeys keys; CTAs past n_active exit
+// at once.  Per active CTA:
 //   1. q_norm RMSNorm + RoPE of the g query heads of KV head h (bf16 rounding points
 //      of model.py:198 / 70-78); the CTA whose slice holds `pos` also normalises,
 //      RoPEs and writes k (and v = rms(v_raw), or rms(k_raw) for k==v layers) into
 //      the cache (model.py:200-206).
-//   2. scores s = bf16(q.k) (scale 1.0, rounded to bf16 like the reference einsum)
-//      for all g heads, held in shared memory; local max m and sum l per head.
-//   3. acc = sum_j exp(s_j - m) v_j in fp32 (registers, then a shared-memory reduce).
-//   4. (m, l, acc) to the partial buffer; the last CTA of head h (atomic counter)
-//      merges the nsplit partials with the usual max-rescaling, divides by the total
-//      mass and rounds the context to bf16.
+//   2. every group of LK lanes owns a strided set of keys and runs an online softmax
+//      over them: scores s = bf16(q.k) (scale 1.0, rounded like the reference einsum),
+//      running max / mass, and acc += exp(s - m) v in fp32 registers; K and V of a
+//      batch of keys are loaded together.
+//   3. the lane groups are merged through shared memory into (m, l, acc[g][d]), which
+//      goes to the partial buffer; the last CTA of head h (atomic counter) merges the
+//      n_active partials with max-rescaling and rounds the context to bf16.
 // Difference from the reference: it rounds the normalised probabilities to bf16
-// before P.V; here P.V uses fp32 unnormalised weights and the context is rounded
-// once -- closer to exact arithmetic, within the tolerance the parity tests state.
+// before P.V; here P.V uses fp32 weights and the context is rounded once -- closer
+// to exact arithmetic, within the tolerance the parity tests state.
 #pragma once
 
 #include "g4_common.cuh"
@@ -27,6 +29,7 @@ namespace g4 {
 constexpr int kAttnThreads = 256;
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnMaxChunk = 1024;  // keys per CTA
+constexpr int kAttnMinKeys = 32;     // keys per CTA before another split is used
 constexpr int kAttnMaxG = 8;         // query heads per KV head handled by one CTA
 constexpr int kAttnMaxD = 512;
 constexpr int kAttnMaxSplit = 256;
@@ -45,193 +48,184 @@ struct AttnArgs {
   int pos_fixed;           // >= 0 overrides ctrl[POS]
   int n_kv, g, d, nsplit, window, k_eq_v, max_len;
   float eps;
+  int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
 
 __host__ __device__ inline int attn_smem_bytes(int g, int d) {
-  // scores [g][kAttnMaxChunk] + acc [g][d] + merge scales [g][kAttnMaxSplit] + misc
-  return g * kAttnMaxChunk * 4 + g * d * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64;
+  // acc [g][d] + lane-group stats [64][g] x 2 + merge scales [g][kAttnMaxSplit] + misc
+  return g * d * 4 + 2 * 64 * g * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64;
 }
 
-// Normalise (optionally with weight w) and optionally RoPE one vector of d elements
-// held as lane-strided registers v[i] = x[lane + 32 i]; results rounded to bf16.
-__device__ inline void warp_norm_rope(float* v, int d, const bf16_t* w, bool rope, int pos,
-                                      const float* inv_freq, float eps) {
-  const int lane = threadIdx.x & 31;
-  const int per = d / 32;
-  float ss = 0.f;
-  for (int i = 0; i < per; ++i) ss += v[i] * v[i];
-  ss = warp_sum(ss);
-  const float r = 1.0f / sqrtf(ss / (float)d + eps);
-  for (int i = 0; i < per; ++i) {
-    float o = v[i] * r;
-    if (w) o = o * bf2f(w[lane + 32 * i]);
-    v[i] = rbf(o);
-  }
-  if (!rope) return;
-  const int half = per / 2;  // element lane+32i pairs with lane+32(i±half)
-  float out[kAttnMaxD / 32];
-  for (int i = 0; i < per; ++i) {
-    const int e = lane + 32 * i;
-    const int fi = e < d / 2 ? e : e - d / 2;
-    const float ang = (float)pos * inv_freq[fi];
-    float sn, cs;
-    sincosf(ang, &sn, &cs);
-    const float rot = i < half ? -v[i + half] : v[i - half];
-    out[i] = rbf(rbf(v[i] * rbf(cs)) + rbf(rot * rbf(sn)));
-  }
-  for (int i = 0; i < per; ++i) v[i] = out[i];
-}
-
-// CPL = 16-byte chunks of a head vector per lane: 1 for d <= 256, 2 for d = 512.
-template <int CPL>
+// D = head dim, G = query heads per KV head on this rank.  Every loop below has a
+// compile-time trip count, so the code executed once per CTA stays small.
+template <int D, int G>
 __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  constexpr int PER = D / 32;                 // elements per lane of one head vector
+  constexpr int LK = D / 8 < 32 ? D / 8 : 32; // lanes per key
+  constexpr int KPW = 32 / LK;                // lane groups per warp
+  constexpr int CPL = (D / 8) / LK;           // 16-byte chunks per lane of a key row
+  constexpr int NGRP = kAttnWarps * KPW;      // lane groups per CTA
+  constexpr int HG = (CPL == 2 && G == 8) ? 4 : G;  // heads kept in registers at once
   extern __shared__ __align__(16) unsigned char attn_smem[];
-  float* sc = reinterpret_cast<float*>(attn_smem);                 // [g][kAttnMaxChunk]
-  float* acc_s = sc + a.g * kAttnMaxChunk;                          // [g][d]
-  float* scale_s = acc_s + a.g * a.d;                               // [g][kAttnMaxSplit]
-  float* ml = scale_s + a.g * kAttnMaxSplit;                        // m[g], l[g]
+  float* acc_s = reinterpret_cast<float*>(attn_smem);               // [G][D]
+  float* gm = acc_s + G * D;                                         // [NGRP][G]
+  float* gl = gm + 64 * G;                                           // [NGRP][G]
+  float* scale_s = gl + 64 * G;                                      // [G][kAttnMaxSplit]
+  float* ml = scale_s + G * kAttnMaxSplit;                           // M[G], L[G]
   int* flag = reinterpret_cast<int*>(ml + 2 * kAttnMaxG);
-  __shared__ __align__(16) bf16_t q_s[kAttnMaxG * kAttnMaxD];
+  __shared__ __align__(16) bf16_t q_s[G * D];
 
   pdl_trigger();
-  pdl_wait();
-
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hk = blockIdx.x / a.nsplit, sp = blockIdx.x % a.nsplit;
-  const int d = a.d, g = a.g, per = d / 32;
+  // constants before the dependency wait: norm weights, RoPE frequencies of this lane
+  float wq[PER], wk[PER], fr[PER];
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    const int e = lane + 32 * i;
+    wq[i] = bf2f(a.q_norm[e]);
+    wk[i] = bf2f(a.k_norm[e]);
+    fr[i] = a.inv_freq[e < D / 2 ? e : e - D / 2];
+  }
+  pdl_wait();
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 2);
+
   const int pos = a.pos_fixed >= 0 ? a.pos_fixed : ldcg_i(a.ctrl + G4_CTRL_POS);
+  if (pos < 0 || pos >= a.max_len) {  // never index the cache out of bounds
+    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
+    return;
+  }
   const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
   const int nlive = pos - start + 1;
-  const int chunk = (nlive + a.nsplit - 1) / a.nsplit;
+  int chunk = (nlive + a.nsplit - 1) / a.nsplit;
+  if (chunk < kAttnMinKeys) chunk = kAttnMinKeys;
+  const int n_active = (nlive + chunk - 1) / chunk;
+  if (sp >= n_active) return;
   const int k0 = start + sp * chunk;
   const int k1 = min(pos + 1, k0 + chunk);
-  int n = max(0, k1 - k0);
-  if (n > kAttnMaxChunk) {  // host sizes nsplit so this cannot happen; never overrun smem
+  int n = k1 - k0;
+  if (n > kAttnMaxChunk) {  // host sizes nsplit so this cannot happen; stay in bounds
     if (threadIdx.x == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_MBAR_TIMEOUT);
     n = kAttnMaxChunk;
   }
-  const size_t row_stride = (size_t)a.n_kv * d;
+  const size_t row_stride = (size_t)a.n_kv * D;
   const bf16_t* qraw = a.qkv;
-  const bf16_t* kraw = a.qkv + (size_t)a.n_kv * g * d;
-  const bf16_t* vraw = a.k_eq_v ? kraw : kraw + (size_t)a.n_kv * d;
+  const bf16_t* kraw = a.qkv + (size_t)a.n_kv * G * D;
+  const bf16_t* vraw = a.k_eq_v ? kraw : kraw + (size_t)a.n_kv * D;
 
-  // ---- 1. q heads (and the new k/v if this split holds pos)
+  // ---- 1. q heads (and the new k/v if this split holds pos): one warp per vector
   const bool has_new = (pos >= k0 && pos < k1);
-  const int nvec = g + (has_new ? 2 : 0);
-  for (int vi = warp; vi < nvec; vi += kAttnWarps) {
-    float v[kAttnMaxD / 32];
-    const bf16_t* src;
-    const bf16_t* w;
-    bool rope;
-    if (vi < g) {
-      src = qraw + ((size_t)hk * g + vi) * d;
-      w = a.q_norm;
-      rope = true;
-    } else if (vi == g) {
-      src = kraw + (size_t)hk * d;
-      w = a.k_norm;
-      rope = true;
-    } else {
-      src = vraw + (size_t)hk * d;
-      w = nullptr;
-      rope = false;
+  const int nvec = G + (has_new ? 2 : 0);
+  for (int vi = warp; vi < nvec; vi += kAttnWarps) {  // warp-uniform
+    const bf16_t* src = vi < G ? qraw + ((size_t)hk * G + vi) * D
+                               : (vi == G ? kraw + (size_t)hk * D : vraw + (size_t)hk * D);
+    const bool rope = vi <= G;
+    float v[PER];
+    float ss = 0.f;
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      v[i] = bf2f(ldcg_bf(src + lane + 32 * i));
+      ss += v[i] * v[i];
     }
-    for (int i = 0; i < per; ++i) v[i] = bf2f(ldcg_bf(src + lane + 32 * i));
-    warp_norm_rope(v, d, w, rope, pos, a.inv_freq, a.eps);
-    if (vi < g) {
-      for (int i = 0; i < per; ++i) q_s[vi * d + lane + 32 * i] = f2bf(v[i]);
+    ss = warp_sum(ss);
+    const float r = 1.0f / sqrtf(ss / (float)D + a.eps);
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      float o = v[i] * r;
+      if (vi < G) o = o * wq[i];
+      else if (vi == G) o = o * wk[i];
+      v[i] = rbf(o);
+    }
+    if (rope) {  // rotate-half RoPE in bf16 arithmetic (model.py:70-78)
+      float out[PER];
+#pragma unroll
+      for (int i = 0; i < PER; ++i) {
+        float sn, cs;
+        sincosf((float)pos * fr[i], &sn, &cs);
+        const float rot = i < PER / 2 ? -v[i + PER / 2] : v[i - PER / 2];
+        out[i] = rbf(rbf(v[i] * rbf(cs)) + rbf(rot * rbf(sn)));
+      }
+#pragma unroll
+      for (int i = 0; i < PER; ++i) v[i] = out[i];
+    }
+    if (vi < G) {
+#pragma unroll
+      for (int i = 0; i < PER; ++i) q_s[vi * D + lane + 32 * i] = f2bf(v[i]);
     } else {
-      bf16_t* dst = (vi == g ? a.cache_k : a.cache_v) + (size_t)pos * row_stride + (size_t)hk * d;
-      for (int i = 0; i < per; ++i) dst[lane + 32 * i] = f2bf(v[i]);
+      bf16_t* dst = (vi == G ? a.cache_k : a.cache_v) + (size_t)pos * row_stride + (size_t)hk * D;
+#pragma unroll
+      for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(v[i]);
     }
   }
-  for (int i = threadIdx.x; i < g * d; i += kAttnThreads) acc_s[i] = 0.f;
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) acc_s[i] = 0.f;
   __threadfence_block();
   __syncthreads();
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 3);
 
-  // ---- 2. scores
-  const int LK = min(32, d / 8);   // lanes per key
-  const int KPW = 32 / LK;         // keys per warp pass
+  // ---- 2. online softmax per lane group over its keys
   const int gi_lane = lane / LK, li = lane % LK;
-  uint4 qr[kAttnMaxG][CPL];
-#pragma unroll
-  for (int h = 0; h < kAttnMaxG; ++h)
-#pragma unroll
-    for (int c = 0; c < CPL; ++c)
-      if (h < g) qr[h][c] = reinterpret_cast<const uint4*>(q_s + h * d)[li + c * LK];
-  const bf16_t* kbase = a.cache_k + (size_t)hk * d;
-  for (int j0 = warp * KPW; j0 < n; j0 += kAttnWarps * KPW * 4) {
-    uint4 kr[4][CPL];
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int j = j0 + m * kAttnWarps * KPW + gi_lane;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c)
-        if (j < n) kr[m][c] = ldcg_u4(kbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
-    }
-#pragma unroll
-    for (int m = 0; m < 4; ++m) {
-      const int j = j0 + m * kAttnWarps * KPW + gi_lane;
-#pragma unroll
-      for (int h = 0; h < kAttnMaxG; ++h) {
-        if (h >= g) break;
-        float s = 0.f;
-        if (j < n) {
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) s = dot8(kr[m][c], qr[h][c], s);
-        }
-        s = group_sum(s, LK);
-        if (li == 0 && j < n) sc[h * kAttnMaxChunk + j] = rbf(s);
-      }
-    }
-  }
-  __syncthreads();
-
-  // ---- softmax statistics per head (one warp per head)
-  for (int h = warp; h < g; h += kAttnWarps) {
-    float m = -INFINITY;
-    for (int j = lane; j < n; j += 32) m = fmaxf(m, sc[h * kAttnMaxChunk + j]);
-    m = warp_max(m);
-    float l = 0.f;
-    for (int j = lane; j < n; j += 32) {
-      const float p = expf(sc[h * kAttnMaxChunk + j] - m);
-      sc[h * kAttnMaxChunk + j] = p;
-      l += p;
-    }
-    l = warp_sum(l);
-    if (lane == 0) {
-      ml[h] = m;
-      ml[kAttnMaxG + h] = l;
-    }
-  }
-  __syncthreads();
-
-  // ---- 3. P.V, heads in groups so the accumulators stay in registers
-  const bf16_t* vbase = a.cache_v + (size_t)hk * d;
-  constexpr int HG = CPL == 1 ? kAttnMaxG : kAttnMaxG / 2;
-  for (int h0 = 0; h0 < g; h0 += HG) {
-    float acc[HG][CPL * 8];
+  const int grp = warp * KPW + gi_lane;
+  const bf16_t* kbase = a.cache_k + (size_t)hk * D;
+  const bf16_t* vbase = a.cache_v + (size_t)hk * D;
+#pragma unroll 1
+  for (int h0 = 0; h0 < G; h0 += HG) {
+    uint4 qr[HG][CPL];
 #pragma unroll
     for (int h = 0; h < HG; ++h)
 #pragma unroll
+      for (int c = 0; c < CPL; ++c) qr[h][c] = reinterpret_cast<const uint4*>(q_s + (h0 + h) * D)[li + c * LK];
+    float m_run[HG], l_run[HG], acc[HG][CPL * 8];
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      m_run[h] = -INFINITY;
+      l_run[h] = 0.f;
+#pragma unroll
       for (int e = 0; e < CPL * 8; ++e) acc[h][e] = 0.f;
-    for (int j0 = warp * KPW; j0 < n; j0 += kAttnWarps * KPW * 4) {
-      uint4 vr[4][CPL];
+    }
+    // The loop bound is warp-uniform (jw depends on the warp only): every lane of a
+    // warp runs the same iterations, so the shuffles in group_sum always see a full
+    // warp.  Lane group gi_lane takes keys jw + gi_lane + m*NGRP.
+#pragma unroll 1
+    for (int jw = warp * KPW; jw < n; jw += NGRP * 4) {
+      const int j0 = jw + gi_lane;
+      uint4 kr[4][CPL], vr[4][CPL];
 #pragma unroll
       for (int m = 0; m < 4; ++m) {
-        const int j = j0 + m * kAttnWarps * KPW + gi_lane;
+        const int j = j0 + m * NGRP;
 #pragma unroll
-        for (int c = 0; c < CPL; ++c)
-          if (j < n) vr[m][c] = ldcg_u4(vbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
+        for (int c = 0; c < CPL; ++c) {
+          if (j < n) {
+            kr[m][c] = ldcg_u4(kbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
+            vr[m][c] = ldcg_u4(vbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
+          } else {
+            kr[m][c] = make_uint4(0, 0, 0, 0);
+            vr[m][c] = make_uint4(0, 0, 0, 0);
+          }
+        }
       }
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int j = j0 + m * kAttnWarps * KPW + gi_lane;
-        if (j >= n) continue;
+      for (int h = 0; h < HG; ++h) {
+        float sc[4];
+        float mx = m_run[h];
 #pragma unroll
-        for (int h = 0; h < HG; ++h) {
-          if (h0 + h >= g) break;
-          const float p = sc[(h0 + h) * kAttnMaxChunk + j];
+        for (int m = 0; m < 4; ++m) {
+          float s = 0.f;
+#pragma unroll
+          for (int c = 0; c < CPL; ++c) s = dot8(kr[m][c], qr[h][c], s);
+          s = rbf(group_sum(s, LK));
+          sc[m] = (j0 + m * NGRP < n) ? s : -INFINITY;
+          mx = fmaxf(mx, sc[m]);
+        }
+        const float corr = mx == -INFINITY ? 1.f : expf(m_run[h] - mx);
+        m_run[h] = mx;
+        l_run[h] *= corr;
+#pragma unroll
+        for (int e = 0; e < CPL * 8; ++e) acc[h][e] *= corr;
+#pragma unroll
+        for (int m = 0; m < 4; ++m) {
+          const float p = sc[m] == -INFINITY ? 0.f : expf(sc[m] - mx);
+          l_run[h] += p;
 #pragma unroll
           for (int c = 0; c < CPL; ++c) {
             const uint4 v = vr[m][c];
@@ -248,72 +242,93 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         }
       }
     }
-    // reduce over the key groups of the warp, then over warps (shared atomics)
+    // ---- 3. merge lane groups: CTA max, then rescaled shared-memory sums
+    if (li == 0) {
 #pragma unroll
-    for (int h = 0; h < HG; ++h) {
-      if (h0 + h >= g) break;
-#pragma unroll
-      for (int e = 0; e < CPL * 8; ++e) {
-        float v = acc[h][e];
-        for (int o = LK; o < 32; o <<= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-        if (gi_lane == 0) {
-          const int c = e / 8;
-          atomicAdd(&acc_s[(h0 + h) * d + (li + c * LK) * 8 + (e & 7)], v);
-        }
+      for (int h = 0; h < HG; ++h) {
+        gm[grp * G + h0 + h] = m_run[h];
+        gl[grp * G + h0 + h] = l_run[h];
       }
     }
+    __syncthreads();
+    if (threadIdx.x < HG) {
+      const int h = h0 + threadIdx.x;
+      float M = -INFINITY;
+      for (int q = 0; q < NGRP; ++q) M = fmaxf(M, gm[q * G + h]);
+      float L = 0.f;
+      for (int q = 0; q < NGRP; ++q) {
+        const float mq = gm[q * G + h];
+        L += mq == -INFINITY ? 0.f : gl[q * G + h] * expf(mq - M);
+      }
+      ml[h] = M;
+      ml[kAttnMaxG + h] = L;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int h = 0; h < HG; ++h) {
+      const float f = m_run[h] == -INFINITY ? 0.f : expf(m_run[h] - ml[h0 + h]);
+      if (f != 0.f) {
+#pragma unroll
+        for (int e = 0; e < CPL * 8; ++e)
+          atomicAdd(&acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)], acc[h][e] * f);
+      }
+    }
+    __syncthreads();
   }
-  __syncthreads();
 
-  // ---- 4. partials, then the last CTA of this KV head merges them
-  float* pbase = a.part + ((size_t)hk * a.nsplit + sp) * g * (d + 2);
-  for (int i = threadIdx.x; i < g * (d + 2); i += kAttnThreads) {
-    const int h = i / (d + 2), e = i % (d + 2);
-    float v;
-    if (e == 0) v = n > 0 ? ml[h] : -INFINITY;
-    else if (e == 1) v = n > 0 ? ml[kAttnMaxG + h] : 0.f;
-    else v = acc_s[h * d + e - 2];
-    pbase[i] = v;
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
+  // ---- 4. partials, then the last active CTA of this KV head merges them
+  float* pbase = a.part + ((size_t)hk * a.nsplit + sp) * G * (D + 2);
+  for (int i = threadIdx.x; i < G * (D + 2); i += kAttnThreads) {
+    const int h = i / (D + 2), e = i % (D + 2);
+    pbase[i] = e == 0 ? ml[h] : (e == 1 ? ml[kAttnMaxG + h] : acc_s[h * D + e - 2]);
   }
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int old = atomic_add_acq_rel_gpu(a.counters + hk, 1);
-    *flag = (old == a.nsplit - 1);
+    *flag = (old == n_active - 1);
   }
   __syncthreads();
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 5);
   if (!*flag) return;
   __threadfence();
-  const float* hbase = a.part + (size_t)hk * a.nsplit * g * (d + 2);
-  for (int h = warp; h < g; h += kAttnWarps) {
+  const float* hbase = a.part + (size_t)hk * a.nsplit * G * (D + 2);
+  for (int h = warp; h < G; h += kAttnWarps) {  // warp-uniform
     float M = -INFINITY;
-    for (int s = lane; s < a.nsplit; s += 32) {
-      const float* p = hbase + ((size_t)s * g + h) * (d + 2);
-      if (ldcg_f(p + 1) > 0.f) M = fmaxf(M, ldcg_f(p));
-    }
+    for (int s2 = lane; s2 < n_active; s2 += 32) M = fmaxf(M, ldcg_f(hbase + ((size_t)s2 * G + h) * (D + 2)));
     M = warp_max(M);
     float L = 0.f;
-    for (int s = lane; s < a.nsplit; s += 32) {
-      const float* p = hbase + ((size_t)s * g + h) * (d + 2);
-      const float l = ldcg_f(p + 1);
-      const float f = l > 0.f ? expf(ldcg_f(p) - M) : 0.f;
-      scale_s[h * kAttnMaxSplit + s] = f;
-      L += l * f;
+    for (int s2 = lane; s2 < n_active; s2 += 32) {
+      const float* p = hbase + ((size_t)s2 * G + h) * (D + 2);
+      const float f = expf(ldcg_f(p) - M);
+      scale_s[h * kAttnMaxSplit + s2] = f;
+      L += ldcg_f(p + 1) * f;
     }
     L = warp_sum(L);
     if (lane == 0) ml[h] = L;
   }
   __syncthreads();
-  for (int i = threadIdx.x; i < g * d; i += kAttnThreads) {
-    const int h = i / d, e = i % d;
+  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
+    const int h = i / D, e = i % D;
+    const float* src = hbase + (size_t)h * (D + 2) + 2 + e;
+    const size_t sstride = (size_t)G * (D + 2);
     float o = 0.f;
-    for (int s = 0; s < a.nsplit; ++s) {
-      const float f = scale_s[h * kAttnMaxSplit + s];
-      if (f != 0.f) o = fmaf(ldcg_f(hbase + ((size_t)s * g + h) * (d + 2) + 2 + e), f, o);
+    int s2 = 0;
+    for (; s2 + 4 <= n_active; s2 += 4) {
+      float v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = ldcg_f(src + (s2 + u) * sstride);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) o = fmaf(v[u], scale_s[h * kAttnMaxSplit + s2 + u], o);
     }
-    a.ctx[((size_t)hk * g + h) * d + e] = f2bf(o / ml[h]);
+    for (; s2 < n_active; ++s2) o = fmaf(ldcg_f(src + s2 * sstride), scale_s[h * kAttnMaxSplit + s2], o);
+    a.ctx[((size_t)hk * G + h) * D + e] = f2bf(o / ml[h]);
   }
-  if (threadIdx.x == 0) atomicExch(a.counters + hk, 0);
+  if (threadIdx.x == 0) {
+    atomicExch(a.counters + hk, 0);
+    G4_TRACE_EV(a.trace_id, 6);
+  }
 }
 
 }  // namespace g4

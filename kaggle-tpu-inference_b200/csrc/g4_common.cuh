@@ -221,6 +221,29 @@ __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int t
   return true;
 }
 
+// ------------------------------------------------------------------ timeline tracing
+// Built only with -DG4_TRACE (libg4b200_trace.so): %globaltimer stamps of selected
+// events for four sample CTAs (first, second, middle, last) of every launch whose
+// trace id is in [0, kTraceLaunches); read back with g4_trace_read.
+constexpr int kTraceLaunches = 512, kTraceCtas = 4, kTraceEvents = 8;
+#ifdef G4_TRACE
+__device__ unsigned long long g4_trace_buf[kTraceLaunches][kTraceCtas][kTraceEvents];
+__device__ __forceinline__ int trace_cta_slot() {
+  const int b = blockIdx.x, n = gridDim.x;
+  return b == 0 ? 0 : (b == 1 ? 1 : (b == n / 2 ? 2 : (b == n - 1 ? 3 : -1)));
+}
+#define G4_TRACE_EV(id, ev)                                                         \
+  do {                                                                              \
+    const int s_ = ::g4::trace_cta_slot();                                          \
+    if (s_ >= 0 && (id) >= 0 && (id) < ::g4::kTraceLaunches)                        \
+      ::g4::g4_trace_buf[(id)][s_][(ev)] = ::g4::globaltimer_ns();                  \
+  } while (0)
+#else
+#define G4_TRACE_EV(id, ev) \
+  do {                      \
+  } while (0)
+#endif
+
 // ------------------------------------------------------------------ block reductions
 // Sum of `v` over the first `nthreads` threads of the block (a multiple of 32), using
 // `red` (>= 32 floats of shared memory) and named barrier `bar_id`.

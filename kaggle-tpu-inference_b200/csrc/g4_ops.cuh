@@ -17,6 +17,12 @@
 //   LM LmHeadOp     combine(last layer), final norm, tied lm_head shard, softcap,
 //                   argmax (last CTA; argmax exchange across ranks) -> next token
 //
+// Prologue vectors (norm weights; the previous kernel's outputs at world 1) arrive in
+// the shared staging area by bulk copies (OpBase::cc / ac, offsets planned on the
+// host); the vector math runs as short loops over shared memory, thread t owning the
+// elements h = t, t+256, ...  Input vectors of the matrix products are fp32 in shared
+// memory (values exactly bf16) and move to registers in the engine.
+//
 // Rounding follows the reference's bf16 graph: every einsum output is rounded to bf16
 // after fp32 accumulation, norms run in fp32 and round once, elementwise products of
 // bf16 operands round after each product.  With world > 1 the row-parallel partial
@@ -28,7 +34,7 @@
 
 namespace g4 {
 
-constexpr int kMaxPer = 16;        // hidden elements per consumer thread (H <= 4096)
+constexpr int kMaxHidden = 4096;
 constexpr int kBarReduce = 2;      // named barrier id for prologue block reductions
 constexpr int kSites = 3;          // exchange sites: attention out, FFN out, argmax
 constexpr int kSiteAttn = 0, kSiteFfn = 1, kSiteArgmax = 2;
@@ -45,7 +51,6 @@ constexpr int kCntRouter = 0, kCntLm = 1, kCntSigAttn = 2, kCntSigFfn = 3;
 constexpr int kNumCounters = 32;
 
 struct Common {
-  int* ctrl;
   int* counters;
   char* xbase[kMaxWorld];  // exchange buffer of every rank, mapped in this process
   int rank, world;
@@ -63,9 +68,9 @@ __device__ inline float* xslot(const Common& c, int peer, int site, int parity, 
   return reinterpret_cast<float*>(c.xbase[peer] + kXFlagBytes) +
          (size_t)((site * 2 + parity) * kMaxWorld + src) * c.xpayload;
 }
-__device__ inline int read_step(const Common& c) { return ldcg_i(c.ctrl + G4_CTRL_STEP); }
-__device__ inline int site_use(const Common& c, int site, int layer) {
-  return site == kSiteArgmax ? read_step(c) : read_step(c) * c.nlayers + layer;
+__device__ inline int site_use(const int* ctrl, const Common& c, int site, int layer) {
+  const int step = ldcg_i(ctrl + G4_CTRL_STEP);
+  return site == kSiteArgmax ? step : step * c.nlayers + layer;
 }
 
 // All consumer threads: make this CTA's peer stores visible, then the last CTA of the
@@ -85,127 +90,150 @@ __device__ inline void xchg_signal(const Common& c, int site, int use, int count
 }
 
 // Thread 0 waits for every rank's flag of (site, use); result broadcast to consumers.
-__device__ inline bool xchg_wait(const Common& c, int site, int use, Smem& sm) {
+__device__ inline bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
   if (threadIdx.x == 0) {
     int ok = 1;
-    const int tmo = ldcg_i(c.ctrl + G4_CTRL_TIMEOUT_US);
+    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
     for (int src = 0; src < c.world && ok; ++src)
-      ok = wait_flag_geq(xflag(c, c.rank, site, use & 1, src), use + 1, tmo,
-                         c.ctrl + G4_CTRL_STATUS);
+      ok = wait_flag_geq(xflag(c, c.rank, site, use & 1, src), use + 1, tmo, ctrl + G4_CTRL_STATUS);
     sm.ints[kSmemOk] = ok;
   }
   named_bar(kBarReduce, kConsumerThreads);
   return sm.ints[kSmemOk] != 0;
 }
 
-// ------------------------------------------------------------------ vector helpers
-// Consumer thread t owns hidden elements h = t + 256*i.
-#define G4_FOR_H(c, i, h)                                      \
-  _Pragma("unroll") for (int i = 0; i < kMaxPer; ++i)          \
-    for (int h = (int)threadIdx.x + i * kConsumerThreads; h < (c).H && i < kMaxPer; h = (c).H)
-
-__device__ inline float rms_scale(float ss, int n, float eps) {
+// ------------------------------------------------------------------ staged vectors
+__device__ __forceinline__ const bf16_t* sbf(const Smem& sm, int off) {
+  return reinterpret_cast<const bf16_t*>(sm.stg + off);
+}
+__device__ __forceinline__ float* sf(const Smem& sm, int off) {
+  return reinterpret_cast<float*>(sm.stg + off);
+}
+__device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
   return 1.0f / sqrtf(ss / (float)n + eps);
+}
+__device__ __forceinline__ float bsum(float v, Smem& sm) {
+  return block_sum(v, sm.red, kConsumerThreads, kBarReduce);
 }
 
 // Output of layer `tail` from the previous kernels (model.py:312-322):
 //   h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2, h = rms(h1+h2)*pf, x = (resmid + h)*scalar.
+// Staged inputs: pf1/pf2/pf (bf16 constants); world 1: mlp (fp32), moe and resmid
+// (bf16).  Result x (bf16 values) in the fp32 temporary t0.
 struct Tail {
   const bf16_t* resmid;  // residual after attention (bf16 [H])
-  const float* mlp;      // world==1: dense-MLP down output (fp32 [H])
-  const bf16_t* moe;     // world==1: MoE output, per-expert bf16 sums (bf16 [H])
-  const bf16_t *pf1, *pf2, *pf, *scalar;
+  const bf16_t* scalar;  // layer_scalar [1]
   int layer;
+  int o_pf1, o_pf2, o_pf;   // staged constants
+  int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ inline bool layer_output(const Common& c, const Tail& t, float* x, Smem& sm) {
-  float m[kMaxPer], mo[kMaxPer];
+__device__ inline bool layer_output(int* ctrl, const Common& c, const Tail& t, int o_t0,
+                                    int o_t1, Smem& sm) {
+  float* t0 = sf(sm, o_t0);
+  float* t1 = sf(sm, o_t1);
+  const int H = c.H, tid = threadIdx.x;
   bool ok = true;
+  float s1 = 0.f, s2 = 0.f;
   if (c.world == 1) {
-    G4_FOR_H(c, i, h) {
-      m[i] = rbf(ldcg_f(t.mlp + h));
-      mo[i] = bf2f(ldcg_bf(t.moe + h));
+    const float* mlp = sf(sm, t.o_mlp);
+    const bf16_t* moe = sbf(sm, t.o_moe);
+    for (int h = tid; h < H; h += kConsumerThreads) {
+      const float m = rbf(mlp[h]), mo = bf2f(moe[h]);
+      t0[h] = m;
+      t1[h] = mo;
+      s1 += m * m;
+      s2 += mo * mo;
     }
   } else {
-    const int use = site_use(c, kSiteFfn, t.layer);
-    ok = xchg_wait(c, kSiteFfn, use, sm);
-    G4_FOR_H(c, i, h) {
+    const int use = site_use(ctrl, c, kSiteFfn, t.layer);
+    ok = xchg_wait(ctrl, c, kSiteFfn, use, sm);
+    for (int h = tid; h < H; h += kConsumerThreads) {
       float a = 0.f, b = 0.f;
       for (int src = 0; src < c.world; ++src) {
         const float* sl = xslot(c, c.rank, kSiteFfn, use & 1, src);
         a += ldcg_f(sl + h);
-        b += ldcg_f(sl + c.H + h);
+        b += ldcg_f(sl + H + h);
       }
-      m[i] = rbf(a);
-      mo[i] = rbf(b);
+      const float m = rbf(a), mo = rbf(b);
+      t0[h] = m;
+      t1[h] = mo;
+      s1 += m * m;
+      s2 += mo * mo;
     }
   }
-  float s1 = 0.f, s2 = 0.f;
-  G4_FOR_H(c, i, h) {
-    s1 += m[i] * m[i];
-    s2 += mo[i] * mo[i];
-  }
-  const float r1 = rms_scale(block_sum(s1, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-  const float r2 = rms_scale(block_sum(s2, sm.red + 32, kConsumerThreads, kBarReduce), c.H, c.eps);
+  const float r1 = rms_scale(bsum(s1, sm), H, c.eps);
+  const float r2 = rms_scale(bsum(s2, sm), H, c.eps);
+  const bf16_t *pf1 = sbf(sm, t.o_pf1), *pf2 = sbf(sm, t.o_pf2), *pf = sbf(sm, t.o_pf);
   float s3 = 0.f;
-  G4_FOR_H(c, i, h) {
-    const float h1 = rbf((m[i] * r1) * bf2f(t.pf1[h]));
-    const float h2 = rbf((mo[i] * r2) * bf2f(t.pf2[h]));
-    m[i] = rbf(h1 + h2);
-    s3 += m[i] * m[i];
+  for (int h = tid; h < H; h += kConsumerThreads) {
+    const float v = rbf(rbf((t0[h] * r1) * bf2f(pf1[h])) + rbf((t1[h] * r2) * bf2f(pf2[h])));
+    t0[h] = v;
+    s3 += v * v;
   }
-  const float r3 = rms_scale(block_sum(s3, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
+  const float r3 = rms_scale(bsum(s3, sm), H, c.eps);
   const float sc = bf2f(t.scalar[0]);
-  G4_FOR_H(c, i, h) {
-    const float hn = rbf((m[i] * r3) * bf2f(t.pf[h]));
-    const float xv = rbf(bf2f(ldcg_bf(t.resmid + h)) + hn);
-    x[i] = rbf(xv * sc);
+  for (int h = tid; h < H; h += kConsumerThreads) {
+    const float res = bf2f(sbf(sm, t.o_res)[h]);
+    t0[h] = rbf(rbf(res + rbf((t0[h] * r3) * bf2f(pf[h]))) * sc);
   }
   return ok;
 }
 
-// rms(x) * w rounded to bf16, stored as the bf16 input vector `dst` (smem).
-__device__ inline void norm_to_smem(const Common& c, const float* x, const bf16_t* w,
-                                    bf16_t* dst, Smem& sm) {
+// dst[h] = rbf(rms(x) * w[h]) for the fp32 vector x (smem), bf16 weight w (smem).
+__device__ inline void norm_into(const Common& c, const float* x, const bf16_t* w, float* dst,
+                                 Smem& sm) {
   float s = 0.f;
-  G4_FOR_H(c, i, h) s += x[i] * x[i];
-  const float r = rms_scale(block_sum(s, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-  G4_FOR_H(c, i, h) dst[h] = f2bf((x[i] * r) * bf2f(w[h]));
+  for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) s += x[h] * x[h];
+  const float r = rms_scale(bsum(s, sm), c.H, c.eps);
+  for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) dst[h] = rbf((x[h] * r) * bf2f(w[h]));
+}
+
+// Convert a staged bf16 vector of n elements into the fp32 input vector dst.
+__device__ inline void widen(const bf16_t* src, int n, float* dst) {
+  for (int i = threadIdx.x; i < n; i += kConsumerThreads) dst[i] = bf2f(src[i]);
+}
+
+__device__ inline bool wait_both(Smem& sm, int* ctrl) {
+  int* st = ctrl + G4_CTRL_STATUS;
+  const bool a = wait_copies(sm, 0, st);
+  const bool b = wait_copies(sm, 1, st);
+  return a && b;
 }
 
 // ================================================================== K1: q|k|v
-struct QkvOp {
+struct QkvOp : OpBase {
   Common c;
-  int* ctrl;  // == c.ctrl (the engine reads op.ctrl)
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
   const bf16_t* w;     // [rows, H]: q rows, k rows, v rows of this rank
-  const bf16_t* w_in;  // input_layernorm
   bf16_t* out;         // q|k|v projections (bf16 [rows])
   bf16_t* xres;        // layer input x (bf16 [H]), written by CTA 0
+  int o_win, o_t0, o_t1;
   // layer 0: token embedding
   const bf16_t* embed;  // replicated [V, H]
   const int* tokens_in;
   const int* tokens_out;
   int vocab;
+  int max_len;
   float embed_scale;  // bf16(sqrt(H)) as float
   Tail tail;          // layer > 0
 
+  __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int) const { return false; }
   __device__ void load_dependent(Smem&) const {}
   __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, w + (size_t)u0 * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
-  __device__ const bf16_t* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(sm.x0);
+  __device__ const float* xvec(int, int, const Smem& sm) const {
+    return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    float x[kMaxPer];
-    bool ok = true;
+    pdl_wait();
+    bool ok = wait_both(sm, ctrl);
+    float* t0 = sf(sm, o_t0);
     if (c.layer == 0) {
-      const int pos = ldcg_i(ctrl + G4_CTRL_POS);
+      int pos = ldcg_i(ctrl + G4_CTRL_POS);
+      if (pos < 0 || pos >= max_len) pos = 0;  // flagged by the attention / lm_head kernels
       const int forced = ldcg_i(ctrl + G4_CTRL_FORCED_LEN);
       int tok = pos < forced ? ldcg_i(tokens_in + pos) : ldcg_i(tokens_out + pos);
       if (tok < 0 || tok >= vocab) {
@@ -213,75 +241,67 @@ struct QkvOp {
         tok = 0;
       }
       const bf16_t* row = embed + (size_t)tok * c.H;
-      G4_FOR_H(c, i, h) x[i] = rbf(bf2f(row[h]) * embed_scale);
+      for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) t0[h] = rbf(bf2f(row[h]) * embed_scale);
     } else {
-      ok = layer_output(c, tail, x, sm);
+      ok = layer_output(ctrl, c, tail, o_t0, o_t1, sm) && ok;
     }
-    if (blockIdx.x == 0) G4_FOR_H(c, i, h) xres[h] = f2bf(x[i]);
-    norm_to_smem(c, x, w_in, reinterpret_cast<bf16_t*>(sm.x0), sm);
+    if (blockIdx.x == 0)
+      for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) xres[h] = f2bf(t0[h]);
+    norm_into(c, t0, sbf(sm, o_win), reinterpret_cast<float*>(sm.x0), sm);
     return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const float* res, Smem&, bool ok) const {
+  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     if (ok && (int)threadIdx.x < n) out[u0 + threadIdx.x] = f2bf(res[threadIdx.x]);
   }
   __device__ void finish(Smem&, bool) const {}
 };
 
 // ================================================================== K3: o_proj
-struct OProjOp {
+struct OProjOp : OpBase {
   Common c;
-  int* ctrl;
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
-  const bf16_t* w;    // [H, Kc]
-  const bf16_t* ctx;  // attention context (bf16 [Kc])
-  float* out;         // world==1: o_proj output (fp32 [H])
+  const bf16_t* w;  // [H, Kc]
+  float* out;       // world==1: o_proj output (fp32 [H])
   int Kc;
+  int o_ctx;        // staged ctx (bf16 [Kc])
 
+  __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int) const { return false; }
   __device__ void load_dependent(Smem&) const {}
   __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), bar, pol);
   }
-  __device__ const bf16_t* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(sm.x0);
+  __device__ const float* xvec(int, int, const Smem& sm) const {
+    return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    const uint4* src = reinterpret_cast<const uint4*>(ctx);
-    uint4* dst = reinterpret_cast<uint4*>(sm.x0);
-    for (int i = threadIdx.x; i < Kc / 8; i += kConsumerThreads) dst[i] = ldcg_u4(src + i);
-    return true;
+    pdl_wait();
+    const bool ok = wait_both(sm, ctrl);
+    widen(sbf(sm, o_ctx), Kc, reinterpret_cast<float*>(sm.x0));
+    return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const float* res, Smem& sm, bool ok) const {
+  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     if (!ok || (int)threadIdx.x >= n) return;
     const int u = u0 + threadIdx.x;
     const float v = res[threadIdx.x];
     if (c.world == 1) {
       out[u] = v;
     } else {
-      const int use = site_use(c, kSiteAttn, c.layer);
+      const int use = site_use(ctrl, c, kSiteAttn, c.layer);
       for (int p = 0; p < c.world; ++p) xslot(c, p, kSiteAttn, use & 1, c.rank)[u] = v;
     }
   }
   __device__ void finish(Smem&, bool) const {
-    if (c.world > 1) xchg_signal(c, kSiteAttn, site_use(c, kSiteAttn, c.layer), kCntSigAttn);
+    if (c.world > 1) xchg_signal(c, kSiteAttn, site_use(ctrl, c, kSiteAttn, c.layer), kCntSigAttn);
   }
 };
 
 // ================================================================== K4: router + MLP gate|up
-struct RouterMlpOp {
+struct RouterMlpOp : OpBase {
   Common c;
-  int* ctrl;
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
-  const float* o_in;     // world==1: o_proj output (fp32 [H])
-  const bf16_t* xres;    // layer input
-  const bf16_t *n_post_attn, *n_pre_ff, *n_pre_ff2, *router_scale;
-  bf16_t* resmid;        // out: residual after attention (CTA 0)
-  bf16_t* h2;            // out: MoE input (CTA 0)
+  const bf16_t* xres;      // layer input (world > 1 path reads it directly)
+  bf16_t* resmid;          // out: residual after attention (CTA 0)
+  bf16_t* h2;              // out: MoE input (CTA 0)
   const bf16_t* router_w;  // [E, H]
   const bf16_t* pes;       // per_expert_scale [E]
   const bf16_t* gate;      // [I_local, H]
@@ -292,7 +312,13 @@ struct RouterMlpOp {
   bf16_t* mlp_act;         // out [I_local]
   int E, topk;
   float hinv;              // bf16(H^-0.5) as float
+  int o_wpa, o_wff, o_wff2, o_wrs;  // staged constants
+  int o_o, o_x;                     // staged activations: o_proj out (fp32), x (bf16)
+  int o_t0, o_t1;
+  int block_mode;                   // 1: the input is already the MoE input (g4_moe_block)
+  const bf16_t* block_x;
 
+  __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int) const { return false; }
   __device__ void load_dependent(Smem&) const {}
   __device__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
@@ -305,56 +331,75 @@ struct RouterMlpOp {
       bulk_g2s(stage + bytes, up + (size_t)u0 * c.H, bytes, bar, pol);
     }
   }
-  __device__ const bf16_t* xvec(int s, int, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(s == 0 ? sm.x0 : sm.x1);
+  __device__ const float* xvec(int s, int, const Smem& sm) const {
+    return reinterpret_cast<const float*>(s == 0 ? sm.x0 : sm.x1);
   }
   __device__ bool prologue(Smem& sm) const {
-    float o[kMaxPer];
-    bool ok = true;
-    if (c.world == 1) {
-      G4_FOR_H(c, i, h) o[i] = rbf(ldcg_f(o_in + h));
+    pdl_wait();
+    bool ok = wait_both(sm, ctrl);
+    const int H = c.H, tid = threadIdx.x;
+    float* t0 = sf(sm, o_t0);
+    float* t1 = sf(sm, o_t1);
+    if (!block_mode) {
+      // attention output (summed over ranks), then x = residual + rms(attn)*post_attn
+      float s = 0.f;
+      if (c.world == 1) {
+        const float* o = sf(sm, o_o);
+        for (int h = tid; h < H; h += kConsumerThreads) {
+          const float v = rbf(o[h]);
+          t0[h] = v;
+          s += v * v;
+        }
+      } else {
+        const int use = site_use(ctrl, c, kSiteAttn, c.layer);
+        ok = xchg_wait(ctrl, c, kSiteAttn, use, sm) && ok;
+        for (int h = tid; h < H; h += kConsumerThreads) {
+          float a = 0.f;
+          for (int src = 0; src < c.world; ++src) a += ldcg_f(xslot(c, c.rank, kSiteAttn, use & 1, src) + h);
+          const float v = rbf(a);
+          t0[h] = v;
+          s += v * v;
+        }
+      }
+      const float r = rms_scale(bsum(s, sm), H, c.eps);
+      const bf16_t* wpa = sbf(sm, o_wpa);
+      float s2 = 0.f;
+      for (int h = tid; h < H; h += kConsumerThreads) {
+        const float xin = bf2f(sbf(sm, o_x)[h]);
+        const float v = rbf(xin + rbf((t0[h] * r) * bf2f(wpa[h])));  // model.py:303-304
+        t0[h] = v;
+        s2 += v * v;
+        if (blockIdx.x == 0) resmid[h] = f2bf(v);
+      }
+      // MLP input (model.py:310) and MoE input (model.py:315)
+      const float r2 = rms_scale(bsum(s2, sm), H, c.eps);
+      const bf16_t *wff = sbf(sm, o_wff), *wff2 = sbf(sm, o_wff2);
+      float* xm = reinterpret_cast<float*>(sm.x1);
+      for (int h = tid; h < H; h += kConsumerThreads) {
+        xm[h] = rbf((t0[h] * r2) * bf2f(wff[h]));
+        const float v = rbf((t0[h] * r2) * bf2f(wff2[h]));
+        t1[h] = v;
+        if (blockIdx.x == 0) h2[h] = f2bf(v);
+      }
     } else {
-      const int use = site_use(c, kSiteAttn, c.layer);
-      ok = xchg_wait(c, kSiteAttn, use, sm);
-      G4_FOR_H(c, i, h) {
-        float a = 0.f;
-        for (int src = 0; src < c.world; ++src) a += ldcg_f(xslot(c, c.rank, kSiteAttn, use & 1, src) + h);
-        o[i] = rbf(a);
+      for (int h = tid; h < H; h += kConsumerThreads) {
+        const float v = bf2f(ldcg_bf(block_x + h));
+        t1[h] = v;
+        if (blockIdx.x == 0) h2[h] = f2bf(v);
       }
     }
-    // x = residual + rms(attn)*post_attention_layernorm      (model.py:303-304)
-    float s = 0.f;
-    G4_FOR_H(c, i, h) s += o[i] * o[i];
-    float r = rms_scale(block_sum(s, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-    s = 0.f;
-    G4_FOR_H(c, i, h) {
-      const float a = rbf((o[i] * r) * bf2f(n_post_attn[h]));
-      o[i] = rbf(bf2f(ldcg_bf(xres + h)) + a);
-      s += o[i] * o[i];
-    }
-    if (blockIdx.x == 0) G4_FOR_H(c, i, h) resmid[h] = f2bf(o[i]);
-    // MLP input (model.py:310) and MoE input (model.py:315)
-    r = rms_scale(block_sum(s, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-    bf16_t* xm = reinterpret_cast<bf16_t*>(sm.x1);
-    float s2 = 0.f;
-    G4_FOR_H(c, i, h) {
-      xm[h] = f2bf((o[i] * r) * bf2f(n_pre_ff[h]));
-      const float v = rbf((o[i] * r) * bf2f(n_pre_ff2[h]));
-      if (blockIdx.x == 0) h2[h] = f2bf(v);
-      o[i] = v;
-      s2 += v * v;
-    }
     // router input: rms(h2) * scale * H^-1/2                 (model.py:225-226)
-    r = rms_scale(block_sum(s2, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-    bf16_t* xr = reinterpret_cast<bf16_t*>(sm.x0);
-    G4_FOR_H(c, i, h) {
-      const float v = rbf(rbf(rbf(o[i] * r) * bf2f(router_scale[h])) * hinv);
-      xr[h] = f2bf(v);
-    }
-    if (threadIdx.x == 0) sm.ints[kSmemRouterDone] = 0;
+    float s3 = 0.f;
+    for (int h = tid; h < H; h += kConsumerThreads) s3 += t1[h] * t1[h];
+    const float r3 = rms_scale(bsum(s3, sm), H, c.eps);
+    const bf16_t* wrs = sbf(sm, o_wrs);
+    float* xr = reinterpret_cast<float*>(sm.x0);
+    for (int h = tid; h < H; h += kConsumerThreads)
+      xr[h] = rbf(rbf(rbf(t1[h] * r3) * bf2f(wrs[h])) * hinv);
+    if (tid == 0) sm.ints[kSmemRouterDone] = 0;
     return ok;
   }
-  __device__ void epilogue(int s, int u0, int n, const float* res, Smem& sm, bool ok) const {
+  __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (s == 0) {
       if (ok && t < n) router_logits[u0 + t] = rbf(res[t]);
@@ -382,27 +427,40 @@ struct RouterMlpOp {
     if (!sm.ints[kSmemLast] || threadIdx.x >= 32) return;
     __threadfence();
     const int lane = threadIdx.x;
+    // Each lane holds logits e = lane + 32 j; softmax and the top-k selection run in
+    // registers (ties -> lower expert index, like a stable top-k).
+    constexpr int kPer = 8;  // E <= 256
+    float p[kPer];
     float mx = -INFINITY;
-    for (int e = lane; e < E; e += 32) mx = fmaxf(mx, ldcg_f(router_logits + e));
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      p[j] = e < E ? ldcg_f(router_logits + e) : -INFINITY;
+      mx = fmaxf(mx, p[j]);
+    }
     mx = warp_max(mx);
     float sum = 0.f;
-    for (int e = lane; e < E; e += 32) sum += expf(ldcg_f(router_logits + e) - mx);
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      const int e = lane + 32 * j;
+      p[j] = e < E ? expf(p[j] - mx) : 0.f;
+      sum += p[j];
+    }
     sum = warp_sum(sum);
-    // probabilities live in sm.flts[0..E) is too small for E=128: recompute per pass
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) p[j] = (lane + 32 * j) < E ? p[j] / sum : -INFINITY;
+    unsigned taken = 0;
     float wsum = 0.f;
-    int chosen[kMaxTopK];
-    float chosen_p[kMaxTopK];
+    int sel_i = 0;
+    float sel_p = 0.f;
     for (int k = 0; k < topk; ++k) {
       float bv = -INFINITY;
       int bi = 0x7fffffff;
-      for (int e = lane; e < E; e += 32) {
-        bool taken = false;
-        for (int q = 0; q < k; ++q) taken |= (chosen[q] == e);
-        if (taken) continue;
-        const float p = expf(ldcg_f(router_logits + e) - mx) / sum;
-        if (p > bv || (p == bv && e < bi)) {
-          bv = p;
-          bi = e;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        if (!((taken >> j) & 1u) && p[j] > bv) {  // j ascending: ties keep the lower e
+          bv = p[j];
+          bi = lane + 32 * j;
         }
       }
 #pragma unroll
@@ -414,28 +472,32 @@ struct RouterMlpOp {
           bi = oi;
         }
       }
-      chosen[k] = bi;
-      chosen_p[k] = bv;
+      if ((bi & 31) == lane) taken |= 1u << (bi >> 5);
+      if (lane == k) {
+        sel_i = bi;
+        sel_p = bv;
+      }
       wsum += bv;
     }
-    if (lane == 0) {
-      for (int k = 0; k < topk; ++k) {
-        top_idx[k] = chosen[k];
-        top_w[k] = (chosen_p[k] / wsum) * bf2f(pes[chosen[k]]);
-      }
+    if (lane < topk) {
+      top_idx[lane] = sel_i;
+      top_w[lane] = (sel_p / wsum) * bf2f(pes[sel_i]);
     }
   }
 };
 
 // ================================================================== K5: MLP down + expert gate|up
-struct MoeUpOp {
+__device__ inline void load_expert_ids(const int* top_idx, int topk, Smem& sm) {
+  int e[kMaxTopK];
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k) e[k] = k < topk ? ldcg_i(top_idx + k) : 0;  // all in flight
+#pragma unroll
+  for (int k = 0; k < kMaxTopK; ++k)
+    if (k < topk) sm.ints[kSmemExp + k] = e[k];
+}
+
+struct MoeUpOp : OpBase {
   Common c;
-  int* ctrl;
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
-  const bf16_t* h2;        // MoE input [H]
-  const bf16_t* mlp_act;   // [I_local]
   const int* top_idx;      // [K]
   const float* top_w;      // [K]
   const bf16_t* mlp_down;  // [H, I_local]
@@ -443,11 +505,11 @@ struct MoeUpOp {
   float* mlp_out;          // out: fp32 [H]
   bf16_t* moe_act;         // out: [K, F]
   int I, F, topk;
+  int o_h2, o_act;         // staged activations (bf16)
 
+  __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int s) const { return s == 1; }
-  __device__ void load_dependent(Smem& sm) const {
-    for (int k = 0; k < topk; ++k) sm.ints[kSmemExp + k] = ldcg_i(top_idx + k);
-  }
+  __device__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
   __device__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem& sm) const {
     if (s == 0) {
@@ -460,20 +522,18 @@ struct MoeUpOp {
       bulk_g2s(stage + bytes, gate_up + ((e * 2 + 1) * F + f0) * c.H, bytes, bar, pol);
     }
   }
-  __device__ const bf16_t* xvec(int s, int, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(s == 0 ? sm.x1 : sm.x0);
+  __device__ const float* xvec(int s, int, const Smem& sm) const {
+    return reinterpret_cast<const float*>(s == 0 ? sm.x1 : sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    uint4* d0 = reinterpret_cast<uint4*>(sm.x0);
-    uint4* d1 = reinterpret_cast<uint4*>(sm.x1);
-    for (int i = threadIdx.x; i < c.H / 8; i += kConsumerThreads)
-      d0[i] = ldcg_u4(reinterpret_cast<const uint4*>(h2) + i);
-    for (int i = threadIdx.x; i < I / 8; i += kConsumerThreads)
-      d1[i] = ldcg_u4(reinterpret_cast<const uint4*>(mlp_act) + i);
+    pdl_wait();
+    const bool ok = wait_both(sm, ctrl);
+    widen(sbf(sm, o_h2), c.H, reinterpret_cast<float*>(sm.x0));
+    widen(sbf(sm, o_act), I, reinterpret_cast<float*>(sm.x1));
     if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
-    return true;
+    return ok;
   }
-  __device__ void epilogue(int s, int u0, int n, const float* res, Smem& sm, bool ok) const {
+  __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     if (s == 0) {
@@ -489,23 +549,18 @@ struct MoeUpOp {
 };
 
 // ================================================================== K6: expert down
-struct MoeDownOp {
+struct MoeDownOp : OpBase {
   Common c;
-  int* ctrl;
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
-  const bf16_t* moe_act;  // [K, F]
   const int* top_idx;
   const bf16_t* down;     // [E, H, F]
   const float* mlp_out;   // world>1: this rank's MLP partial, sent with the MoE partial
   bf16_t* moe_out;        // world==1: bf16 [H]
   int F, topk;
+  int o_act;              // staged expert activations (bf16 [K, F])
 
+  __device__ int xmode(int) const { return 1; }  // warp w <-> expert slot w % topk
   __device__ bool seg_dependent(int) const { return true; }
-  __device__ void load_dependent(Smem& sm) const {
-    for (int k = 0; k < topk; ++k) sm.ints[kSmemExp + k] = ldcg_i(top_idx + k);
-  }
+  __device__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
   __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem& sm) const {
     const uint32_t bytes = (uint32_t)(n * F * 2);
@@ -514,16 +569,16 @@ struct MoeDownOp {
       bulk_g2s(stage + (size_t)k * bytes, down + (e * c.H + u0) * F, bytes, bar, pol);
     }
   }
-  __device__ const bf16_t* xvec(int, int j, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(sm.x0) + j * F;
+  __device__ const float* xvec(int, int j, const Smem& sm) const {
+    return reinterpret_cast<const float*>(sm.x0) + j * F;
   }
   __device__ bool prologue(Smem& sm) const {
-    uint4* d0 = reinterpret_cast<uint4*>(sm.x0);
-    for (int i = threadIdx.x; i < topk * F / 8; i += kConsumerThreads)
-      d0[i] = ldcg_u4(reinterpret_cast<const uint4*>(moe_act) + i);
-    return true;
+    pdl_wait();
+    const bool ok = wait_both(sm, ctrl);
+    widen(sbf(sm, o_act), topk * F, reinterpret_cast<float*>(sm.x0));
+    return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const float* res, Smem&, bool ok) const {
+  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     const int u = u0 + t;
@@ -536,7 +591,7 @@ struct MoeDownOp {
       float sacc = 0.f;
       for (int k = 0; k < topk; ++k) sacc += res[k * n + t];
       const float mv = ldcg_f(mlp_out + u);
-      const int use = site_use(c, kSiteFfn, c.layer);
+      const int use = site_use(ctrl, c, kSiteFfn, c.layer);
       for (int p = 0; p < c.world; ++p) {
         float* sl = xslot(c, p, kSiteFfn, use & 1, c.rank);
         sl[u] = mv;
@@ -545,41 +600,40 @@ struct MoeDownOp {
     }
   }
   __device__ void finish(Smem&, bool) const {
-    if (c.world > 1) xchg_signal(c, kSiteFfn, site_use(c, kSiteFfn, c.layer), kCntSigFfn);
+    if (c.world > 1) xchg_signal(c, kSiteFfn, site_use(ctrl, c, kSiteFfn, c.layer), kCntSigFfn);
   }
 };
 
 // ================================================================== LM head + argmax
-struct LmHeadOp {
+struct LmHeadOp : OpBase {
   Common c;
-  int* ctrl;
-  int nseg;
-  SegDesc seg[kMaxSeg];
-  int xbytes[2];
   Tail tail;
-  const bf16_t* final_norm;
-  const bf16_t* embed;  // replicated [V, H]; this rank reads rows [vbegin, vbegin+V_local)
+  int o_wn, o_t0, o_t1;  // staged final norm weight, temporaries
+  const bf16_t* embed;   // replicated [V, H]; this rank reads rows [vbegin, vbegin+V_local)
   int vbegin;
-  float* logits;        // [V_local] fp32 (written when control[WRITE_LOGITS] != 0)
-  float* cand_v;        // scratch [gridDim]
-  int* cand_i;          // scratch [gridDim]
-  int* tokens_out;      // [max_len + 1]
-  int* tokens_host;     // optional mapped pinned host mirror of tokens_out
-  float softcap;        // <= 0: none
+  float* logits;         // [V_local] fp32 (written when control[WRITE_LOGITS] != 0)
+  float* cand_v;         // scratch [gridDim]
+  int* cand_i;           // scratch [gridDim]
+  int* tokens_out;       // [max_len + 1]
+  int* tokens_host;      // optional mapped pinned host mirror of tokens_out
+  int max_len;
+  float softcap;         // <= 0: none
 
+  __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int) const { return false; }
   __device__ void load_dependent(Smem&) const {}
   __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
-  __device__ const bf16_t* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const bf16_t*>(sm.x0);
+  __device__ const float* xvec(int, int, const Smem& sm) const {
+    return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    float x[kMaxPer];
-    bool ok = layer_output(c, tail, x, sm);
-    norm_to_smem(c, x, final_norm, reinterpret_cast<bf16_t*>(sm.x0), sm);
+    pdl_wait();
+    bool ok = wait_both(sm, ctrl);
+    ok = layer_output(ctrl, c, tail, o_t0, o_t1, sm) && ok;
+    norm_into(c, sf(sm, o_t0), sbf(sm, o_wn), reinterpret_cast<float*>(sm.x0), sm);
     float* bv = reinterpret_cast<float*>(sm.x1);
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;
     bv[threadIdx.x] = -INFINITY;
@@ -588,7 +642,7 @@ struct LmHeadOp {
     named_bar(kBarReduce, kConsumerThreads);
     return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const float* res, Smem& sm, bool ok) const {
+  __device__ void epilogue(int, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     const int u = u0 + t;
@@ -633,13 +687,12 @@ struct LmHeadOp {
       }
     }
     named_bar(kBarReduce, kConsumerThreads);
-    if (!sm.ints[kSmemLast] || threadIdx.x != 0) return;
-    // last CTA: reduce the per-CTA candidates in CTA order (deterministic)
+    if (!sm.ints[kSmemLast] || threadIdx.x >= 32) return;
+    // last CTA: one warp reduces the per-CTA candidates (max value, then lowest index)
     __threadfence();
-    atomicExch(c.counters + kCntLm, 0);
     float v = -INFINITY;
     int ix = 0x7fffffff;
-    for (int b = 0; b < (int)gridDim.x; ++b) {
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += 32) {
       const float cv = ldcg_f(cand_v + b);
       const int ci = ldcg_i(cand_i + b);
       if (cv > v || (cv == v && ci < ix)) {
@@ -647,9 +700,20 @@ struct LmHeadOp {
         ix = ci;
       }
     }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+      const float ov = __shfl_xor_sync(0xffffffffu, v, o);
+      const int oi = __shfl_xor_sync(0xffffffffu, ix, o);
+      if (ov > v || (ov == v && oi < ix)) {
+        v = ov;
+        ix = oi;
+      }
+    }
+    if (threadIdx.x != 0) return;
+    atomicExch(c.counters + kCntLm, 0);
     int token = ix == 0x7fffffff ? 0 : vbegin + ix;
     if (c.world > 1) {
-      const int use = site_use(c, kSiteArgmax, 0);
+      const int use = site_use(ctrl, c, kSiteArgmax, 0);
       for (int p = 0; p < c.world; ++p) {
         float* sl = xslot(c, p, kSiteArgmax, use & 1, c.rank);
         sl[0] = v;
@@ -675,6 +739,10 @@ struct LmHeadOp {
       token = gi == 0x7fffffff ? 0 : gi;
     }
     const int pos = ldcg_i(ctrl + G4_CTRL_POS);
+    if (pos < 0 || pos >= max_len) {  // the step consumed no valid position
+      atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
+      return;
+    }
     tokens_out[pos + 1] = token;
     if (tokens_host) tokens_host[pos + 1] = token;
     ctrl[G4_CTRL_POS] = pos + 1;

@@ -150,7 +150,7 @@ static cudaError_t launch_pdl(Kernel k, dim3 grid, dim3 block, size_t smem, cuda
   return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
-template <class Op>
+template <class Op, int CPLM>
 static int prepare_kernel(int smem) {
   static std::mutex mu;
   static std::map<int, int> done;  // device -> max smem configured
@@ -158,46 +158,85 @@ static int prepare_kernel(int smem) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (done[dev] >= smem) return G4_OK;
-  G4_CUDA(cudaFuncSetAttribute(gemv_kernel<Op>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
+  G4_CUDA(cudaFuncSetAttribute(gemv_kernel<Op, CPLM>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
           G4_ERR_LAUNCH);
   done[dev] = smem;
   return G4_OK;
 }
 
-static int prepare_attention(int smem) {
+// Register bucket (max input chunks per lane) of an operator's launch.
+template <class Op>
+static int op_cplm(const Op& op) {
+  int m = 1;
+  for (int s = 0; s < op.nseg; ++s)
+    if (op.seg[s].units > 0 && seg_cpl(op.seg[s]) > m) m = seg_cpl(op.seg[s]);
+  return m <= 4 ? 4 : (m <= 8 ? 8 : (m <= 12 ? 12 : (m <= 16 ? 16 : 0)));
+}
+
+// The attention kernel instantiation for (head dim, query heads per KV head).
+typedef void (*AttnKernel)(AttnArgs);
+template <int D>
+static AttnKernel attn_kernel_for_g(int g) {
+  switch (g) {
+    case 1: return attn_decode_kernel<D, 1>;
+    case 2: return attn_decode_kernel<D, 2>;
+    case 4: return attn_decode_kernel<D, 4>;
+    case 8: return attn_decode_kernel<D, 8>;
+    default: return nullptr;
+  }
+}
+static AttnKernel attn_kernel_for(int d, int g) {
+  switch (d) {
+    case 64: return attn_kernel_for_g<64>(g);
+    case 128: return attn_kernel_for_g<128>(g);
+    case 256: return attn_kernel_for_g<256>(g);
+    case 512: return attn_kernel_for_g<512>(g);
+    default: return nullptr;
+  }
+}
+
+static int prepare_attention(int d, int g) {
   static std::mutex mu;
-  static std::map<int, int> done;
+  static std::map<std::pair<int, int>, int> done;
   int dev = 0;
   cudaGetDevice(&dev);
+  AttnKernel k = attn_kernel_for(d, g);
+  if (!k) return fail(G4_ERR_SHAPE, "attention: head_dim %d with %d query heads per KV head", d, g);
+  const int smem = attn_smem_bytes(g, d);
   std::lock_guard<std::mutex> lock(mu);
-  if (done[dev] >= smem) return G4_OK;
-  G4_CUDA(cudaFuncSetAttribute(attn_decode_kernel<1>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          G4_ERR_LAUNCH);
-  G4_CUDA(cudaFuncSetAttribute(attn_decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem),
-          G4_ERR_LAUNCH);
-  done[dev] = smem;
+  int& have = done[{dev, d * 16 + g}];
+  if (have >= smem) return G4_OK;
+  G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), G4_ERR_LAUNCH);
+  have = smem;
+  return G4_OK;
+}
+
+template <class Op, int CPLM>
+static int launch_gemv_t(const Op& op, int grid, cudaStream_t st) {
+  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes});
+  int rc = prepare_kernel<Op, CPLM>(smem);
+  if (rc) return rc;
+  cudaError_t e = launch_pdl(gemv_kernel<Op, CPLM>, dim3(grid), dim3(kGemvThreads), smem, st, op);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "gemv launch: %s", cudaGetErrorString(e));
   return G4_OK;
 }
 
 template <class Op>
 static int launch_gemv(const Op& op, int grid, cudaStream_t st) {
-  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1]});
-  int rc = prepare_kernel<Op>(smem);
-  if (rc) return rc;
-  cudaError_t e = launch_pdl(gemv_kernel<Op>, dim3(grid), dim3(kGemvThreads), smem, st, op);
-  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "gemv launch: %s", cudaGetErrorString(e));
-  return G4_OK;
+  switch (op_cplm(op)) {
+    case 4: return launch_gemv_t<Op, 4>(op, grid, st);
+    case 8: return launch_gemv_t<Op, 8>(op, grid, st);
+    case 12: return launch_gemv_t<Op, 12>(op, grid, st);
+    case 16: return launch_gemv_t<Op, 16>(op, grid, st);
+    default: return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank");
+  }
 }
 
 static int launch_attention(const AttnArgs& a, cudaStream_t st) {
-  const int smem = attn_smem_bytes(a.g, a.d);
-  int rc = prepare_attention(smem);
+  int rc = prepare_attention(a.d, a.g);
   if (rc) return rc;
-  cudaError_t e;
-  if (a.d <= 256)
-    e = launch_pdl(attn_decode_kernel<1>, dim3(a.n_kv * a.nsplit), dim3(kAttnThreads), smem, st, a);
-  else
-    e = launch_pdl(attn_decode_kernel<2>, dim3(a.n_kv * a.nsplit), dim3(kAttnThreads), smem, st, a);
+  cudaError_t e = launch_pdl(attn_kernel_for(a.d, a.g), dim3(a.n_kv * a.nsplit), dim3(kAttnThreads),
+                             attn_smem_bytes(a.g, a.d), st, a);
   if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(e));
   return G4_OK;
 }
@@ -290,11 +329,12 @@ extern "C" int g4_model_create(const g4_config* cfg, const unsigned char* layer_
   const int G = world;
   if (!c.enable_moe_block) return fail(G4_ERR_SHAPE, "only MoE (enable_moe_block) models are supported");
   if (c.hidden_size % 8 != 0) return fail(G4_ERR_SHAPE, "hidden_size must be a multiple of 8");
-  if (c.hidden_size > kMaxPer * kConsumerThreads) return fail(G4_ERR_SHAPE, "hidden_size > 4096");
+  if (c.hidden_size > kMaxHidden) return fail(G4_ERR_SHAPE, "hidden_size > 4096");
   if (c.intermediate_size % (8 * G) || c.moe_intermediate_size % (8 * G) || c.vocab_size % G)
     return fail(G4_ERR_SHAPE, "intermediate / moe_intermediate / vocab not divisible by 8*world");
-  if (c.top_k_experts > kMaxTopK || c.top_k_experts > c.num_experts)
-    return fail(G4_ERR_SHAPE, "top_k_experts > %d", kMaxTopK);
+  if (c.top_k_experts > kMaxTopK || c.top_k_experts > c.num_experts || c.num_experts > 256 ||
+      kConsumerWarps % c.top_k_experts)
+    return fail(G4_ERR_SHAPE, "top_k_experts must divide %d; num_experts <= 256", kConsumerWarps);
   G4_CUDA(cudaSetDevice(device), G4_ERR_CUDA);
   g4_model* m = new g4_model();
   m->cfg = c;
@@ -329,7 +369,7 @@ extern "C" int g4_model_create(const g4_config* cfg, const unsigned char* layer_
       l.n_kv = kv;
       l.g = gfull / G;
     }
-    if (l.g > kAttnMaxG || l.d % 64 || l.d > kAttnMaxD) {
+    if (l.g > kAttnMaxG || (l.g & (l.g - 1)) || (l.d != 64 && l.d != 128 && l.d != 256 && l.d != 512)) {
       delete m;
       return fail(G4_ERR_SHAPE, "layer %d: head_dim %d / group %d unsupported", i, l.d, l.g);
     }
@@ -343,6 +383,12 @@ extern "C" int g4_model_create(const g4_config* cfg, const unsigned char* layer_
       return fail(G4_ERR_SHAPE, "layer %d: context %d too long for the split-KV limits", i, max_len);
     }
   }
+  for (const LayerDev& l : m->L)
+    if (l.rows_q > 4096 || c.hidden_size > 4096 || m->I_local > 4096) {
+      delete m;
+      return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank "
+                                "(o_proj of %d heads x %d at world %d)", l.n_kv * l.g, l.d, world);
+    }
   *out = m;
   return G4_OK;
 }
@@ -439,7 +485,6 @@ extern "C" int g4_model_set_comm(g4_model* m, g4_comm* c) {
 
 static Common make_common(const g4_model* m, int layer) {
   Common c{};
-  c.ctrl = m->ctrl;
   c.counters = m->counters;
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = m->comm ? m->comm->peer[p] : nullptr;
   c.rank = m->rank;
@@ -452,17 +497,45 @@ static Common make_common(const g4_model* m, int layer) {
   return c;
 }
 
-static Tail make_tail(const g4_model* m, int layer) {
+// Host planning of an operator's shared staging area and prologue bulk copies.
+struct Stager {
+  OpBase* op;
+  int off = 0;
+  explicit Stager(OpBase* o) : op(o) { op->ncc = op->nac = 0; }
+  int space(int bytes) {
+    const int o = off;
+    off += align_up(bytes, 128);
+    op->stgbytes = off;
+    return o;
+  }
+  int constant(const void* src, int bytes) {
+    const int o = space(bytes);
+    op->cc[op->ncc++] = Copy{src, o, bytes};
+    return o;
+  }
+  int activation(const void* src, int bytes) {
+    const int o = space(bytes);
+    op->ac[op->nac++] = Copy{src, o, bytes};
+    return o;
+  }
+};
+
+// Staged inputs of "layer `layer` output" (model.py:312-322) for the next kernel.
+static Tail plan_tail(const g4_model* m, int layer, Stager& sg) {
   const LayerDev& l = m->L[layer];
+  const int H = m->H;
   Tail t{};
   t.resmid = m->resmid;
-  t.mlp = m->mlp_out;
-  t.moe = m->moe_out;
-  t.pf1 = l.n_post_ff1;
-  t.pf2 = l.n_post_ff2;
-  t.pf = l.n_post_ff;
   t.scalar = l.scalar;
   t.layer = layer;
+  t.o_pf1 = sg.constant(l.n_post_ff1, H * 2);
+  t.o_pf2 = sg.constant(l.n_post_ff2, H * 2);
+  t.o_pf = sg.constant(l.n_post_ff, H * 2);
+  if (m->world == 1) {
+    t.o_mlp = sg.activation(m->mlp_out, H * 4);
+    t.o_moe = sg.activation(m->moe_out, H * 2);
+  }
+  t.o_res = sg.activation(m->resmid, H * 2);
   return t;
 }
 
@@ -551,19 +624,26 @@ extern "C" int g4_model_finalize(g4_model* m) {
     a.c = cm;
     a.ctrl = m->ctrl;
     a.nseg = 1;
+    a.trace_id = i * 8 + 0;
     a.seg[0] = SegDesc{l.rows_q + l.rows_k + l.rows_v, 1, H, 0};
-    a.xbytes[0] = H * 2;
+    a.xbytes[0] = H * 4;
     a.xbytes[1] = 0;
+    {
+      Stager sg(&a);
+      a.o_win = sg.constant(l.n_in, H * 2);
+      if (i > 0) a.tail = plan_tail(m, i - 1, sg);
+      a.o_t0 = sg.space(H * 4);
+      a.o_t1 = sg.space(H * 4);
+    }
     a.w = l.qkv;
-    a.w_in = l.n_in;
     a.out = m->qkv_raw;
     a.xres = m->xres;
     a.embed = m->embed;
     a.tokens_in = m->tokens_in;
     a.tokens_out = m->tokens_out;
     a.vocab = c.vocab_size;
+    a.max_len = m->max_len;
     a.embed_scale = host_bf16_round(std::sqrt((float)H));
-    if (i > 0) a.tail = make_tail(m, i - 1);
 
     AttnArgs& t = m->k2[i];
     t = AttnArgs{};
@@ -586,16 +666,21 @@ extern "C" int g4_model_finalize(g4_model* m) {
     t.k_eq_v = l.k_eq_v;
     t.max_len = m->max_len;
     t.eps = c.rms_norm_eps;
+    t.trace_id = i * 8 + 1;
 
     OProjOp& o = m->k3[i];
     o = OProjOp{};
     o.c = cm;
     o.ctrl = m->ctrl;
     o.nseg = 1;
+    o.trace_id = i * 8 + 2;
     o.seg[0] = SegDesc{H, 1, l.rows_q, 0};
-    o.xbytes[0] = l.rows_q * 2;
+    o.xbytes[0] = l.rows_q * 4;
+    {
+      Stager sg(&o);
+      o.o_ctx = sg.activation(m->ctx, l.rows_q * 2);
+    }
     o.w = l.o;
-    o.ctx = m->ctx;
     o.out = m->o_out;
     o.Kc = l.rows_q;
 
@@ -604,16 +689,23 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.c = cm;
     r.ctrl = m->ctrl;
     r.nseg = 2;
+    r.trace_id = i * 8 + 3;
     r.seg[0] = SegDesc{m->E, 1, H, 0};
     r.seg[1] = SegDesc{m->I_local, 2, H, 0};
-    r.xbytes[0] = H * 2;
-    r.xbytes[1] = H * 2;
-    r.o_in = m->o_out;
+    r.xbytes[0] = H * 4;
+    r.xbytes[1] = H * 4;
+    {
+      Stager sg(&r);
+      r.o_wpa = sg.constant(l.n_post_attn, H * 2);
+      r.o_wff = sg.constant(l.n_pre_ff, H * 2);
+      r.o_wff2 = sg.constant(l.n_pre_ff2, H * 2);
+      r.o_wrs = sg.constant(l.router_scale, H * 2);
+      if (m->world == 1) r.o_o = sg.activation(m->o_out, H * 4);
+      r.o_x = sg.activation(m->xres, H * 2);
+      r.o_t0 = sg.space(H * 4);
+      r.o_t1 = sg.space(H * 4);
+    }
     r.xres = m->xres;
-    r.n_post_attn = l.n_post_attn;
-    r.n_pre_ff = l.n_pre_ff;
-    r.n_pre_ff2 = l.n_pre_ff2;
-    r.router_scale = l.router_scale;
     r.resmid = m->resmid;
     r.h2 = m->h2;
     r.router_w = l.router;
@@ -633,12 +725,16 @@ extern "C" int g4_model_finalize(g4_model* m) {
     u.c = cm;
     u.ctrl = m->ctrl;
     u.nseg = 2;
+    u.trace_id = i * 8 + 4;
     u.seg[0] = SegDesc{H, 1, m->I_local, 0};
     u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local};
-    u.xbytes[0] = H * 2;
-    u.xbytes[1] = m->I_local * 2;
-    u.h2 = m->h2;
-    u.mlp_act = m->mlp_act;
+    u.xbytes[0] = H * 4;
+    u.xbytes[1] = m->I_local * 4;
+    {
+      Stager sg(&u);
+      u.o_h2 = sg.activation(m->h2, H * 2);
+      u.o_act = sg.activation(m->mlp_act, m->I_local * 2);
+    }
     u.top_idx = m->top_idx;
     u.top_w = m->top_w;
     u.mlp_down = l.down;
@@ -654,9 +750,13 @@ extern "C" int g4_model_finalize(g4_model* m) {
     dn.c = cm;
     dn.ctrl = m->ctrl;
     dn.nseg = 1;
+    dn.trace_id = i * 8 + 5;
     dn.seg[0] = SegDesc{H, m->topk, m->F_local, 0};
-    dn.xbytes[0] = m->topk * m->F_local * 2;
-    dn.moe_act = m->moe_act;
+    dn.xbytes[0] = m->topk * m->F_local * 4;
+    {
+      Stager sg(&dn);
+      dn.o_act = sg.activation(m->moe_act, m->topk * m->F_local * 2);
+    }
     dn.top_idx = m->top_idx;
     dn.down = l.exp_down;
     dn.mlp_out = m->mlp_out;
@@ -670,17 +770,24 @@ extern "C" int g4_model_finalize(g4_model* m) {
     lm.c = make_common(m, nl - 1);
     lm.ctrl = m->ctrl;
     lm.nseg = 1;
+    lm.trace_id = nl * 8;
     lm.seg[0] = SegDesc{m->V_local, 1, H, 0};
-    lm.xbytes[0] = H * 2;
+    lm.xbytes[0] = H * 4;
     lm.xbytes[1] = kConsumerThreads * 8;
-    lm.tail = make_tail(m, nl - 1);
-    lm.final_norm = m->final_norm;
+    {
+      Stager sg(&lm);
+      lm.o_wn = sg.constant(m->final_norm, H * 2);
+      lm.tail = plan_tail(m, nl - 1, sg);
+      lm.o_t0 = sg.space(H * 4);
+      lm.o_t1 = sg.space(H * 4);
+    }
     lm.embed = m->embed;
     lm.vbegin = m->vbegin;
     lm.logits = m->logits;
     lm.cand_v = m->cand_v;
     lm.cand_i = m->cand_i;
     lm.tokens_out = m->tokens_out;
+    lm.max_len = m->max_len;
     lm.softcap = c.final_logit_softcapping;
   }
   // RoPE tables live in a small device buffer shared by all layers of a type.
@@ -702,7 +809,14 @@ extern "C" int g4_model_finalize(g4_model* m) {
 
 template <class Op>
 static int prepare_op(const Op& op) {
-  return prepare_kernel<Op>(gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1]}));
+  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes});
+  switch (op_cplm(op)) {
+    case 4: return prepare_kernel<Op, 4>(smem);
+    case 8: return prepare_kernel<Op, 8>(smem);
+    case 12: return prepare_kernel<Op, 12>(smem);
+    case 16: return prepare_kernel<Op, 16>(smem);
+    default: return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank");
+  }
 }
 
 static int prepare_all(g4_model* m) {
@@ -711,7 +825,7 @@ static int prepare_all(g4_model* m) {
     if ((rc = prepare_op(m->k1[i])) || (rc = prepare_op(m->k3[i])) || (rc = prepare_op(m->k4[i])) ||
         (rc = prepare_op(m->k5[i])) || (rc = prepare_op(m->k6[i])))
       return rc;
-    if ((rc = prepare_attention(attn_smem_bytes(m->k2[i].g, m->k2[i].d)))) return rc;
+    if ((rc = prepare_attention(m->k2[i].d, m->k2[i].g))) return rc;
   }
   return prepare_op(m->lm);
 }
@@ -798,6 +912,20 @@ extern "C" int g4_model_profile(g4_model* m, void* stream, int steps, float* ms_
   return rc;
 }
 
+extern "C" int g4_trace_read(void* host_dst, long long bytes) {
+#ifdef G4_TRACE
+  const long long need = (long long)sizeof(unsigned long long) * kTraceLaunches * kTraceCtas * kTraceEvents;
+  if (!host_dst || bytes < need) return fail(G4_ERR_ARG, "g4_trace_read: need %lld bytes", need);
+  G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
+  G4_CUDA(cudaMemcpyFromSymbol(host_dst, g4_trace_buf, need), G4_ERR_CUDA);
+  return G4_OK;
+#else
+  (void)host_dst;
+  (void)bytes;
+  return fail(G4_ERR_STATE, "library built without -DG4_TRACE");
+#endif
+}
+
 extern "C" int g4_model_kernel_count(const g4_model* m) {
   return m ? 6 * (int)m->L.size() + 1 : 0;
 }
@@ -825,10 +953,21 @@ extern "C" int g4_graph_capture(g4_model* m, void* stream) {
   // kernel attributes are set outside of the capture
   int rc;
   if ((rc = prepare_all(m))) return rc;
-  G4_CUDA(cudaStreamBeginCapture(st, cudaStreamCaptureModeThreadLocal), G4_ERR_LAUNCH);
-  rc = enqueue_step(m, st);
+  // Capture on a private stream: the caller's stream may be the legacy default stream,
+  // which cannot be captured; capturing executes nothing, and the graph is launched
+  // on the caller's stream by g4_graph_launch.
+  (void)st;
+  cudaStream_t cap = nullptr;
+  G4_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), G4_ERR_CUDA);
+  cudaError_t e0 = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);
+  if (e0 != cudaSuccess) {
+    cudaStreamDestroy(cap);
+    return fail(G4_ERR_LAUNCH, "cudaStreamBeginCapture: %s", cudaGetErrorString(e0));
+  }
+  rc = enqueue_step(m, cap);
   cudaGraph_t g = nullptr;
-  cudaError_t e = cudaStreamEndCapture(st, &g);
+  cudaError_t e = cudaStreamEndCapture(cap, &g);
+  cudaStreamDestroy(cap);
   if (rc) {
     if (g) cudaGraphDestroy(g);
     return rc;
@@ -880,7 +1019,17 @@ struct BlockScratch {
 std::mutex g_block_mu;
 std::map<int, BlockScratch> g_block_scratch;
 
-// Per-device scratch shared by the block entry points (grown on demand, kept).
+// Per-device scratch shared by the block entry points (grown on demand, kept).  Its
+// head has a fixed layout so the zero-at-rest counters never move between calls of
+// different shapes: [attention counters | MoE counters | attention control | RoPE
+// table | variable-size area].
+constexpr size_t kBlockAttnCounters = 0;     // int[kBlockMaxKv]
+constexpr int kBlockMaxKv = 64;
+constexpr size_t kBlockMoeCounters = 256;    // int[kNumCounters]
+constexpr size_t kBlockCtrl = 512;           // int[G4_CTRL_WORDS] (attention block only)
+constexpr size_t kBlockInvFreq = 1024;       // float[kAttnMaxD / 2]
+constexpr size_t kBlockPartOffset = 2048;    // attention partials / MoE staging
+
 char* block_scratch(size_t bytes) {
   int dev = 0;
   cudaGetDevice(&dev);
@@ -909,8 +1058,7 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
                                    void* stream) {
   if (!qkv_raw || !q_norm || !k_norm || !cache_k || !cache_v || !ctx)
     return fail(G4_ERR_ARG, "g4_attention_decode: null pointer");
-  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || head_dim % 64 || head_dim > kAttnMaxD ||
-      n_q_heads / n_kv_heads > kAttnMaxG)
+  if (n_kv_heads <= 0 || n_q_heads % n_kv_heads || !attn_kernel_for(head_dim, n_q_heads / n_kv_heads))
     return fail(G4_ERR_SHAPE, "g4_attention_decode: heads %d/%d dim %d unsupported", n_q_heads,
                 n_kv_heads, head_dim);
   if (pos < 0 || pos >= max_len) return fail(G4_ERR_ARG, "g4_attention_decode: pos %d out of [0,%d)", pos, max_len);
@@ -921,9 +1069,9 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   const int max_live = window > 0 ? std::min(window, max_len) : max_len;
   const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
   if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
+  if (n_kv_heads > kBlockMaxKv) return fail(G4_ERR_SHAPE, "g4_attention_decode: > %d KV heads", kBlockMaxKv);
   const size_t part = (size_t)n_kv_heads * nsplit * g * (head_dim + 2) * 4;
-  const size_t need = part + 256 + (size_t)n_kv_heads * 4 + 256 + G4_CTRL_WORDS * 4 + 256 + head_dim * 2;
-  char* s = block_scratch(need);
+  char* s = block_scratch(kBlockPartOffset + part);
   if (!s) return fail(G4_ERR_NOMEM, "g4_attention_decode: scratch allocation failed");
   AttnArgs a{};
   a.qkv = static_cast<const bf16_t*>(qkv_raw);
@@ -932,13 +1080,10 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   a.cache_k = static_cast<bf16_t*>(cache_k);
   a.cache_v = static_cast<bf16_t*>(cache_v);
   a.ctx = static_cast<bf16_t*>(ctx);
-  a.part = reinterpret_cast<float*>(s);
-  size_t off = (part + 255) / 256 * 256;
-  a.counters = reinterpret_cast<int*>(s + off);
-  off += ((size_t)n_kv_heads * 4 + 255) / 256 * 256;
-  a.ctrl = reinterpret_cast<int*>(s + off);
-  off += 256;
-  float* inv = reinterpret_cast<float*>(s + off);
+  a.counters = reinterpret_cast<int*>(s + kBlockAttnCounters);
+  a.ctrl = reinterpret_cast<int*>(s + kBlockCtrl);
+  float* inv = reinterpret_cast<float*>(s + kBlockInvFreq);
+  a.part = reinterpret_cast<float*>(s + kBlockPartOffset);
   std::vector<float> tab(head_dim / 2);
   rope_inv_freq(head_dim, theta, partial_rotary, tab.data());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -954,21 +1099,22 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   a.k_eq_v = k_eq_v;
   a.max_len = max_len;
   a.eps = eps;
+  a.trace_id = -1;
   return launch_attention(a, st);
 }
 
-// A standalone MoE block reuses the layer kernels K4 (router only), K5 (experts
-// gate|up only) and K6 (down + fused all-reduce push), plus a small reduce kernel for
-// world > 1 that plays the role of the next layer's prologue.
-__global__ void moe_block_reduce_kernel(Common c, bf16_t* out) {
+// A standalone MoE block reuses the layer kernels K4 (router only, block mode), K5
+// (experts gate|up only) and K6 (down + fused all-reduce push), plus a small reduce
+// kernel for world > 1 that plays the role of the next layer's prologue.
+__global__ void moe_block_reduce_kernel(Common c, int* ctrl, bf16_t* out) {
   pdl_wait();
   __shared__ int ok;
-  const int use = site_use(c, kSiteFfn, c.layer);
+  const int use = site_use(ctrl, c, kSiteFfn, c.layer);
   if (threadIdx.x == 0) {
     int good = 1;
-    const int tmo = ldcg_i(c.ctrl + G4_CTRL_TIMEOUT_US);
+    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
     for (int src = 0; src < c.world && good; ++src)
-      good = wait_flag_geq(xflag(c, c.rank, kSiteFfn, use & 1, src), use + 1, tmo, c.ctrl + G4_CTRL_STATUS);
+      good = wait_flag_geq(xflag(c, c.rank, kSiteFfn, use & 1, src), use + 1, tmo, ctrl + G4_CTRL_STATUS);
     ok = good;
   }
   __syncthreads();
@@ -979,29 +1125,8 @@ __global__ void moe_block_reduce_kernel(Common c, bf16_t* out) {
     out[h] = f2bf(s);
   }
   __syncthreads();
-  if (threadIdx.x == 0) atomicAdd(c.ctrl + G4_CTRL_STEP, 1);  // single block: no reader left
+  if (threadIdx.x == 0) atomicAdd(ctrl + G4_CTRL_STEP, 1);  // single block: no reader left
 }
-
-// Router-only prologue: the block input is already the MoE input h2.
-struct RouterOnlyOp : RouterMlpOp {
-  const bf16_t* x_in;
-  __device__ bool prologue(Smem& sm) const {
-    float o[kMaxPer];
-    float s = 0.f;
-    G4_FOR_H(c, i, h) {
-      o[i] = bf2f(x_in[h]);
-      s += o[i] * o[i];
-    }
-    const float r = rms_scale(block_sum(s, sm.red, kConsumerThreads, kBarReduce), c.H, c.eps);
-    bf16_t* xr = reinterpret_cast<bf16_t*>(sm.x0);
-    G4_FOR_H(c, i, h) {
-      if (blockIdx.x == 0) h2[h] = f2bf(o[i]);
-      xr[h] = f2bf(rbf(rbf(rbf(o[i] * r) * bf2f(router_scale[h])) * hinv));
-    }
-    if (threadIdx.x == 0) sm.ints[kSmemRouterDone] = 0;
-    return true;
-  }
-};
 
 extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* comm, const void* x,
                             const void* router_proj, const void* router_scale,
@@ -1015,22 +1140,23 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   if (world > 1 && (!comm || !comm->open || comm->world != world || comm->rank != rank))
     return fail(G4_ERR_ARG, "g4_moe_block: world > 1 needs an opened communicator");
   const int H = cfg->hidden_size, E = cfg->num_experts, K = cfg->top_k_experts;
-  if (cfg->moe_intermediate_size % (8 * world) || H % 8 || H > kMaxPer * kConsumerThreads || K > kMaxTopK)
+  if (cfg->moe_intermediate_size % (8 * world) || H % 8 || H > kMaxHidden || K > kMaxTopK ||
+      E > 256 || K > E || kConsumerWarps % K)
     return fail(G4_ERR_SHAPE, "g4_moe_block: unsupported shape");
   const int F = cfg->moe_intermediate_size / world;
   int dev = 0, nsm = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
-  // scratch: h2[H] bf16, router logits[E], top (idx,w), act[K*F], counters
-  size_t off = 0;
+  // scratch: h2[H] bf16, router logits[E], top (idx,w), act[K*F], mlp placeholder[H]
+  size_t off = kBlockPartOffset;
   auto take = [&](size_t b) {
     size_t o = off;
     off += (b + 255) / 256 * 256;
     return o;
   };
   const size_t o_h2 = take((size_t)H * 2), o_rl = take((size_t)E * 4), o_ti = take(kMaxTopK * 4),
-               o_tw = take(kMaxTopK * 4), o_act = take((size_t)K * F * 2), o_cnt = take(kNumCounters * 4),
-               o_mlp = take((size_t)H * 4);
+               o_tw = take(kMaxTopK * 4), o_act = take((size_t)K * F * 2), o_mlp = take((size_t)H * 4),
+               o_z = take(256);
   char* s = block_scratch(off);
   if (!s) return fail(G4_ERR_NOMEM, "g4_moe_block: scratch allocation failed");
   g4_comm* cm = comm;
@@ -1042,8 +1168,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Common c{};
-  c.ctrl = control;
-  c.counters = reinterpret_cast<int*>(s + o_cnt);
+  c.counters = reinterpret_cast<int*>(s + kBlockMoeCounters);
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = cm->peer[p];
   c.rank = rank;
   c.world = world;
@@ -1055,15 +1180,22 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   int* tidx = top_idx ? top_idx : reinterpret_cast<int*>(s + o_ti);
   float* tw = top_w ? top_w : reinterpret_cast<float*>(s + o_tw);
 
-  RouterOnlyOp r{};
+  RouterMlpOp r{};
+  r.trace_id = -1;
   r.c = c;
   r.ctrl = control;
   r.nseg = 1;
   r.seg[0] = SegDesc{E, 1, H, 0};
-  r.xbytes[0] = H * 2;
+  r.xbytes[0] = H * 4;
   r.xbytes[1] = 0;
-  r.x_in = static_cast<const bf16_t*>(x);
-  r.router_scale = static_cast<const bf16_t*>(router_scale);
+  {
+    Stager sg(&r);
+    r.o_wrs = sg.constant(router_scale, H * 2);
+    r.o_t0 = sg.space(H * 4);
+    r.o_t1 = sg.space(H * 4);
+  }
+  r.block_mode = 1;
+  r.block_x = static_cast<const bf16_t*>(x);
   r.h2 = reinterpret_cast<bf16_t*>(s + o_h2);
   r.router_w = static_cast<const bf16_t*>(router_proj);
   r.pes = static_cast<const bf16_t*>(per_expert_scale);
@@ -1075,15 +1207,19 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   r.hinv = host_bf16_round(std::pow((float)H, -0.5f));
 
   MoeUpOp u{};
+  u.trace_id = -1;
   u.c = c;
   u.ctrl = control;
   u.nseg = 2;
   u.seg[0] = SegDesc{0, 1, 8, 0};
   u.seg[1] = SegDesc{K * F, 2, H, F};
-  u.xbytes[0] = H * 2;
-  u.xbytes[1] = 16;
-  u.h2 = r.h2;
-  u.mlp_act = r.h2;  // unused (segment 0 is empty)
+  u.xbytes[0] = H * 4;
+  u.xbytes[1] = 32;
+  {
+    Stager sg(&u);
+    u.o_h2 = sg.activation(r.h2, H * 2);
+    u.o_act = sg.activation(s + o_z, 16);  // segment 0 is empty: one zero chunk
+  }
   u.top_idx = tidx;
   u.top_w = tw;
   u.mlp_down = static_cast<const bf16_t*>(down);
@@ -1095,12 +1231,16 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   u.topk = K;
 
   MoeDownOp dn{};
+  dn.trace_id = -1;
   dn.c = c;
   dn.ctrl = control;
   dn.nseg = 1;
   dn.seg[0] = SegDesc{H, K, F, 0};
-  dn.xbytes[0] = K * F * 2;
-  dn.moe_act = u.moe_act;
+  dn.xbytes[0] = K * F * 4;
+  {
+    Stager sg(&dn);
+    dn.o_act = sg.activation(u.moe_act, K * F * 2);
+  }
   dn.top_idx = tidx;
   dn.down = static_cast<const bf16_t*>(down);
   dn.mlp_out = u.mlp_out;
@@ -1114,7 +1254,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   if (!rc) rc = launch_gemv(u, nsm, st);
   if (!rc) rc = launch_gemv(dn, nsm, st);
   if (!rc && world > 1) {
-    cudaError_t e = launch_pdl(moe_block_reduce_kernel, dim3(1), dim3(512), 0, st, c,
+    cudaError_t e = launch_pdl(moe_block_reduce_kernel, dim3(1), dim3(512), 0, st, c, control,
                                static_cast<bf16_t*>(out));
     if (e != cudaSuccess) rc = fail(G4_ERR_LAUNCH, "reduce launch: %s", cudaGetErrorString(e));
   }

@@ -25,6 +25,7 @@ G4_ERR_CUDA = -7
 G4_STATUS_PEER_TIMEOUT = 0x1
 G4_STATUS_MBAR_TIMEOUT = 0x2
 G4_STATUS_BAD_TOKEN = 0x4
+G4_STATUS_POS_OVERFLOW = 0x8
 
 CTRL_POS, CTRL_STEP, CTRL_FORCED_LEN, CTRL_STATUS, CTRL_TIMEOUT_US, CTRL_WRITE_LOGITS = range(6)
 CTRL_WORDS = 16
@@ -35,7 +36,7 @@ EXPORTS = (
     "g4_model_create", "g4_model_set_tensor", "g4_model_set_comm", "g4_model_finalize",
     "g4_step", "g4_graph_capture", "g4_graph_launch", "g4_model_status",
     "g4_model_kernel_count", "g4_model_host_tokens", "g4_model_profile", "g4_model_destroy",
-    "g4_moe_block", "g4_attention_decode",
+    "g4_moe_block", "g4_attention_decode", "g4_trace_read",
 )
 
 
@@ -78,11 +79,12 @@ def lib() -> ctypes.CDLL:
     global _lib
     if _lib is not None:
         return _lib
-    if not os.path.exists(LIB):
+    path = os.environ.get("G4B200_LIB", LIB)  # e.g. the -DG4_TRACE build
+    if not os.path.exists(path):
         raise RuntimeError(
-            f"{LIB} is missing: build it with `python -m gemma4_b200.build` "
+            f"{path} is missing: build it with `python -m gemma4_b200.build` "
             "(the B200 path has no fallback)")
-    L = ctypes.CDLL(LIB)
+    L = ctypes.CDLL(path)
     L.g4_version.restype = c_char_p
     L.g4_strerror.restype = c_char_p
     L.g4_strerror.argtypes = [c_int]
@@ -104,8 +106,9 @@ def lib() -> ctypes.CDLL:
     L.g4_model_host_tokens.argtypes = [c_void_p, POINTER(POINTER(c_int))]
     L.g4_model_profile.argtypes = [c_void_p, c_void_p, c_int, POINTER(c_float), c_int]
     L.g4_model_destroy.argtypes = [c_void_p]
+    L.g4_trace_read.argtypes = [c_void_p, c_longlong]
     L.g4_moe_block.argtypes = [POINTER(G4Config), c_int, c_int, c_void_p] + [c_void_p] * 11
-    L.g4_attention_decode.argtypes = ([c_void_p] * 5 + [c_int] * 8 + [c_float] * 3
+    L.g4_attention_decode.argtypes = ([c_void_p] * 5 + [c_int] * 7 + [c_float] * 3
                                       + [c_void_p, c_void_p])
     for name in EXPORTS:
         if name not in ("g4_version", "g4_strerror", "g4_last_error"):

@@ -18,6 +18,7 @@ ROOT = os.path.dirname(PKG_DIR)                      # kaggle-tpu-inference_b200
 CSRC = os.path.join(ROOT, "csrc")
 INCLUDE = os.path.join(os.path.dirname(ROOT), "include")
 LIB = os.path.join(PKG_DIR, "libg4b200.so")
+LIB_TRACE = os.path.join(PKG_DIR, "libg4b200_trace.so")  # -DG4_TRACE timeline build
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -38,25 +39,27 @@ def nvcc() -> str:
     return path
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+def up_to_date(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force: bool = False, verbose: bool = False) -> str:
-    if not force and up_to_date():
-        return LIB
+def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
+    """Compile the library (``trace=True``: the -DG4_TRACE timeline build)."""
+    lib = LIB_TRACE if trace else LIB
+    if not force and up_to_date(lib):
+        return lib
     units = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
-    tmp = LIB + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, "-I", INCLUDE, "-o", tmp, *units]
+    tmp = lib + ".tmp"
+    cmd = [nvcc(), *NVCC_FLAGS, *(["-DG4_TRACE"] if trace else []), "-I", INCLUDE, "-o", tmp, *units]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose=True))
+    print(build(force="--force" in sys.argv, verbose=True, trace="--trace" in sys.argv))

@@ -47,4 +47,4 @@ def test_argument_validation_before_cuda():
     assert lib.g4_comm_create(0, 3, 2, 2816, ctypes.byref(out)) == N.G4_ERR_ARG
     assert lib.g4_step(None, None) == N.G4_ERR_ARG
     assert b"null" in lib.g4_last_error()
-    assert lib.g4_attention_decode(*([None] * 5), *([0] * 8), 0.0, 0.0, 0.0, None, None) == N.G4_ERR_ARG
+    assert lib.g4_attention_decode(*([None] * 5), *([0] * 7), 0.0, 0.0, 0.0, None, None) == N.G4_ERR_ARG
