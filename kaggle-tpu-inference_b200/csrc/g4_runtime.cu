@@ -1264,3 +1264,102 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   }
   return rc;
 }
+
+// ------------------------------------------------------------------ allocation-free attention
+// Some callers cannot allocate device memory when they call into the library: code that
+// runs while its stream is being recorded into a CUDA graph (an allocation there breaks
+// the recording), servers that reserve their whole memory budget at start-up and must
+// not grow afterwards, and hosts whose own allocator owns the device and forbids other
+// allocations.  g4_attention_decode allocates its scratch (split-KV partials and merge
+// counters) on first use; g4_attention_decode_noalloc computes exactly the same thing but
+// keeps that scratch in the fixed device array below, which the library carries in every
+// GPU it is loaded on until the process exits.
+//
+// Layout of the array: [0, 256) merge counters (one per KV head, zero between calls),
+// [256, 512) control block (status word), [512, 1536) RoPE table, [2048, end) partials.
+constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;  // 4 MiB per device
+constexpr size_t kNoAllocPartOffset = 2048;
+static __device__ __align__(256) unsigned char g4_noalloc_scratch[kNoAllocScratchBytes];
+
+namespace {
+constexpr int kNoAllocMaxDevices = 64;
+std::mutex g_noalloc_mu;
+unsigned char* g_noalloc_ptr[kNoAllocMaxDevices];  // device address of the array, per device
+
+// The array's name is only a host-side stand-in in host code: its device address must be
+// looked up on each device, with that device current, before a kernel can be given it.
+int noalloc_scratch(int dev, unsigned char** out) {
+  if (dev < 0 || dev >= kNoAllocMaxDevices) return fail(G4_ERR_ARG, "device %d out of range", dev);
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  if (!g_noalloc_ptr[dev]) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g4_noalloc_scratch);
+    if (e != cudaSuccess || !p)
+      return fail(G4_ERR_CUDA, "cudaGetSymbolAddress(g4_noalloc_scratch): %s", cudaGetErrorString(e));
+    g_noalloc_ptr[dev] = static_cast<unsigned char*>(p);
+  }
+  *out = g_noalloc_ptr[dev];
+  return G4_OK;
+}
+}  // namespace
+
+extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_norm,
+                                           const void* k_norm, void* cache_k, void* cache_v,
+                                           int max_len, int n_q_heads, int n_kv_heads,
+                                           int head_dim, int k_eq_v, int pos, int window,
+                                           float theta, float partial_rotary, float eps,
+                                           void* ctx, void* stream) {
+  if (!qkv_raw || !q_norm || !k_norm || !cache_k || !cache_v || !ctx)
+    return fail(G4_ERR_ARG, "g4_attention_decode_noalloc: null pointer");
+  if (n_kv_heads <= 0 || n_kv_heads > kBlockMaxKv || n_q_heads % n_kv_heads ||
+      !attn_kernel_for(head_dim, n_q_heads / n_kv_heads))
+    return fail(G4_ERR_SHAPE, "g4_attention_decode_noalloc: heads %d/%d dim %d unsupported",
+                n_q_heads, n_kv_heads, head_dim);
+  if (pos < 0 || pos >= max_len)
+    return fail(G4_ERR_ARG, "g4_attention_decode_noalloc: pos %d out of [0,%d)", pos, max_len);
+  int dev = 0, nsm = 148;
+  G4_CUDA(cudaGetDevice(&dev), G4_ERR_CUDA);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const int g = n_q_heads / n_kv_heads;
+  const int max_live = window > 0 ? std::min(window, max_len) : max_len;
+  const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
+  if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
+  const size_t part = (size_t)n_kv_heads * nsplit * g * (head_dim + 2) * 4;
+  if (part > kNoAllocScratchBytes - kNoAllocPartOffset)
+    return fail(G4_ERR_SHAPE,
+                "g4_attention_decode_noalloc: needs %zu bytes of split-KV partials, the fixed "
+                "scratch holds %zu (use g4_attention_decode)",
+                part, kNoAllocScratchBytes - kNoAllocPartOffset);
+  unsigned char* s = nullptr;
+  int rc = noalloc_scratch(dev, &s);
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  // The array keeps the previous call's contents: zero the counters and status word.
+  G4_CUDA(cudaMemsetAsync(s, 0, 512, st), G4_ERR_CUDA);
+  float tab[kAttnMaxD / 2];  // host table on the stack: no host allocation either
+  rope_inv_freq(head_dim, theta, partial_rotary, tab);
+  G4_CUDA(cudaMemcpyAsync(s + 1024, tab, sizeof(float) * (head_dim / 2), cudaMemcpyHostToDevice, st),
+          G4_ERR_CUDA);
+  AttnArgs a{};
+  a.qkv = static_cast<const bf16_t*>(qkv_raw);
+  a.q_norm = static_cast<const bf16_t*>(q_norm);
+  a.k_norm = static_cast<const bf16_t*>(k_norm);
+  a.cache_k = static_cast<bf16_t*>(cache_k);
+  a.cache_v = static_cast<bf16_t*>(cache_v);
+  a.ctx = static_cast<bf16_t*>(ctx);
+  a.counters = reinterpret_cast<int*>(s);
+  a.ctrl = reinterpret_cast<int*>(s + 256);
+  a.inv_freq = reinterpret_cast<const float*>(s + 1024);
+  a.part = reinterpret_cast<float*>(s + kNoAllocPartOffset);
+  a.pos_fixed = pos;
+  a.n_kv = n_kv_heads;
+  a.g = g;
+  a.d = head_dim;
+  a.nsplit = nsplit;
+  a.window = window;
+  a.k_eq_v = k_eq_v;
+  a.max_len = max_len;
+  a.eps = eps;
+  a.trace_id = -1;
+  return launch_attention(a, st);
+}

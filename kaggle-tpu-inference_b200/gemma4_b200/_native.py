@@ -36,7 +36,7 @@ EXPORTS = (
     "g4_model_create", "g4_model_set_tensor", "g4_model_set_comm", "g4_model_finalize",
     "g4_step", "g4_graph_capture", "g4_graph_launch", "g4_model_status",
     "g4_model_kernel_count", "g4_model_host_tokens", "g4_model_profile", "g4_model_destroy",
-    "g4_moe_block", "g4_attention_decode", "g4_trace_read",
+    "g4_moe_block", "g4_attention_decode", "g4_trace_read", "g4_attention_decode_noalloc",
 )
 
 
@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
     L.g4_moe_block.argtypes = [POINTER(G4Config), c_int, c_int, c_void_p] + [c_void_p] * 11
     L.g4_attention_decode.argtypes = ([c_void_p] * 5 + [c_int] * 7 + [c_float] * 3
                                       + [c_void_p, c_void_p])
+    L.g4_attention_decode_noalloc.argtypes = L.g4_attention_decode.argtypes
     for name in EXPORTS:
         if name not in ("g4_version", "g4_strerror", "g4_last_error"):
             getattr(L, name).restype = c_int
