@@ -41,9 +41,14 @@ sys.path.insert(0, os.path.join(ROOT, "kaggle-tpu-inference_b200"))
 METRIC = "decode tok/s @32K ctx, bs=1"
 FALLBACK_HBM_GBS = 6650.0
 
-# DRAM traffic per launch of the dominant kernel class from an ncu capture; see
-# profiles/ (None until a capture of the current kernels exists).
-NCU_TRAFFIC_BYTES_PER_LAUNCH: dict = {}
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each kernel
+# class, from the ncu capture summarised in profiles/decode_layer_ncu_full_small.md
+# (profiling case with 32 experts: per-layer bytes equal the full model's, except the
+# router rows, 0.54 MB more with 128 experts, added to router_mlp_up).
+NCU_TRAFFIC_BYTES_PER_LAUNCH: dict = {
+    "qkv": 46.28e6, "o_proj": 23.12e6, "router_mlp_up": 24.66e6,
+    "mlp_down_experts_up": 76.54e6, "experts_down": 31.78e6,
+}
 
 
 def parse_args():
