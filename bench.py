@@ -13,9 +13,14 @@ value       tokens/s of the captured step graph, K steps between CUDA events on 
 e2e         the same metric through the public API: Engine.generate() with the prompt
             uploaded from host memory and every token read back to the host, wall
             clock from the call to the last token (includes prefill).
-roofline    the kernel class with the largest time share (per-class CUDA-event timing
-            of event-separated steps): algorithmic bytes per launch / mean duration,
-            against the measured HBM copy peak (MEASURED_PEAKS.json).
+roofline    the dominant kernel.  With the default step-kernel engine that is the one
+            persistent kernel of the step (one launch per token): algorithmic bytes
+            per token (weights + live KV) / mean launch duration from the same CUDA
+            events, against the measured HBM copy peak (MEASURED_PEAKS.json).  With
+            --engine ops it is the kernel class with the largest time share of
+            event-separated per-op steps.
+op_kernels  per-class time shares of event-separated per-op steps (both engines; the
+            per-op kernels compute the same operators as the step kernel).
 cpu_baseline  the CPU oracle (restatement of the reference forward, oracle/) timing a
             bounded sample of full-size decode steps on the host cores (rank 0, N=1).
 
@@ -41,6 +46,10 @@ sys.path.insert(0, os.path.join(ROOT, "kaggle-tpu-inference_b200"))
 METRIC = "decode tok/s @32K ctx, bs=1"
 FALLBACK_HBM_GBS = 6650.0
 
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the step
+# kernel, keyed by (world, layers); filled from an ncu capture of the step kernel.
+NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {}
+
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each kernel
 # class, from the ncu capture summarised in profiles/decode_layer_ncu_full_small.md
 # (profiling case with 32 experts: per-layer bytes equal the full model's, except the
@@ -65,6 +74,7 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=1)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--engine", choices=["step", "ops"], default="step")
     # profiling knobs (smaller models for ncu captures); defaults are config 4
     ap.add_argument("--layers", type=int, default=30)
     ap.add_argument("--experts", type=int, default=128)
@@ -281,7 +291,8 @@ def main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     mesh = Mesh(rank, world, local)
-    eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh)
+    eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh,
+                 engine=args.engine)
     eng.compile_all()
     m = eng.model
     prompt = prompt_ids(cfg, args.prompt_len, args.seed)
@@ -316,27 +327,39 @@ def main() -> int:
     value = args.steps / (ms / 1000.0)
     pos_avg = len(prompt) + args.warmup + args.steps // 2
 
-    # ---- per-kernel-class timing (event-separated steps, same stream)
+    # ---- per-kernel-class timing of the per-op kernels (event-separated steps)
     prof = m.profile(args.profile_steps)
     barrier()
     m.check_status()
     cb = class_bytes(cfg, world, pos_avg)
     total_ms = sum(prof.values())
-    dom = max(prof, key=prof.get)
-    launches = {"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers) * args.profile_steps
-    dom_ms = prof[dom] / launches
-    dom_bytes = cb[dom] / ({"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers))
     peak, peak_kind = peaks()
-    achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
-    traffic = NCU_TRAFFIC_BYTES_PER_LAUNCH.get(dom)
-    roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
-                "frac": achieved / peak, "peak_kind": peak_kind, "traffic": traffic,
-                "algorithmic_bytes_per_launch": dom_bytes, "mean_launch_ms": dom_ms,
-                "time_share": prof[dom] / total_ms}
+    op_kernels = {"ms_per_step": total_ms / args.profile_steps,
+                  "share": {k: v / total_ms for k, v in prof.items()}}
     sb = step_bytes(cfg, pos_avg)
+    if args.engine == "step":
+        # one persistent kernel per token: bytes per launch = this rank's step bytes
+        rank_bytes = sum(cb.values())
+        launch_ms = ms / args.steps
+        achieved = rank_bytes / (launch_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": "step_kernel", "achieved": achieved, "peak": peak,
+                    "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
+                    "traffic": NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH.get((world, args.layers)),
+                    "algorithmic_bytes_per_launch": rank_bytes, "mean_launch_ms": launch_ms,
+                    "time_share": 1.0}
+    else:
+        dom = max(prof, key=prof.get)
+        launches = {"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers) * args.profile_steps
+        dom_ms = prof[dom] / launches
+        dom_bytes = cb[dom] / ({"lm_head_argmax": 1}.get(dom, cfg.num_hidden_layers))
+        achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
+        roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
+                    "frac": achieved / peak, "peak_kind": peak_kind,
+                    "traffic": NCU_TRAFFIC_BYTES_PER_LAUNCH.get(dom),
+                    "algorithmic_bytes_per_launch": dom_bytes, "mean_launch_ms": dom_ms,
+                    "time_share": prof[dom] / total_ms}
     step_roof = {"achieved_aggregate_gbs": sb * value / 1e9, "peak_aggregate_gbs": peak * world,
-                 "frac": sb * value / 1e9 / (peak * world), "bytes_per_token": sb,
-                 "kernel_share": {k: v / total_ms for k, v in prof.items()}}
+                 "frac": sb * value / 1e9 / (peak * world), "bytes_per_token": sb}
 
     # ---- end to end through Engine.generate (host prompt, host token reads)
     e2e = None
@@ -371,7 +394,8 @@ def main() -> int:
             "warmup": args.warmup, "ms_per_step": ms / args.steps, "higher_is_better": True,
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
-            "step_roofline": step_roof, "cpu_baseline": cpu,
+            "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
+            "cpu_baseline": cpu,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

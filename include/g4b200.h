@@ -128,6 +128,19 @@ int g4_graph_capture(g4_model* model, void* stream);
 int g4_graph_launch(g4_model* model, void* stream, int count);
 int g4_model_status(g4_model* model, void* stream, int* status_out);
 int g4_model_kernel_count(const g4_model* model); /* kernels launched per step */
+/* Decode-step engine (no reference counterpart: the reference's step is one XLA
+ * program).  G4_ENGINE_STEP_KERNEL (default): one persistent cooperative kernel per
+ * token, one CTA per SM, grid barriers between the operators and one weight ring
+ * across the whole step.  G4_ENGINE_OP_KERNELS: 6 kernels per layer + 1, chained by
+ * programmatic dependent launch (per-kernel profiling, g4_model_profile).  Both give
+ * bit-identical results.  Call before g4_graph_capture (G4_ERR_STATE after).  With the
+ * step kernel, a set timeout bit (G4_STATUS_PEER_TIMEOUT / G4_STATUS_MBAR_TIMEOUT)
+ * makes every later step a no-op until the host clears it; g4_model_status, on
+ * finding any bit set, also clears the library's barrier and counter words so that
+ * the next step after the host clears STATUS starts clean. */
+#define G4_ENGINE_STEP_KERNEL 0
+#define G4_ENGINE_OP_KERNELS 1
+int g4_model_set_engine(g4_model* model, int engine);
 /* Mapped pinned host mirror (int32[max_len+1]) of tokens_out, written by each step's
  * last kernel; lets the host read token i after step i's event without a copy that
  * would queue behind later steps (engine.py:196-200 lookahead read).  Call after

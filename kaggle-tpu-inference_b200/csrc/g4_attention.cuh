@@ -14,9 +14,11 @@
 //      over them: scores s = bf16(q.k) (scale 1.0, rounded like the reference einsum),
 //      running max / mass, and acc += exp(s - m) v in fp32 registers; K and V of a
 //      batch of keys are loaded together.
-//   3. the lane groups are merged through shared memory into (m, l, acc[g][d]), which
-//      goes to the partial buffer; the last CTA of head h (atomic counter) merges the
-//      n_active partials with max-rescaling and rounds the context to bf16.
+//   3. the lane groups are merged in a fixed order (butterfly within a warp, then warp
+//      by warp through shared memory) into (m, l, acc[g][d]), which goes to the
+//      partial buffer; the last CTA of head h (atomic counter) merges the n_active
+//      partials in split order with max-rescaling and rounds the context to bf16.
+//      Every sum has a fixed order: results are bitwise reproducible.
 // Difference from the reference: it rounds the normalised probabilities to bf16
 // before P.V; here P.V uses fp32 weights and the context is rounded once -- closer
 // to exact arithmetic, within the tolerance the parity tests state.
@@ -53,33 +55,33 @@ struct AttnArgs {
 
 __host__ __device__ inline int attn_smem_bytes(int g, int d) {
   // acc [g][d] + lane-group stats [64][g] x 2 + merge scales [g][kAttnMaxSplit] + misc
-  return g * d * 4 + 2 * 64 * g * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64;
+  // + the normalised query heads q_s [g][d] (bf16)
+  return g * d * 4 + 2 * 64 * g * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2;
 }
 
-// D = head dim, G = query heads per KV head on this rank.  Every loop below has a
-// compile-time trip count, so the code executed once per CTA stays small.
+// One work item (KV head hk, split sp) of decode attention, run by the kAttnThreads
+// threads 0..kAttnThreads-1 of the block with named barrier `bar` among them and
+// `smem` (attn_smem_bytes(G, D), 16-byte aligned) as scratch.  Every exit is taken by
+// all of these threads together.  D = head dim, G = query heads per KV head on this
+// rank; every loop has a compile-time trip count.
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+__device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, unsigned char* smem, int bar) {
   constexpr int PER = D / 32;                 // elements per lane of one head vector
   constexpr int LK = D / 8 < 32 ? D / 8 : 32; // lanes per key
   constexpr int KPW = 32 / LK;                // lane groups per warp
   constexpr int CPL = (D / 8) / LK;           // 16-byte chunks per lane of a key row
   constexpr int NGRP = kAttnWarps * KPW;      // lane groups per CTA
   constexpr int HG = (CPL == 2 && G == 8) ? 4 : G;  // heads kept in registers at once
-  extern __shared__ __align__(16) unsigned char attn_smem[];
-  float* acc_s = reinterpret_cast<float*>(attn_smem);               // [G][D]
+  float* acc_s = reinterpret_cast<float*>(smem);                     // [G][D]
   float* gm = acc_s + G * D;                                         // [NGRP][G]
   float* gl = gm + 64 * G;                                           // [NGRP][G]
   float* scale_s = gl + 64 * G;                                      // [G][kAttnMaxSplit]
   float* ml = scale_s + G * kAttnMaxSplit;                           // M[G], L[G]
   int* flag = reinterpret_cast<int*>(ml + 2 * kAttnMaxG);
-  __shared__ __align__(16) bf16_t q_s[G * D];
+  bf16_t* q_s = reinterpret_cast<bf16_t*>(flag + 16);                // [G][D]
 
-  pdl_trigger();
-  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 0);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int hk = blockIdx.x / a.nsplit, sp = blockIdx.x % a.nsplit;
-  // constants before the dependency wait: norm weights, RoPE frequencies of this lane
+  // norm weights, RoPE frequencies of this lane
   float wq[PER], wk[PER], fr[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
@@ -88,12 +90,9 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     wk[i] = bf2f(a.k_norm[e]);
     fr[i] = a.inv_freq[e < D / 2 ? e : e - D / 2];
   }
-  pdl_wait();
-  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 2);
-
   const int pos = a.pos_fixed >= 0 ? a.pos_fixed : ldcg_i(a.ctrl + G4_CTRL_POS);
   if (pos < 0 || pos >= a.max_len) {  // never index the cache out of bounds
-    if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
+    if (threadIdx.x == 0 && hk == 0 && sp == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
     return;
   }
   const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
@@ -160,7 +159,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
   }
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads) acc_s[i] = 0.f;
   __threadfence_block();
-  __syncthreads();
+  named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 3);
 
   // ---- 2. online softmax per lane group over its keys
@@ -250,7 +249,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
         gl[grp * G + h0 + h] = l_run[h];
       }
     }
-    __syncthreads();
+    named_bar(bar, kAttnThreads);
     if (threadIdx.x < HG) {
       const int h = h0 + threadIdx.x;
       float M = -INFINITY;
@@ -263,17 +262,31 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
       ml[h] = M;
       ml[kAttnMaxG + h] = L;
     }
-    __syncthreads();
+    named_bar(bar, kAttnThreads);
+    // rescale to the CTA max, sum the KPW lane groups of a warp with a butterfly (every
+    // lane ends with the same bits), then add the warps into acc_s in warp order: a
+    // fixed summation order, so results do not depend on scheduling
 #pragma unroll
     for (int h = 0; h < HG; ++h) {
       const float f = m_run[h] == -INFINITY ? 0.f : expf(m_run[h] - ml[h0 + h]);
-      if (f != 0.f) {
 #pragma unroll
-        for (int e = 0; e < CPL * 8; ++e)
-          atomicAdd(&acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)], acc[h][e] * f);
-      }
+      for (int e = 0; e < CPL * 8; ++e) acc[h][e] *= f;
     }
-    __syncthreads();
+#pragma unroll
+    for (int o = LK; o < 32; o <<= 1)
+#pragma unroll
+      for (int h = 0; h < HG; ++h)
+#pragma unroll
+        for (int e = 0; e < CPL * 8; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
+    for (int q = 0; q < kAttnWarps; ++q) {
+      if (warp == q && gi_lane == 0) {
+#pragma unroll
+        for (int h = 0; h < HG; ++h)
+#pragma unroll
+          for (int e = 0; e < CPL * 8; ++e) acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)] += acc[h][e];
+      }
+      named_bar(bar, kAttnThreads);
+    }
   }
 
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
@@ -284,14 +297,16 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     pbase[i] = e == 0 ? ml[h] : (e == 1 ? ml[kAttnMaxG + h] : acc_s[h * D + e - 2]);
   }
   __threadfence();
-  __syncthreads();
+  named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) {
     const int old = atomic_add_acq_rel_gpu(a.counters + hk, 1);
     *flag = (old == n_active - 1);
   }
-  __syncthreads();
+  named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 5);
-  if (!*flag) return;
+  const bool merge = *flag != 0;
+  named_bar(bar, kAttnThreads);  // every thread has read the flag before it is reused
+  if (!merge) return;
   __threadfence();
   const float* hbase = a.part + (size_t)hk * a.nsplit * G * (D + 2);
   for (int h = warp; h < G; h += kAttnWarps) {  // warp-uniform
@@ -308,7 +323,7 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     L = warp_sum(L);
     if (lane == 0) ml[h] = L;
   }
-  __syncthreads();
+  named_bar(bar, kAttnThreads);
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
     const int h = i / D, e = i % D;
     const float* src = hbase + (size_t)h * (D + 2) + 2 + e;
@@ -329,6 +344,18 @@ __global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_
     atomicExch(a.counters + hk, 0);
     G4_TRACE_EV(a.trace_id, 6);
   }
+  named_bar(bar, kAttnThreads);  // shared scratch free for the caller's next use
+}
+
+// Standalone launch: grid = n_kv x nsplit, one item per CTA.
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ __align__(16) unsigned char attn_smem[];
+  pdl_trigger();
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 0);
+  pdl_wait();
+  if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 2);
+  attn_item<D, G>(a, blockIdx.x / a.nsplit, blockIdx.x % a.nsplit, attn_smem, 1);
 }
 
 }  // namespace g4

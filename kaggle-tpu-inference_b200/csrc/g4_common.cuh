@@ -194,6 +194,19 @@ __device__ __forceinline__ int atomic_add_acq_rel_gpu(int* p, int v) {
   return old;
 }
 
+// GPU-scope acquire/release accessors for flags between CTAs of one launch.
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ void st_release_gpu(int* p, int v) {
+  asm volatile("st.release.gpu.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
 // L2-coherent loads for data produced by other kernels or other GPUs (bypass L1).
 __device__ __forceinline__ float ldcg_f(const float* p) { return __ldcg(p); }
 __device__ __forceinline__ int ldcg_i(const int* p) { return __ldcg(p); }
@@ -227,7 +240,8 @@ __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int t
 // trace id is in [0, kTraceLaunches); read back with g4_trace_read.
 constexpr int kTraceLaunches = 512, kTraceCtas = 4, kTraceEvents = 8;
 #ifdef G4_TRACE
-__device__ unsigned long long g4_trace_buf[kTraceLaunches][kTraceCtas][kTraceEvents];
+// one buffer per device module (each translation unit of the library is its own module)
+static __device__ unsigned long long g4_trace_buf[kTraceLaunches][kTraceCtas][kTraceEvents];
 __device__ __forceinline__ int trace_cta_slot() {
   const int b = blockIdx.x, n = gridDim.x;
   return b == 0 ? 0 : (b == 1 ? 1 : (b == n / 2 ? 2 : (b == n - 1 ? 3 : -1)));

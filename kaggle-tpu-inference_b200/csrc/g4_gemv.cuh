@@ -2,34 +2,32 @@
 //
 // Every matrix product of the decode step is y = W x with a bf16 weight W that is
 // read exactly once per token, so the step is HBM-bound: the engine's job is to keep
-// HBM busy from the first to the last byte of every kernel and to spend as little
-// fixed time per kernel as possible.
+// HBM busy from the first to the last byte of the step.
 //
 //  * One CTA per SM (grid = #SMs).  Warp 8 is a producer: one lane streams the CTA's
-//    share of the weights into a ring of kStages shared-memory stages with TMA bulk
-//    copies (cp.async.bulk, L2 evict-first), each stage guarded by a full/empty
-//    mbarrier pair.  Warps 0-7 consume: a warp takes a whole staged row and dots it
-//    with the input vector, which each lane keeps in registers (the chunks it always
-//    touches), so the only shared-memory traffic of the dot products is the weights
-//    themselves; then a fused epilogue (rounding, GELU gating, router/argmax staging,
-//    peer stores).
-//  * Prologue data movement is bulk copies too: before griddepcontrol.wait the
-//    producer copies the kernel's constant vectors (norm weights) into a shared
-//    staging area and issues the first weight stages (weights never depend on the
-//    previous kernel); right after the wait it copies the activation vectors.  The
-//    consumers then run short loops over shared memory -- no long unrolled code, no
-//    chains of dependent global loads at kernel start.
+//    share of the weights into a ring of shared-memory stages with TMA bulk copies
+//    (cp.async.bulk, L2 evict-first), each stage guarded by a full/empty mbarrier
+//    pair.  Warps 0-7 consume: a warp takes a whole staged row and dots it with the
+//    input vector, which each lane keeps in registers (the chunks it always touches),
+//    so the only shared-memory traffic of the dot products is the weights themselves;
+//    then a fused epilogue (rounding, GELU gating, router/argmax staging, peer stores).
+//  * Prologue vectors (norm weights, the previous op's outputs) are staged in shared
+//    memory before the operator's prologue runs; the consumers then run short loops
+//    over shared memory -- no chains of dependent global loads at op start.
 //  * Work split: the CTA's byte range of the concatenated segments (byte-balanced, so
 //    mixed segments such as router rows + MLP gate/up rows stay balanced); a tile is
 //    up to a stage's worth of consecutive units of one segment.
+//  * Two drivers share the producer/consumer pieces below: gemv_kernel runs one
+//    operator per launch (PDL-chained); the persistent step kernel (g4_step.cuh) runs
+//    the whole decode step in one launch with one ring across all operators.
 //
 // Operators derive from OpBase and add:
 //   __device__ bool seg_dependent(int s) const;   // addresses need prior results
-//   __device__ void load_dependent(Smem&) const;  // producer lane, after pdl_wait
+//   __device__ void load_dependent(Smem&) const;  // producer lane, once they exist
 //   __device__ void issue(int s,int u0,int n,unsigned char* stage,uint64_t* bar,
 //                         uint64_t pol,const Smem&) const;   // producer: bulk copies
-//   __device__ int xmode(int s) const;            // see gemv_kernel
-//   __device__ bool prologue(Smem&) const;        // consumers (calls pdl_wait)
+//   __device__ int xmode(int s) const;            // see consume_tiles
+//   __device__ bool prologue(Smem&) const;        // consumers, staged vectors present
 //   __device__ const float* xvec(int s,int j,const Smem&) const;   // fp32 input
 //   __device__ void epilogue(int s,int u0,int n,const Res& res,Smem&,bool ok) const;
 //   __device__ void finish(Smem&, bool ok) const; // consumers, after all tiles
@@ -42,13 +40,20 @@ namespace g4 {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kStages = 4;
-constexpr int kStageBytes = 22528;  // 4 rows of 2816 bf16; 4 stages ~ 88 KB in flight
+constexpr int kStages = 4;          // ring depth of the per-op kernels
+constexpr int kMaxStages = 16;      // ring depth limit (persistent step kernel)
+constexpr int kStageBytes = 22528;  // 4 rows of 2816 bf16
 constexpr int kMaxTileRows = 256;
+constexpr int kResBufs = 2;         // per-tile result buffers (alternating)
 constexpr int kMaxSeg = 3;
 constexpr int kMaxCopies = 6;
 constexpr int kBarConsumers = 1;  // named barrier id used by the consumer warps
-constexpr int kSmemDead = 63;     // Smem::ints slot: CTA gave up after a timed-out wait
+constexpr int kMaxSmemBytes = 232448;  // 227 KB opt-in shared memory per CTA
+// Smem::ints slots used by the engine (operators use 0..39)
+constexpr int kSmemSeq = 40;      // launch sequence number (persistent step kernel)
+constexpr int kSmemIssued = 41;   // tiles issued by the producer lane so far
+constexpr int kSmemProdExit = 42; // producer lane has issued its last copy
+constexpr int kSmemDead = 63;     // CTA gave up after a timed-out wait
 
 struct SegDesc {
   int units;  // number of work units
@@ -72,7 +77,7 @@ struct OpBase {
   SegDesc seg[kMaxSeg];
   int xbytes[2];  // bytes of the two fp32 input vectors in shared memory
   int stgbytes;   // bytes of the staging area (constant + activation vectors)
-  int ncc, nac;   // constant copies (before griddepcontrol.wait) / activation copies
+  int ncc, nac;   // constant copies / activation copies
   int trace_id;   // launch id for the optional timeline tracer (-DG4_TRACE)
   Copy cc[kMaxCopies];
   Copy ac[kMaxCopies];
@@ -92,11 +97,11 @@ struct Smem {
   uint64_t* full;
   uint64_t* empty;
   uint64_t* pbar;    // [2]: constants copied, activations copied
-  float* res;        // [kStages][kMaxTileRows]
+  float* res;        // [kResBufs][kMaxTileRows]
   float* red;        // [64] block-reduction scratch
   int* ints;         // [64] small shared ints (expert ids, flags, argmax indices)
   float* flts;       // [64] small shared floats (routing weights, argmax values)
-  unsigned char* x0; // input vector 0 (fp32)
+  unsigned char* x0; // input vector 0 (fp32); also the start of the auxiliary area
   unsigned char* x1; // input vector 1 (fp32)
   unsigned char* stg;  // staging area of the prologue copies
   unsigned char* stages;
@@ -108,31 +113,39 @@ struct SmemSizes {
 
 __host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
-// Layout: [bars][res][red][ints][flts][x0][x1][stg][stages]
-__host__ __device__ inline int gemv_smem_bytes(SmemSizes z) {
-  int off = (2 * kStages + 2) * 8;
+__host__ __device__ inline int smem_head_bytes(int stages) {
+  int off = (2 * stages + 2) * 8;
   off = align_up(off, 16);
-  off += kStages * kMaxTileRows * 4;
+  off += kResBufs * kMaxTileRows * 4;
   off += 256 * 3;
-  off = align_up(off, 128);
-  off += align_up(z.x0, 128) + align_up(z.x1, 128) + align_up(z.stg, 128);
+  return align_up(off, 128);
+}
+
+// Bytes of the auxiliary area [x0][x1][stg].
+__host__ __device__ inline int smem_aux_bytes(SmemSizes z) {
+  return align_up(z.x0, 128) + align_up(z.x1, 128) + align_up(z.stg, 128);
+}
+
+// Layout: [bars][res][red][ints][flts][aux: x0 x1 stg][stages]; `aux` >= smem_aux_bytes
+__host__ __device__ inline int gemv_smem_bytes(int aux, int stages) {
+  int off = smem_head_bytes(stages) + aux;
   off = align_up(off, 1024);
-  off += kStages * kStageBytes;
+  off += stages * kStageBytes;
   return off + 1024;  // slack for base alignment
 }
 
-__device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z) {
+__device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z, int aux, int stages) {
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   Smem s;
   int off = 0;
   s.full = reinterpret_cast<uint64_t*>(base + off);
-  s.empty = s.full + kStages;
-  s.pbar = s.empty + kStages;
-  off += (2 * kStages + 2) * 8;
+  s.empty = s.full + stages;
+  s.pbar = s.empty + stages;
+  off += (2 * stages + 2) * 8;
   off = align_up(off, 16);
   s.res = reinterpret_cast<float*>(base + off);
-  off += kStages * kMaxTileRows * 4;
+  off += kResBufs * kMaxTileRows * 4;
   s.red = reinterpret_cast<float*>(base + off);
   off += 256;
   s.ints = reinterpret_cast<int*>(base + off);
@@ -141,11 +154,9 @@ __device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z) {
   off += 256;
   off = align_up(off, 128);
   s.x0 = base + off;
-  off += align_up(z.x0, 128);
-  s.x1 = base + off;
-  off += align_up(z.x1, 128);
-  s.stg = base + off;
-  off += align_up(z.stg, 128);
+  s.x1 = s.x0 + align_up(z.x0, 128);
+  s.stg = s.x1 + align_up(z.x1, 128);
+  off += aux;
   off = align_up(off, 1024);
   s.stages = base + off;
   return s;
@@ -183,8 +194,8 @@ __device__ inline int tile_units(const SegDesc& sd, int u, int ue) {
   return n;
 }
 
-// Producer lane: issue a list of prologue copies completing on `bar` (arrives once,
-// with the total byte count, even when the list is empty).
+// Issue a list of prologue copies completing on `bar` (arrives once, with the total
+// byte count, even when the list is empty).
 __device__ inline void issue_copies(const Copy* cp, int n, unsigned char* stg, uint64_t* bar) {
   uint32_t bytes = 0;
   for (int i = 0; i < n; ++i) bytes += (uint32_t)cp[i].bytes;
@@ -201,8 +212,76 @@ __device__ inline void issue_copies(const Copy* cp, int n, unsigned char* stg, u
 
 // Consumers: wait until the prologue copies of phase `which` (0 constants, 1
 // activations) have landed.
-__device__ inline bool wait_copies(Smem& sm, int which, int* status) {
-  return mbar_wait(&sm.pbar[which], 0, status);
+__device__ inline bool wait_copies(Smem& sm, int which, uint32_t parity, int* status) {
+  return mbar_wait(&sm.pbar[which], parity, status);
+}
+
+// Position in the stage ring, advanced identically by the producer lane and the
+// consumers of a CTA.
+struct RingPos {
+  int st = 0;         // stage index
+  uint32_t ph = 0;    // parity of the stage's current fill
+  bool wrapped = false;  // the ring has been filled once (the producer waits for `empty`)
+  int tiles = 0;      // tiles passed so far
+  __device__ __forceinline__ void next(int stages) {
+    ++tiles;
+    if (++st == stages) {
+      st = 0;
+      ph ^= 1u;
+      wrapped = true;
+    }
+  }
+};
+
+// Producer lane: fill the next stage with tile (s, u0, n) of `op`.  Returns false
+// (after setting the CTA dead flag) when the stage never became free.
+template <class Op>
+__device__ __forceinline__ bool produce_tile(const Op& op, int s, int u0, int n, Smem& sm, RingPos& rp,
+                                             int stages, uint64_t pol, int* status) {
+  volatile int* dead = sm.ints + kSmemDead;
+  if (rp.wrapped) {
+    // bounded wait for the consumers to release the stage; leave early if they died
+    if (!mbar_try_wait(&sm.empty[rp.st], rp.ph ^ 1u)) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&sm.empty[rp.st], rp.ph ^ 1u)) {
+        if (*dead) return false;
+        if (globaltimer_ns() - t0 > kLocalTimeoutNs) {
+          atomicOr(status, G4_STATUS_MBAR_TIMEOUT);
+          *dead = 1;
+          return false;
+        }
+      }
+    }
+  }
+  mbar_arrive_expect_tx(&sm.full[rp.st], (uint32_t)(n * seg_unit_bytes(op.seg[s])));
+  op.issue(s, u0, n, sm.stages + (size_t)rp.st * kStageBytes, &sm.full[rp.st], pol, sm);
+  rp.next(stages);
+  reinterpret_cast<volatile int*>(sm.ints)[kSmemIssued] = rp.tiles;
+  return true;
+}
+
+// Producer lane: mark the end of issuing (normal or abandoned).
+__device__ __forceinline__ void producer_exit(Smem& sm) {
+  __threadfence_block();
+  reinterpret_cast<volatile int*>(sm.ints)[kSmemProdExit] = 1;
+}
+
+// Consumer thread 0 before the CTA exits after a failure: wait (bounded) for the
+// producer to stop issuing, then for every issued stage past `rp` (the first tile
+// thread 0 did not see complete), so that no bulk copy is still writing into this
+// CTA's shared memory at exit.
+__device__ inline void drain_ring(Smem& sm, RingPos rp, int stages) {
+  volatile int* v = reinterpret_cast<volatile int*>(sm.ints);
+  const uint64_t t0 = globaltimer_ns();
+  while (!v[kSmemProdExit] && globaltimer_ns() - t0 < kLocalTimeoutNs) __nanosleep(256);
+  __threadfence_block();
+  const int issued = v[kSmemIssued];
+  while (rp.tiles < issued) {
+    const uint64_t t1 = globaltimer_ns();
+    while (!mbar_try_wait(&sm.full[rp.st], rp.ph) && globaltimer_ns() - t1 < kLocalTimeoutNs) {
+    }
+    rp.next(stages);
+  }
 }
 
 // Per-tile results (one fp32 dot product per staged row), indexed by row.
@@ -235,12 +314,13 @@ struct XRegs {
 #pragma unroll
     for (int i = 0; i < CPLM; ++i) {
       const int c = lane + 32 * i;
+      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;  // every element written: no live-in
       if (c < C) {
-        const float4 a = reinterpret_cast<const float4*>(x)[2 * c];
-        const float4 b = reinterpret_cast<const float4*>(x)[2 * c + 1];
-        v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-        v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+        a = reinterpret_cast<const float4*>(x)[2 * c];
+        b = reinterpret_cast<const float4*>(x)[2 * c + 1];
       }
+      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
+      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
     }
   }
   // Warp-wide dot product of one staged row (C chunks) with the registers.
@@ -262,91 +342,42 @@ struct XRegs {
 // Chunks per lane needed by a segment.
 __host__ __device__ inline int seg_cpl(const SegDesc& s) { return ((s.K >> 3) + 31) / 32; }
 
-// xmode of a segment (Op::xmode(s)): 0 = one input vector for every sub-row (warps
-// take whole rows); 1 = sub-row j has its own input vector (top-k expert slices of
-// the MoE down projection): warp w owns sub-row j = w % nsub and its vector stays in
-// registers for the whole kernel (nsub must divide the consumer warp count).
-template <class Op, int CPLM>
-__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ Op op) {
-  extern __shared__ unsigned char g4_dyn_smem[];
-  Smem sm = carve_smem(g4_dyn_smem, SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes});
+// Consumers: every tile of `op` owned by this CTA, in ring order.  xmode of a segment
+// (Op::xmode(s)): 0 = one input vector for every sub-row (warps take whole rows); 1 =
+// sub-row j has its own input vector (top-k expert slices of the MoE down projection):
+// warp w owns sub-row j = w % nsub and its vector stays in registers for the whole
+// segment (nsub must divide the consumer warp count).  In xmode 0, row r goes to warp
+// kConsumerWarps-1-r (mod the warp count): with fewer rows than warps, warp 0 -- whose
+// thread 0 also runs the ring bookkeeping of the step kernel -- has no row.
+// Every consumer thread executes the same sequence of named barriers whatever happens,
+// so a timed-out wait (which marks the CTA dead) can never strand a warp at a barrier:
+// after it, the remaining tiles are skipped without waiting.
+// `wp` advances only over the tiles this thread saw complete (the drain starts there).
+// Hooks (all consumer threads call them, in this order per tile):
+//   h.before_wait(rp)  -- before the wait for the tile at rp (step kernel: make sure
+//                         it has been issued)
+//   h.release(st)      -- lane 0 of each warp, after its dot products (per-op kernel:
+//                         arrive on the stage's empty barrier)
+//   h.after_bar(rp)    -- after the barrier that ends the tile's dot products, before
+//                         the epilogue (step kernel: refill the freed stage)
+struct NoHooks {
+  __device__ __forceinline__ void before_wait(const RingPos&) {}
+  __device__ __forceinline__ void release(Smem&, int) {}
+  __device__ __forceinline__ void after_bar(const RingPos&) {}
+};
+struct EmptyBarrierHooks {
+  __device__ __forceinline__ void before_wait(const RingPos&) {}
+  __device__ __forceinline__ void release(Smem& sm, int st) { mbar_arrive(&sm.empty[st]); }
+  __device__ __forceinline__ void after_bar(const RingPos&) {}
+};
+
+template <class Op, int CPLM, class Hooks>
+__device__ __forceinline__ void consume_tiles(const Op& op, Smem& sm, RingPos& rp, RingPos& wp,
+                                              int stages, bool ok, int* status, Hooks& h,
+                                              XRegs<CPLM>& xr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  int* status = op.ctrl + G4_CTRL_STATUS;
-
-  if (threadIdx.x == 0) {
-    for (int i = 0; i < kStages; ++i) {
-      mbar_init(&sm.full[i], 1);
-      mbar_init(&sm.empty[i], kConsumerWarps);
-    }
-    mbar_init(&sm.pbar[0], 1);
-    mbar_init(&sm.pbar[1], 1);
-    mbar_init_fence();
-  }
-  __syncthreads();
-  pdl_trigger();
-  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 0);
-
-  if (warp == kConsumerWarps) {
-    // ------------------------------------------------------------ producer
-    if (lane == 0) {
-      const uint64_t pol = l2_evict_first_policy();
-      issue_copies(op.cc, op.ncc, sm.stg, &sm.pbar[0]);  // constants: before the wait
-      bool waited = false, dep_loaded = false;
-      int t = 0;
-      for (int s = 0; s < op.nseg; ++s) {
-        int ub, ue;
-        cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
-        if (ub >= ue) continue;
-        if (op.seg_dependent(s) && !dep_loaded) {
-          if (!waited) {
-            pdl_wait();
-            G4_TRACE_EV(op.trace_id, 2);
-            waited = true;
-            issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
-          }
-          op.load_dependent(sm);
-          dep_loaded = true;
-        }
-        for (int u = ub; u < ue; ++t) {
-          const int n = tile_units(op.seg[s], u, ue);
-          const int st = t % kStages;
-          if (t >= kStages) {
-            if (!waited) {  // the first stages are in flight: now wait, then activations
-              pdl_wait();
-              G4_TRACE_EV(op.trace_id, 2);
-              waited = true;
-              issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
-            }
-            if (!mbar_wait(&sm.empty[st], ((t / kStages) - 1) & 1, status)) return;
-          }
-          mbar_arrive_expect_tx(&sm.full[st], (uint32_t)(n * seg_unit_bytes(op.seg[s])));
-          op.issue(s, u, n, sm.stages + (size_t)st * kStageBytes, &sm.full[st], pol, sm);
-          if (t == 0) G4_TRACE_EV(op.trace_id, 1);
-          u += n;
-        }
-      }
-      if (!waited) {
-        pdl_wait();
-        G4_TRACE_EV(op.trace_id, 2);
-        issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
-      }
-      G4_TRACE_EV(op.trace_id, 7);
-    }
-    return;
-  }
-
-  // -------------------------------------------------------------- consumers
-  // Every consumer thread executes the same sequence of named barriers whatever
-  // happens, so a timed-out wait (which marks the CTA dead) can never strand a warp
-  // at a barrier: after it, the remaining tiles are skipped without waiting.
   volatile int* dead = sm.ints + kSmemDead;
-  if (threadIdx.x == 0) *dead = 0;
-  named_bar(kBarConsumers, kConsumerThreads);
-  bool ok = op.prologue(sm);  // griddepcontrol.wait, staged vectors, vector math
-  named_bar(kBarConsumers, kConsumerThreads);
-  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 3);
-  XRegs<CPLM> xr;
-  int t = 0;
+  bool first = true;
   for (int s = 0; s < op.nseg; ++s) {
     int ub, ue;
     cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
@@ -356,21 +387,24 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     const int xm = op.xmode(s);
     const int sub = xm ? warp % sd.nsub : 0;
     xr.load(op.xvec(s, sub, sm), C);
-    for (int u = ub; u < ue; ++t) {
+    for (int u = ub; u < ue;) {
       const int n = tile_units(sd, u, ue);
-      const int st = t % kStages;
+      const int st = rp.st;
+      h.before_wait(rp);
       bool live = (*dead == 0);
-      if (live && !mbar_wait(&sm.full[st], (t / kStages) & 1, status)) {
+      if (live && !mbar_wait(&sm.full[st], rp.ph, status)) {
         *dead = 1;
         live = false;
       }
-      if (t == 0 && threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 4);
-      float* res = sm.res + st * kMaxTileRows;
+      if (live) wp.next(stages);
+      if (first && threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 4);
+      first = false;
+      float* res = sm.res + (rp.tiles & (kResBufs - 1)) * kMaxTileRows;
       if (ok && live) {
         const unsigned char* stage = sm.stages + (size_t)st * kStageBytes;
         const int rowbytes = sd.K * 2;
         if (xm == 0) {
-          for (int r = warp; r < n * sd.nsub; r += kConsumerWarps) {  // warp-uniform
+          for (int r = kConsumerWarps - 1 - warp; r < n * sd.nsub; r += kConsumerWarps) {  // warp-uniform
             const float v = xr.dot_row(reinterpret_cast<const uint4*>(stage + (size_t)r * rowbytes), C);
             if (lane == 0) res[r] = v;
           }
@@ -384,15 +418,104 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
         }
       }
       __syncwarp();
-      if (lane == 0 && live) mbar_arrive(&sm.empty[st]);
+      if (lane == 0 && live) h.release(sm, st);
       named_bar(kBarConsumers, kConsumerThreads);
+      h.after_bar(rp);
       op.epilogue(s, u, n, Res{res}, sm, ok && (*dead == 0));
       u += n;
+      rp.next(stages);
     }
   }
+}
+
+// Weight-streaming kernel of one operator (the per-op launch mode of the decode step).
+template <class Op, int CPLM>
+__global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_constant__ Op op) {
+  extern __shared__ unsigned char g4_dyn_smem[];
+  const SmemSizes z{op.xbytes[0], op.xbytes[1], op.stgbytes};
+  Smem sm = carve_smem(g4_dyn_smem, z, smem_aux_bytes(z), kStages);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  int* status = op.ctrl + G4_CTRL_STATUS;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kConsumerWarps);
+    }
+    mbar_init(&sm.pbar[0], 1);
+    mbar_init(&sm.pbar[1], 1);
+    mbar_init_fence();
+    sm.ints[kSmemDead] = 0;
+    sm.ints[kSmemIssued] = 0;
+    sm.ints[kSmemProdExit] = 0;
+  }
+  __syncthreads();
+  pdl_trigger();
+  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 0);
+
+  if (warp == kConsumerWarps) {
+    // ------------------------------------------------------------ producer
+    // Constants and the first kStages weight tiles go out before griddepcontrol.wait
+    // (weights never depend on the previous kernel); the activation copies right after.
+    if (lane == 0) {
+      const uint64_t pol = l2_evict_first_policy();
+      issue_copies(op.cc, op.ncc, sm.stg, &sm.pbar[0]);
+      bool waited = false, dep_loaded = false, alive = true;
+      RingPos rp;
+      for (int s = 0; s < op.nseg && alive; ++s) {
+        int ub, ue;
+        cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
+        if (ub >= ue) continue;
+        if (op.seg_dependent(s) && !dep_loaded) {
+          if (!waited) {
+            pdl_wait();
+            G4_TRACE_EV(op.trace_id, 2);
+            waited = true;
+            issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
+          }
+          op.load_dependent(sm);
+          dep_loaded = true;
+        }
+        for (int u = ub; u < ue && alive;) {
+          const int n = tile_units(op.seg[s], u, ue);
+          if (rp.wrapped && !waited) {
+            pdl_wait();
+            G4_TRACE_EV(op.trace_id, 2);
+            waited = true;
+            issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
+          }
+          alive = produce_tile(op, s, u, n, sm, rp, kStages, pol, status);
+          if (rp.tiles == 1) G4_TRACE_EV(op.trace_id, 1);
+          u += n;
+        }
+      }
+      if (!waited) {
+        pdl_wait();
+        G4_TRACE_EV(op.trace_id, 2);
+        issue_copies(op.ac, op.nac, sm.stg, &sm.pbar[1]);
+      }
+      producer_exit(sm);
+      G4_TRACE_EV(op.trace_id, 7);
+    }
+    return;
+  }
+
+  // -------------------------------------------------------------- consumers
+  pdl_wait();
+  bool ok = wait_copies(sm, 0, 0, status);
+  ok = wait_copies(sm, 1, 0, status) && ok;
+  ok = op.prologue(sm) && ok;  // staged vectors, vector math
+  named_bar(kBarConsumers, kConsumerThreads);
+  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 3);
+  RingPos rp, wp;
+  EmptyBarrierHooks hooks;
+  XRegs<CPLM> xr;
+  consume_tiles<Op, CPLM>(op, sm, rp, wp, kStages, ok, status, hooks, xr);
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 5);
-  op.finish(sm, ok && (*dead == 0));
+  op.finish(sm, ok && (sm.ints[kSmemDead] == 0));
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 6);
+  named_bar(kBarConsumers, kConsumerThreads);
+  if (threadIdx.x == 0 && sm.ints[kSmemDead]) drain_ring(sm, wp, kStages);
 }
 
 }  // namespace g4

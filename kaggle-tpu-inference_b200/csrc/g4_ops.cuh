@@ -19,8 +19,8 @@
 //
 // Prologue vectors (norm weights; the previous kernel's outputs at world 1) arrive in
 // the shared staging area by bulk copies (OpBase::cc / ac, offsets planned on the
-// host); the vector math runs as short loops over shared memory, thread t owning the
-// elements h = t, t+256, ...  Input vectors of the matrix products are fp32 in shared
+// host) before prologue() runs; the vector math runs as short loops over shared memory,
+// thread t owning the elements h = t, t+256, ...  Input vectors of the matrix products are fp32 in shared
 // memory (values exactly bf16) and move to registers in the engine.
 //
 // Rounding follows the reference's bf16 graph: every einsum output is rounded to bf16
@@ -41,7 +41,7 @@ constexpr int kSiteAttn = 0, kSiteFfn = 1, kSiteArgmax = 2;
 constexpr int kXFlagBytes = kSites * 2 * kMaxWorld * 128;
 // Smem::ints slots
 constexpr int kSmemExp = 0;        // [0,16) expert ids (producer copy)
-constexpr int kSmemRouterDone = 32;
+constexpr int kSmemRouterEnd = 32;  // end of this CTA's router units (0: none)
 constexpr int kSmemLast = 33;
 constexpr int kSmemOk = 34;
 constexpr int kSmemWriteLogits = 35;
@@ -119,7 +119,8 @@ __device__ __forceinline__ float bsum(float v, Smem& sm) {
 // Output of layer `tail` from the previous kernels (model.py:312-322):
 //   h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2, h = rms(h1+h2)*pf, x = (resmid + h)*scalar.
 // Staged inputs: pf1/pf2/pf (bf16 constants); world 1: mlp (fp32), moe and resmid
-// (bf16).  Result x (bf16 values) in the fp32 temporary t0.
+// (bf16).  Result x (bf16 values) in the fp32 temporary t0.  t0 may alias the staged
+// mlp vector (each element is read before it is overwritten by the same thread).
 struct Tail {
   const bf16_t* resmid;  // residual after attention (bf16 [H])
   const bf16_t* scalar;  // layer_scalar [1]
@@ -128,10 +129,8 @@ struct Tail {
   int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ inline bool layer_output(int* ctrl, const Common& c, const Tail& t, int o_t0,
-                                    int o_t1, Smem& sm) {
-  float* t0 = sf(sm, o_t0);
-  float* t1 = sf(sm, o_t1);
+__device__ inline bool layer_output(int* ctrl, const Common& c, const Tail& t, float* t0,
+                                    float* t1, Smem& sm) {
   const int H = c.H, tid = threadIdx.x;
   bool ok = true;
   float s1 = 0.f, s2 = 0.f;
@@ -194,20 +193,13 @@ __device__ inline void widen(const bf16_t* src, int n, float* dst) {
   for (int i = threadIdx.x; i < n; i += kConsumerThreads) dst[i] = bf2f(src[i]);
 }
 
-__device__ inline bool wait_both(Smem& sm, int* ctrl) {
-  int* st = ctrl + G4_CTRL_STATUS;
-  const bool a = wait_copies(sm, 0, st);
-  const bool b = wait_copies(sm, 1, st);
-  return a && b;
-}
-
 // ================================================================== K1: q|k|v
 struct QkvOp : OpBase {
   Common c;
   const bf16_t* w;     // [rows, H]: q rows, k rows, v rows of this rank
   bf16_t* out;         // q|k|v projections (bf16 [rows])
   bf16_t* xres;        // layer input x (bf16 [H]), written by CTA 0
-  int o_win, o_t0, o_t1;
+  int o_win, o_t0;
   // layer 0: token embedding
   const bf16_t* embed;  // replicated [V, H]
   const int* tokens_in;
@@ -228,9 +220,9 @@ struct QkvOp : OpBase {
     return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    bool ok = wait_both(sm, ctrl);
+    bool ok = true;
     float* t0 = sf(sm, o_t0);
+    float* t1 = reinterpret_cast<float*>(sm.x0);  // dead before x0 is written
     if (c.layer == 0) {
       int pos = ldcg_i(ctrl + G4_CTRL_POS);
       if (pos < 0 || pos >= max_len) pos = 0;  // flagged by the attention / lm_head kernels
@@ -243,7 +235,7 @@ struct QkvOp : OpBase {
       const bf16_t* row = embed + (size_t)tok * c.H;
       for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) t0[h] = rbf(bf2f(row[h]) * embed_scale);
     } else {
-      ok = layer_output(ctrl, c, tail, o_t0, o_t1, sm) && ok;
+      ok = layer_output(ctrl, c, tail, t0, t1, sm) && ok;
     }
     if (blockIdx.x == 0)
       for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) xres[h] = f2bf(t0[h]);
@@ -275,10 +267,8 @@ struct OProjOp : OpBase {
     return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    const bool ok = wait_both(sm, ctrl);
     widen(sbf(sm, o_ctx), Kc, reinterpret_cast<float*>(sm.x0));
-    return ok;
+    return true;
   }
   __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     if (!ok || (int)threadIdx.x >= n) return;
@@ -314,9 +304,10 @@ struct RouterMlpOp : OpBase {
   float hinv;              // bf16(H^-0.5) as float
   int o_wpa, o_wff, o_wff2, o_wrs;  // staged constants
   int o_o, o_x;                     // staged activations: o_proj out (fp32), x (bf16)
-  int o_t0, o_t1;
+  int o_t0;
   int block_mode;                   // 1: the input is already the MoE input (g4_moe_block)
   const bf16_t* block_x;
+  int* ready;                       // step kernel: router flag of this layer (else null)
 
   __device__ int xmode(int) const { return 0; }
   __device__ bool seg_dependent(int) const { return false; }
@@ -335,11 +326,10 @@ struct RouterMlpOp : OpBase {
     return reinterpret_cast<const float*>(s == 0 ? sm.x0 : sm.x1);
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    bool ok = wait_both(sm, ctrl);
+    bool ok = true;
     const int H = c.H, tid = threadIdx.x;
     float* t0 = sf(sm, o_t0);
-    float* t1 = sf(sm, o_t1);
+    float* t1 = reinterpret_cast<float*>(sm.x0);  // becomes the router input in place
     if (!block_mode) {
       // attention output (summed over ranks), then x = residual + rms(attn)*post_attn
       float s = 0.f;
@@ -396,26 +386,39 @@ struct RouterMlpOp : OpBase {
     float* xr = reinterpret_cast<float*>(sm.x0);
     for (int h = tid; h < H; h += kConsumerThreads)
       xr[h] = rbf(rbf(rbf(t1[h] * r3) * bf2f(wrs[h])) * hinv);
-    if (tid == 0) sm.ints[kSmemRouterDone] = 0;
+    if (tid == 0) {
+      int ub, ue;
+      cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
+      sm.ints[kSmemRouterEnd] = ub < ue ? ue : 0;
+    }
     return ok;
   }
   __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (s == 0) {
       if (ok && t < n) router_logits[u0 + t] = rbf(res[t]);
-      if (t == 0) sm.ints[kSmemRouterDone] += n;
+      // right after this CTA's last router tile (identical test on every thread):
+      // count its rows in; the CTA completing all E logits selects the top-k now,
+      // early in the operator, so the expert weights can stream behind it
+      if (u0 + n == sm.ints[kSmemRouterEnd]) router_done(router_units(), sm);
     } else if (ok && t < n) {
       const float g = rbf(res[t]), u = rbf(res[n + t]);
       mlp_act[u0 + t] = f2bf(rbf(gelu_tanh(g)) * u);
     }
   }
-  __device__ void finish(Smem& sm, bool) const {
-    // The CTA that completes the router's E logits selects the top-k (model.py:227-232).
+  __device__ void finish(Smem&, bool) const {}
+  // Router units this CTA owns (its range of segment 0).
+  __device__ int router_units() const {
+    int ub, ue;
+    cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
+    return ue - ub;
+  }
+  // The CTA that completes the router's E logits selects the top-k (model.py:227-232).
+  __device__ void router_done(int mine, Smem& sm) const {
     __threadfence();
     named_bar(kBarReduce, kConsumerThreads);
     if (threadIdx.x == 0) {
       int last = 0;
-      const int mine = sm.ints[kSmemRouterDone];
       if (mine > 0) {
         int old = atomic_add_acq_rel_gpu(c.counters + kCntRouter, mine);
         last = (old + mine == E);
@@ -424,7 +427,9 @@ struct RouterMlpOp : OpBase {
       sm.ints[kSmemLast] = last;
     }
     named_bar(kBarReduce, kConsumerThreads);
-    if (!sm.ints[kSmemLast] || threadIdx.x >= 32) return;
+    const bool last = sm.ints[kSmemLast] != 0;
+    named_bar(kBarReduce, kConsumerThreads);  // the flag slot is reused by later code
+    if (!last || threadIdx.x >= 32) return;
     __threadfence();
     const int lane = threadIdx.x;
     // Each lane holds logits e = lane + 32 j; softmax and the top-k selection run in
@@ -483,6 +488,11 @@ struct RouterMlpOp : OpBase {
       top_idx[lane] = sel_i;
       top_w[lane] = (sel_p / wsum) * bf2f(pes[sel_i]);
     }
+    __syncwarp();
+    if (lane == 0 && ready) {  // the step kernel's producers wait for this flag
+      __threadfence();
+      st_release_gpu(ready, sm.ints[kSmemSeq] + 1);
+    }
   }
 };
 
@@ -526,12 +536,10 @@ struct MoeUpOp : OpBase {
     return reinterpret_cast<const float*>(s == 0 ? sm.x1 : sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    const bool ok = wait_both(sm, ctrl);
     widen(sbf(sm, o_h2), c.H, reinterpret_cast<float*>(sm.x0));
     widen(sbf(sm, o_act), I, reinterpret_cast<float*>(sm.x1));
     if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
-    return ok;
+    return true;
   }
   __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
@@ -573,10 +581,8 @@ struct MoeDownOp : OpBase {
     return reinterpret_cast<const float*>(sm.x0) + j * F;
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    const bool ok = wait_both(sm, ctrl);
     widen(sbf(sm, o_act), topk * F, reinterpret_cast<float*>(sm.x0));
-    return ok;
+    return true;
   }
   __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     const int t = threadIdx.x;
@@ -608,7 +614,7 @@ struct MoeDownOp : OpBase {
 struct LmHeadOp : OpBase {
   Common c;
   Tail tail;
-  int o_wn, o_t0, o_t1;  // staged final norm weight, temporaries
+  int o_wn, o_t0;        // staged final norm weight, temporary
   const bf16_t* embed;   // replicated [V, H]; this rank reads rows [vbegin, vbegin+V_local)
   int vbegin;
   float* logits;         // [V_local] fp32 (written when control[WRITE_LOGITS] != 0)
@@ -630,9 +636,7 @@ struct LmHeadOp : OpBase {
     return reinterpret_cast<const float*>(sm.x0);
   }
   __device__ bool prologue(Smem& sm) const {
-    pdl_wait();
-    bool ok = wait_both(sm, ctrl);
-    ok = layer_output(ctrl, c, tail, o_t0, o_t1, sm) && ok;
+    const bool ok = layer_output(ctrl, c, tail, sf(sm, o_t0), reinterpret_cast<float*>(sm.x0), sm);
     norm_into(c, sf(sm, o_t0), sbf(sm, o_wn), reinterpret_cast<float*>(sm.x0), sm);
     float* bv = reinterpret_cast<float*>(sm.x1);
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;

@@ -1,11 +1,13 @@
 // Host runtime of g4b200: communicator, model plan, step launcher, graph capture and
 // the C ABI declared in include/g4b200.h.
 //
-// A decode step is 6 kernels per layer + 1 (embedding is fused into layer 0's first
-// kernel, the argmax into the lm_head kernel).  All kernels are launched with the
-// programmatic-stream-serialization attribute so each one is scheduled while its
-// predecessor drains and prefetches its weights before griddepcontrol.wait; the whole
-// step is captured once into a CUDA graph and replayed per token.
+// A decode step runs in one of two engines over the same operator plans:
+//   G4_ENGINE_STEP_KERNEL (default): one persistent cooperative launch per token
+//     (g4_step.cuh) with a single weight ring across all operators;
+//   G4_ENGINE_OP_KERNELS: 6 kernels per layer + 1 (embedding fused into layer 0's
+//     first kernel, the argmax into the lm_head kernel), chained with programmatic
+//     dependent launches.
+// Either step is captured once into a CUDA graph and replayed per token.
 #include <cuda_runtime.h>
 
 #include <cmath>
@@ -19,6 +21,7 @@
 
 #include "g4_attention.cuh"
 #include "g4_ops.cuh"
+#include "g4_step.cuh"
 
 using namespace g4;
 
@@ -213,7 +216,7 @@ static int prepare_attention(int d, int g) {
 
 template <class Op, int CPLM>
 static int launch_gemv_t(const Op& op, int grid, cudaStream_t st) {
-  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes});
+  const int smem = gemv_smem_bytes(smem_aux_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes}), kStages);
   int rc = prepare_kernel<Op, CPLM>(smem);
   if (rc) return rc;
   cudaError_t e = launch_pdl(gemv_kernel<Op, CPLM>, dim3(grid), dim3(kGemvThreads), smem, st, op);
@@ -305,6 +308,14 @@ struct g4_model {
   std::vector<MoeUpOp> k5;
   std::vector<MoeDownOp> k6;
   LmHeadOp lm{};
+  // persistent step kernel
+  int engine = G4_ENGINE_STEP_KERNEL;
+  StepProgram prog{};
+  int step_cplm = 0;
+  const void* step_kernel = nullptr;
+  char* prog_mem = nullptr;  // device copies of the operator plans
+  bool prog_dirty = true;    // host plans changed since the last upload
+  int* sync = nullptr;       // kNumSyncWords (library scratch)
   float* rope_tab = nullptr;
   int* tokens_host = nullptr;  // mapped pinned mirror of tokens_out (g4_model_host_tokens)
   cudaGraph_t graph = nullptr;
@@ -539,6 +550,162 @@ static Tail plan_tail(const g4_model* m, int layer, Stager& sg) {
   return t;
 }
 
+static const StepVariant* find_step_variant(const g4_model* m);
+
+// Register bucket of a launch whose longest matrix row needs `chunks_per_lane`.
+static int cplm_bucket(int m) { return m <= 4 ? 4 : (m <= 8 ? 8 : (m <= 12 ? 12 : (m <= 16 ? 16 : 0))); }
+
+template <class Op>
+static void step_sizes(const Op& op, SmemSizes& z, int& cpl) {
+  z.x0 = std::max(z.x0, op.xbytes[0]);
+  z.x1 = std::max(z.x1, op.xbytes[1]);
+  z.stg = std::max(z.stg, op.stgbytes);
+  for (int s = 0; s < op.nseg; ++s)
+    if (op.seg[s].units > 0) cpl = std::max(cpl, seg_cpl(op.seg[s]));
+}
+
+// Shared-memory plan of the persistent step kernel: the auxiliary area holds the
+// largest operator's vectors and staging (or the attention scratch); the ring gets
+// every remaining byte (kMaxStages at most).  Device copies of the plans are made by
+// upload_step_program.
+static int plan_step_program(g4_model* m) {
+  const int nl = (int)m->L.size();
+  if (nl > kNumSyncWords - kSyncRouter) return fail(G4_ERR_SHAPE, "too many layers for the step kernel");
+  SmemSizes z{0, 0, 0};
+  int cpl = 1;
+  for (int i = 0; i < nl; ++i) {
+    step_sizes(m->k1[i], z, cpl);
+    step_sizes(m->k3[i], z, cpl);
+    step_sizes(m->k4[i], z, cpl);
+    step_sizes(m->k5[i], z, cpl);
+    step_sizes(m->k6[i], z, cpl);
+  }
+  step_sizes(m->lm, z, cpl);
+  int aux = smem_aux_bytes(z);
+  for (const LayerDev& l : m->L) aux = std::max(aux, align_up(attn_smem_bytes(l.g, l.d), 128));
+  int optin = 0;
+  cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
+  const int limit = std::min(kMaxSmemBytes, optin > 0 ? optin : kMaxSmemBytes);
+  int stages = kMaxStages;
+  while (stages >= 3 && gemv_smem_bytes(aux, stages) > limit) --stages;
+  if (stages < 3) return fail(G4_ERR_SHAPE, "step kernel: %d bytes of vectors leave no room for the ring", aux);
+  m->step_cplm = cplm_bucket(cpl);
+  if (!m->step_cplm) return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank");
+  // default engine: the step kernel when a variant for these shapes is compiled in
+  m->engine = find_step_variant(m) ? G4_ENGINE_STEP_KERNEL : G4_ENGINE_OP_KERNELS;
+  StepProgram& p = m->prog;
+  p = StepProgram{};
+  p.sync = m->sync;
+  p.ctrl = m->ctrl;
+  p.nlayers = nl;
+  p.stages = stages;
+  p.z = z;
+  p.aux = aux;
+  const size_t bytes = (sizeof(QkvOp) + sizeof(AttnArgs) + sizeof(OProjOp) + sizeof(RouterMlpOp) +
+                        sizeof(MoeUpOp) + sizeof(MoeDownOp) + 6 * 256) * (size_t)nl +
+                       sizeof(LmHeadOp) + 256;
+  if (cudaMalloc(&m->prog_mem, bytes) != cudaSuccess) return fail(G4_ERR_NOMEM, "step program");
+  m->prog_dirty = true;
+  return G4_OK;
+}
+
+// Copy the host plans into the program's device arrays (after any host-side change,
+// e.g. g4_model_host_tokens, and before the step kernel's first launch or capture).
+static int upload_step_program(g4_model* m) {
+  if (!m->prog_dirty) return G4_OK;
+  const size_t nl = m->L.size();
+  char* d = m->prog_mem;
+  size_t off = 0;
+  auto put = [&](const void* src, size_t bytes) -> char* {
+    char* dst = d + off;
+    off += (bytes + 255) / 256 * 256;
+    cudaMemcpy(dst, src, bytes, cudaMemcpyHostToDevice);
+    return dst;
+  };
+  StepProgram& p = m->prog;
+  p.k1 = reinterpret_cast<const QkvOp*>(put(m->k1.data(), nl * sizeof(QkvOp)));
+  p.k2 = reinterpret_cast<const AttnArgs*>(put(m->k2.data(), nl * sizeof(AttnArgs)));
+  p.k3 = reinterpret_cast<const OProjOp*>(put(m->k3.data(), nl * sizeof(OProjOp)));
+  p.k4 = reinterpret_cast<const RouterMlpOp*>(put(m->k4.data(), nl * sizeof(RouterMlpOp)));
+  p.k5 = reinterpret_cast<const MoeUpOp*>(put(m->k5.data(), nl * sizeof(MoeUpOp)));
+  p.k6 = reinterpret_cast<const MoeDownOp*>(put(m->k6.data(), nl * sizeof(MoeDownOp)));
+  p.lm = reinterpret_cast<const LmHeadOp*>(put(&m->lm, sizeof(LmHeadOp)));
+  G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
+  m->prog_dirty = false;
+  return G4_OK;
+}
+
+// ------------------------------------------------------------------ step variants
+static std::vector<StepVariant>& step_variants() {
+  static std::vector<StepVariant> v;  // filled by static initialisers of g4_step_*.cu
+  return v;
+}
+void g4::register_step_variant(const StepVariant& v) { step_variants().push_back(v); }
+
+// Attention shape of the sliding / full layers on this rank (a model without one kind
+// uses the other's).
+static void attn_shapes(const g4_model* m, int& ds, int& gs, int& df, int& gf) {
+  ds = gs = df = gf = 0;
+  for (const LayerDev& l : m->L) {
+    if (l.full) { df = l.d; gf = l.g; }
+    else { ds = l.d; gs = l.g; }
+  }
+  if (!ds) { ds = df; gs = gf; }
+  if (!df) { df = ds; gf = gs; }
+}
+
+// The compiled step-kernel variant for this model (smallest register bucket that
+// holds its longest row), or null.
+static const StepVariant* find_step_variant(const g4_model* m) {
+  int ds, gs, df, gf;
+  attn_shapes(m, ds, gs, df, gf);
+  for (const LayerDev& l : m->L)
+    if ((l.full ? (l.d != df || l.g != gf) : (l.d != ds || l.g != gs))) return nullptr;
+  const StepVariant* best = nullptr;
+  for (const StepVariant& v : step_variants())
+    if (v.ds == ds && v.gs == gs && v.df == df && v.gf == gf && v.cplm >= m->step_cplm &&
+        (!best || v.cplm < best->cplm))
+      best = &v;
+  return best;
+}
+
+// Kernel attributes and the residency check of the cooperative launch.
+static int prepare_step(g4_model* m) {
+  const StepVariant* v = find_step_variant(m);
+  if (!v) return fail(G4_ERR_SHAPE, "no step-kernel variant for this model's shapes");
+  const int smem = step_smem_bytes(m->prog);
+  cudaFuncAttributes fa{};
+  G4_CUDA(cudaFuncGetAttributes(&fa, v->kernel), G4_ERR_LAUNCH);
+  if (fa.numRegs != kStepLaunchRegs)  // the setmaxnreg split is sized for this count
+    return fail(G4_ERR_LAUNCH, "step kernel built with %d registers per thread, expected %d", fa.numRegs,
+                kStepLaunchRegs);
+  G4_CUDA(cudaFuncSetAttribute(v->kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), G4_ERR_LAUNCH);
+  int per_sm = 0;
+  G4_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, v->kernel, kStepThreads, smem),
+          G4_ERR_LAUNCH);
+  if (per_sm < 1) return fail(G4_ERR_LAUNCH, "step kernel does not fit on an SM (%d bytes)", smem);
+  m->step_kernel = v->kernel;
+  return upload_step_program(m);
+}
+
+static int launch_step(g4_model* m, cudaStream_t st) {
+  if (!m->step_kernel) return fail(G4_ERR_STATE, "step kernel not prepared");
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(m->nsm);
+  cfg.blockDim = dim3(kStepThreads);
+  cfg.dynamicSmemBytes = step_smem_bytes(m->prog);
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeCooperative;  // every CTA resident: grid barriers are safe
+  attr[0].val.cooperative = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  void* args[] = {&m->prog};
+  cudaError_t e = cudaLaunchKernelExC(&cfg, m->step_kernel, args);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "step kernel launch: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
 extern "C" int g4_model_finalize(g4_model* m) {
   if (!m) return fail(G4_ERR_ARG, "g4_model_finalize: null model");
   if (m->finalized) return G4_OK;
@@ -583,6 +750,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
   const size_t o_part = take(max_part * 4), o_acnt = take(max_nkv * 4);
   const size_t o_cv = take((size_t)m->nsm * 4), o_ci = take((size_t)m->nsm * 4);
   const size_t o_cnt = take(kNumCounters * 4);
+  const size_t o_sync = take(kNumSyncWords * 4);
   if (cudaMalloc(&m->scratch, off) != cudaSuccess)
     return fail(G4_ERR_NOMEM, "scratch cudaMalloc(%zu) failed", off);
   cudaMemset(m->scratch, 0, off);
@@ -605,6 +773,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
   m->cand_v = (float*)(s + o_cv);
   m->cand_i = (int*)(s + o_ci);
   m->counters = (int*)(s + o_cnt);
+  m->sync = (int*)(s + o_sync);
 
   // ---- plans
   const g4_config& c = m->cfg;
@@ -632,8 +801,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
       Stager sg(&a);
       a.o_win = sg.constant(l.n_in, H * 2);
       if (i > 0) a.tail = plan_tail(m, i - 1, sg);
-      a.o_t0 = sg.space(H * 4);
-      a.o_t1 = sg.space(H * 4);
+      // the layer-output temporary may overwrite the staged MLP output (read first)
+      a.o_t0 = (i > 0 && m->world == 1) ? a.tail.o_mlp : sg.space(H * 4);
     }
     a.w = l.qkv;
     a.out = m->qkv_raw;
@@ -702,8 +871,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
       r.o_wrs = sg.constant(l.router_scale, H * 2);
       if (m->world == 1) r.o_o = sg.activation(m->o_out, H * 4);
       r.o_x = sg.activation(m->xres, H * 2);
-      r.o_t0 = sg.space(H * 4);
-      r.o_t1 = sg.space(H * 4);
+      // the residual temporary may overwrite the staged o_proj output (read first)
+      r.o_t0 = m->world == 1 ? r.o_o : sg.space(H * 4);
     }
     r.xres = m->xres;
     r.resmid = m->resmid;
@@ -719,6 +888,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.E = m->E;
     r.topk = m->topk;
     r.hinv = hinv;
+    r.ready = m->sync + kSyncRouter + i;
 
     MoeUpOp& u = m->k5[i];
     u = MoeUpOp{};
@@ -778,8 +948,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
       Stager sg(&lm);
       lm.o_wn = sg.constant(m->final_norm, H * 2);
       lm.tail = plan_tail(m, nl - 1, sg);
-      lm.o_t0 = sg.space(H * 4);
-      lm.o_t1 = sg.space(H * 4);
+      lm.o_t0 = m->world == 1 ? lm.tail.o_mlp : sg.space(H * 4);
     }
     lm.embed = m->embed;
     lm.vbegin = m->vbegin;
@@ -802,6 +971,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
     m->rope_tab = dev;
     for (int i = 0; i < nl; ++i) m->k2[i].inv_freq = m->L[i].full ? dev + dsl / 2 : dev;
   }
+  int rc = plan_step_program(m);
+  if (rc) return rc;
   G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
   m->finalized = true;
   return G4_OK;
@@ -809,7 +980,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
 
 template <class Op>
 static int prepare_op(const Op& op) {
-  const int smem = gemv_smem_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes});
+  const int smem = gemv_smem_bytes(smem_aux_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes}), kStages);
   switch (op_cplm(op)) {
     case 4: return prepare_kernel<Op, 4>(smem);
     case 8: return prepare_kernel<Op, 8>(smem);
@@ -820,6 +991,7 @@ static int prepare_op(const Op& op) {
 }
 
 static int prepare_all(g4_model* m) {
+  if (m->engine == G4_ENGINE_STEP_KERNEL) return prepare_step(m);
   int rc;
   for (size_t i = 0; i < m->L.size(); ++i) {
     if ((rc = prepare_op(m->k1[i])) || (rc = prepare_op(m->k3[i])) || (rc = prepare_op(m->k4[i])) ||
@@ -831,6 +1003,7 @@ static int prepare_all(g4_model* m) {
 }
 
 static int enqueue_step(g4_model* m, cudaStream_t st) {
+  if (m->engine == G4_ENGINE_STEP_KERNEL) return launch_step(m, st);
   const int nl = (int)m->L.size();
   int rc;
   for (int i = 0; i < nl; ++i) {
@@ -856,6 +1029,7 @@ extern "C" int g4_model_host_tokens(g4_model* m, int** host_ptr) {
     int* dptr = nullptr;
     G4_CUDA(cudaHostGetDevicePointer((void**)&dptr, m->tokens_host, 0), G4_ERR_CUDA);
     m->lm.tokens_host = dptr;
+    m->prog_dirty = true;
   }
   *host_ptr = m->tokens_host;
   return G4_OK;
@@ -918,6 +1092,14 @@ extern "C" int g4_trace_read(void* host_dst, long long bytes) {
   if (!host_dst || bytes < need) return fail(G4_ERR_ARG, "g4_trace_read: need %lld bytes", need);
   G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
   G4_CUDA(cudaMemcpyFromSymbol(host_dst, g4_trace_buf, need), G4_ERR_CUDA);
+  // every step-kernel variant is its own device module with its own buffer: merge
+  // (per slot, the latest stamp)
+  unsigned long long* dst = static_cast<unsigned long long*>(host_dst);
+  std::vector<unsigned long long> tmp((size_t)need / 8);
+  for (const StepVariant& v : step_variants()) {
+    if (v.trace_read(tmp.data(), need) != 0) continue;
+    for (size_t i = 0; i < tmp.size(); ++i) dst[i] = std::max(dst[i], tmp[i]);
+  }
   return G4_OK;
 #else
   (void)host_dst;
@@ -927,13 +1109,29 @@ extern "C" int g4_trace_read(void* host_dst, long long bytes) {
 }
 
 extern "C" int g4_model_kernel_count(const g4_model* m) {
-  return m ? 6 * (int)m->L.size() + 1 : 0;
+  if (!m) return 0;
+  return m->engine == G4_ENGINE_STEP_KERNEL ? 1 : 6 * (int)m->L.size() + 1;
+}
+
+extern "C" int g4_model_set_engine(g4_model* m, int engine) {
+  if (!m) return fail(G4_ERR_ARG, "g4_model_set_engine: null model");
+  if (engine != G4_ENGINE_STEP_KERNEL && engine != G4_ENGINE_OP_KERNELS)
+    return fail(G4_ERR_ARG, "g4_model_set_engine: unknown engine %d", engine);
+  if (m->gexec) return fail(G4_ERR_STATE, "g4_model_set_engine after g4_graph_capture");
+  if (engine == G4_ENGINE_STEP_KERNEL && m->finalized && !find_step_variant(m))
+    return fail(G4_ERR_SHAPE, "no step-kernel variant for this model's shapes");
+  m->engine = engine;
+  return G4_OK;
 }
 
 extern "C" int g4_step(g4_model* m, void* stream) {
   if (!m) return fail(G4_ERR_ARG, "g4_step: null model");
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_step before g4_model_finalize");
   G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  if (m->engine == G4_ENGINE_STEP_KERNEL) {
+    int rc = prepare_step(m);
+    if (rc) return rc;
+  }
   return enqueue_step(m, static_cast<cudaStream_t>(stream));
 }
 
@@ -993,7 +1191,20 @@ extern "C" int g4_model_status(g4_model* m, void* stream, int* status_out) {
   int st = 0;
   G4_CUDA(cudaMemcpy(&st, m->ctrl + G4_CTRL_STATUS, 4, cudaMemcpyDeviceToHost), G4_ERR_CUDA);
   if (status_out) *status_out = st;
-  if (st) return fail(G4_ERR_TIMEOUT, "device status word 0x%x", st);
+  if (st) {
+    // A step that gave up may leave grid-barrier arrivals, router flags and "last
+    // CTA" counters mid-count; the kernels do not start while STATUS is set, so the
+    // library's words are cleared here, before the caller clears STATUS.
+    if (m->finalized) {
+      cudaMemset(m->counters, 0, kNumCounters * 4);
+      size_t nkv = 0;
+      for (const LayerDev& l : m->L) nkv = std::max(nkv, (size_t)l.n_kv);
+      cudaMemset(m->attn_cnt, 0, nkv * 4);
+      cudaMemset(m->sync, 0, kNumSyncWords * 4);
+      cudaDeviceSynchronize();
+    }
+    return fail(G4_ERR_TIMEOUT, "device status word 0x%x", st);
+  }
   return G4_OK;
 }
 
@@ -1003,6 +1214,7 @@ extern "C" int g4_model_destroy(g4_model* m) {
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   if (m->graph) cudaGraphDestroy(m->graph);
   if (m->rope_tab) cudaFree(m->rope_tab);
+  if (m->prog_mem) cudaFree(m->prog_mem);
   if (m->tokens_host) cudaFreeHost(m->tokens_host);
   if (m->scratch) cudaFree(m->scratch);
   if (m->own_comm) g4_comm_destroy(m->own_comm);
@@ -1192,7 +1404,6 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
     Stager sg(&r);
     r.o_wrs = sg.constant(router_scale, H * 2);
     r.o_t0 = sg.space(H * 4);
-    r.o_t1 = sg.space(H * 4);
   }
   r.block_mode = 1;
   r.block_x = static_cast<const bf16_t*>(x);

@@ -1,0 +1,418 @@
+// Persistent decode-step kernel: the whole forward step of one token
+// (gemma4_tpu/model.py:333-386, driven by engine.py:57-83) in ONE launch.
+//
+// The per-op launch mode pays, at every one of the 6 L + 1 kernel boundaries, a
+// drained weight ring, a cold parameter fetch and the prologue's dependency chain
+// while HBM idles.  Here one CTA per SM (cooperative launch, so every CTA is
+// resident) runs the operator program
+//
+//   for l in layers: QKV, ATTENTION, O_PROJ, ROUTER+MLP, MLP_DOWN+EXPERTS_UP, EXPERTS_DOWN
+//   LM_HEAD
+//
+// with a grid barrier between consecutive operators, and ONE ring of weight stages
+// per CTA that runs across the whole program: the producer lane walks the CTA's tiles
+// of every operator in program order, so while the consumers wait at a barrier, run
+// a prologue or compute attention, the ring already holds the next operator's
+// weights.  Weight addresses never depend on activations except the expert tiles,
+// for which the producer waits on the layer's router flag; the router's top-k is
+// published as soon as the router rows are done (they come first in their
+// operator), so the expert weights stream in while the dense MLP rows are still
+// being consumed.
+//
+// Warp specialisation with register reallocation: 12 warps, launched at 168
+// registers per thread.  The 4 warps of the producer warpgroup drop to 40
+// (setmaxnreg.dec; lane 0 of warp 8 issues the TMA bulk copies, L2 evict-first), the
+// 8 consumer warps rise to 232 (setmaxnreg.inc): 8*32*232 + 4*32*40 = 64512 =
+// 384*168, so the increase is always satisfiable.  232 registers keep the input
+// vector of a 4096-long row (16 chunks x 8 floats per lane) in registers.  The host
+// launches only a build whose kernel uses exactly 168 registers per thread.
+//
+// Synchronisation (all waits bounded by %globaltimer; a timed-out wait sets a status
+// bit, and every CTA gives up at its next wait once a timeout bit is set):
+//   * grid barrier: a monotonic arrival counter; operator p starts when it reaches
+//     p * gridDim.  The CTA whose arrival completes the final count resets it and
+//     advances the launch sequence number, so the next launch starts from zero.
+//   * router flags: flag[l] = seq + 1 once the top-k of layer l is in memory.
+//   * prologue vectors: norm-weight constants by bulk copy, issued by thread 0 right
+//     after the previous operator (before the barrier wait); the previous operator's
+//     outputs by the consumer threads with L2 loads after it.
+// The per-op launch mode and this kernel share the operators (g4_ops.cuh), the tile
+// loop (g4_gemv.cuh) and the attention items (g4_attention.cuh), and every sum has a
+// fixed order, so both compute bit-identical results.
+#pragma once
+
+#include "g4_attention.cuh"
+#include "g4_ops.cuh"
+
+namespace g4 {
+
+constexpr int kStepThreads = kConsumerThreads + 128;  // 2 consumer warpgroups + 1 producer warpgroup
+constexpr int kStepLaunchRegs = 168;     // registers per thread at launch (65536 / 384, rounded)
+constexpr int kStepConsumerRegs = 232;   // after setmaxnreg.inc
+constexpr int kStepProducerRegs = 40;    // after setmaxnreg.dec
+static_assert(kConsumerThreads * kStepConsumerRegs + 128 * kStepProducerRegs <= kStepThreads * kStepLaunchRegs,
+              "register reallocation exceeds the launch allocation");
+
+// Device words of the step kernel (one int array in scratch, zero at rest).
+constexpr int kSyncBarrier = 0;   // grid barrier arrivals of the current launch
+constexpr int kSyncSeq = 1;       // launches completed
+constexpr int kSyncRouter = 32;   // [layers] router flags
+constexpr int kNumSyncWords = kSyncRouter + 256;
+
+struct StepProgram {
+  const QkvOp* k1;
+  const AttnArgs* k2;
+  const OProjOp* k3;
+  const RouterMlpOp* k4;
+  const MoeUpOp* k5;
+  const MoeDownOp* k6;
+  const LmHeadOp* lm;
+  int* sync;       // kNumSyncWords ints
+  int* ctrl;
+  int nlayers;
+  int stages;      // ring depth
+  SmemSizes z;     // x0 / x1 / staging sizes (maximum over the operators)
+  int aux;         // bytes of the auxiliary area (>= smem_aux_bytes(z), attention scratch)
+};
+
+__host__ __device__ inline int step_smem_bytes(const StepProgram& p) {
+  return gemv_smem_bytes(p.aux, p.stages);
+}
+
+// Named barrier that also ANDs a predicate over the consumer threads: a decision
+// every consumer thread takes identically.
+__device__ __forceinline__ bool consumers_all(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(kBarConsumers), "r"(kConsumerThreads)
+      : "memory");
+  return r != 0;
+}
+
+constexpr int kStatusTimeouts = G4_STATUS_PEER_TIMEOUT | G4_STATUS_MBAR_TIMEOUT;
+
+// Spin until `pred(value)` holds for *p (acquire), bounded; gives up early when a
+// timeout bit is already set anywhere.  Returns false after setting a status bit.
+template <class Pred>
+__device__ inline bool spin_until(const int* p, Pred pred, int* status, int timeout_us) {
+  if (pred(ld_acquire_gpu(p))) return true;
+  const uint64_t limit = static_cast<uint64_t>(timeout_us > 0 ? timeout_us : 2000000) * 1000ull;
+  const uint64_t t0 = globaltimer_ns();
+  int n = 0;
+  while (!pred(ld_acquire_gpu(p))) {
+    if ((++n & 63) == 0) {
+      if (ldcg_i(status) & kStatusTimeouts) return false;
+      if (globaltimer_ns() - t0 > limit) {
+        atomicOr(status, G4_STATUS_MBAR_TIMEOUT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// Consumer-thread copy of the activation vectors of an operator into the staging
+// area (L2 loads: the data was written by other CTAs of this launch).  All loads of a
+// thread are in flight before its first store.
+__device__ inline void stage_activations(const Copy* cp, int n, unsigned char* stg) {
+  constexpr int U = 8;
+  int pre[kMaxCopies + 1];
+  pre[0] = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxCopies; ++i) pre[i + 1] = pre[i] + (i < n ? cp[i].bytes / 16 : 0);
+  const int total = pre[kMaxCopies];
+  for (int base = threadIdx.x; base < total; base += kConsumerThreads * U) {
+    uint4 v[U];
+    int dst[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int g = base + u * kConsumerThreads;
+      dst[u] = -1;
+      if (g < total) {
+        int c = 0;
+#pragma unroll
+        for (int i = 1; i < kMaxCopies; ++i) c += (g >= pre[i]) ? 1 : 0;
+        const int k = g - pre[c];
+        v[u] = ldcg_u4(reinterpret_cast<const unsigned char*>(cp[c].src) + (size_t)k * 16);
+        dst[u] = cp[c].dst + k * 16;
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u)
+      if (dst[u] >= 0) *reinterpret_cast<uint4*>(stg + dst[u]) = v[u];
+  }
+}
+
+// Program order: phase p is layer p / 6, kind p % 6 (0 qkv, 1 attention, 2 o_proj,
+// 3 router+MLP, 4 MLP down+experts up, 5 experts down); phase 6 L is the LM head.
+template <class F>
+__device__ __forceinline__ void with_gemv_op(const StepProgram& P, int p, F&& f) {
+  const int l = p / 6, k = p - 6 * l;
+  if (l == P.nlayers) f(*P.lm);
+  else if (k == 0) f(P.k1[l]);
+  else if (k == 2) f(P.k3[l]);
+  else if (k == 3) f(P.k4[l]);
+  else if (k == 4) f(P.k5[l]);
+  else if (k == 5) f(P.k6[l]);
+}
+
+// Producer lane: every weight tile of one operator owned by this CTA.
+template <class Op>
+__device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepProgram& P, Smem& sm, RingPos& rp,
+                                           uint64_t pol, int seq) {
+  int* status = P.ctrl + G4_CTRL_STATUS;
+  bool dep_loaded = false;
+  for (int s = 0; s < op.nseg; ++s) {
+    int ub, ue;
+    cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
+    if (ub >= ue) continue;
+    if (op.seg_dependent(s) && !dep_loaded) {
+      const int want = seq + 1;
+      if (!spin_until(P.sync + kSyncRouter + layer, [want](int v) { return v == want; }, status,
+                      ldcg_i(P.ctrl + G4_CTRL_TIMEOUT_US))) {
+        sm.ints[kSmemDead] = 1;
+        return false;
+      }
+      op.load_dependent(sm);
+      dep_loaded = true;
+    }
+    for (int u = ub; u < ue;) {
+      const int n = tile_units(op.seg[s], u, ue);
+      if (!produce_tile(op, s, u, n, sm, rp, P.stages, pol, status)) return false;
+      u += n;
+    }
+  }
+  return true;
+}
+
+static __device__ __noinline__ void produce_step(const StepProgram& P, Smem& sm, int seq) {
+  const uint64_t pol = l2_evict_first_policy();
+  RingPos rp;
+  bool ok = true;
+  const int L = P.nlayers;
+  for (int p = 0; p < 6 * L && ok; ++p) {
+    const int l = p / 6, k = p - 6 * l;
+    switch (k) {
+      case 0: ok = produce_op(P.k1[l], l, P, sm, rp, pol, seq); break;
+      case 1: break;
+      case 2: ok = produce_op(P.k3[l], l, P, sm, rp, pol, seq); break;
+      case 3: ok = produce_op(P.k4[l], l, P, sm, rp, pol, seq); break;
+      case 4: ok = produce_op(P.k5[l], l, P, sm, rp, pol, seq); break;
+      default: ok = produce_op(P.k6[l], l, P, sm, rp, pol, seq);
+    }
+  }
+  if (ok) produce_op(*P.lm, L - 1, P, sm, rp, pol, seq);
+  producer_exit(sm);
+}
+
+using StepHooks = EmptyBarrierHooks;
+
+// Per-CTA state of the consumer side.
+struct PhaseState {
+  int phase = 0;      // operator index in the program
+  bool live = true;   // identical on every consumer thread
+  RingPos rp, wp;     // ring position (all tiles) / tiles seen complete
+};
+
+// Start of operator ps.phase: wait for every CTA to finish the previous operator,
+// then for this operator's constants.
+__device__ __forceinline__ void phase_begin(const StepProgram& P, Smem& sm, PhaseState& ps, int trace_id) {
+  int* status = P.ctrl + G4_CTRL_STATUS;
+  bool ok = sm.ints[kSmemDead] == 0;
+  if (threadIdx.x == 0 && ok) {
+    if (ps.phase > 0) {
+      const int target = ps.phase * (int)gridDim.x;
+      ok = spin_until(P.sync + kSyncBarrier, [target](int v) { return v >= target; }, status,
+                      ldcg_i(P.ctrl + G4_CTRL_TIMEOUT_US));
+      __threadfence();
+    }
+    if (ok) ok = mbar_wait(&sm.pbar[0], ps.phase & 1, status);
+    if (!ok) sm.ints[kSmemDead] = 1;
+    G4_TRACE_EV(trace_id, 0);
+  }
+  ps.live = consumers_all(ok && sm.ints[kSmemDead] == 0);
+}
+
+// End of operator ps.phase: all of this CTA's stores done -> issue the next
+// operator's constant copies (the staging area is free; an empty list still
+// completes the barrier phase the next operator waits for) -> arrive.
+__device__ __forceinline__ void phase_end(const StepProgram& P, Smem& sm, PhaseState& ps, const OpBase* next) {
+  named_bar(kBarConsumers, kConsumerThreads);
+  if (threadIdx.x == 0) {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads -> async writes
+    if (next) issue_copies(next->cc, next->ncc, sm.stg, &sm.pbar[0]);
+    else issue_copies(nullptr, 0, sm.stg, &sm.pbar[0]);
+    __threadfence();
+    red_release_gpu_add(P.sync + kSyncBarrier, 1);
+  }
+  ++ps.phase;
+}
+
+// Consumer side of one matrix-product operator up to (not including) its arrival.
+template <class Op, int CPLM>
+__device__ __forceinline__ void gemv_phase_body(const Op& op, const StepProgram& P, Smem& sm, PhaseState& ps,
+                                                StepHooks& h, XRegs<CPLM>& xr) {
+  int* status = P.ctrl + G4_CTRL_STATUS;
+  phase_begin(P, sm, ps, op.trace_id);
+  bool ok = ps.live;
+  if (ps.live) {
+    stage_activations(op.ac, op.nac, sm.stg);
+    named_bar(kBarConsumers, kConsumerThreads);
+    ok = op.prologue(sm);
+    named_bar(kBarConsumers, kConsumerThreads);
+    if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 3);
+  }
+  // The tile loop runs even when this CTA is dead: it then only advances the ring
+  // position (no waits), keeping the consumer threads in step.
+  consume_tiles<Op, CPLM>(op, sm, ps.rp, ps.wp, P.stages, ok && ps.live, status, h, xr);
+  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 5);
+  if (consumers_all(ps.live)) op.finish(sm, ok && sm.ints[kSmemDead] == 0);
+  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 6);
+}
+
+template <class Op, int CPLM>
+__device__ __forceinline__ void run_gemv_phase(const Op& op, const StepProgram& P, Smem& sm, PhaseState& ps,
+                                               StepHooks& h, XRegs<CPLM>& xr, const OpBase* next) {
+  gemv_phase_body<Op, CPLM>(op, P, sm, ps, h, xr);
+  phase_end(P, sm, ps, next);
+}
+
+// Attention items of this CTA for one layer.
+template <int D, int G>
+__device__ __forceinline__ void attn_items(const AttnArgs& a, unsigned char* scratch) {
+  const int items = a.n_kv * a.nsplit;
+  for (int it = blockIdx.x; it < items; it += gridDim.x)
+    attn_item<D, G>(a, it / a.nsplit, it % a.nsplit, scratch, kBarConsumers);
+}
+
+template <int DS, int GS, int DF, int GF>
+__device__ __forceinline__ void run_attention_phase(const AttnArgs& a, const StepProgram& P, Smem& sm,
+                                                    PhaseState& ps, const OpBase* next) {
+  phase_begin(P, sm, ps, a.trace_id);
+  if (ps.live) {  // the auxiliary area is free during attention
+    if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0);
+    else if (a.d == DF && a.g == GF) attn_items<DF, GF>(a, sm.x0);
+  }
+  phase_end(P, sm, ps, next);
+}
+
+// Wait (bounded) for every issued tile thread 0 did not see complete, so that no
+// bulk copy still writes into this CTA's shared memory when it exits after a failure.
+__device__ inline void drain_issued(Smem& sm, RingPos rp, int issued, int stages) {
+  while (rp.tiles < issued) {
+    const uint64_t t0 = globaltimer_ns();
+    while (!mbar_try_wait(&sm.full[rp.st], rp.ph) && globaltimer_ns() - t0 < kLocalTimeoutNs) {
+    }
+    rp.next(stages);
+  }
+}
+
+// CPLM: input-vector chunks per lane of the longest row; (DS, GS) / (DF, GF): head dim
+// and query heads per KV head of the sliding / full attention layers on this rank.
+template <int CPLM, int DS, int GS, int DF, int GF>
+__global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_constant__ StepProgram P) {
+  extern __shared__ unsigned char g4_dyn_smem[];
+  Smem sm = carve_smem(g4_dyn_smem, P.z, P.aux, P.stages);
+  int* status = P.ctrl + G4_CTRL_STATUS;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < P.stages; ++i) {
+      mbar_init(&sm.full[i], 1);
+      mbar_init(&sm.empty[i], kConsumerWarps);
+    }
+    sm.ints[kSmemIssued] = 0;
+    sm.ints[kSmemProdExit] = 0;
+    mbar_init(&sm.pbar[0], 1);
+    mbar_init(&sm.pbar[1], 1);
+    mbar_init_fence();
+    // a step never starts on top of an unhandled timeout (barrier arrivals, flags and
+    // counters may be mid-count): the host clears the status and the library's words
+    // first.  BAD_TOKEN / POS_OVERFLOW leave the step's synchronisation intact.
+    sm.ints[kSmemDead] = (ldcg_i(status) & kStatusTimeouts) != 0;
+    sm.ints[kSmemSeq] = ldcg_i(P.sync + kSyncSeq);
+  }
+  __syncthreads();
+  if (sm.ints[kSmemDead]) return;  // read after the barrier: identical on every thread
+  const int seq = sm.ints[kSmemSeq];
+
+  // warp-uniform split: warps 8-11 (one warpgroup) produce, warps 0-7 consume
+  if (threadIdx.x >= kConsumerThreads) {
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(kStepProducerRegs) : "memory");
+    if (threadIdx.x == kConsumerThreads) produce_step(P, sm, seq);
+    return;
+  }
+  asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kStepConsumerRegs) : "memory");
+  PhaseState ps;
+  XRegs<CPLM> xr;  // one input vector for every operator (kept in registers)
+  StepHooks h;
+  if (threadIdx.x == 0) issue_copies(P.k1[0].cc, P.k1[0].ncc, sm.stg, &sm.pbar[0]);
+  const int L = P.nlayers;
+  for (int p = 0; p < 6 * L; ++p) {
+    const int l = p / 6, k = p - 6 * l;
+    switch (k) {
+      case 0: run_gemv_phase<QkvOp, CPLM>(P.k1[l], P, sm, ps, h, xr, nullptr); break;
+      case 1: run_attention_phase<DS, GS, DF, GF>(P.k2[l], P, sm, ps, &P.k3[l]); break;
+      case 2: run_gemv_phase<OProjOp, CPLM>(P.k3[l], P, sm, ps, h, xr, &P.k4[l]); break;
+      case 3: run_gemv_phase<RouterMlpOp, CPLM>(P.k4[l], P, sm, ps, h, xr, &P.k5[l]); break;
+      case 4: run_gemv_phase<MoeUpOp, CPLM>(P.k5[l], P, sm, ps, h, xr, &P.k6[l]); break;
+      default:
+        run_gemv_phase<MoeDownOp, CPLM>(P.k6[l], P, sm, ps, h, xr,
+                                        l + 1 < L ? (const OpBase*)&P.k1[l + 1] : (const OpBase*)P.lm);
+    }
+  }
+  // LM head; its arrival is the final one of the launch
+  gemv_phase_body<LmHeadOp, CPLM>(*P.lm, P, sm, ps, h, xr);
+  named_bar(kBarConsumers, kConsumerThreads);
+  if (threadIdx.x == 0) {
+    __threadfence();
+    const int total = (ps.phase + 1) * (int)gridDim.x;
+    const int old = atomicAdd(P.sync + kSyncBarrier, 1);
+    if (old == total - 1) {  // every CTA has passed its last wait: reset for the next launch
+      atomicExch(P.sync + kSyncBarrier, 0);
+      atomicAdd(P.sync + kSyncSeq, 1);
+    }
+    if (sm.ints[kSmemDead]) drain_ring(sm, ps.wp, P.stages);
+  }
+}
+
+// ------------------------------------------------------------------ variants
+// Each instantiation of step_kernel lives in its own translation unit
+// (g4_step_*.cu, compiled in parallel) and registers itself with the runtime.
+struct StepVariant {
+  int cplm, ds, gs, df, gf;
+  const void* kernel;
+  int (*trace_read)(void* dst, long long bytes);  // this module's timeline buffer
+};
+void register_step_variant(const StepVariant& v);  // g4_runtime.cu
+
+}  // namespace g4
+
+#ifdef G4_TRACE
+#define G4_STEP_TRACE_READER                                                              \
+  static int g4_step_trace_read(void* dst, long long bytes) {                             \
+    const long long need = (long long)sizeof(g4::g4_trace_buf);                           \
+    if (bytes < need) return -1;                                                          \
+    return cudaMemcpyFromSymbol(dst, g4::g4_trace_buf, need) == cudaSuccess ? 0 : -1;     \
+  }
+#else
+#define G4_STEP_TRACE_READER \
+  static int g4_step_trace_read(void*, long long) { return -1; }
+#endif
+
+// One variant per translation unit.
+#define G4_STEP_VARIANT(C, DS, GS, DF, GF)                                                \
+  namespace {                                                                             \
+  G4_STEP_TRACE_READER                                                                    \
+  struct StepVariantRegistration {                                                        \
+    StepVariantRegistration() {                                                           \
+      g4::register_step_variant(g4::StepVariant{                                          \
+          C, DS, GS, DF, GF, reinterpret_cast<const void*>(&g4::step_kernel<C, DS, GS, DF, GF>), \
+          &g4_step_trace_read});                                                          \
+    }                                                                                     \
+  } g4_step_variant_registration;                                                         \
+  }

@@ -1,0 +1,6 @@
+// Persistent decode-step kernel instantiation: rows up to 4096 elements
+// (16 input chunks per lane), sliding layers head_dim 256 with 2 query heads per KV
+// head, full layers head_dim 256 with 8 (per rank).
+#include "g4_step.cuh"
+
+G4_STEP_VARIANT(16, 256, 2, 256, 8)

@@ -46,14 +46,47 @@ def up_to_date(lib: str = LIB) -> bool:
     return all(os.path.getmtime(s) <= t for s in sources())
 
 
-def build(force: bool = False, verbose: bool = False, trace: bool = False) -> str:
-    """Compile the library (``trace=True``: the -DG4_TRACE timeline build)."""
+def _headers() -> list[str]:
+    return sorted(glob.glob(os.path.join(CSRC, "*.cuh")) + glob.glob(os.path.join(INCLUDE, "*.h")))
+
+
+def build(force: bool = False, verbose: bool = False, trace: bool = False, jobs: int = 0) -> str:
+    """Compile the library (``trace=True``: the -DG4_TRACE timeline build).
+
+    Every translation unit (the runtime, and one per persistent step-kernel variant)
+    is compiled to its own object in parallel, then linked; objects newer than their
+    source and every header are reused.
+    """
     lib = LIB_TRACE if trace else LIB
     if not force and up_to_date(lib):
         return lib
+    objdir = os.path.join(PKG_DIR, "_build_trace" if trace else "_build")
+    os.makedirs(objdir, exist_ok=True)
     units = sorted(glob.glob(os.path.join(CSRC, "*.cu")))
+    newest_header = max(os.path.getmtime(h) for h in _headers())
+    extra = ["-DG4_TRACE"] if trace else []
+    compile_flags = [f for f in NVCC_FLAGS if f != "-shared"]
+
+    def obj_of(u: str) -> str:
+        return os.path.join(objdir, os.path.basename(u)[:-3] + ".o")
+
+    def compile_one(u: str) -> None:
+        o = obj_of(u)
+        if not force and os.path.exists(o) and os.path.getmtime(o) >= max(os.path.getmtime(u), newest_header):
+            return
+        cmd = [nvcc(), *compile_flags, *extra, "-I", INCLUDE, "-c", "-o", o + ".tmp", u]
+        if verbose:
+            print(" ".join(cmd), flush=True)
+        subprocess.run(cmd, check=True)
+        os.replace(o + ".tmp", o)
+
+    from concurrent.futures import ThreadPoolExecutor
+
+    with ThreadPoolExecutor(max_workers=jobs or os.cpu_count() or 4) as ex:
+        list(ex.map(compile_one, units))
     tmp = lib + ".tmp"
-    cmd = [nvcc(), *NVCC_FLAGS, *(["-DG4_TRACE"] if trace else []), "-I", INCLUDE, "-o", tmp, *units]
+    cmd = [nvcc(), "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", tmp,
+           *[obj_of(u) for u in units]]
     if verbose:
         print(" ".join(cmd), flush=True)
     subprocess.run(cmd, check=True)

@@ -49,6 +49,7 @@ class Engine:
         random_seed: int | None = None,
         random_std: float = 0.02,
         mesh: Mesh | None = None,
+        engine: str = "step",
     ):
         if batch != 1:
             raise NotImplementedError("the B200 decode path runs batch 1 (engine.py:167 fills row 0)")
@@ -73,7 +74,7 @@ class Engine:
         self.load_seconds = time.time() - t0
 
         self.comm = Comm(self.mesh, self.cfg.hidden_size) if self.mesh.world > 1 else None
-        self.model = DecodeModel(self.cfg, shard, self.mesh, max_len, self.comm)
+        self.model = DecodeModel(self.cfg, shard, self.mesh, max_len, self.comm, engine=engine)
         self.params = shard
         self.param_bytes = param_bytes(self.cfg)
         self.cache_bytes = cache_bytes(self.cfg, batch, max_len)

@@ -51,7 +51,7 @@ class DecodeModel:
     """Per-rank native model.  ``shard``: native tensor name -> CUDA tensor."""
 
     def __init__(self, cfg: TextConfig, shard: dict, mesh: Mesh, max_len: int,
-                 comm: Comm | None = None, timeout_us: int = 2_000_000):
+                 comm: Comm | None = None, timeout_us: int = 2_000_000, engine: str = "step"):
         L = N.lib()
         self.cfg, self.mesh, self.max_len = cfg, mesh, max_len
         self.device = torch.device("cuda", mesh.device)
@@ -86,6 +86,10 @@ class DecodeModel:
             if comm is not None:
                 N.check(L.g4_model_set_comm(self.handle, comm.handle), "g4_model_set_comm")
             N.check(L.g4_model_finalize(self.handle), "g4_model_finalize")
+            if engine not in N.ENGINES:
+                raise ValueError(f"engine must be one of {sorted(N.ENGINES)}")
+            self.engine = engine
+            N.check(L.g4_model_set_engine(self.handle, N.ENGINES[engine]), "g4_model_set_engine")
             hp = ctypes.POINTER(ctypes.c_int)()
             N.check(L.g4_model_host_tokens(self.handle, ctypes.byref(hp)), "g4_model_host_tokens")
             self.tokens_host = np.ctypeslib.as_array(hp, shape=(max_len + 1,))
@@ -136,7 +140,8 @@ class DecodeModel:
                       "experts_down", "lm_head_argmax")
 
     def profile(self, steps: int) -> dict:
-        """Summed ms per kernel class over ``steps`` event-separated steps."""
+        """Summed ms per kernel class over ``steps`` event-separated steps (always the
+        per-op kernels, whatever the engine: a persistent step has no kernel classes)."""
         out = (ctypes.c_float * 7)()
         with torch.cuda.device(self.device):
             N.check(N.lib().g4_model_profile(self.handle, N.stream_handle(), steps, out, 7),
@@ -144,7 +149,9 @@ class DecodeModel:
         return dict(zip(self.KERNEL_CLASSES, [float(v) for v in out]))
 
     def check_status(self):
-        """Synchronise and raise if a bounded device wait gave up."""
+        """Synchronise and raise if a status bit is set (a bounded device wait gave up,
+        a bad token, a position overflow).  With the step kernel, steps after a set bit
+        do nothing until ``reset`` clears it."""
         st = ctypes.c_int(0)
         with torch.cuda.device(self.device):
             rc = N.lib().g4_model_status(self.handle, N.stream_handle(), ctypes.byref(st))

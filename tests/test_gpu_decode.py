@@ -23,9 +23,9 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-def _run_gpu(cfg, params, prompt, n_new, max_len, use_graph=True):
+def _run_gpu(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step"):
     shard = rank_shard(cfg, params.__getitem__, Mesh(0, 1, 0), DEV)
-    m = DecodeModel(cfg, shard, Mesh(0, 1, 0), max_len)
+    m = DecodeModel(cfg, shard, Mesh(0, 1, 0), max_len, engine=engine)
     m.reset(prompt, write_logits=True)
     logits = []
     for _ in range(len(prompt) + n_new - 1):
@@ -39,8 +39,8 @@ def _run_gpu(cfg, params, prompt, n_new, max_len, use_graph=True):
     return torch.stack(logits).cpu(), ids, host
 
 
-def _compare(cfg, params, prompt, n_new, max_len, use_graph=True):
-    lg, ids, host = _run_gpu(cfg, params, prompt, n_new, max_len, use_graph)
+def _compare(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step"):
+    lg, ids, host = _run_gpu(cfg, params, prompt, n_new, max_len, use_graph, engine)
     assert ids == host, "mapped host token mirror disagrees with the device ring"
     o = Oracle(cfg, params, mode="bf16")
     ref, ref_ids = o.greedy_generate(prompt, n_new, max_len, teacher=ids)
@@ -54,27 +54,73 @@ def _compare(cfg, params, prompt, n_new, max_len, use_graph=True):
     return worst, agree, decided, ids, ref_ids
 
 
-def test_tiny_config1_teacher_forced_and_greedy():
+@pytest.mark.parametrize("engine", ["step", "ops"])
+def test_tiny_config1_teacher_forced_and_greedy(engine):
     """128-token prompt, 32 greedy tokens."""
     from golden.make_golden import CONFIG1_NEW, config1_inputs
 
     cfg, params, prompt = config1_inputs()
-    worst, agree, decided, ids, _ = _compare(cfg, params, prompt, CONFIG1_NEW, 160)
+    worst, agree, decided, ids, _ = _compare(cfg, params, prompt, CONFIG1_NEW, 160, engine=engine)
     assert worst >= 0.9999, worst
     assert bool(agree[decided].all()), (agree.logical_not() & decided).nonzero()
     golden = np.load("tests/golden/oracle_config1.npz")
     same = (np.array(ids) == golden["ids"]).mean()
-    print(f"config1: worst corr {worst:.6f}, decided {int(decided.sum())}/{len(decided)}, "
+    print(f"config1 [{engine}]: worst corr {worst:.6f}, decided {int(decided.sum())}/{len(decided)}, "
           f"free-running ids equal to golden: {same:.3f}")
 
 
-def test_graph_and_direct_launch_agree():
+@pytest.mark.parametrize("engine", ["step", "ops"])
+def test_graph_and_direct_launch_agree(engine):
     cfg = tiny_parity_config()
     params = random_params(cfg, 7)
     prompt = list(range(5, 25))
-    a = _run_gpu(cfg, params, prompt, 6, 64, use_graph=True)
-    b = _run_gpu(cfg, params, prompt, 6, 64, use_graph=False)
+    a = _run_gpu(cfg, params, prompt, 6, 64, use_graph=True, engine=engine)
+    b = _run_gpu(cfg, params, prompt, 6, 64, use_graph=False, engine=engine)
     assert torch.equal(a[0], b[0]) and a[1] == b[1]
+
+
+def test_step_kernel_matches_op_kernels_bitwise():
+    """The persistent step kernel and the per-op kernels share every operator, tile
+    loop and attention item: identical logits and tokens, real layer shapes."""
+    cfg = make_config(num_hidden_layers=2, layer_types=(SLIDING, FULL), num_experts=16,
+                      vocab_size=16384)
+    params = random_params(cfg, 5)
+    prompt = list(range(100, 109))
+    a = _run_gpu(cfg, params, prompt, 5, 64, engine="step")
+    b = _run_gpu(cfg, params, prompt, 5, 64, engine="ops")
+    assert torch.equal(a[0], b[0]) and a[1] == b[1]
+
+
+def test_status_bit_stops_steps_until_cleared():
+    """A set timeout bit (planted by the host, as if a bounded wait had given up)
+    turns later steps of the step kernel into no-ops; check_status reports it and
+    reset() resumes with correct results."""
+    cfg = tiny_parity_config()
+    params = random_params(cfg, 11)
+    prompt = list(range(3, 12))
+    ref_logits, ref_ids, _ = _run_gpu(cfg, params, prompt, 4, 32)
+    shard = rank_shard(cfg, params.__getitem__, Mesh(0, 1, 0), DEV)
+    m = DecodeModel(cfg, shard, Mesh(0, 1, 0), 32)
+    m.reset(prompt, write_logits=True)
+    m.step(2)
+    torch.cuda.synchronize()
+    pos = int(m.ctrl[0])
+    m.ctrl[3] = 0x2  # MBAR_TIMEOUT
+    m.step(3)
+    torch.cuda.synchronize()
+    assert int(m.ctrl[0]) == pos, "a step ran with the status bit set"
+    with pytest.raises(RuntimeError):
+        m.check_status()
+    m.reset(prompt, write_logits=True)
+    got = []
+    for _ in range(len(prompt) + 3):
+        m.step(1)
+        got.append(m.logits.clone())
+    torch.cuda.synchronize()
+    m.check_status()
+    ids = m.tokens_out[len(prompt):len(prompt) + 4].cpu().tolist()
+    m.close()
+    assert ids == ref_ids and torch.equal(torch.stack(got).cpu(), ref_logits)
 
 
 def test_real_layer_shapes_two_layers():
