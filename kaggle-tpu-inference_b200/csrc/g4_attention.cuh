@@ -53,7 +53,7 @@ struct AttnArgs {
   int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
 
-__host__ __device__ inline int attn_smem_bytes(int g, int d) {
+__host__ __device__ __forceinline__ int attn_smem_bytes(int g, int d) {
   // acc [g][d] + lane-group stats [64][g] x 2 + merge scales [g][kAttnMaxSplit] + misc
   // + the normalised query heads q_s [g][d] (bf16)
   return g * d * 4 + 2 * 64 * g * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2;

@@ -26,9 +26,7 @@
 //   __device__ void load_dependent(Smem&) const;  // producer lane, once they exist
 //   __device__ void issue(int s,int u0,int n,unsigned char* stage,uint64_t* bar,
 //                         uint64_t pol,const Smem&) const;   // producer: bulk copies
-//   __device__ int xmode(int s) const;            // see consume_tiles
 //   __device__ bool prologue(Smem&) const;        // consumers, staged vectors present
-//   __device__ const float* xvec(int s,int j,const Smem&) const;   // fp32 input
 //   __device__ void epilogue(int s,int u0,int n,const Res& res,Smem&,bool ok) const;
 //   __device__ void finish(Smem&, bool ok) const; // consumers, after all tiles
 #pragma once
@@ -40,15 +38,16 @@ namespace g4 {
 constexpr int kConsumerWarps = 8;
 constexpr int kConsumerThreads = kConsumerWarps * 32;
 constexpr int kGemvThreads = kConsumerThreads + 32;
-constexpr int kStages = 4;          // ring depth of the per-op kernels
+constexpr int kStages = 3;          // ring depth of the per-op kernels
 constexpr int kMaxStages = 16;      // ring depth limit (persistent step kernel)
-constexpr int kStageBytes = 22528;  // 4 rows of 2816 bf16
+constexpr int kStageBytes = 45056;  // 8 rows of 2816 bf16: one row per consumer warp
 constexpr int kMaxTileRows = 256;
 constexpr int kResBufs = 2;         // per-tile result buffers (alternating)
 constexpr int kMaxSeg = 3;
 constexpr int kMaxCopies = 6;
 constexpr int kBarConsumers = 1;  // named barrier id used by the consumer warps
 constexpr int kMaxSmemBytes = 232448;  // 227 KB opt-in shared memory per CTA
+constexpr int kOpCopyBytes = 640;      // shared copy of the current operator (step kernel)
 // Smem::ints slots used by the engine (operators use 0..39)
 constexpr int kSmemSeq = 40;      // launch sequence number (persistent step kernel)
 constexpr int kSmemIssued = 41;   // tiles issued by the producer lane so far
@@ -71,10 +70,16 @@ struct Copy {
 };
 
 // Fields every operator carries (filled on the host when the step is planned).
+// Input vector of segment s: the fp32 vector x<xsel[s]> in shared memory; with
+// xsub[s] > 0 (the MoE down projection) sub-row j has its own vector at x0 + j*xsub[s]
+// floats and warp w owns sub-row j = w % nsub, its vector in registers for the whole
+// segment (nsub must divide the consumer warp count).
 struct OpBase {
   int* ctrl;
   int nseg;
   SegDesc seg[kMaxSeg];
+  int xsel[kMaxSeg];
+  int xsub[kMaxSeg];
   int xbytes[2];  // bytes of the two fp32 input vectors in shared memory
   int stgbytes;   // bytes of the staging area (constant + activation vectors)
   int ncc, nac;   // constant copies / activation copies
@@ -83,9 +88,9 @@ struct OpBase {
   Copy ac[kMaxCopies];
 };
 
-__host__ __device__ inline int seg_unit_bytes(const SegDesc& s) { return s.nsub * s.K * 2; }
+__host__ __device__ __forceinline__ int seg_unit_bytes(const SegDesc& s) { return s.nsub * s.K * 2; }
 
-__host__ __device__ inline int seg_max_units(const SegDesc& s) {
+__host__ __device__ __forceinline__ int seg_max_units(const SegDesc& s) {
   int by_bytes = kStageBytes / seg_unit_bytes(s);
   int by_rows = kMaxTileRows / s.nsub;
   int m = by_bytes < by_rows ? by_bytes : by_rows;
@@ -101,6 +106,7 @@ struct Smem {
   float* red;        // [64] block-reduction scratch
   int* ints;         // [64] small shared ints (expert ids, flags, argmax indices)
   float* flts;       // [64] small shared floats (routing weights, argmax values)
+  unsigned char* opc;  // [kOpCopyBytes] the current operator's plan (step kernel)
   unsigned char* x0; // input vector 0 (fp32); also the start of the auxiliary area
   unsigned char* x1; // input vector 1 (fp32)
   unsigned char* stg;  // staging area of the prologue copies
@@ -111,30 +117,31 @@ struct SmemSizes {
   int x0, x1, stg;
 };
 
-__host__ __device__ inline int align_up(int v, int a) { return (v + a - 1) / a * a; }
+__host__ __device__ __forceinline__ int align_up(int v, int a) { return (v + a - 1) / a * a; }
 
-__host__ __device__ inline int smem_head_bytes(int stages) {
+__host__ __device__ __forceinline__ int smem_head_bytes(int stages) {
   int off = (2 * stages + 2) * 8;
   off = align_up(off, 16);
   off += kResBufs * kMaxTileRows * 4;
   off += 256 * 3;
+  off += kOpCopyBytes;
   return align_up(off, 128);
 }
 
 // Bytes of the auxiliary area [x0][x1][stg].
-__host__ __device__ inline int smem_aux_bytes(SmemSizes z) {
+__host__ __device__ __forceinline__ int smem_aux_bytes(SmemSizes z) {
   return align_up(z.x0, 128) + align_up(z.x1, 128) + align_up(z.stg, 128);
 }
 
-// Layout: [bars][res][red][ints][flts][aux: x0 x1 stg][stages]; `aux` >= smem_aux_bytes
-__host__ __device__ inline int gemv_smem_bytes(int aux, int stages) {
+// Layout: [bars][res][red][ints][flts][opc][aux: x0 x1 stg][stages]; `aux` >= smem_aux_bytes
+__host__ __device__ __forceinline__ int gemv_smem_bytes(int aux, int stages) {
   int off = smem_head_bytes(stages) + aux;
   off = align_up(off, 1024);
   off += stages * kStageBytes;
   return off + 1024;  // slack for base alignment
 }
 
-__device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z, int aux, int stages) {
+__device__ __forceinline__ Smem carve_smem(unsigned char* raw, SmemSizes z, int aux, int stages) {
   unsigned char* base =
       reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(raw) + 1023) & ~uintptr_t(1023));
   Smem s;
@@ -152,6 +159,8 @@ __device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z, int aux, int 
   off += 256;
   s.flts = reinterpret_cast<float*>(base + off);
   off += 256;
+  s.opc = base + off;
+  off += kOpCopyBytes;
   off = align_up(off, 128);
   s.x0 = base + off;
   s.x1 = s.x0 + align_up(z.x0, 128);
@@ -164,7 +173,7 @@ __device__ inline Smem carve_smem(unsigned char* raw, SmemSizes z, int aux, int 
 
 // Units of segment `s` owned by CTA `cta`: those whose first byte lies in the CTA's
 // slice of the concatenated byte space of all segments.
-__device__ inline void cta_unit_range(const SegDesc* seg, int nseg, int s, int cta, int ncta,
+__device__ __forceinline__ void cta_unit_range(const SegDesc* seg, int nseg, int s, int cta, int ncta,
                                       int& ub, int& ue) {
   long long total = 0, cum = 0;
   for (int i = 0; i < nseg; ++i) {
@@ -184,7 +193,7 @@ __device__ inline void cta_unit_range(const SegDesc* seg, int nseg, int s, int c
   ue = first_unit_at(b1);
 }
 
-__device__ inline int tile_units(const SegDesc& sd, int u, int ue) {
+__device__ __forceinline__ int tile_units(const SegDesc& sd, int u, int ue) {
   int n = seg_max_units(sd);
   if (ue - u < n) n = ue - u;
   if (sd.group > 0) {
@@ -196,7 +205,7 @@ __device__ inline int tile_units(const SegDesc& sd, int u, int ue) {
 
 // Issue a list of prologue copies completing on `bar` (arrives once, with the total
 // byte count, even when the list is empty).
-__device__ inline void issue_copies(const Copy* cp, int n, unsigned char* stg, uint64_t* bar) {
+__device__ __forceinline__ void issue_copies(const Copy* cp, int n, unsigned char* stg, uint64_t* bar) {
   uint32_t bytes = 0;
   for (int i = 0; i < n; ++i) bytes += (uint32_t)cp[i].bytes;
   mbar_arrive_expect_tx(bar, bytes);
@@ -212,7 +221,7 @@ __device__ inline void issue_copies(const Copy* cp, int n, unsigned char* stg, u
 
 // Consumers: wait until the prologue copies of phase `which` (0 constants, 1
 // activations) have landed.
-__device__ inline bool wait_copies(Smem& sm, int which, uint32_t parity, int* status) {
+__device__ __forceinline__ bool wait_copies(Smem& sm, int which, uint32_t parity, int* status) {
   return mbar_wait(&sm.pbar[which], parity, status);
 }
 
@@ -270,7 +279,7 @@ __device__ __forceinline__ void producer_exit(Smem& sm) {
 // producer to stop issuing, then for every issued stage past `rp` (the first tile
 // thread 0 did not see complete), so that no bulk copy is still writing into this
 // CTA's shared memory at exit.
-__device__ inline void drain_ring(Smem& sm, RingPos rp, int stages) {
+__device__ __forceinline__ void drain_ring(Smem& sm, RingPos rp, int stages) {
   volatile int* v = reinterpret_cast<volatile int*>(sm.ints);
   const uint64_t t0 = globaltimer_ns();
   while (!v[kSmemProdExit] && globaltimer_ns() - t0 < kLocalTimeoutNs) __nanosleep(256);
@@ -290,65 +299,93 @@ struct Res {
   __device__ __forceinline__ float operator[](int r) const { return p[r]; }
 };
 
-// 8-element dot product of a bf16 chunk with 8 fp32 values held in registers.
-__device__ __forceinline__ float dot8r(const uint4 w, const float* x, float acc) {
-  acc = fmaf(bf_lo(w.x), x[0], acc);
-  acc = fmaf(bf_hi(w.x), x[1], acc);
-  acc = fmaf(bf_lo(w.y), x[2], acc);
-  acc = fmaf(bf_hi(w.y), x[3], acc);
-  acc = fmaf(bf_lo(w.z), x[4], acc);
-  acc = fmaf(bf_hi(w.z), x[5], acc);
-  acc = fmaf(bf_lo(w.w), x[6], acc);
-  acc = fmaf(bf_hi(w.w), x[7], acc);
+// 8-element dot product of a bf16 weight chunk with 8 bf16 input values packed in
+// 4 words; products and sums in fp32 (the products of two bf16 values are exact).
+__device__ __forceinline__ float dot8p(const uint4 w, const uint4 x, float acc) {
+  acc = fmaf(bf_lo(w.x), bf_lo(x.x), acc);
+  acc = fmaf(bf_hi(w.x), bf_hi(x.x), acc);
+  acc = fmaf(bf_lo(w.y), bf_lo(x.y), acc);
+  acc = fmaf(bf_hi(w.y), bf_hi(x.y), acc);
+  acc = fmaf(bf_lo(w.z), bf_lo(x.z), acc);
+  acc = fmaf(bf_hi(w.z), bf_hi(x.z), acc);
+  acc = fmaf(bf_lo(w.w), bf_lo(x.w), acc);
+  acc = fmaf(bf_hi(w.w), bf_hi(x.w), acc);
   return acc;
 }
 
 // Input-vector chunks of one lane: chunk c = lane + 32 i, i < CPLM (CPLM = max chunks
 // per lane of the kernel).  The weights are the only shared-memory traffic of the dot
-// products; the input vector never leaves registers.
+// products; the input vector never leaves registers.  Every input vector of the step
+// holds bf16 values (widened to fp32 in shared memory), so a lane keeps them packed,
+// two per register: 4 registers per chunk.
 template <int CPLM>
 struct XRegs {
-  float v[CPLM][8];
+  uint4 v[CPLM];
   __device__ __forceinline__ void load(const float* x, int C) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < CPLM; ++i) {
       const int c = lane + 32 * i;
-      float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;  // every element written: no live-in
+      uint4 p = make_uint4(0u, 0u, 0u, 0u);  // every element written: no live-in
       if (c < C) {
-        a = reinterpret_cast<const float4*>(x)[2 * c];
-        b = reinterpret_cast<const float4*>(x)[2 * c + 1];
+        const uint4 a = reinterpret_cast<const uint4*>(x)[2 * c];      // fp32 bits
+        const uint4 b = reinterpret_cast<const uint4*>(x)[2 * c + 1];
+        p.x = (a.x >> 16) | (a.y & 0xffff0000u);  // exact: the values are bf16
+        p.y = (a.z >> 16) | (a.w & 0xffff0000u);
+        p.z = (b.x >> 16) | (b.y & 0xffff0000u);
+        p.w = (b.z >> 16) | (b.w & 0xffff0000u);
       }
-      v[i][0] = a.x; v[i][1] = a.y; v[i][2] = a.z; v[i][3] = a.w;
-      v[i][4] = b.x; v[i][5] = b.y; v[i][6] = b.z; v[i][7] = b.w;
+      v[i] = p;
     }
   }
-  // Warp-wide dot product of one staged row (C chunks) with the registers.
-  __device__ __forceinline__ float dot_row(const uint4* w, int C) const {
+  // Warp-wide dot product of one staged row with the registers, NC iterations of 32
+  // chunks: every iteration but the last covers whole warps of chunks, the last is
+  // guarded unless FULL (C == 32 NC).  A compile-time trip count keeps the body free
+  // of per-lane guards (a runtime bound on every unrolled iteration costs ~2.5x).
+  template <int NC, bool FULL>
+  __device__ __forceinline__ float dot_row_n(const uint4* w, int C) const {
     const int lane = threadIdx.x & 31;
     float a0 = 0.f, a1 = 0.f;
 #pragma unroll
-    for (int i = 0; i < CPLM; ++i) {
+    for (int i = 0; i < NC; ++i) {
       const int c = lane + 32 * i;
-      if (c < C) {
-        if (i & 1) a1 = dot8r(w[c], v[i], a1);
-        else a0 = dot8r(w[c], v[i], a0);
+      if (FULL || i < NC - 1 || c < C) {
+        if (i & 1) a1 = dot8p(w[c], v[i], a1);
+        else a0 = dot8p(w[c], v[i], a0);
       }
     }
     return warp_sum(a0 + a1);
   }
+  // C chunks (C <= 32 CPLM): dispatch on the trip count.
+  __device__ __forceinline__ float dot_row(const uint4* w, int C) const {
+    const int nc = (C + 31) >> 5;
+    const bool full = (C & 31) == 0;
+    switch (nc) {
+#define G4_DOT_CASE(N)                                                      \
+  case N:                                                                   \
+    if (N <= CPLM) {                                                        \
+      constexpr int M = N <= CPLM ? N : 1;                                  \
+      return full ? dot_row_n<M, true>(w, C) : dot_row_n<M, false>(w, C);   \
+    }                                                                       \
+    break;
+      G4_DOT_CASE(1) G4_DOT_CASE(2) G4_DOT_CASE(3) G4_DOT_CASE(4) G4_DOT_CASE(5) G4_DOT_CASE(6)
+      G4_DOT_CASE(7) G4_DOT_CASE(8) G4_DOT_CASE(9) G4_DOT_CASE(10) G4_DOT_CASE(11) G4_DOT_CASE(12)
+      G4_DOT_CASE(13) G4_DOT_CASE(14) G4_DOT_CASE(15) G4_DOT_CASE(16)
+#undef G4_DOT_CASE
+      default: break;
+    }
+    return 0.f;
+  }
 };
 
 // Chunks per lane needed by a segment.
-__host__ __device__ inline int seg_cpl(const SegDesc& s) { return ((s.K >> 3) + 31) / 32; }
+__host__ __device__ __forceinline__ int seg_cpl(const SegDesc& s) { return ((s.K >> 3) + 31) / 32; }
 
-// Consumers: every tile of `op` owned by this CTA, in ring order.  xmode of a segment
-// (Op::xmode(s)): 0 = one input vector for every sub-row (warps take whole rows); 1 =
-// sub-row j has its own input vector (top-k expert slices of the MoE down projection):
-// warp w owns sub-row j = w % nsub and its vector stays in registers for the whole
-// segment (nsub must divide the consumer warp count).  In xmode 0, row r goes to warp
-// kConsumerWarps-1-r (mod the warp count): with fewer rows than warps, warp 0 -- whose
-// thread 0 also runs the ring bookkeeping of the step kernel -- has no row.
+// Consumers: every tile of the operator `ob` owned by this CTA, in ring order.  With
+// one vector for every sub-row (xsub == 0) row r goes to warp kConsumerWarps-1-r (mod
+// the warp count): with fewer rows than warps, warp 0 -- whose thread 0 also waits at
+// the grid barriers of the step kernel -- has no row.  After each tile's barrier,
+// epi(s, u0, n, res, ok) runs on every consumer thread (the operator's epilogue).
 // Every consumer thread executes the same sequence of named barriers whatever happens,
 // so a timed-out wait (which marks the CTA dead) can never strand a warp at a barrier:
 // after it, the remaining tiles are skipped without waiting.
@@ -371,22 +408,26 @@ struct EmptyBarrierHooks {
   __device__ __forceinline__ void after_bar(const RingPos&) {}
 };
 
-template <class Op, int CPLM, class Hooks>
-__device__ __forceinline__ void consume_tiles(const Op& op, Smem& sm, RingPos& rp, RingPos& wp,
-                                              int stages, bool ok, int* status, Hooks& h,
-                                              XRegs<CPLM>& xr) {
+// The input vector lives here, in the one place the loop is instantiated: a register
+// array shared by several inlined copies stays in local memory instead.
+template <int CPLM, class Hooks, class Epi>
+__device__ __forceinline__ void consume_segments(const OpBase& ob, Smem& sm, RingPos& rp, RingPos& wp,
+                                                 int stages, bool ok, int* status, Hooks& h, Epi&& epi) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  XRegs<CPLM> xr;
   volatile int* dead = sm.ints + kSmemDead;
   bool first = true;
-  for (int s = 0; s < op.nseg; ++s) {
+  const int nseg = ob.nseg;
+  for (int s = 0; s < nseg; ++s) {
     int ub, ue;
-    cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
+    cta_unit_range(ob.seg, nseg, s, blockIdx.x, gridDim.x, ub, ue);
     if (ub >= ue) continue;
-    const SegDesc sd = op.seg[s];
+    const SegDesc sd = ob.seg[s];
     const int C = sd.K >> 3;
-    const int xm = op.xmode(s);
-    const int sub = xm ? warp % sd.nsub : 0;
-    xr.load(op.xvec(s, sub, sm), C);
+    const int xsub = ob.xsub[s];
+    const int sub = xsub ? warp % sd.nsub : 0;
+    const float* xv = reinterpret_cast<const float*>(ob.xsel[s] ? sm.x1 : sm.x0) + sub * xsub;
+    xr.load(xv, C);
     for (int u = ub; u < ue;) {
       const int n = tile_units(sd, u, ue);
       const int st = rp.st;
@@ -397,13 +438,13 @@ __device__ __forceinline__ void consume_tiles(const Op& op, Smem& sm, RingPos& r
         live = false;
       }
       if (live) wp.next(stages);
-      if (first && threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 4);
+      if (first && threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 4);
       first = false;
       float* res = sm.res + (rp.tiles & (kResBufs - 1)) * kMaxTileRows;
       if (ok && live) {
         const unsigned char* stage = sm.stages + (size_t)st * kStageBytes;
         const int rowbytes = sd.K * 2;
-        if (xm == 0) {
+        if (xsub == 0) {
           for (int r = kConsumerWarps - 1 - warp; r < n * sd.nsub; r += kConsumerWarps) {  // warp-uniform
             const float v = xr.dot_row(reinterpret_cast<const uint4*>(stage + (size_t)r * rowbytes), C);
             if (lane == 0) res[r] = v;
@@ -421,7 +462,7 @@ __device__ __forceinline__ void consume_tiles(const Op& op, Smem& sm, RingPos& r
       if (lane == 0 && live) h.release(sm, st);
       named_bar(kBarConsumers, kConsumerThreads);
       h.after_bar(rp);
-      op.epilogue(s, u, n, Res{res}, sm, ok && (*dead == 0));
+      epi(s, u, n, Res{res}, ok && (*dead == 0));
       u += n;
       rp.next(stages);
     }
@@ -509,8 +550,8 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 3);
   RingPos rp, wp;
   EmptyBarrierHooks hooks;
-  XRegs<CPLM> xr;
-  consume_tiles<Op, CPLM>(op, sm, rp, wp, kStages, ok, status, hooks, xr);
+  consume_segments<CPLM>(op, sm, rp, wp, kStages, ok, status, hooks,
+                         [&](int s, int u0, int n, const Res& r, bool eok) { op.epilogue(s, u0, n, r, sm, eok); });
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 5);
   op.finish(sm, ok && (sm.ints[kSmemDead] == 0));
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 6);

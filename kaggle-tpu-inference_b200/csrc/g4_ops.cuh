@@ -61,21 +61,21 @@ struct Common {
 };
 
 // ------------------------------------------------------------------ exchange
-__device__ inline int* xflag(const Common& c, int peer, int site, int parity, int src) {
+__device__ __forceinline__ int* xflag(const Common& c, int peer, int site, int parity, int src) {
   return reinterpret_cast<int*>(c.xbase[peer] + ((site * 2 + parity) * kMaxWorld + src) * 128);
 }
-__device__ inline float* xslot(const Common& c, int peer, int site, int parity, int src) {
+__device__ __forceinline__ float* xslot(const Common& c, int peer, int site, int parity, int src) {
   return reinterpret_cast<float*>(c.xbase[peer] + kXFlagBytes) +
          (size_t)((site * 2 + parity) * kMaxWorld + src) * c.xpayload;
 }
-__device__ inline int site_use(const int* ctrl, const Common& c, int site, int layer) {
+__device__ __forceinline__ int site_use(const int* ctrl, const Common& c, int site, int layer) {
   const int step = ldcg_i(ctrl + G4_CTRL_STEP);
   return site == kSiteArgmax ? step : step * c.nlayers + layer;
 }
 
 // All consumer threads: make this CTA's peer stores visible, then the last CTA of the
 // grid publishes flag value use+1 to every rank.
-__device__ inline void xchg_signal(const Common& c, int site, int use, int counter_id) {
+__device__ __forceinline__ void xchg_signal(const Common& c, int site, int use, int counter_id) {
   __threadfence_system();
   named_bar(kBarReduce, kConsumerThreads);
   if (threadIdx.x == 0) {
@@ -90,7 +90,7 @@ __device__ inline void xchg_signal(const Common& c, int site, int use, int count
 }
 
 // Thread 0 waits for every rank's flag of (site, use); result broadcast to consumers.
-__device__ inline bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
+__device__ __forceinline__ bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
   if (threadIdx.x == 0) {
     int ok = 1;
     const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
@@ -129,7 +129,7 @@ struct Tail {
   int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ inline bool layer_output(int* ctrl, const Common& c, const Tail& t, float* t0,
+__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, float* t0,
                                     float* t1, Smem& sm) {
   const int H = c.H, tid = threadIdx.x;
   bool ok = true;
@@ -180,7 +180,7 @@ __device__ inline bool layer_output(int* ctrl, const Common& c, const Tail& t, f
 }
 
 // dst[h] = rbf(rms(x) * w[h]) for the fp32 vector x (smem), bf16 weight w (smem).
-__device__ inline void norm_into(const Common& c, const float* x, const bf16_t* w, float* dst,
+__device__ __forceinline__ void norm_into(const Common& c, const float* x, const bf16_t* w, float* dst,
                                  Smem& sm) {
   float s = 0.f;
   for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) s += x[h] * x[h];
@@ -189,7 +189,7 @@ __device__ inline void norm_into(const Common& c, const float* x, const bf16_t* 
 }
 
 // Convert a staged bf16 vector of n elements into the fp32 input vector dst.
-__device__ inline void widen(const bf16_t* src, int n, float* dst) {
+__device__ __forceinline__ void widen(const bf16_t* src, int n, float* dst) {
   for (int i = threadIdx.x; i < n; i += kConsumerThreads) dst[i] = bf2f(src[i]);
 }
 
@@ -209,17 +209,13 @@ struct QkvOp : OpBase {
   float embed_scale;  // bf16(sqrt(H)) as float
   Tail tail;          // layer > 0
 
-  __device__ int xmode(int) const { return 0; }
-  __device__ bool seg_dependent(int) const { return false; }
-  __device__ void load_dependent(Smem&) const {}
-  __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int) const { return false; }
+  __device__ __forceinline__ void load_dependent(Smem&) const {}
+  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, w + (size_t)u0 * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
-  __device__ const float* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const float*>(sm.x0);
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
     float* t0 = sf(sm, o_t0);
     float* t1 = reinterpret_cast<float*>(sm.x0);  // dead before x0 is written
@@ -242,10 +238,10 @@ struct QkvOp : OpBase {
     norm_into(c, t0, sbf(sm, o_win), reinterpret_cast<float*>(sm.x0), sm);
     return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     if (ok && (int)threadIdx.x < n) out[u0 + threadIdx.x] = f2bf(res[threadIdx.x]);
   }
-  __device__ void finish(Smem&, bool) const {}
+  __device__ __forceinline__ void finish(Smem&, bool) const {}
 };
 
 // ================================================================== K3: o_proj
@@ -256,21 +252,17 @@ struct OProjOp : OpBase {
   int Kc;
   int o_ctx;        // staged ctx (bf16 [Kc])
 
-  __device__ int xmode(int) const { return 0; }
-  __device__ bool seg_dependent(int) const { return false; }
-  __device__ void load_dependent(Smem&) const {}
-  __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int) const { return false; }
+  __device__ __forceinline__ void load_dependent(Smem&) const {}
+  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), bar, pol);
   }
-  __device__ const float* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const float*>(sm.x0);
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     widen(sbf(sm, o_ctx), Kc, reinterpret_cast<float*>(sm.x0));
     return true;
   }
-  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     if (!ok || (int)threadIdx.x >= n) return;
     const int u = u0 + threadIdx.x;
     const float v = res[threadIdx.x];
@@ -281,7 +273,7 @@ struct OProjOp : OpBase {
       for (int p = 0; p < c.world; ++p) xslot(c, p, kSiteAttn, use & 1, c.rank)[u] = v;
     }
   }
-  __device__ void finish(Smem&, bool) const {
+  __device__ __forceinline__ void finish(Smem&, bool) const {
     if (c.world > 1) xchg_signal(c, kSiteAttn, site_use(ctrl, c, kSiteAttn, c.layer), kCntSigAttn);
   }
 };
@@ -309,10 +301,9 @@ struct RouterMlpOp : OpBase {
   const bf16_t* block_x;
   int* ready;                       // step kernel: router flag of this layer (else null)
 
-  __device__ int xmode(int) const { return 0; }
-  __device__ bool seg_dependent(int) const { return false; }
-  __device__ void load_dependent(Smem&) const {}
-  __device__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int) const { return false; }
+  __device__ __forceinline__ void load_dependent(Smem&) const {}
+  __device__ __forceinline__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     const uint32_t bytes = (uint32_t)(n * c.H * 2);
     if (s == 0) {
@@ -322,10 +313,7 @@ struct RouterMlpOp : OpBase {
       bulk_g2s(stage + bytes, up + (size_t)u0 * c.H, bytes, bar, pol);
     }
   }
-  __device__ const float* xvec(int s, int, const Smem& sm) const {
-    return reinterpret_cast<const float*>(s == 0 ? sm.x0 : sm.x1);
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
     const int H = c.H, tid = threadIdx.x;
     float* t0 = sf(sm, o_t0);
@@ -393,7 +381,7 @@ struct RouterMlpOp : OpBase {
     }
     return ok;
   }
-  __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
+  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (s == 0) {
       if (ok && t < n) router_logits[u0 + t] = rbf(res[t]);
@@ -406,15 +394,15 @@ struct RouterMlpOp : OpBase {
       mlp_act[u0 + t] = f2bf(rbf(gelu_tanh(g)) * u);
     }
   }
-  __device__ void finish(Smem&, bool) const {}
+  __device__ __forceinline__ void finish(Smem&, bool) const {}
   // Router units this CTA owns (its range of segment 0).
-  __device__ int router_units() const {
+  __device__ __forceinline__ int router_units() const {
     int ub, ue;
     cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
     return ue - ub;
   }
   // The CTA that completes the router's E logits selects the top-k (model.py:227-232).
-  __device__ void router_done(int mine, Smem& sm) const {
+  __device__ __forceinline__ void router_done(int mine, Smem& sm) const {
     __threadfence();
     named_bar(kBarReduce, kConsumerThreads);
     if (threadIdx.x == 0) {
@@ -497,7 +485,7 @@ struct RouterMlpOp : OpBase {
 };
 
 // ================================================================== K5: MLP down + expert gate|up
-__device__ inline void load_expert_ids(const int* top_idx, int topk, Smem& sm) {
+__device__ __forceinline__ void load_expert_ids(const int* top_idx, int topk, Smem& sm) {
   int e[kMaxTopK];
 #pragma unroll
   for (int k = 0; k < kMaxTopK; ++k) e[k] = k < topk ? ldcg_i(top_idx + k) : 0;  // all in flight
@@ -517,10 +505,9 @@ struct MoeUpOp : OpBase {
   int I, F, topk;
   int o_h2, o_act;         // staged activations (bf16)
 
-  __device__ int xmode(int) const { return 0; }
-  __device__ bool seg_dependent(int s) const { return s == 1; }
-  __device__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
-  __device__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int s) const { return s == 1; }
+  __device__ __forceinline__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
+  __device__ __forceinline__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem& sm) const {
     if (s == 0) {
       bulk_g2s(stage, mlp_down + (size_t)u0 * I, (uint32_t)(n * I * 2), bar, pol);
@@ -532,16 +519,13 @@ struct MoeUpOp : OpBase {
       bulk_g2s(stage + bytes, gate_up + ((e * 2 + 1) * F + f0) * c.H, bytes, bar, pol);
     }
   }
-  __device__ const float* xvec(int s, int, const Smem& sm) const {
-    return reinterpret_cast<const float*>(s == 0 ? sm.x1 : sm.x0);
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     widen(sbf(sm, o_h2), c.H, reinterpret_cast<float*>(sm.x0));
     widen(sbf(sm, o_act), I, reinterpret_cast<float*>(sm.x1));
     if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
     return true;
   }
-  __device__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
+  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     if (s == 0) {
@@ -553,7 +537,7 @@ struct MoeUpOp : OpBase {
       moe_act[u] = f2bf(rbf(rbf(gelu_tanh(g)) * up) * rbf(sm.flts[k]));
     }
   }
-  __device__ void finish(Smem&, bool) const {}
+  __device__ __forceinline__ void finish(Smem&, bool) const {}
 };
 
 // ================================================================== K6: expert down
@@ -566,10 +550,9 @@ struct MoeDownOp : OpBase {
   int F, topk;
   int o_act;              // staged expert activations (bf16 [K, F])
 
-  __device__ int xmode(int) const { return 1; }  // warp w <-> expert slot w % topk
-  __device__ bool seg_dependent(int) const { return true; }
-  __device__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
-  __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int) const { return true; }
+  __device__ __forceinline__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
+  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem& sm) const {
     const uint32_t bytes = (uint32_t)(n * F * 2);
     for (int k = 0; k < topk; ++k) {
@@ -577,14 +560,11 @@ struct MoeDownOp : OpBase {
       bulk_g2s(stage + (size_t)k * bytes, down + (e * c.H + u0) * F, bytes, bar, pol);
     }
   }
-  __device__ const float* xvec(int, int j, const Smem& sm) const {
-    return reinterpret_cast<const float*>(sm.x0) + j * F;
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     widen(sbf(sm, o_act), topk * F, reinterpret_cast<float*>(sm.x0));
     return true;
   }
-  __device__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     const int u = u0 + t;
@@ -605,7 +585,7 @@ struct MoeDownOp : OpBase {
       }
     }
   }
-  __device__ void finish(Smem&, bool) const {
+  __device__ __forceinline__ void finish(Smem&, bool) const {
     if (c.world > 1) xchg_signal(c, kSiteFfn, site_use(ctrl, c, kSiteFfn, c.layer), kCntSigFfn);
   }
 };
@@ -625,17 +605,13 @@ struct LmHeadOp : OpBase {
   int max_len;
   float softcap;         // <= 0: none
 
-  __device__ int xmode(int) const { return 0; }
-  __device__ bool seg_dependent(int) const { return false; }
-  __device__ void load_dependent(Smem&) const {}
-  __device__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
+  __device__ __forceinline__ bool seg_dependent(int) const { return false; }
+  __device__ __forceinline__ void load_dependent(Smem&) const {}
+  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
                         const Smem&) const {
     bulk_g2s(stage, embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
-  __device__ const float* xvec(int, int, const Smem& sm) const {
-    return reinterpret_cast<const float*>(sm.x0);
-  }
-  __device__ bool prologue(Smem& sm) const {
+  __device__ __forceinline__ bool prologue(Smem& sm) const {
     const bool ok = layer_output(ctrl, c, tail, sf(sm, o_t0), reinterpret_cast<float*>(sm.x0), sm);
     norm_into(c, sf(sm, o_t0), sbf(sm, o_wn), reinterpret_cast<float*>(sm.x0), sm);
     float* bv = reinterpret_cast<float*>(sm.x1);
@@ -646,7 +622,7 @@ struct LmHeadOp : OpBase {
     named_bar(kBarReduce, kConsumerThreads);
     return ok;
   }
-  __device__ void epilogue(int, int u0, int n, const Res& res, Smem& sm, bool ok) const {
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem& sm, bool ok) const {
     const int t = threadIdx.x;
     if (!ok || t >= n) return;
     const int u = u0 + t;
@@ -660,7 +636,7 @@ struct LmHeadOp : OpBase {
       bi[t] = u;
     }
   }
-  __device__ void finish(Smem& sm, bool ok) const {
+  __device__ __forceinline__ void finish(Smem& sm, bool ok) const {
     float* bv = reinterpret_cast<float*>(sm.x1);
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;
     named_bar(kBarReduce, kConsumerThreads);

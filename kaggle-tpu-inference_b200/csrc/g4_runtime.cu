@@ -861,6 +861,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.trace_id = i * 8 + 3;
     r.seg[0] = SegDesc{m->E, 1, H, 0};
     r.seg[1] = SegDesc{m->I_local, 2, H, 0};
+    r.xsel[1] = 1;  // router rows: x0 (router input); MLP gate|up: x1 (MLP input)
     r.xbytes[0] = H * 4;
     r.xbytes[1] = H * 4;
     {
@@ -898,6 +899,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     u.trace_id = i * 8 + 4;
     u.seg[0] = SegDesc{H, 1, m->I_local, 0};
     u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local};
+    u.xsel[0] = 1;  // MLP down: x1 (activation); experts gate|up: x0 (MoE input)
     u.xbytes[0] = H * 4;
     u.xbytes[1] = m->I_local * 4;
     {
@@ -922,6 +924,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     dn.nseg = 1;
     dn.trace_id = i * 8 + 5;
     dn.seg[0] = SegDesc{H, m->topk, m->F_local, 0};
+    dn.xsub[0] = m->F_local;  // expert slot j: activation j at x0 + j*F
     dn.xbytes[0] = m->topk * m->F_local * 4;
     {
       Stager sg(&dn);
@@ -1424,6 +1427,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   u.nseg = 2;
   u.seg[0] = SegDesc{0, 1, 8, 0};
   u.seg[1] = SegDesc{K * F, 2, H, F};
+  u.xsel[0] = 1;
   u.xbytes[0] = H * 4;
   u.xbytes[1] = 32;
   {
@@ -1447,6 +1451,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   dn.ctrl = control;
   dn.nseg = 1;
   dn.seg[0] = SegDesc{H, K, F, 0};
+  dn.xsub[0] = F;
   dn.xbytes[0] = K * F * 4;
   {
     Stager sg(&dn);

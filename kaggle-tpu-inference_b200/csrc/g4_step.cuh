@@ -20,12 +20,11 @@
 // being consumed.
 //
 // Warp specialisation with register reallocation: 12 warps, launched at 168
-// registers per thread.  The 4 warps of the producer warpgroup drop to 40
+// registers per thread.  The 4 warps of the producer warpgroup drop to 56
 // (setmaxnreg.dec; lane 0 of warp 8 issues the TMA bulk copies, L2 evict-first), the
-// 8 consumer warps rise to 232 (setmaxnreg.inc): 8*32*232 + 4*32*40 = 64512 =
-// 384*168, so the increase is always satisfiable.  232 registers keep the input
-// vector of a 4096-long row (16 chunks x 8 floats per lane) in registers.  The host
-// launches only a build whose kernel uses exactly 168 registers per thread.
+// 8 consumer warps rise to 224 (setmaxnreg.inc): 8*32*224 + 4*32*56 = 64512 =
+// 384*168, so the increase is always satisfiable.  The host launches only a build
+// whose kernel uses exactly 168 registers per thread.
 //
 // Synchronisation (all waits bounded by %globaltimer; a timed-out wait sets a status
 // bit, and every CTA gives up at its next wait once a timeout bit is set):
@@ -48,8 +47,8 @@ namespace g4 {
 
 constexpr int kStepThreads = kConsumerThreads + 128;  // 2 consumer warpgroups + 1 producer warpgroup
 constexpr int kStepLaunchRegs = 168;     // registers per thread at launch (65536 / 384, rounded)
-constexpr int kStepConsumerRegs = 232;   // after setmaxnreg.inc
-constexpr int kStepProducerRegs = 40;    // after setmaxnreg.dec
+constexpr int kStepConsumerRegs = 224;   // after setmaxnreg.inc
+constexpr int kStepProducerRegs = 56;    // after setmaxnreg.dec
 static_assert(kConsumerThreads * kStepConsumerRegs + 128 * kStepProducerRegs <= kStepThreads * kStepLaunchRegs,
               "register reallocation exceeds the launch allocation");
 
@@ -75,7 +74,7 @@ struct StepProgram {
   int aux;         // bytes of the auxiliary area (>= smem_aux_bytes(z), attention scratch)
 };
 
-__host__ __device__ inline int step_smem_bytes(const StepProgram& p) {
+__host__ __device__ __forceinline__ int step_smem_bytes(const StepProgram& p) {
   return gemv_smem_bytes(p.aux, p.stages);
 }
 
@@ -99,7 +98,7 @@ constexpr int kStatusTimeouts = G4_STATUS_PEER_TIMEOUT | G4_STATUS_MBAR_TIMEOUT;
 // Spin until `pred(value)` holds for *p (acquire), bounded; gives up early when a
 // timeout bit is already set anywhere.  Returns false after setting a status bit.
 template <class Pred>
-__device__ inline bool spin_until(const int* p, Pred pred, int* status, int timeout_us) {
+__device__ __forceinline__ bool spin_until(const int* p, Pred pred, int* status, int timeout_us) {
   if (pred(ld_acquire_gpu(p))) return true;
   const uint64_t limit = static_cast<uint64_t>(timeout_us > 0 ? timeout_us : 2000000) * 1000ull;
   const uint64_t t0 = globaltimer_ns();
@@ -119,7 +118,7 @@ __device__ inline bool spin_until(const int* p, Pred pred, int* status, int time
 // Consumer-thread copy of the activation vectors of an operator into the staging
 // area (L2 loads: the data was written by other CTAs of this launch).  All loads of a
 // thread are in flight before its first store.
-__device__ inline void stage_activations(const Copy* cp, int n, unsigned char* stg) {
+__device__ __forceinline__ void stage_activations(const Copy* cp, int n, unsigned char* stg) {
   constexpr int U = 8;
   int pre[kMaxCopies + 1];
   pre[0] = 0;
@@ -190,7 +189,9 @@ __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepPr
   return true;
 }
 
-static __device__ __noinline__ void produce_step(const StepProgram& P, Smem& sm, int seq) {
+// Not inlined (its own register budget after setmaxnreg.dec); Smem by value, so the
+// consumers' copy never has its address taken.
+static __device__ __noinline__ void produce_step(const StepProgram& P, Smem sm, int seq) {
   const uint64_t pol = l2_evict_first_policy();
   RingPos rp;
   bool ok = true;
@@ -253,33 +254,97 @@ __device__ __forceinline__ void phase_end(const StepProgram& P, Smem& sm, PhaseS
   ++ps.phase;
 }
 
+// Operator kinds of the program (phase p: layer p / 6, kind p % 6; phase 6 L: LM head).
+constexpr int kKindQkv = 0, kKindAttn = 1, kKindOProj = 2, kKindRouterMlp = 3, kKindMoeUp = 4,
+              kKindMoeDown = 5, kKindLm = 6;
+
+// The matrix-product operator of (layer, kind), or null for attention.
+__device__ __forceinline__ const OpBase* op_base(const StepProgram& P, int l, int kind) {
+  switch (kind) {
+    case kKindQkv: return &P.k1[l];
+    case kKindOProj: return &P.k3[l];
+    case kKindRouterMlp: return &P.k4[l];
+    case kKindMoeUp: return &P.k5[l];
+    case kKindMoeDown: return &P.k6[l];
+    case kKindLm: return P.lm;
+    default: return nullptr;
+  }
+}
+
+__device__ __forceinline__ int op_bytes(int kind) {
+  switch (kind) {
+    case kKindQkv: return (int)sizeof(QkvOp);
+    case kKindOProj: return (int)sizeof(OProjOp);
+    case kKindRouterMlp: return (int)sizeof(RouterMlpOp);
+    case kKindMoeUp: return (int)sizeof(MoeUpOp);
+    case kKindMoeDown: return (int)sizeof(MoeDownOp);
+    default: return (int)sizeof(LmHeadOp);
+  }
+}
+static_assert(sizeof(QkvOp) <= kOpCopyBytes && sizeof(OProjOp) <= kOpCopyBytes &&
+                  sizeof(RouterMlpOp) <= kOpCopyBytes && sizeof(MoeUpOp) <= kOpCopyBytes &&
+                  sizeof(MoeDownOp) <= kOpCopyBytes && sizeof(LmHeadOp) <= kOpCopyBytes,
+              "operator plan larger than its shared-memory copy");
+static_assert(sizeof(MoeDownOp) % 8 == 0 && sizeof(QkvOp) % 8 == 0, "plans are copied in 8-byte words");
+
 // Consumer side of one matrix-product operator up to (not including) its arrival.
-template <class Op, int CPLM>
-__device__ __forceinline__ void gemv_phase_body(const Op& op, const StepProgram& P, Smem& sm, PhaseState& ps,
-                                                StepHooks& h, XRegs<CPLM>& xr) {
+// One tile loop serves every operator (only the epilogue, a switch on the kind,
+// differs): one hot loop in the instruction cache and one register allocation.  The
+// operator's plan is copied into shared memory first: every later read of a plan
+// field (per tile, in the epilogue) is a shared-memory load rather than a global load
+// that cannot be hoisted past the epilogue's global stores.
+template <int CPLM>
+__device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int kind, Smem& sm,
+                                                PhaseState& ps, StepHooks& h) {
   int* status = P.ctrl + G4_CTRL_STATUS;
-  phase_begin(P, sm, ps, op.trace_id);
+  {
+    const uint2* src = reinterpret_cast<const uint2*>(op_base(P, l, kind));
+    const int words = op_bytes(kind) / 8;
+    if ((int)threadIdx.x < words) reinterpret_cast<uint2*>(sm.opc)[threadIdx.x] = __ldg(src + threadIdx.x);
+  }
+  phase_begin(P, sm, ps, op_base(P, l, kind)->trace_id);  // its barrier publishes the copy
+  const OpBase& ob = *reinterpret_cast<const OpBase*>(sm.opc);
   bool ok = ps.live;
   if (ps.live) {
-    stage_activations(op.ac, op.nac, sm.stg);
+    stage_activations(ob.ac, ob.nac, sm.stg);
     named_bar(kBarConsumers, kConsumerThreads);
-    ok = op.prologue(sm);
+    switch (kind) {
+      case kKindQkv: ok = reinterpret_cast<const QkvOp*>(sm.opc)->prologue(sm); break;
+      case kKindOProj: ok = reinterpret_cast<const OProjOp*>(sm.opc)->prologue(sm); break;
+      case kKindRouterMlp: ok = reinterpret_cast<const RouterMlpOp*>(sm.opc)->prologue(sm); break;
+      case kKindMoeUp: ok = reinterpret_cast<const MoeUpOp*>(sm.opc)->prologue(sm); break;
+      case kKindMoeDown: ok = reinterpret_cast<const MoeDownOp*>(sm.opc)->prologue(sm); break;
+      default: ok = reinterpret_cast<const LmHeadOp*>(sm.opc)->prologue(sm); break;
+    }
     named_bar(kBarConsumers, kConsumerThreads);
-    if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 3);
+    if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 3);
   }
   // The tile loop runs even when this CTA is dead: it then only advances the ring
   // position (no waits), keeping the consumer threads in step.
-  consume_tiles<Op, CPLM>(op, sm, ps.rp, ps.wp, P.stages, ok && ps.live, status, h, xr);
-  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 5);
-  if (consumers_all(ps.live)) op.finish(sm, ok && sm.ints[kSmemDead] == 0);
-  if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 6);
-}
-
-template <class Op, int CPLM>
-__device__ __forceinline__ void run_gemv_phase(const Op& op, const StepProgram& P, Smem& sm, PhaseState& ps,
-                                               StepHooks& h, XRegs<CPLM>& xr, const OpBase* next) {
-  gemv_phase_body<Op, CPLM>(op, P, sm, ps, h, xr);
-  phase_end(P, sm, ps, next);
+  consume_segments<CPLM>(ob, sm, ps.rp, ps.wp, P.stages, ok && ps.live, status, h,
+                         [&](int s, int u0, int n, const Res& r, bool eok) {
+                           switch (kind) {
+                             case kKindQkv: reinterpret_cast<const QkvOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             case kKindOProj: reinterpret_cast<const OProjOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             case kKindRouterMlp: reinterpret_cast<const RouterMlpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             case kKindMoeUp: reinterpret_cast<const MoeUpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             case kKindMoeDown: reinterpret_cast<const MoeDownOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             default: reinterpret_cast<const LmHeadOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                           }
+                         });
+  if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 5);
+  if (consumers_all(ps.live)) {
+    const bool fok = ok && sm.ints[kSmemDead] == 0;
+    switch (kind) {
+      case kKindQkv: reinterpret_cast<const QkvOp*>(sm.opc)->finish(sm, fok); break;
+      case kKindOProj: reinterpret_cast<const OProjOp*>(sm.opc)->finish(sm, fok); break;
+      case kKindRouterMlp: reinterpret_cast<const RouterMlpOp*>(sm.opc)->finish(sm, fok); break;
+      case kKindMoeUp: reinterpret_cast<const MoeUpOp*>(sm.opc)->finish(sm, fok); break;
+      case kKindMoeDown: reinterpret_cast<const MoeDownOp*>(sm.opc)->finish(sm, fok); break;
+      default: reinterpret_cast<const LmHeadOp*>(sm.opc)->finish(sm, fok); break;
+    }
+  }
+  if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 6);
 }
 
 // Attention items of this CTA for one layer.
@@ -290,20 +355,9 @@ __device__ __forceinline__ void attn_items(const AttnArgs& a, unsigned char* scr
     attn_item<D, G>(a, it / a.nsplit, it % a.nsplit, scratch, kBarConsumers);
 }
 
-template <int DS, int GS, int DF, int GF>
-__device__ __forceinline__ void run_attention_phase(const AttnArgs& a, const StepProgram& P, Smem& sm,
-                                                    PhaseState& ps, const OpBase* next) {
-  phase_begin(P, sm, ps, a.trace_id);
-  if (ps.live) {  // the auxiliary area is free during attention
-    if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0);
-    else if (a.d == DF && a.g == GF) attn_items<DF, GF>(a, sm.x0);
-  }
-  phase_end(P, sm, ps, next);
-}
-
 // Wait (bounded) for every issued tile thread 0 did not see complete, so that no
 // bulk copy still writes into this CTA's shared memory when it exits after a failure.
-__device__ inline void drain_issued(Smem& sm, RingPos rp, int issued, int stages) {
+__device__ __forceinline__ void drain_issued(Smem& sm, RingPos rp, int issued, int stages) {
   while (rp.tiles < issued) {
     const uint64_t t0 = globaltimer_ns();
     while (!mbar_try_wait(&sm.full[rp.st], rp.ph) && globaltimer_ns() - t0 < kLocalTimeoutNs) {
@@ -348,25 +402,27 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
   }
   asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(kStepConsumerRegs) : "memory");
   PhaseState ps;
-  XRegs<CPLM> xr;  // one input vector for every operator (kept in registers)
   StepHooks h;
   if (threadIdx.x == 0) issue_copies(P.k1[0].cc, P.k1[0].ncc, sm.stg, &sm.pbar[0]);
+  // One loop over the program (the LM head is its last phase): every operator's tile
+  // loop is the same inlined code.  The next operator's constants are copied at the end
+  // of each phase; the LM head's arrival is the final one of the launch.
   const int L = P.nlayers;
-  for (int p = 0; p < 6 * L; ++p) {
-    const int l = p / 6, k = p - 6 * l;
-    switch (k) {
-      case 0: run_gemv_phase<QkvOp, CPLM>(P.k1[l], P, sm, ps, h, xr, nullptr); break;
-      case 1: run_attention_phase<DS, GS, DF, GF>(P.k2[l], P, sm, ps, &P.k3[l]); break;
-      case 2: run_gemv_phase<OProjOp, CPLM>(P.k3[l], P, sm, ps, h, xr, &P.k4[l]); break;
-      case 3: run_gemv_phase<RouterMlpOp, CPLM>(P.k4[l], P, sm, ps, h, xr, &P.k5[l]); break;
-      case 4: run_gemv_phase<MoeUpOp, CPLM>(P.k5[l], P, sm, ps, h, xr, &P.k6[l]); break;
-      default:
-        run_gemv_phase<MoeDownOp, CPLM>(P.k6[l], P, sm, ps, h, xr,
-                                        l + 1 < L ? (const OpBase*)&P.k1[l + 1] : (const OpBase*)P.lm);
+  for (int p = 0; p <= 6 * L; ++p) {
+    const int l = p / 6, k = p == 6 * L ? kKindLm : p - 6 * l;
+    if (k == kKindAttn) {
+      phase_begin(P, sm, ps, P.k2[l].trace_id);
+      if (ps.live) {  // the auxiliary area is free during attention
+        const AttnArgs& a = P.k2[l];
+        if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0);
+        else if (a.d == DF && a.g == GF) attn_items<DF, GF>(a, sm.x0);
+      }
+    } else {
+      gemv_phase_body<CPLM>(P, l, k, sm, ps, h);
     }
+    if (p < 6 * L)
+      phase_end(P, sm, ps, op_base(P, (p + 1) / 6, (p + 1) == 6 * L ? kKindLm : (p + 1) % 6));
   }
-  // LM head; its arrival is the final one of the launch
-  gemv_phase_body<LmHeadOp, CPLM>(*P.lm, P, sm, ps, h, xr);
   named_bar(kBarConsumers, kConsumerThreads);
   if (threadIdx.x == 0) {
     __threadfence();
