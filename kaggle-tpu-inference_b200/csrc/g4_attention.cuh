@@ -71,7 +71,10 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   constexpr int KPW = 32 / LK;                // lane groups per warp
   constexpr int CPL = (D / 8) / LK;           // 16-byte chunks per lane of a key row
   constexpr int NGRP = kAttnWarps * KPW;      // lane groups per CTA
-  constexpr int HG = (CPL == 2 && G == 8) ? 4 : G;  // heads kept in registers at once
+  // heads kept in registers at once: at most 4, so that the item fits the step
+  // kernel's register budget next to everything else (more heads = one more pass
+  // over the keys, which then come from L2)
+  constexpr int HG = G > 4 ? 4 : G;
   float* acc_s = reinterpret_cast<float*>(smem);                     // [G][D]
   float* gm = acc_s + G * D;                                         // [NGRP][G]
   float* gl = gm + 64 * G;                                           // [NGRP][G]

@@ -52,6 +52,7 @@ constexpr int kOpCopyBytes = 640;      // shared copy of the current operator (s
 constexpr int kSmemSeq = 40;      // launch sequence number (persistent step kernel)
 constexpr int kSmemIssued = 41;   // tiles issued by the producer lane so far
 constexpr int kSmemProdExit = 42; // producer lane has issued its last copy
+constexpr int kSmemRangesGiven = 43;  // 1: the CTA's unit ranges come from a host table
 constexpr int kSmemDead = 63;     // CTA gave up after a timed-out wait
 
 struct SegDesc {
@@ -70,17 +71,17 @@ struct Copy {
 };
 
 // Fields every operator carries (filled on the host when the step is planned).
-// Input vector of segment s: the fp32 vector x<xsel[s]> in shared memory; with
+// Input vector of segment s: the bf16 vector x<xsel[s]> in shared memory; with
 // xsub[s] > 0 (the MoE down projection) sub-row j has its own vector at x0 + j*xsub[s]
 // floats and warp w owns sub-row j = w % nsub, its vector in registers for the whole
 // segment (nsub must divide the consumer warp count).
-struct OpBase {
+struct alignas(16) OpBase {  // 16-byte multiple: plans are moved with bulk copies
   int* ctrl;
   int nseg;
   SegDesc seg[kMaxSeg];
   int xsel[kMaxSeg];
   int xsub[kMaxSeg];
-  int xbytes[2];  // bytes of the two fp32 input vectors in shared memory
+  int xbytes[2];  // bytes of the two bf16 input vectors in shared memory
   int stgbytes;   // bytes of the staging area (constant + activation vectors)
   int ncc, nac;   // constant copies / activation copies
   int trace_id;   // launch id for the optional timeline tracer (-DG4_TRACE)
@@ -106,9 +107,10 @@ struct Smem {
   float* red;        // [64] block-reduction scratch
   int* ints;         // [64] small shared ints (expert ids, flags, argmax indices)
   float* flts;       // [64] small shared floats (routing weights, argmax values)
-  unsigned char* opc;  // [kOpCopyBytes] the current operator's plan (step kernel)
-  unsigned char* x0; // input vector 0 (fp32); also the start of the auxiliary area
-  unsigned char* x1; // input vector 1 (fp32)
+  unsigned char* opc;  // [kOpCopyBytes] the current operator's plan (step kernel consumers)
+  unsigned char* popc; // [2][kOpCopyBytes] plans of the producer lane (step kernel)
+  unsigned char* x0; // input vector 0 (bf16); also the start of the auxiliary area
+  unsigned char* x1; // input vector 1 (bf16)
   unsigned char* stg;  // staging area of the prologue copies
   unsigned char* stages;
 };
@@ -124,7 +126,8 @@ __host__ __device__ __forceinline__ int smem_head_bytes(int stages) {
   off = align_up(off, 16);
   off += kResBufs * kMaxTileRows * 4;
   off += 256 * 3;
-  off += kOpCopyBytes;
+  off = align_up(off, 16);
+  off += 3 * kOpCopyBytes;
   return align_up(off, 128);
 }
 
@@ -133,7 +136,7 @@ __host__ __device__ __forceinline__ int smem_aux_bytes(SmemSizes z) {
   return align_up(z.x0, 128) + align_up(z.x1, 128) + align_up(z.stg, 128);
 }
 
-// Layout: [bars][res][red][ints][flts][opc][aux: x0 x1 stg][stages]; `aux` >= smem_aux_bytes
+// Layout: [bars][res][red][ints][flts][opc][popc][aux: x0 x1 stg][stages]; `aux` >= smem_aux_bytes
 __host__ __device__ __forceinline__ int gemv_smem_bytes(int aux, int stages) {
   int off = smem_head_bytes(stages) + aux;
   off = align_up(off, 1024);
@@ -159,8 +162,11 @@ __device__ __forceinline__ Smem carve_smem(unsigned char* raw, SmemSizes z, int 
   off += 256;
   s.flts = reinterpret_cast<float*>(base + off);
   off += 256;
+  off = align_up(off, 16);
   s.opc = base + off;
   off += kOpCopyBytes;
+  s.popc = base + off;
+  off += 2 * kOpCopyBytes;
   off = align_up(off, 128);
   s.x0 = base + off;
   s.x1 = s.x0 + align_up(z.x0, 128);
@@ -173,8 +179,8 @@ __device__ __forceinline__ Smem carve_smem(unsigned char* raw, SmemSizes z, int 
 
 // Units of segment `s` owned by CTA `cta`: those whose first byte lies in the CTA's
 // slice of the concatenated byte space of all segments.
-__device__ __forceinline__ void cta_unit_range(const SegDesc* seg, int nseg, int s, int cta, int ncta,
-                                      int& ub, int& ue) {
+__host__ __device__ __forceinline__ void cta_unit_range(const SegDesc* seg, int nseg, int s, int cta, int ncta,
+                                                        int& ub, int& ue) {
   long long total = 0, cum = 0;
   for (int i = 0; i < nseg; ++i) {
     long long b = (long long)seg[i].units * seg_unit_bytes(seg[i]);
@@ -316,26 +322,18 @@ __device__ __forceinline__ float dot8p(const uint4 w, const uint4 x, float acc) 
 // Input-vector chunks of one lane: chunk c = lane + 32 i, i < CPLM (CPLM = max chunks
 // per lane of the kernel).  The weights are the only shared-memory traffic of the dot
 // products; the input vector never leaves registers.  Every input vector of the step
-// holds bf16 values (widened to fp32 in shared memory), so a lane keeps them packed,
-// two per register: 4 registers per chunk.
+// holds bf16 values (bf16 in shared memory too), so a lane keeps them packed, two per
+// register: 4 registers per chunk.
 template <int CPLM>
 struct XRegs {
   uint4 v[CPLM];
-  __device__ __forceinline__ void load(const float* x, int C) {
+  // x: the bf16 input vector in shared memory; chunk c is 8 consecutive elements.
+  __device__ __forceinline__ void load(const bf16_t* x, int C) {
     const int lane = threadIdx.x & 31;
 #pragma unroll
     for (int i = 0; i < CPLM; ++i) {
       const int c = lane + 32 * i;
-      uint4 p = make_uint4(0u, 0u, 0u, 0u);  // every element written: no live-in
-      if (c < C) {
-        const uint4 a = reinterpret_cast<const uint4*>(x)[2 * c];      // fp32 bits
-        const uint4 b = reinterpret_cast<const uint4*>(x)[2 * c + 1];
-        p.x = (a.x >> 16) | (a.y & 0xffff0000u);  // exact: the values are bf16
-        p.y = (a.z >> 16) | (a.w & 0xffff0000u);
-        p.z = (b.x >> 16) | (b.y & 0xffff0000u);
-        p.w = (b.z >> 16) | (b.w & 0xffff0000u);
-      }
-      v[i] = p;
+      v[i] = c < C ? reinterpret_cast<const uint4*>(x)[c] : make_uint4(0u, 0u, 0u, 0u);
     }
   }
   // Warp-wide dot product of one staged row with the registers, NC iterations of 32
@@ -410,9 +408,12 @@ struct EmptyBarrierHooks {
 
 // The input vector lives here, in the one place the loop is instantiated: a register
 // array shared by several inlined copies stays in local memory instead.
+// `ranges` (step kernel): this CTA's precomputed [ub, ue) per segment (int2[kMaxSeg]),
+// or null to compute them here.
 template <int CPLM, class Hooks, class Epi>
 __device__ __forceinline__ void consume_segments(const OpBase& ob, Smem& sm, RingPos& rp, RingPos& wp,
-                                                 int stages, bool ok, int* status, Hooks& h, Epi&& epi) {
+                                                 int stages, bool ok, int* status, Hooks& h, Epi&& epi,
+                                                 const int2* ranges = nullptr) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   XRegs<CPLM> xr;
   volatile int* dead = sm.ints + kSmemDead;
@@ -420,13 +421,18 @@ __device__ __forceinline__ void consume_segments(const OpBase& ob, Smem& sm, Rin
   const int nseg = ob.nseg;
   for (int s = 0; s < nseg; ++s) {
     int ub, ue;
-    cta_unit_range(ob.seg, nseg, s, blockIdx.x, gridDim.x, ub, ue);
+    if (ranges) {
+      ub = ranges[s].x;
+      ue = ranges[s].y;
+    } else {
+      cta_unit_range(ob.seg, nseg, s, blockIdx.x, gridDim.x, ub, ue);
+    }
     if (ub >= ue) continue;
     const SegDesc sd = ob.seg[s];
     const int C = sd.K >> 3;
     const int xsub = ob.xsub[s];
     const int sub = xsub ? warp % sd.nsub : 0;
-    const float* xv = reinterpret_cast<const float*>(ob.xsel[s] ? sm.x1 : sm.x0) + sub * xsub;
+    const bf16_t* xv = reinterpret_cast<const bf16_t*>(ob.xsel[s] ? sm.x1 : sm.x0) + sub * xsub;
     xr.load(xv, C);
     for (int u = ub; u < ue;) {
       const int n = tile_units(sd, u, ue);
@@ -489,6 +495,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
     sm.ints[kSmemDead] = 0;
     sm.ints[kSmemIssued] = 0;
     sm.ints[kSmemProdExit] = 0;
+    sm.ints[kSmemRangesGiven] = 0;
   }
   __syncthreads();
   pdl_trigger();

@@ -42,6 +42,7 @@ constexpr int kXFlagBytes = kSites * 2 * kMaxWorld * 128;
 // Smem::ints slots
 constexpr int kSmemExp = 0;        // [0,16) expert ids (producer copy)
 constexpr int kSmemRouterEnd = 32;  // end of this CTA's router units (0: none)
+constexpr int kSmemRouterMine = 36; // number of this CTA's router units
 constexpr int kSmemLast = 33;
 constexpr int kSmemOk = 34;
 constexpr int kSmemWriteLogits = 35;
@@ -112,15 +113,46 @@ __device__ __forceinline__ float* sf(const Smem& sm, int off) {
 __device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
   return 1.0f / sqrtf(ss / (float)n + eps);
 }
-__device__ __forceinline__ float bsum(float v, Smem& sm) {
-  return block_sum(v, sm.red, kConsumerThreads, kBarReduce);
+// Prologue vectors of length H live in registers: thread t owns h = t + 256 j.
+constexpr int kPerThread = kMaxHidden / kConsumerThreads;
+
+// Block sum over the consumer threads with ONE barrier: warp partials go to slot
+// `slot` of Smem::red (8 slots of 8 floats; a prologue gives each reduction its own
+// slot, and the barriers between prologues order the reuse).  Fixed summation order,
+// identical on every thread.
+__device__ __forceinline__ float bsum1(float v, Smem& sm, int slot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  if (lane == 0) sm.red[slot * kConsumerWarps + warp] = v;
+  named_bar(kBarReduce, kConsumerThreads);
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) s += sm.red[slot * kConsumerWarps + i];
+  return s;
+}
+// Two independent sums in one barrier (slots `slot` and `slot + 1`).
+__device__ __forceinline__ float2 bsum2(float a, float b, Smem& sm, int slot) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  a = warp_sum(a);
+  b = warp_sum(b);
+  if (lane == 0) {
+    sm.red[slot * kConsumerWarps + warp] = a;
+    sm.red[(slot + 1) * kConsumerWarps + warp] = b;
+  }
+  named_bar(kBarReduce, kConsumerThreads);
+  float sa = 0.f, sb = 0.f;
+#pragma unroll
+  for (int i = 0; i < kConsumerWarps; ++i) {
+    sa += sm.red[slot * kConsumerWarps + i];
+    sb += sm.red[(slot + 1) * kConsumerWarps + i];
+  }
+  return make_float2(sa, sb);
 }
 
 // Output of layer `tail` from the previous kernels (model.py:312-322):
 //   h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2, h = rms(h1+h2)*pf, x = (resmid + h)*scalar.
 // Staged inputs: pf1/pf2/pf (bf16 constants); world 1: mlp (fp32), moe and resmid
-// (bf16).  Result x (bf16 values) in the fp32 temporary t0.  t0 may alias the staged
-// mlp vector (each element is read before it is overwritten by the same thread).
+// (bf16).  Result x (bf16 values) in registers (uses reduction slots 0-2).
 struct Tail {
   const bf16_t* resmid;  // residual after attention (bf16 [H])
   const bf16_t* scalar;  // layer_scalar [1]
@@ -129,68 +161,93 @@ struct Tail {
   int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, float* t0,
-                                    float* t1, Smem& sm) {
+__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, Smem& sm,
+                                             float (&x)[kPerThread]) {
   const int H = c.H, tid = threadIdx.x;
   bool ok = true;
+  float a[kPerThread], b[kPerThread];
   float s1 = 0.f, s2 = 0.f;
   if (c.world == 1) {
     const float* mlp = sf(sm, t.o_mlp);
     const bf16_t* moe = sbf(sm, t.o_moe);
-    for (int h = tid; h < H; h += kConsumerThreads) {
-      const float m = rbf(mlp[h]), mo = bf2f(moe[h]);
-      t0[h] = m;
-      t1[h] = mo;
-      s1 += m * m;
-      s2 += mo * mo;
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const int h = tid + j * kConsumerThreads;
+      a[j] = 0.f;
+      b[j] = 0.f;
+      if (h < H) {
+        a[j] = rbf(mlp[h]);
+        b[j] = bf2f(moe[h]);
+        s1 += a[j] * a[j];
+        s2 += b[j] * b[j];
+      }
     }
   } else {
     const int use = site_use(ctrl, c, kSiteFfn, t.layer);
     ok = xchg_wait(ctrl, c, kSiteFfn, use, sm);
-    for (int h = tid; h < H; h += kConsumerThreads) {
-      float a = 0.f, b = 0.f;
-      for (int src = 0; src < c.world; ++src) {
-        const float* sl = xslot(c, c.rank, kSiteFfn, use & 1, src);
-        a += ldcg_f(sl + h);
-        b += ldcg_f(sl + H + h);
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const int h = tid + j * kConsumerThreads;
+      a[j] = 0.f;
+      b[j] = 0.f;
+      if (h < H) {
+        float sa = 0.f, sb = 0.f;
+        for (int src = 0; src < c.world; ++src) {
+          const float* sl = xslot(c, c.rank, kSiteFfn, use & 1, src);
+          sa += ldcg_f(sl + h);
+          sb += ldcg_f(sl + H + h);
+        }
+        a[j] = rbf(sa);
+        b[j] = rbf(sb);
+        s1 += a[j] * a[j];
+        s2 += b[j] * b[j];
       }
-      const float m = rbf(a), mo = rbf(b);
-      t0[h] = m;
-      t1[h] = mo;
-      s1 += m * m;
-      s2 += mo * mo;
     }
   }
-  const float r1 = rms_scale(bsum(s1, sm), H, c.eps);
-  const float r2 = rms_scale(bsum(s2, sm), H, c.eps);
+  const float2 ss = bsum2(s1, s2, sm, 0);
+  const float r1 = rms_scale(ss.x, H, c.eps), r2 = rms_scale(ss.y, H, c.eps);
   const bf16_t *pf1 = sbf(sm, t.o_pf1), *pf2 = sbf(sm, t.o_pf2), *pf = sbf(sm, t.o_pf);
   float s3 = 0.f;
-  for (int h = tid; h < H; h += kConsumerThreads) {
-    const float v = rbf(rbf((t0[h] * r1) * bf2f(pf1[h])) + rbf((t1[h] * r2) * bf2f(pf2[h])));
-    t0[h] = v;
-    s3 += v * v;
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int h = tid + j * kConsumerThreads;
+    if (h < H) {
+      a[j] = rbf(rbf((a[j] * r1) * bf2f(pf1[h])) + rbf((b[j] * r2) * bf2f(pf2[h])));
+      s3 += a[j] * a[j];
+    }
   }
-  const float r3 = rms_scale(bsum(s3, sm), H, c.eps);
+  const float r3 = rms_scale(bsum1(s3, sm, 2), H, c.eps);
   const float sc = bf2f(t.scalar[0]);
-  for (int h = tid; h < H; h += kConsumerThreads) {
-    const float res = bf2f(sbf(sm, t.o_res)[h]);
-    t0[h] = rbf(rbf(res + rbf((t0[h] * r3) * bf2f(pf[h]))) * sc);
+  const bf16_t* res = sbf(sm, t.o_res);
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int h = tid + j * kConsumerThreads;
+    x[j] = 0.f;
+    if (h < H) x[j] = rbf(rbf(bf2f(res[h]) + rbf((a[j] * r3) * bf2f(pf[h]))) * sc);
   }
   return ok;
 }
 
-// dst[h] = rbf(rms(x) * w[h]) for the fp32 vector x (smem), bf16 weight w (smem).
-__device__ __forceinline__ void norm_into(const Common& c, const float* x, const bf16_t* w, float* dst,
-                                 Smem& sm) {
+// dst[h] = bf16(rms(x) * w[h]) for x in registers, bf16 weight w (smem); slot `slot`.
+__device__ __forceinline__ void norm_into(const Common& c, const float (&x)[kPerThread], const bf16_t* w,
+                                          bf16_t* dst, Smem& sm, int slot) {
+  const int H = c.H, tid = threadIdx.x;
   float s = 0.f;
-  for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) s += x[h] * x[h];
-  const float r = rms_scale(bsum(s, sm), c.H, c.eps);
-  for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) dst[h] = rbf((x[h] * r) * bf2f(w[h]));
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j)
+    if (tid + j * kConsumerThreads < H) s += x[j] * x[j];
+  const float r = rms_scale(bsum1(s, sm, slot), H, c.eps);
+#pragma unroll
+  for (int j = 0; j < kPerThread; ++j) {
+    const int h = tid + j * kConsumerThreads;
+    if (h < H) dst[h] = f2bf((x[j] * r) * bf2f(w[h]));
+  }
 }
 
-// Convert a staged bf16 vector of n elements into the fp32 input vector dst.
-__device__ __forceinline__ void widen(const bf16_t* src, int n, float* dst) {
-  for (int i = threadIdx.x; i < n; i += kConsumerThreads) dst[i] = bf2f(src[i]);
+// Copy a staged bf16 vector of n elements (n % 8 == 0) into an input vector.
+__device__ __forceinline__ void copy_vec(const bf16_t* src, int n, unsigned char* dst) {
+  for (int i = threadIdx.x; i < n / 8; i += kConsumerThreads)
+    reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
 }
 
 // ================================================================== K1: q|k|v
@@ -199,7 +256,7 @@ struct QkvOp : OpBase {
   const bf16_t* w;     // [rows, H]: q rows, k rows, v rows of this rank
   bf16_t* out;         // q|k|v projections (bf16 [rows])
   bf16_t* xres;        // layer input x (bf16 [H]), written by CTA 0
-  int o_win, o_t0;
+  int o_win;
   // layer 0: token embedding
   const bf16_t* embed;  // replicated [V, H]
   const int* tokens_in;
@@ -217,25 +274,34 @@ struct QkvOp : OpBase {
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
-    float* t0 = sf(sm, o_t0);
-    float* t1 = reinterpret_cast<float*>(sm.x0);  // dead before x0 is written
+    float x[kPerThread];
+    const int H = c.H, tid = threadIdx.x;
     if (c.layer == 0) {
       int pos = ldcg_i(ctrl + G4_CTRL_POS);
       if (pos < 0 || pos >= max_len) pos = 0;  // flagged by the attention / lm_head kernels
       const int forced = ldcg_i(ctrl + G4_CTRL_FORCED_LEN);
       int tok = pos < forced ? ldcg_i(tokens_in + pos) : ldcg_i(tokens_out + pos);
       if (tok < 0 || tok >= vocab) {
-        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_BAD_TOKEN);
+        if (tid == 0 && blockIdx.x == 0) atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_BAD_TOKEN);
         tok = 0;
       }
-      const bf16_t* row = embed + (size_t)tok * c.H;
-      for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) t0[h] = rbf(bf2f(row[h]) * embed_scale);
+      const bf16_t* row = embed + (size_t)tok * H;
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int h = tid + j * kConsumerThreads;
+        x[j] = h < H ? rbf(bf2f(row[h]) * embed_scale) : 0.f;
+      }
     } else {
-      ok = layer_output(ctrl, c, tail, t0, t1, sm) && ok;
+      ok = layer_output(ctrl, c, tail, sm, x);
     }
-    if (blockIdx.x == 0)
-      for (int h = threadIdx.x; h < c.H; h += kConsumerThreads) xres[h] = f2bf(t0[h]);
-    norm_into(c, t0, sbf(sm, o_win), reinterpret_cast<float*>(sm.x0), sm);
+    if (blockIdx.x == 0) {
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int h = tid + j * kConsumerThreads;
+        if (h < H) xres[h] = f2bf(x[j]);
+      }
+    }
+    norm_into(c, x, sbf(sm, o_win), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     return ok;
   }
   __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
@@ -259,7 +325,7 @@ struct OProjOp : OpBase {
     bulk_g2s(stage, w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), bar, pol);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
-    widen(sbf(sm, o_ctx), Kc, reinterpret_cast<float*>(sm.x0));
+    copy_vec(sbf(sm, o_ctx), Kc, sm.x0);
     return true;
   }
   __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
@@ -296,7 +362,6 @@ struct RouterMlpOp : OpBase {
   float hinv;              // bf16(H^-0.5) as float
   int o_wpa, o_wff, o_wff2, o_wrs;  // staged constants
   int o_o, o_x;                     // staged activations: o_proj out (fp32), x (bf16)
-  int o_t0;
   int block_mode;                   // 1: the input is already the MoE input (g4_moe_block)
   const bf16_t* block_x;
   int* ready;                       // step kernel: router flag of this layer (else null)
@@ -316,68 +381,93 @@ struct RouterMlpOp : OpBase {
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
     const int H = c.H, tid = threadIdx.x;
-    float* t0 = sf(sm, o_t0);
-    float* t1 = reinterpret_cast<float*>(sm.x0);  // becomes the router input in place
+    float hv[kPerThread];  // MoE input (model.py:315); the router input derives from it
     if (!block_mode) {
       // attention output (summed over ranks), then x = residual + rms(attn)*post_attn
+      float t[kPerThread];
       float s = 0.f;
       if (c.world == 1) {
         const float* o = sf(sm, o_o);
-        for (int h = tid; h < H; h += kConsumerThreads) {
-          const float v = rbf(o[h]);
-          t0[h] = v;
-          s += v * v;
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+          const int h = tid + j * kConsumerThreads;
+          t[j] = 0.f;
+          if (h < H) {
+            t[j] = rbf(o[h]);
+            s += t[j] * t[j];
+          }
         }
       } else {
         const int use = site_use(ctrl, c, kSiteAttn, c.layer);
         ok = xchg_wait(ctrl, c, kSiteAttn, use, sm) && ok;
-        for (int h = tid; h < H; h += kConsumerThreads) {
-          float a = 0.f;
-          for (int src = 0; src < c.world; ++src) a += ldcg_f(xslot(c, c.rank, kSiteAttn, use & 1, src) + h);
-          const float v = rbf(a);
-          t0[h] = v;
-          s += v * v;
+#pragma unroll
+        for (int j = 0; j < kPerThread; ++j) {
+          const int h = tid + j * kConsumerThreads;
+          t[j] = 0.f;
+          if (h < H) {
+            float a = 0.f;
+            for (int src = 0; src < c.world; ++src) a += ldcg_f(xslot(c, c.rank, kSiteAttn, use & 1, src) + h);
+            t[j] = rbf(a);
+            s += t[j] * t[j];
+          }
         }
       }
-      const float r = rms_scale(bsum(s, sm), H, c.eps);
+      const float r = rms_scale(bsum1(s, sm, 0), H, c.eps);
       const bf16_t* wpa = sbf(sm, o_wpa);
+      const bf16_t* xin = sbf(sm, o_x);
       float s2 = 0.f;
-      for (int h = tid; h < H; h += kConsumerThreads) {
-        const float xin = bf2f(sbf(sm, o_x)[h]);
-        const float v = rbf(xin + rbf((t0[h] * r) * bf2f(wpa[h])));  // model.py:303-304
-        t0[h] = v;
-        s2 += v * v;
-        if (blockIdx.x == 0) resmid[h] = f2bf(v);
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int h = tid + j * kConsumerThreads;
+        if (h < H) {
+          t[j] = rbf(bf2f(xin[h]) + rbf((t[j] * r) * bf2f(wpa[h])));  // model.py:303-304
+          s2 += t[j] * t[j];
+          if (blockIdx.x == 0) resmid[h] = f2bf(t[j]);
+        }
       }
       // MLP input (model.py:310) and MoE input (model.py:315)
-      const float r2 = rms_scale(bsum(s2, sm), H, c.eps);
+      const float r2 = rms_scale(bsum1(s2, sm, 1), H, c.eps);
       const bf16_t *wff = sbf(sm, o_wff), *wff2 = sbf(sm, o_wff2);
-      float* xm = reinterpret_cast<float*>(sm.x1);
-      for (int h = tid; h < H; h += kConsumerThreads) {
-        xm[h] = rbf((t0[h] * r2) * bf2f(wff[h]));
-        const float v = rbf((t0[h] * r2) * bf2f(wff2[h]));
-        t1[h] = v;
-        if (blockIdx.x == 0) h2[h] = f2bf(v);
+      bf16_t* xm = reinterpret_cast<bf16_t*>(sm.x1);
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int h = tid + j * kConsumerThreads;
+        hv[j] = 0.f;
+        if (h < H) {
+          xm[h] = f2bf((t[j] * r2) * bf2f(wff[h]));
+          hv[j] = rbf((t[j] * r2) * bf2f(wff2[h]));
+          if (blockIdx.x == 0) h2[h] = f2bf(hv[j]);
+        }
       }
     } else {
-      for (int h = tid; h < H; h += kConsumerThreads) {
-        const float v = bf2f(ldcg_bf(block_x + h));
-        t1[h] = v;
-        if (blockIdx.x == 0) h2[h] = f2bf(v);
+#pragma unroll
+      for (int j = 0; j < kPerThread; ++j) {
+        const int h = tid + j * kConsumerThreads;
+        hv[j] = 0.f;
+        if (h < H) {
+          hv[j] = bf2f(ldcg_bf(block_x + h));
+          if (blockIdx.x == 0) h2[h] = f2bf(hv[j]);
+        }
       }
     }
     // router input: rms(h2) * scale * H^-1/2                 (model.py:225-226)
     float s3 = 0.f;
-    for (int h = tid; h < H; h += kConsumerThreads) s3 += t1[h] * t1[h];
-    const float r3 = rms_scale(bsum(s3, sm), H, c.eps);
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j)
+      if (tid + j * kConsumerThreads < H) s3 += hv[j] * hv[j];
+    const float r3 = rms_scale(bsum1(s3, sm, 2), H, c.eps);
     const bf16_t* wrs = sbf(sm, o_wrs);
-    float* xr = reinterpret_cast<float*>(sm.x0);
-    for (int h = tid; h < H; h += kConsumerThreads)
-      xr[h] = rbf(rbf(rbf(t1[h] * r3) * bf2f(wrs[h])) * hinv);
-    if (tid == 0) {
+    bf16_t* xr = reinterpret_cast<bf16_t*>(sm.x0);
+#pragma unroll
+    for (int j = 0; j < kPerThread; ++j) {
+      const int h = tid + j * kConsumerThreads;
+      if (h < H) xr[h] = f2bf(rbf(rbf(hv[j] * r3) * bf2f(wrs[h])) * hinv);
+    }
+    if (tid == 0 && !sm.ints[kSmemRangesGiven]) {  // else the step kernel set them
       int ub, ue;
       cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
       sm.ints[kSmemRouterEnd] = ub < ue ? ue : 0;
+      sm.ints[kSmemRouterMine] = ue - ub;
     }
     return ok;
   }
@@ -388,19 +478,13 @@ struct RouterMlpOp : OpBase {
       // right after this CTA's last router tile (identical test on every thread):
       // count its rows in; the CTA completing all E logits selects the top-k now,
       // early in the operator, so the expert weights can stream behind it
-      if (u0 + n == sm.ints[kSmemRouterEnd]) router_done(router_units(), sm);
+      if (u0 + n == sm.ints[kSmemRouterEnd]) router_done(sm.ints[kSmemRouterMine], sm);
     } else if (ok && t < n) {
       const float g = rbf(res[t]), u = rbf(res[n + t]);
       mlp_act[u0 + t] = f2bf(rbf(gelu_tanh(g)) * u);
     }
   }
   __device__ __forceinline__ void finish(Smem&, bool) const {}
-  // Router units this CTA owns (its range of segment 0).
-  __device__ __forceinline__ int router_units() const {
-    int ub, ue;
-    cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
-    return ue - ub;
-  }
   // The CTA that completes the router's E logits selects the top-k (model.py:227-232).
   __device__ __forceinline__ void router_done(int mine, Smem& sm) const {
     __threadfence();
@@ -520,8 +604,8 @@ struct MoeUpOp : OpBase {
     }
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
-    widen(sbf(sm, o_h2), c.H, reinterpret_cast<float*>(sm.x0));
-    widen(sbf(sm, o_act), I, reinterpret_cast<float*>(sm.x1));
+    copy_vec(sbf(sm, o_h2), c.H, sm.x0);
+    copy_vec(sbf(sm, o_act), I, sm.x1);
     if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
     return true;
   }
@@ -561,7 +645,7 @@ struct MoeDownOp : OpBase {
     }
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
-    widen(sbf(sm, o_act), topk * F, reinterpret_cast<float*>(sm.x0));
+    copy_vec(sbf(sm, o_act), topk * F, sm.x0);
     return true;
   }
   __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
@@ -594,7 +678,7 @@ struct MoeDownOp : OpBase {
 struct LmHeadOp : OpBase {
   Common c;
   Tail tail;
-  int o_wn, o_t0;        // staged final norm weight, temporary
+  int o_wn;              // staged final norm weight
   const bf16_t* embed;   // replicated [V, H]; this rank reads rows [vbegin, vbegin+V_local)
   int vbegin;
   float* logits;         // [V_local] fp32 (written when control[WRITE_LOGITS] != 0)
@@ -612,8 +696,9 @@ struct LmHeadOp : OpBase {
     bulk_g2s(stage, embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
-    const bool ok = layer_output(ctrl, c, tail, sf(sm, o_t0), reinterpret_cast<float*>(sm.x0), sm);
-    norm_into(c, sf(sm, o_t0), sbf(sm, o_wn), reinterpret_cast<float*>(sm.x0), sm);
+    float x[kPerThread];
+    const bool ok = layer_output(ctrl, c, tail, sm, x);
+    norm_into(c, x, sbf(sm, o_wn), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     float* bv = reinterpret_cast<float*>(sm.x1);
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;
     bv[threadIdx.x] = -INFINITY;

@@ -587,7 +587,7 @@ static int plan_step_program(g4_model* m) {
   cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, m->device);
   const int limit = std::min(kMaxSmemBytes, optin > 0 ? optin : kMaxSmemBytes);
   int stages = kMaxStages;
-  while (stages >= 3 && gemv_smem_bytes(aux, stages) > limit) --stages;
+  while (stages >= 3 && gemv_smem_bytes(aux, stages) + step_range_bytes(nl) > limit) --stages;
   if (stages < 3) return fail(G4_ERR_SHAPE, "step kernel: %d bytes of vectors leave no room for the ring", aux);
   m->step_cplm = cplm_bucket(cpl);
   if (!m->step_cplm) return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank");
@@ -601,9 +601,10 @@ static int plan_step_program(g4_model* m) {
   p.stages = stages;
   p.z = z;
   p.aux = aux;
+  const size_t range_bytes = (size_t)m->nsm * step_range_bytes(nl);
   const size_t bytes = (sizeof(QkvOp) + sizeof(AttnArgs) + sizeof(OProjOp) + sizeof(RouterMlpOp) +
                         sizeof(MoeUpOp) + sizeof(MoeDownOp) + 6 * 256) * (size_t)nl +
-                       sizeof(LmHeadOp) + 256;
+                       sizeof(LmHeadOp) + 256 + range_bytes + 256;
   if (cudaMalloc(&m->prog_mem, bytes) != cudaSuccess) return fail(G4_ERR_NOMEM, "step program");
   m->prog_dirty = true;
   return G4_OK;
@@ -630,6 +631,27 @@ static int upload_step_program(g4_model* m) {
   p.k5 = reinterpret_cast<const MoeUpOp*>(put(m->k5.data(), nl * sizeof(MoeUpOp)));
   p.k6 = reinterpret_cast<const MoeDownOp*>(put(m->k6.data(), nl * sizeof(MoeDownOp)));
   p.lm = reinterpret_cast<const LmHeadOp*>(put(&m->lm, sizeof(LmHeadOp)));
+  // unit ranges of every matrix-product phase for every CTA ([CTA][phase][kRangeSlots])
+  {
+    const int nops = step_nops((int)nl);
+    std::vector<int2> tab((size_t)m->nsm * nops * kRangeSlots, make_int2(0, 0));
+    for (int i = 0; i < nops; ++i) {
+      const int l = i / 5, r = i - 5 * l;
+      const OpBase* op = i == nops - 1 ? static_cast<const OpBase*>(&m->lm)
+                         : r == 0      ? static_cast<const OpBase*>(&m->k1[l])
+                         : r == 1      ? static_cast<const OpBase*>(&m->k3[l])
+                         : r == 2      ? static_cast<const OpBase*>(&m->k4[l])
+                         : r == 3      ? static_cast<const OpBase*>(&m->k5[l])
+                                       : static_cast<const OpBase*>(&m->k6[l]);
+      for (int cta = 0; cta < m->nsm; ++cta)
+        for (int sg = 0; sg < op->nseg; ++sg) {
+          int ub, ue;
+          cta_unit_range(op->seg, op->nseg, sg, cta, m->nsm, ub, ue);
+          tab[((size_t)cta * nops + i) * kRangeSlots + sg] = make_int2(ub, ue);
+        }
+    }
+    p.ranges = reinterpret_cast<const int2*>(put(tab.data(), tab.size() * sizeof(int2)));
+  }
   G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
   m->prog_dirty = false;
   return G4_OK;
@@ -795,14 +817,12 @@ extern "C" int g4_model_finalize(g4_model* m) {
     a.nseg = 1;
     a.trace_id = i * 8 + 0;
     a.seg[0] = SegDesc{l.rows_q + l.rows_k + l.rows_v, 1, H, 0};
-    a.xbytes[0] = H * 4;
+    a.xbytes[0] = H * 2;
     a.xbytes[1] = 0;
     {
       Stager sg(&a);
       a.o_win = sg.constant(l.n_in, H * 2);
       if (i > 0) a.tail = plan_tail(m, i - 1, sg);
-      // the layer-output temporary may overwrite the staged MLP output (read first)
-      a.o_t0 = (i > 0 && m->world == 1) ? a.tail.o_mlp : sg.space(H * 4);
     }
     a.w = l.qkv;
     a.out = m->qkv_raw;
@@ -844,7 +864,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     o.nseg = 1;
     o.trace_id = i * 8 + 2;
     o.seg[0] = SegDesc{H, 1, l.rows_q, 0};
-    o.xbytes[0] = l.rows_q * 4;
+    o.xbytes[0] = l.rows_q * 2;
     {
       Stager sg(&o);
       o.o_ctx = sg.activation(m->ctx, l.rows_q * 2);
@@ -862,8 +882,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.seg[0] = SegDesc{m->E, 1, H, 0};
     r.seg[1] = SegDesc{m->I_local, 2, H, 0};
     r.xsel[1] = 1;  // router rows: x0 (router input); MLP gate|up: x1 (MLP input)
-    r.xbytes[0] = H * 4;
-    r.xbytes[1] = H * 4;
+    r.xbytes[0] = H * 2;
+    r.xbytes[1] = H * 2;
     {
       Stager sg(&r);
       r.o_wpa = sg.constant(l.n_post_attn, H * 2);
@@ -872,8 +892,6 @@ extern "C" int g4_model_finalize(g4_model* m) {
       r.o_wrs = sg.constant(l.router_scale, H * 2);
       if (m->world == 1) r.o_o = sg.activation(m->o_out, H * 4);
       r.o_x = sg.activation(m->xres, H * 2);
-      // the residual temporary may overwrite the staged o_proj output (read first)
-      r.o_t0 = m->world == 1 ? r.o_o : sg.space(H * 4);
     }
     r.xres = m->xres;
     r.resmid = m->resmid;
@@ -900,8 +918,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
     u.seg[0] = SegDesc{H, 1, m->I_local, 0};
     u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local};
     u.xsel[0] = 1;  // MLP down: x1 (activation); experts gate|up: x0 (MoE input)
-    u.xbytes[0] = H * 4;
-    u.xbytes[1] = m->I_local * 4;
+    u.xbytes[0] = H * 2;
+    u.xbytes[1] = m->I_local * 2;
     {
       Stager sg(&u);
       u.o_h2 = sg.activation(m->h2, H * 2);
@@ -925,7 +943,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     dn.trace_id = i * 8 + 5;
     dn.seg[0] = SegDesc{H, m->topk, m->F_local, 0};
     dn.xsub[0] = m->F_local;  // expert slot j: activation j at x0 + j*F
-    dn.xbytes[0] = m->topk * m->F_local * 4;
+    dn.xbytes[0] = m->topk * m->F_local * 2;
     {
       Stager sg(&dn);
       dn.o_act = sg.activation(m->moe_act, m->topk * m->F_local * 2);
@@ -945,13 +963,12 @@ extern "C" int g4_model_finalize(g4_model* m) {
     lm.nseg = 1;
     lm.trace_id = nl * 8;
     lm.seg[0] = SegDesc{m->V_local, 1, H, 0};
-    lm.xbytes[0] = H * 4;
+    lm.xbytes[0] = H * 2;
     lm.xbytes[1] = kConsumerThreads * 8;
     {
       Stager sg(&lm);
       lm.o_wn = sg.constant(m->final_norm, H * 2);
       lm.tail = plan_tail(m, nl - 1, sg);
-      lm.o_t0 = m->world == 1 ? lm.tail.o_mlp : sg.space(H * 4);
     }
     lm.embed = m->embed;
     lm.vbegin = m->vbegin;
@@ -1401,12 +1418,11 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   r.ctrl = control;
   r.nseg = 1;
   r.seg[0] = SegDesc{E, 1, H, 0};
-  r.xbytes[0] = H * 4;
+  r.xbytes[0] = H * 2;
   r.xbytes[1] = 0;
   {
     Stager sg(&r);
     r.o_wrs = sg.constant(router_scale, H * 2);
-    r.o_t0 = sg.space(H * 4);
   }
   r.block_mode = 1;
   r.block_x = static_cast<const bf16_t*>(x);
@@ -1428,8 +1444,8 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   u.seg[0] = SegDesc{0, 1, 8, 0};
   u.seg[1] = SegDesc{K * F, 2, H, F};
   u.xsel[0] = 1;
-  u.xbytes[0] = H * 4;
-  u.xbytes[1] = 32;
+  u.xbytes[0] = H * 2;
+  u.xbytes[1] = 16;
   {
     Stager sg(&u);
     u.o_h2 = sg.activation(r.h2, H * 2);
@@ -1452,7 +1468,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   dn.nseg = 1;
   dn.seg[0] = SegDesc{H, K, F, 0};
   dn.xsub[0] = F;
-  dn.xbytes[0] = K * F * 4;
+  dn.xbytes[0] = K * F * 2;
   {
     Stager sg(&dn);
     dn.o_act = sg.activation(u.moe_act, K * F * 2);

@@ -68,14 +68,22 @@ struct StepProgram {
   const LmHeadOp* lm;
   int* sync;       // kNumSyncWords ints
   int* ctrl;
+  const int2* ranges;  // [CTA][matrix-product phase][4] unit ranges per segment
   int nlayers;
   int stages;      // ring depth
   SmemSizes z;     // x0 / x1 / staging sizes (maximum over the operators)
   int aux;         // bytes of the auxiliary area (>= smem_aux_bytes(z), attention scratch)
 };
 
+constexpr int kRangeSlots = 4;  // int2 per phase in the range table (kMaxSeg used)
+
+__host__ __device__ __forceinline__ int step_nops(int nlayers) { return 5 * nlayers + 1; }
+// The CTA's range table follows the ring in shared memory.
+__host__ __device__ __forceinline__ int step_range_bytes(int nlayers) {
+  return step_nops(nlayers) * kRangeSlots * 8;
+}
 __host__ __device__ __forceinline__ int step_smem_bytes(const StepProgram& p) {
-  return gemv_smem_bytes(p.aux, p.stages);
+  return gemv_smem_bytes(p.aux, p.stages) + step_range_bytes(p.nlayers);
 }
 
 // Named barrier that also ANDs a predicate over the consumer threads: a decision
@@ -160,15 +168,21 @@ __device__ __forceinline__ void with_gemv_op(const StepProgram& P, int p, F&& f)
   else if (k == 5) f(P.k6[l]);
 }
 
+// This CTA's unit-range table in shared memory (after the ring).
+__device__ __forceinline__ const int2* step_ranges(const StepProgram& P, const Smem& sm) {
+  return reinterpret_cast<const int2*>(sm.stages + (size_t)P.stages * kStageBytes);
+}
+
 // Producer lane: every weight tile of one operator owned by this CTA.
 template <class Op>
 __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepProgram& P, Smem& sm, RingPos& rp,
-                                           uint64_t pol, int seq) {
+                                           uint64_t pol, int seq, const int2* rng) {
   int* status = P.ctrl + G4_CTRL_STATUS;
   bool dep_loaded = false;
   for (int s = 0; s < op.nseg; ++s) {
     int ub, ue;
-    cta_unit_range(op.seg, op.nseg, s, blockIdx.x, gridDim.x, ub, ue);
+    ub = rng[s].x;
+    ue = rng[s].y;
     if (ub >= ue) continue;
     if (op.seg_dependent(s) && !dep_loaded) {
       const int want = seq + 1;
@@ -189,25 +203,86 @@ __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepPr
   return true;
 }
 
+// The program's matrix-product phases in order (attention phases carry no tiles):
+// index i -> (layer, kind).
+__device__ __forceinline__ void gemv_phase_of(int i, int nlayers, int& l, int& kind) {
+  if (i == 5 * nlayers) {
+    l = nlayers;
+    kind = 6;  // LM head
+    return;
+  }
+  l = i / 5;
+  const int r = i - 5 * l;
+  kind = r == 0 ? 0 : r + 1;  // 0 qkv, 2 o_proj, 3 router+MLP, 4 MLP down+experts up, 5 experts down
+}
+
+__device__ __forceinline__ const OpBase* producer_op(const StepProgram& P, int l, int kind) {
+  switch (kind) {
+    case 0: return &P.k1[l];
+    case 2: return &P.k3[l];
+    case 3: return &P.k4[l];
+    case 4: return &P.k5[l];
+    case 5: return &P.k6[l];
+    default: return P.lm;
+  }
+}
+
+__device__ __forceinline__ int producer_op_bytes(int kind) {
+  switch (kind) {
+    case 0: return (int)sizeof(QkvOp);
+    case 2: return (int)sizeof(OProjOp);
+    case 3: return (int)sizeof(RouterMlpOp);
+    case 4: return (int)sizeof(MoeUpOp);
+    case 5: return (int)sizeof(MoeDownOp);
+    default: return (int)sizeof(LmHeadOp);
+  }
+}
+
+// Producer lane: bulk-copy the plan of matrix-product phase i into its slot (i & 1);
+// completion on Smem::pbar[1], phase i.
+__device__ __forceinline__ void fetch_plan(const StepProgram& P, Smem& sm, int i) {
+  int l, kind;
+  gemv_phase_of(i, P.nlayers, l, kind);
+  const uint32_t bytes = (uint32_t)producer_op_bytes(kind);
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // the slot's old plan was read
+  mbar_arrive_expect_tx(&sm.pbar[1], bytes);
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_addr(sm.popc + (i & 1) * kOpCopyBytes)),
+      "l"(producer_op(P, l, kind)), "r"(bytes), "r"(smem_addr(&sm.pbar[1]))
+      : "memory");
+}
+
 // Not inlined (its own register budget after setmaxnreg.dec); Smem by value, so the
-// consumers' copy never has its address taken.
+// consumers' copy never has its address taken.  The plan of the next operator is
+// fetched into the other shared slot while the current one streams, so the first
+// tile of an operator never waits for its plan.
 static __device__ __noinline__ void produce_step(const StepProgram& P, Smem sm, int seq) {
   const uint64_t pol = l2_evict_first_policy();
+  int* status = P.ctrl + G4_CTRL_STATUS;
   RingPos rp;
+  const int nops = 5 * P.nlayers + 1;
+  fetch_plan(P, sm, 0);
   bool ok = true;
-  const int L = P.nlayers;
-  for (int p = 0; p < 6 * L && ok; ++p) {
-    const int l = p / 6, k = p - 6 * l;
-    switch (k) {
-      case 0: ok = produce_op(P.k1[l], l, P, sm, rp, pol, seq); break;
-      case 1: break;
-      case 2: ok = produce_op(P.k3[l], l, P, sm, rp, pol, seq); break;
-      case 3: ok = produce_op(P.k4[l], l, P, sm, rp, pol, seq); break;
-      case 4: ok = produce_op(P.k5[l], l, P, sm, rp, pol, seq); break;
-      default: ok = produce_op(P.k6[l], l, P, sm, rp, pol, seq);
+  for (int i = 0; i < nops && ok; ++i) {
+    if (!mbar_wait(&sm.pbar[1], i & 1, status)) {
+      sm.ints[kSmemDead] = 1;
+      break;
+    }
+    if (i + 1 < nops) fetch_plan(P, sm, i + 1);
+    int l, kind;
+    gemv_phase_of(i, P.nlayers, l, kind);
+    const unsigned char* slot = sm.popc + (i & 1) * kOpCopyBytes;
+    const int2* rng = step_ranges(P, sm) + i * kRangeSlots;
+    switch (kind) {
+      case 0: ok = produce_op(*reinterpret_cast<const QkvOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
+      case 2: ok = produce_op(*reinterpret_cast<const OProjOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
+      case 3: ok = produce_op(*reinterpret_cast<const RouterMlpOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
+      case 4: ok = produce_op(*reinterpret_cast<const MoeUpOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
+      case 5: ok = produce_op(*reinterpret_cast<const MoeDownOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
+      default: ok = produce_op(*reinterpret_cast<const LmHeadOp*>(slot), l < P.nlayers ? l : P.nlayers - 1, P, sm, rp, pol, seq, rng); break;
     }
   }
-  if (ok) produce_op(*P.lm, L - 1, P, sm, rp, pol, seq);
   producer_exit(sm);
 }
 
@@ -285,7 +360,9 @@ static_assert(sizeof(QkvOp) <= kOpCopyBytes && sizeof(OProjOp) <= kOpCopyBytes &
                   sizeof(RouterMlpOp) <= kOpCopyBytes && sizeof(MoeUpOp) <= kOpCopyBytes &&
                   sizeof(MoeDownOp) <= kOpCopyBytes && sizeof(LmHeadOp) <= kOpCopyBytes,
               "operator plan larger than its shared-memory copy");
-static_assert(sizeof(MoeDownOp) % 8 == 0 && sizeof(QkvOp) % 8 == 0, "plans are copied in 8-byte words");
+static_assert(sizeof(QkvOp) % 16 == 0 && sizeof(OProjOp) % 16 == 0 && sizeof(RouterMlpOp) % 16 == 0 &&
+                  sizeof(MoeUpOp) % 16 == 0 && sizeof(MoeDownOp) % 16 == 0 && sizeof(LmHeadOp) % 16 == 0,
+              "plans are moved in 16-byte units");
 
 // Consumer side of one matrix-product operator up to (not including) its arrival.
 // One tile loop serves every operator (only the epilogue, a switch on the kind,
@@ -307,6 +384,11 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   bool ok = ps.live;
   if (ps.live) {
     stage_activations(ob.ac, ob.nac, sm.stg);
+    if (kind == kKindRouterMlp && threadIdx.x == 0) {
+      const int2 r0 = step_ranges(P, sm)[(l * 5 + 2) * kRangeSlots];
+      sm.ints[kSmemRouterEnd] = r0.x < r0.y ? r0.y : 0;
+      sm.ints[kSmemRouterMine] = r0.y - r0.x;
+    }
     named_bar(kBarConsumers, kConsumerThreads);
     switch (kind) {
       case kKindQkv: ok = reinterpret_cast<const QkvOp*>(sm.opc)->prologue(sm); break;
@@ -321,6 +403,8 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   }
   // The tile loop runs even when this CTA is dead: it then only advances the ring
   // position (no waits), keeping the consumer threads in step.
+  const int gi = kind == kKindLm ? 5 * P.nlayers : l * 5 + (kind == kKindQkv ? 0 : kind - 1);
+  const int2* rng = step_ranges(P, sm) + gi * kRangeSlots;
   consume_segments<CPLM>(ob, sm, ps.rp, ps.wp, P.stages, ok && ps.live, status, h,
                          [&](int s, int u0, int n, const Res& r, bool eok) {
                            switch (kind) {
@@ -331,7 +415,8 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
                              case kKindMoeDown: reinterpret_cast<const MoeDownOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
                              default: reinterpret_cast<const LmHeadOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
                            }
-                         });
+                         },
+                         rng);
   if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 5);
   if (consumers_all(ps.live)) {
     const bool fok = ok && sm.ints[kSmemDead] == 0;
@@ -381,6 +466,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     }
     sm.ints[kSmemIssued] = 0;
     sm.ints[kSmemProdExit] = 0;
+    sm.ints[kSmemRangesGiven] = 1;
     mbar_init(&sm.pbar[0], 1);
     mbar_init(&sm.pbar[1], 1);
     mbar_init_fence();
@@ -389,6 +475,12 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     // first.  BAD_TOKEN / POS_OVERFLOW leave the step's synchronisation intact.
     sm.ints[kSmemDead] = (ldcg_i(status) & kStatusTimeouts) != 0;
     sm.ints[kSmemSeq] = ldcg_i(P.sync + kSyncSeq);
+  }
+  {  // this CTA's unit ranges (host table) into shared memory, after the ring
+    const int n16 = step_range_bytes(P.nlayers) / 16;
+    const uint4* src = reinterpret_cast<const uint4*>(P.ranges) + (size_t)blockIdx.x * n16;
+    uint4* dst = reinterpret_cast<uint4*>(sm.stages + (size_t)P.stages * kStageBytes);
+    for (int i = threadIdx.x; i < n16; i += blockDim.x) dst[i] = __ldg(src + i);
   }
   __syncthreads();
   if (sm.ints[kSmemDead]) return;  // read after the barrier: identical on every thread
