@@ -60,6 +60,7 @@ struct SegDesc {
   int nsub;   // sub-rows per unit (1 plain, 2 gate/up pair, top-k for MoE down)
   int K;      // elements per sub-row (dot length), multiple of 8
   int group;  // tiles never straddle a multiple of `group` units (0 = no constraint)
+  int weight; // cost factor of a unit's bytes in the CTA partition (0 or 1: bytes)
 };
 
 // One bulk copy of the prologue: `bytes` (multiple of 16) from global `src` to the
@@ -90,6 +91,10 @@ struct alignas(16) OpBase {  // 16-byte multiple: plans are moved with bulk copi
 };
 
 __host__ __device__ __forceinline__ int seg_unit_bytes(const SegDesc& s) { return s.nsub * s.K * 2; }
+// Partition cost of one unit: its bytes times the segment's weight.
+__host__ __device__ __forceinline__ long long seg_unit_cost(const SegDesc& s) {
+  return (long long)seg_unit_bytes(s) * (s.weight > 1 ? s.weight : 1);
+}
 
 __host__ __device__ __forceinline__ int seg_max_units(const SegDesc& s) {
   int by_bytes = kStageBytes / seg_unit_bytes(s);
@@ -178,17 +183,17 @@ __device__ __forceinline__ Smem carve_smem(unsigned char* raw, SmemSizes z, int 
 }
 
 // Units of segment `s` owned by CTA `cta`: those whose first byte lies in the CTA's
-// slice of the concatenated byte space of all segments.
+// slice of the concatenated cost space of all segments (bytes x segment weight).
 __host__ __device__ __forceinline__ void cta_unit_range(const SegDesc* seg, int nseg, int s, int cta, int ncta,
                                                         int& ub, int& ue) {
   long long total = 0, cum = 0;
   for (int i = 0; i < nseg; ++i) {
-    long long b = (long long)seg[i].units * seg_unit_bytes(seg[i]);
+    long long b = (long long)seg[i].units * seg_unit_cost(seg[i]);
     if (i < s) cum += b;
     total += b;
   }
   const long long b0 = total * cta / ncta, b1 = total * (cta + 1) / ncta;
-  const long long w = seg_unit_bytes(seg[s]);
+  const long long w = seg_unit_cost(seg[s]);
   auto first_unit_at = [&](long long b) -> int {
     long long rel = b - cum;
     if (rel <= 0) return 0;

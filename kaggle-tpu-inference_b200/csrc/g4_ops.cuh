@@ -113,8 +113,57 @@ __device__ __forceinline__ float* sf(const Smem& sm, int off) {
 __device__ __forceinline__ float rms_scale(float ss, int n, float eps) {
   return 1.0f / sqrtf(ss / (float)n + eps);
 }
-// Prologue vectors of length H live in registers: thread t owns h = t + 256 j.
-constexpr int kPerThread = kMaxHidden / kConsumerThreads;
+// Prologue vectors of length H live in registers in 8-element chunks: thread t owns
+// chunks q = t + 256 j (elements 8q .. 8q+7), j < kChunks; H is a multiple of 8.
+constexpr int kChunks = kMaxHidden / 8 / kConsumerThreads;
+constexpr int kPerThread = kChunks * 8;
+typedef float Vec[kChunks][8];
+
+__device__ __forceinline__ bool chunk_live(int j, int H) {
+  return (int)(threadIdx.x + j * kConsumerThreads) * 8 < H;
+}
+__device__ __forceinline__ int chunk_of(int j) { return threadIdx.x + j * kConsumerThreads; }
+
+__device__ __forceinline__ void unpack8(const uint4 u, float* o) {
+  o[0] = bf_lo(u.x); o[1] = bf_hi(u.x); o[2] = bf_lo(u.y); o[3] = bf_hi(u.y);
+  o[4] = bf_lo(u.z); o[5] = bf_hi(u.z); o[6] = bf_lo(u.w); o[7] = bf_hi(u.w);
+}
+__device__ __forceinline__ uint4 pack8(const float* f) {
+  uint4 u;
+  u.x = (uint32_t)f2bf(f[0]) | ((uint32_t)f2bf(f[1]) << 16);
+  u.y = (uint32_t)f2bf(f[2]) | ((uint32_t)f2bf(f[3]) << 16);
+  u.z = (uint32_t)f2bf(f[4]) | ((uint32_t)f2bf(f[5]) << 16);
+  u.w = (uint32_t)f2bf(f[6]) | ((uint32_t)f2bf(f[7]) << 16);
+  return u;
+}
+// bf16 vector (shared or global, generic loads) -> chunks; dead chunks are zero
+__device__ __forceinline__ void load_bf16(const bf16_t* src, int H, Vec& o) {
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    uint4 u = make_uint4(0u, 0u, 0u, 0u);
+    if (chunk_live(j, H)) u = reinterpret_cast<const uint4*>(src)[chunk_of(j)];
+    unpack8(u, o[j]);
+  }
+}
+// fp32 vector in shared memory -> chunks
+__device__ __forceinline__ void load_f32(const float* src, int H, Vec& o) {
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j) {
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f), b = a;
+    if (chunk_live(j, H)) {
+      a = reinterpret_cast<const float4*>(src)[2 * chunk_of(j)];
+      b = reinterpret_cast<const float4*>(src)[2 * chunk_of(j) + 1];
+    }
+    o[j][0] = a.x; o[j][1] = a.y; o[j][2] = a.z; o[j][3] = a.w;
+    o[j][4] = b.x; o[j][5] = b.y; o[j][6] = b.z; o[j][7] = b.w;
+  }
+}
+// chunks (bf16 values) -> bf16 vector
+__device__ __forceinline__ void store_bf16(bf16_t* dst, int H, const Vec& v) {
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j)
+    if (chunk_live(j, H)) reinterpret_cast<uint4*>(dst)[chunk_of(j)] = pack8(v[j]);
+}
 
 // Block sum over the consumer threads with ONE barrier: warp partials go to slot
 // `slot` of Smem::red (8 slots of 8 floats; a prologue gives each reduction its own
@@ -161,87 +210,92 @@ struct Tail {
   int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, Smem& sm,
-                                             float (&x)[kPerThread]) {
-  const int H = c.H, tid = threadIdx.x;
+__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, Smem& sm, Vec& x) {
+  const int H = c.H;
   bool ok = true;
-  float a[kPerThread], b[kPerThread];
+  Vec a, b;
   float s1 = 0.f, s2 = 0.f;
   if (c.world == 1) {
-    const float* mlp = sf(sm, t.o_mlp);
-    const bf16_t* moe = sbf(sm, t.o_moe);
+    load_f32(sf(sm, t.o_mlp), H, a);
+    load_bf16(sbf(sm, t.o_moe), H, b);
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-      const int h = tid + j * kConsumerThreads;
-      a[j] = 0.f;
-      b[j] = 0.f;
-      if (h < H) {
-        a[j] = rbf(mlp[h]);
-        b[j] = bf2f(moe[h]);
-        s1 += a[j] * a[j];
-        s2 += b[j] * b[j];
-      }
-    }
+    for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[j][e] = rbf(a[j][e]);
   } else {
     const int use = site_use(ctrl, c, kSiteFfn, t.layer);
     ok = xchg_wait(ctrl, c, kSiteFfn, use, sm);
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-      const int h = tid + j * kConsumerThreads;
-      a[j] = 0.f;
-      b[j] = 0.f;
-      if (h < H) {
-        float sa = 0.f, sb = 0.f;
+    for (int j = 0; j < kChunks; ++j) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) a[j][e] = b[j][e] = 0.f;
+      if (chunk_live(j, H)) {
         for (int src = 0; src < c.world; ++src) {
           const float* sl = xslot(c, c.rank, kSiteFfn, use & 1, src);
-          sa += ldcg_f(sl + h);
-          sb += ldcg_f(sl + H + h);
+          const float4* pa = reinterpret_cast<const float4*>(sl) + 2 * chunk_of(j);
+          const float4* pb = reinterpret_cast<const float4*>(sl + H) + 2 * chunk_of(j);
+          const float4 a0 = __ldcg(pa), a1 = __ldcg(pa + 1), b0 = __ldcg(pb), b1 = __ldcg(pb + 1);
+          a[j][0] += a0.x; a[j][1] += a0.y; a[j][2] += a0.z; a[j][3] += a0.w;
+          a[j][4] += a1.x; a[j][5] += a1.y; a[j][6] += a1.z; a[j][7] += a1.w;
+          b[j][0] += b0.x; b[j][1] += b0.y; b[j][2] += b0.z; b[j][3] += b0.w;
+          b[j][4] += b1.x; b[j][5] += b1.y; b[j][6] += b1.z; b[j][7] += b1.w;
         }
-        a[j] = rbf(sa);
-        b[j] = rbf(sb);
-        s1 += a[j] * a[j];
-        s2 += b[j] * b[j];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          a[j][e] = rbf(a[j][e]);
+          b[j][e] = rbf(b[j][e]);
+        }
       }
     }
   }
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      s1 += a[j][e] * a[j][e];
+      s2 += b[j][e] * b[j][e];
+    }
   const float2 ss = bsum2(s1, s2, sm, 0);
   const float r1 = rms_scale(ss.x, H, c.eps), r2 = rms_scale(ss.y, H, c.eps);
-  const bf16_t *pf1 = sbf(sm, t.o_pf1), *pf2 = sbf(sm, t.o_pf2), *pf = sbf(sm, t.o_pf);
+  Vec w1, w2;
+  load_bf16(sbf(sm, t.o_pf1), H, w1);
+  load_bf16(sbf(sm, t.o_pf2), H, w2);
   float s3 = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
-    const int h = tid + j * kConsumerThreads;
-    if (h < H) {
-      a[j] = rbf(rbf((a[j] * r1) * bf2f(pf1[h])) + rbf((b[j] * r2) * bf2f(pf2[h])));
-      s3 += a[j] * a[j];
+  for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      a[j][e] = rbf(rbf((a[j][e] * r1) * w1[j][e]) + rbf((b[j][e] * r2) * w2[j][e]));
+      s3 += a[j][e] * a[j][e];
     }
-  }
   const float r3 = rms_scale(bsum1(s3, sm, 2), H, c.eps);
   const float sc = bf2f(t.scalar[0]);
-  const bf16_t* res = sbf(sm, t.o_res);
+  load_bf16(sbf(sm, t.o_pf), H, w1);
+  load_bf16(sbf(sm, t.o_res), H, w2);
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
-    const int h = tid + j * kConsumerThreads;
-    x[j] = 0.f;
-    if (h < H) x[j] = rbf(rbf(bf2f(res[h]) + rbf((a[j] * r3) * bf2f(pf[h]))) * sc);
-  }
+  for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) x[j][e] = rbf(rbf(w2[j][e] + rbf((a[j][e] * r3) * w1[j][e])) * sc);
   return ok;
 }
 
-// dst[h] = bf16(rms(x) * w[h]) for x in registers, bf16 weight w (smem); slot `slot`.
-__device__ __forceinline__ void norm_into(const Common& c, const float (&x)[kPerThread], const bf16_t* w,
-                                          bf16_t* dst, Smem& sm, int slot) {
-  const int H = c.H, tid = threadIdx.x;
+// dst = bf16(rms(x) * w) for x in registers, bf16 weight w (smem); slot `slot`.
+__device__ __forceinline__ void norm_into(const Common& c, const Vec& x, const bf16_t* w, bf16_t* dst,
+                                          Smem& sm, int slot) {
+  const int H = c.H;
   float s = 0.f;
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j)
-    if (tid + j * kConsumerThreads < H) s += x[j] * x[j];
-  const float r = rms_scale(bsum1(s, sm, slot), H, c.eps);
+  for (int j = 0; j < kChunks; ++j)
 #pragma unroll
-  for (int j = 0; j < kPerThread; ++j) {
-    const int h = tid + j * kConsumerThreads;
-    if (h < H) dst[h] = f2bf((x[j] * r) * bf2f(w[h]));
-  }
+    for (int e = 0; e < 8; ++e) s += x[j][e] * x[j][e];
+  const float r = rms_scale(bsum1(s, sm, slot), H, c.eps);
+  Vec wv, y;
+  load_bf16(w, H, wv);
+#pragma unroll
+  for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+    for (int e = 0; e < 8; ++e) y[j][e] = (x[j][e] * r) * wv[j][e];
+  store_bf16(dst, H, y);
 }
 
 // Copy a staged bf16 vector of n elements (n % 8 == 0) into an input vector.
@@ -274,33 +328,26 @@ struct QkvOp : OpBase {
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
-    float x[kPerThread];
-    const int H = c.H, tid = threadIdx.x;
+    Vec x;
+    const int H = c.H;
     if (c.layer == 0) {
       int pos = ldcg_i(ctrl + G4_CTRL_POS);
       if (pos < 0 || pos >= max_len) pos = 0;  // flagged by the attention / lm_head kernels
       const int forced = ldcg_i(ctrl + G4_CTRL_FORCED_LEN);
       int tok = pos < forced ? ldcg_i(tokens_in + pos) : ldcg_i(tokens_out + pos);
       if (tok < 0 || tok >= vocab) {
-        if (tid == 0 && blockIdx.x == 0) atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_BAD_TOKEN);
+        if (threadIdx.x == 0 && blockIdx.x == 0) atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_BAD_TOKEN);
         tok = 0;
       }
-      const bf16_t* row = embed + (size_t)tok * H;
+      load_bf16(embed + (size_t)tok * H, H, x);
 #pragma unroll
-      for (int j = 0; j < kPerThread; ++j) {
-        const int h = tid + j * kConsumerThreads;
-        x[j] = h < H ? rbf(bf2f(row[h]) * embed_scale) : 0.f;
-      }
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) x[j][e] = rbf(x[j][e] * embed_scale);
     } else {
       ok = layer_output(ctrl, c, tail, sm, x);
     }
-    if (blockIdx.x == 0) {
-#pragma unroll
-      for (int j = 0; j < kPerThread; ++j) {
-        const int h = tid + j * kConsumerThreads;
-        if (h < H) xres[h] = f2bf(x[j]);
-      }
-    }
+    if (blockIdx.x == 0) store_bf16(xres, H, x);
     norm_into(c, x, sbf(sm, o_win), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     return ok;
   }
@@ -381,88 +428,85 @@ struct RouterMlpOp : OpBase {
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
     const int H = c.H, tid = threadIdx.x;
-    float hv[kPerThread];  // MoE input (model.py:315); the router input derives from it
+    Vec hv;  // MoE input (model.py:315); the router input derives from it
     if (!block_mode) {
       // attention output (summed over ranks), then x = residual + rms(attn)*post_attn
-      float t[kPerThread];
-      float s = 0.f;
+      Vec t;
       if (c.world == 1) {
-        const float* o = sf(sm, o_o);
-#pragma unroll
-        for (int j = 0; j < kPerThread; ++j) {
-          const int h = tid + j * kConsumerThreads;
-          t[j] = 0.f;
-          if (h < H) {
-            t[j] = rbf(o[h]);
-            s += t[j] * t[j];
-          }
-        }
+        load_f32(sf(sm, o_o), H, t);
       } else {
         const int use = site_use(ctrl, c, kSiteAttn, c.layer);
         ok = xchg_wait(ctrl, c, kSiteAttn, use, sm) && ok;
 #pragma unroll
-        for (int j = 0; j < kPerThread; ++j) {
-          const int h = tid + j * kConsumerThreads;
-          t[j] = 0.f;
-          if (h < H) {
-            float a = 0.f;
-            for (int src = 0; src < c.world; ++src) a += ldcg_f(xslot(c, c.rank, kSiteAttn, use & 1, src) + h);
-            t[j] = rbf(a);
-            s += t[j] * t[j];
-          }
+        for (int j = 0; j < kChunks; ++j) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) t[j][e] = 0.f;
+          if (chunk_live(j, H))
+            for (int src = 0; src < c.world; ++src) {
+              const float4* p = reinterpret_cast<const float4*>(xslot(c, c.rank, kSiteAttn, use & 1, src)) + 2 * chunk_of(j);
+              const float4 a0 = __ldcg(p), a1 = __ldcg(p + 1);
+              t[j][0] += a0.x; t[j][1] += a0.y; t[j][2] += a0.z; t[j][3] += a0.w;
+              t[j][4] += a1.x; t[j][5] += a1.y; t[j][6] += a1.z; t[j][7] += a1.w;
+            }
         }
       }
+      float s = 0.f;
+#pragma unroll
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          t[j][e] = rbf(t[j][e]);
+          s += t[j][e] * t[j][e];
+        }
       const float r = rms_scale(bsum1(s, sm, 0), H, c.eps);
-      const bf16_t* wpa = sbf(sm, o_wpa);
-      const bf16_t* xin = sbf(sm, o_x);
+      Vec w, xin;
+      load_bf16(sbf(sm, o_wpa), H, w);
+      load_bf16(sbf(sm, o_x), H, xin);
       float s2 = 0.f;
 #pragma unroll
-      for (int j = 0; j < kPerThread; ++j) {
-        const int h = tid + j * kConsumerThreads;
-        if (h < H) {
-          t[j] = rbf(bf2f(xin[h]) + rbf((t[j] * r) * bf2f(wpa[h])));  // model.py:303-304
-          s2 += t[j] * t[j];
-          if (blockIdx.x == 0) resmid[h] = f2bf(t[j]);
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          t[j][e] = rbf(xin[j][e] + rbf((t[j][e] * r) * w[j][e]));  // model.py:303-304
+          s2 += t[j][e] * t[j][e];
         }
-      }
+      if (blockIdx.x == 0) store_bf16(resmid, H, t);
       // MLP input (model.py:310) and MoE input (model.py:315)
       const float r2 = rms_scale(bsum1(s2, sm, 1), H, c.eps);
-      const bf16_t *wff = sbf(sm, o_wff), *wff2 = sbf(sm, o_wff2);
-      bf16_t* xm = reinterpret_cast<bf16_t*>(sm.x1);
+      Vec w2, xm;
+      load_bf16(sbf(sm, o_wff), H, w);
+      load_bf16(sbf(sm, o_wff2), H, w2);
 #pragma unroll
-      for (int j = 0; j < kPerThread; ++j) {
-        const int h = tid + j * kConsumerThreads;
-        hv[j] = 0.f;
-        if (h < H) {
-          xm[h] = f2bf((t[j] * r2) * bf2f(wff[h]));
-          hv[j] = rbf((t[j] * r2) * bf2f(wff2[h]));
-          if (blockIdx.x == 0) h2[h] = f2bf(hv[j]);
+      for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          xm[j][e] = (t[j][e] * r2) * w[j][e];
+          hv[j][e] = rbf((t[j][e] * r2) * w2[j][e]);
         }
-      }
+      store_bf16(reinterpret_cast<bf16_t*>(sm.x1), H, xm);
     } else {
 #pragma unroll
-      for (int j = 0; j < kPerThread; ++j) {
-        const int h = tid + j * kConsumerThreads;
-        hv[j] = 0.f;
-        if (h < H) {
-          hv[j] = bf2f(ldcg_bf(block_x + h));
-          if (blockIdx.x == 0) h2[h] = f2bf(hv[j]);
-        }
+      for (int j = 0; j < kChunks; ++j) {
+        uint4 u = make_uint4(0u, 0u, 0u, 0u);
+        if (chunk_live(j, H)) u = __ldcg(reinterpret_cast<const uint4*>(block_x) + chunk_of(j));
+        unpack8(u, hv[j]);
       }
     }
+    if (blockIdx.x == 0) store_bf16(h2, H, hv);
     // router input: rms(h2) * scale * H^-1/2                 (model.py:225-226)
     float s3 = 0.f;
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j)
-      if (tid + j * kConsumerThreads < H) s3 += hv[j] * hv[j];
-    const float r3 = rms_scale(bsum1(s3, sm, 2), H, c.eps);
-    const bf16_t* wrs = sbf(sm, o_wrs);
-    bf16_t* xr = reinterpret_cast<bf16_t*>(sm.x0);
+    for (int j = 0; j < kChunks; ++j)
 #pragma unroll
-    for (int j = 0; j < kPerThread; ++j) {
-      const int h = tid + j * kConsumerThreads;
-      if (h < H) xr[h] = f2bf(rbf(rbf(hv[j] * r3) * bf2f(wrs[h])) * hinv);
-    }
+      for (int e = 0; e < 8; ++e) s3 += hv[j][e] * hv[j][e];
+    const float r3 = rms_scale(bsum1(s3, sm, 2), H, c.eps);
+    Vec ws, xr;
+    load_bf16(sbf(sm, o_wrs), H, ws);
+#pragma unroll
+    for (int j = 0; j < kChunks; ++j)
+#pragma unroll
+      for (int e = 0; e < 8; ++e) xr[j][e] = rbf(rbf(hv[j][e] * r3) * ws[j][e]) * hinv;
+    store_bf16(reinterpret_cast<bf16_t*>(sm.x0), H, xr);
     if (tid == 0 && !sm.ints[kSmemRangesGiven]) {  // else the step kernel set them
       int ub, ue;
       cta_unit_range(seg, nseg, 0, blockIdx.x, gridDim.x, ub, ue);
@@ -696,7 +740,7 @@ struct LmHeadOp : OpBase {
     bulk_g2s(stage, embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), bar, pol);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
-    float x[kPerThread];
+    Vec x;
     const bool ok = layer_output(ctrl, c, tail, sm, x);
     norm_into(c, x, sbf(sm, o_wn), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     float* bv = reinterpret_cast<float*>(sm.x1);

@@ -879,7 +879,9 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.ctrl = m->ctrl;
     r.nseg = 2;
     r.trace_id = i * 8 + 3;
-    r.seg[0] = SegDesc{m->E, 1, H, 0};
+    // router rows weigh 3x in the partition: the CTA that completes them also runs
+    // the top-k selection, so the router CTAs take fewer MLP rows
+    r.seg[0] = SegDesc{m->E, 1, H, 0, 3};
     r.seg[1] = SegDesc{m->I_local, 2, H, 0};
     r.xsel[1] = 1;  // router rows: x0 (router input); MLP gate|up: x1 (MLP input)
     r.xbytes[0] = H * 2;
@@ -1367,6 +1369,8 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   if (!valid_cfg(cfg) || !x || !router_proj || !router_scale || !per_expert_scale || !gate_up ||
       !down || !out || !control)
     return fail(G4_ERR_ARG, "g4_moe_block: null argument");
+  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+    return fail(G4_ERR_ARG, "g4_moe_block: x and out must be 16-byte aligned");
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
     return fail(G4_ERR_ARG, "g4_moe_block: bad rank/world");
   if (world > 1 && (!comm || !comm->open || comm->world != world || comm->rank != rank))

@@ -295,23 +295,29 @@ struct PhaseState {
   RingPos rp, wp;     // ring position (all tiles) / tiles seen complete
 };
 
-// Start of operator ps.phase: wait for every CTA to finish the previous operator,
-// then for this operator's constants.
+// Start of operator ps.phase: wait for every CTA to finish the previous operator (the
+// operator's constants are waited for later, by wait_constants, just before use).
 __device__ __forceinline__ void phase_begin(const StepProgram& P, Smem& sm, PhaseState& ps, int trace_id) {
   int* status = P.ctrl + G4_CTRL_STATUS;
   bool ok = sm.ints[kSmemDead] == 0;
   if (threadIdx.x == 0 && ok) {
-    if (ps.phase > 0) {
+    if (ps.phase > 0) {  // acquire: the other CTAs' outputs of the previous operator
       const int target = ps.phase * (int)gridDim.x;
       ok = spin_until(P.sync + kSyncBarrier, [target](int v) { return v >= target; }, status,
                       ldcg_i(P.ctrl + G4_CTRL_TIMEOUT_US));
-      __threadfence();
     }
-    if (ok) ok = mbar_wait(&sm.pbar[0], ps.phase & 1, status);
     if (!ok) sm.ints[kSmemDead] = 1;
     G4_TRACE_EV(trace_id, 0);
   }
   ps.live = consumers_all(ok && sm.ints[kSmemDead] == 0);
+}
+
+// This operator's constant copies (issued at the end of the previous operator) have
+// landed; thread 0 waits, the caller's next barrier publishes the result.
+__device__ __forceinline__ void wait_constants(const StepProgram& P, Smem& sm, PhaseState& ps) {
+  if (threadIdx.x == 0 && sm.ints[kSmemDead] == 0 &&
+      !mbar_wait(&sm.pbar[0], ps.phase & 1, P.ctrl + G4_CTRL_STATUS))
+    sm.ints[kSmemDead] = 1;
 }
 
 // End of operator ps.phase: all of this CTA's stores done -> issue the next
@@ -323,7 +329,8 @@ __device__ __forceinline__ void phase_end(const StepProgram& P, Smem& sm, PhaseS
     asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads -> async writes
     if (next) issue_copies(next->cc, next->ncc, sm.stg, &sm.pbar[0]);
     else issue_copies(nullptr, 0, sm.stg, &sm.pbar[0]);
-    __threadfence();
+    // release: this CTA's stores (ordered before by the barrier above) become
+    // visible before the arrival
     red_release_gpu_add(P.sync + kSyncBarrier, 1);
   }
   ++ps.phase;
@@ -384,6 +391,7 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   bool ok = ps.live;
   if (ps.live) {
     stage_activations(ob.ac, ob.nac, sm.stg);
+    wait_constants(P, sm, ps);
     if (kind == kKindRouterMlp && threadIdx.x == 0) {
       const int2 r0 = step_ranges(P, sm)[(l * 5 + 2) * kRangeSlots];
       sm.ints[kSmemRouterEnd] = r0.x < r0.y ? r0.y : 0;
@@ -504,6 +512,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     const int l = p / 6, k = p == 6 * L ? kKindLm : p - 6 * l;
     if (k == kKindAttn) {
       phase_begin(P, sm, ps, P.k2[l].trace_id);
+      wait_constants(P, sm, ps);  // an empty list: completes at once (keeps the parity)
       if (ps.live) {  // the auxiliary area is free during attention
         const AttnArgs& a = P.k2[l];
         if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0);
