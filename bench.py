@@ -335,7 +335,7 @@ def main() -> int:
     total_ms = sum(prof.values())
     peak, peak_kind = peaks()
     op_kernels = {"ms_per_step": total_ms / args.profile_steps,
-                  "share": {k: v / total_ms for k, v in prof.items()}}
+                  "share": {k: v / total_ms for k, v in prof.items()}} if total_ms > 0 else None
     sb = step_bytes(cfg, pos_avg)
     if args.engine == "step":
         # one persistent kernel per token: bytes per launch = this rank's step bytes

@@ -236,15 +236,14 @@ __device__ __forceinline__ bool wait_flag_geq(const int* flag, int target, int t
 
 // ------------------------------------------------------------------ timeline tracing
 // Built only with -DG4_TRACE (libg4b200_trace.so): %globaltimer stamps of selected
-// events for four sample CTAs (first, second, middle, last) of every launch whose
-// trace id is in [0, kTraceLaunches); read back with g4_trace_read.
-constexpr int kTraceLaunches = 512, kTraceCtas = 4, kTraceEvents = 8;
+// events for the first kTraceCtas CTAs of every launch whose trace id is in
+// [0, kTraceLaunches); read back with g4_trace_read.
+constexpr int kTraceLaunches = 512, kTraceCtas = 160, kTraceEvents = 8;
 #ifdef G4_TRACE
 // one buffer per device module (each translation unit of the library is its own module)
 static __device__ unsigned long long g4_trace_buf[kTraceLaunches][kTraceCtas][kTraceEvents];
 __device__ __forceinline__ int trace_cta_slot() {
-  const int b = blockIdx.x, n = gridDim.x;
-  return b == 0 ? 0 : (b == 1 ? 1 : (b == n / 2 ? 2 : (b == n - 1 ? 3 : -1)));
+  return (int)blockIdx.x < kTraceCtas ? (int)blockIdx.x : -1;
 }
 #define G4_TRACE_EV(id, ev)                                                         \
   do {                                                                              \

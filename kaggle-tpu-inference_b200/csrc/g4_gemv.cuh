@@ -49,6 +49,7 @@ constexpr int kBarConsumers = 1;  // named barrier id used by the consumer warps
 constexpr int kMaxSmemBytes = 232448;  // 227 KB opt-in shared memory per CTA
 constexpr int kOpCopyBytes = 640;      // shared copy of the current operator (step kernel)
 // Smem::ints slots used by the engine (operators use 0..39)
+constexpr int kSmemExp = 0;        // [0,16) expert ids (producer copy)
 constexpr int kSmemSeq = 40;      // launch sequence number (persistent step kernel)
 constexpr int kSmemIssued = 41;   // tiles issued by the producer lane so far
 constexpr int kSmemProdExit = 42; // producer lane has issued its last copy
@@ -274,7 +275,11 @@ __device__ __forceinline__ bool produce_tile(const Op& op, int s, int u0, int n,
     }
   }
   mbar_arrive_expect_tx(&sm.full[rp.st], (uint32_t)(n * seg_unit_bytes(op.seg[s])));
-  op.issue(s, u0, n, sm.stages + (size_t)rp.st * kStageBytes, &sm.full[rp.st], pol, sm);
+  unsigned char* stage = sm.stages + (size_t)rp.st * kStageBytes;
+  uint64_t* bar = &sm.full[rp.st];
+  op.copies(s, u0, n, sm.ints + kSmemExp, [&](const void* src, uint32_t bytes, uint32_t off) {
+    bulk_g2s(stage + off, src, bytes, bar, pol);
+  });
   rp.next(stages);
   reinterpret_cast<volatile int*>(sm.ints)[kSmemIssued] = rp.tiles;
   return true;
@@ -359,6 +364,53 @@ struct XRegs {
     }
     return warp_sum(a0 + a1);
   }
+  // Four rows at once (row k at w + k * stride chunks), for short rows: the loads and
+  // accumulators of all four are in flight together, and one transposing reduction
+  // (6 shuffles instead of 4 x 5) leaves row k's sum on lane 8 k.
+  template <int NC, bool FULL>
+  __device__ __forceinline__ float dot_rows4_n(const uint4* w, int stride, int C) const {
+    const int lane = threadIdx.x & 31;
+    float a[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < NC; ++i) {
+      const int c = lane + 32 * i;
+      if (FULL || i < NC - 1 || c < C) {
+        uint4 wk[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) wk[k] = w[k * stride + c];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) a[k] = dot8p(wk[k], v[i], a[k]);
+      }
+    }
+    const bool hi16 = (lane & 16) != 0, hi8 = (lane & 8) != 0;
+    float k0 = hi16 ? a[2] : a[0], k1 = hi16 ? a[3] : a[1];
+    const float s0 = hi16 ? a[0] : a[2], s1 = hi16 ? a[1] : a[3];
+    k0 += __shfl_xor_sync(0xffffffffu, s0, 16);
+    k1 += __shfl_xor_sync(0xffffffffu, s1, 16);
+    float kk = hi8 ? k1 : k0;
+    kk += __shfl_xor_sync(0xffffffffu, hi8 ? k0 : k1, 8);
+#pragma unroll
+    for (int o = 4; o > 0; o >>= 1) kk += __shfl_xor_sync(0xffffffffu, kk, o);
+    return kk;  // lane 8 k: row k (k = 2 * bit4 + bit3 of the lane)
+  }
+  // Rows of at most 4 x 32 chunks: dispatch on the trip count (0.f for longer rows).
+  __device__ __forceinline__ float dot_rows4(const uint4* w, int stride, int C) const {
+    const int nc = (C + 31) >> 5;
+    const bool full = (C & 31) == 0;
+    switch (nc) {
+#define G4_DOT4_CASE(N)                                                                   \
+  case N:                                                                                 \
+    if (N <= CPLM) {                                                                      \
+      constexpr int M = N <= CPLM ? N : 1;                                                \
+      return full ? dot_rows4_n<M, true>(w, stride, C) : dot_rows4_n<M, false>(w, stride, C); \
+    }                                                                                     \
+    break;
+      G4_DOT4_CASE(1) G4_DOT4_CASE(2) G4_DOT4_CASE(3) G4_DOT4_CASE(4)
+#undef G4_DOT4_CASE
+      default: break;
+    }
+    return 0.f;
+  }
   // C chunks (C <= 32 CPLM): dispatch on the trip count.
   __device__ __forceinline__ float dot_row(const uint4* w, int C) const {
     const int nc = (C + 31) >> 5;
@@ -388,7 +440,8 @@ __host__ __device__ __forceinline__ int seg_cpl(const SegDesc& s) { return ((s.K
 // one vector for every sub-row (xsub == 0) row r goes to warp kConsumerWarps-1-r (mod
 // the warp count): with fewer rows than warps, warp 0 -- whose thread 0 also waits at
 // the grid barriers of the step kernel -- has no row.  After each tile's barrier,
-// epi(s, u0, n, res, ok) runs on every consumer thread (the operator's epilogue).
+// epi(s, u0, n, res, ok, t) runs on every consumer thread (the operator's epilogue; t is
+// the thread's row index in it, >= n on threads without a row).
 // Every consumer thread executes the same sequence of named barriers whatever happens,
 // so a timed-out wait (which marks the CTA dead) can never strand a warp at a barrier:
 // after it, the remaining tiles are skipped without waiting.
@@ -462,7 +515,15 @@ __device__ __forceinline__ void consume_segments(const OpBase& ob, Smem& sm, Rin
           }
         } else {
           const int step = kConsumerWarps / sd.nsub;
-          for (int uu = warp / sd.nsub; uu < n; uu += step) {  // warp-uniform
+          int uu = warp / sd.nsub;
+          if (step == 1 && C <= 128) {  // short rows, consecutive for this warp: 4 at a time
+            for (; uu + 3 < n; uu += 4) {  // warp-uniform
+              const int r = sub * n + uu;
+              const float v = xr.dot_rows4(reinterpret_cast<const uint4*>(stage + (size_t)r * rowbytes), C, C);
+              if ((lane & 7) == 0) res[r + (lane >> 3)] = v;
+            }
+          }
+          for (; uu < n; uu += step) {  // warp-uniform
             const int r = sub * n + uu;
             const float v = xr.dot_row(reinterpret_cast<const uint4*>(stage + (size_t)r * rowbytes), C);
             if (lane == 0) res[r] = v;
@@ -473,7 +534,15 @@ __device__ __forceinline__ void consume_segments(const OpBase& ob, Smem& sm, Rin
       if (lane == 0 && live) h.release(sm, st);
       named_bar(kBarConsumers, kConsumerThreads);
       h.after_bar(rp);
-      epi(s, u, n, Res{res}, ok && (*dead == 0));
+      // epilogue row index of this thread: tiles of at most 32 units run their per-unit
+      // work on one warp -- warp 0 when some warps had no row, else a warp that rotates
+      // with the tile, so that no warp adds the epilogue to its dot products every tile
+      int et = threadIdx.x;
+      if (n <= 32) {
+        const int ew = n * sd.nsub < kConsumerWarps ? 0 : (rp.tiles & (kConsumerWarps - 1));
+        et = warp == ew ? lane : kConsumerThreads;
+      }
+      epi(s, u, n, Res{res}, ok && (*dead == 0), et);
       u += n;
       rp.next(stages);
     }
@@ -563,7 +632,7 @@ __global__ void __launch_bounds__(kGemvThreads, 1) gemv_kernel(const __grid_cons
   RingPos rp, wp;
   EmptyBarrierHooks hooks;
   consume_segments<CPLM>(op, sm, rp, wp, kStages, ok, status, hooks,
-                         [&](int s, int u0, int n, const Res& r, bool eok) { op.epilogue(s, u0, n, r, sm, eok); });
+                         [&](int s, int u0, int n, const Res& r, bool eok, int t) { op.epilogue(s, u0, n, r, sm, eok, t); });
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 5);
   op.finish(sm, ok && (sm.ints[kSmemDead] == 0));
   if (threadIdx.x == 0) G4_TRACE_EV(op.trace_id, 6);

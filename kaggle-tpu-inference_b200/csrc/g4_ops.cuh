@@ -40,7 +40,6 @@ constexpr int kSites = 3;          // exchange sites: attention out, FFN out, ar
 constexpr int kSiteAttn = 0, kSiteFfn = 1, kSiteArgmax = 2;
 constexpr int kXFlagBytes = kSites * 2 * kMaxWorld * 128;
 // Smem::ints slots
-constexpr int kSmemExp = 0;        // [0,16) expert ids (producer copy)
 constexpr int kSmemRouterEnd = 32;  // end of this CTA's router units (0: none)
 constexpr int kSmemRouterMine = 36; // number of this CTA's router units
 constexpr int kSmemLast = 33;
@@ -322,9 +321,9 @@ struct QkvOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int) const { return false; }
   __device__ __forceinline__ void load_dependent(Smem&) const {}
-  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem&) const {
-    bulk_g2s(stage, w + (size_t)u0 * c.H, (uint32_t)(n * c.H * 2), bar, pol);
+  template <class Fn>
+  __device__ __forceinline__ void copies(int, int u0, int n, const int*, Fn&& f) const {
+    f(w + (size_t)u0 * c.H, (uint32_t)(n * c.H * 2), 0u);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     bool ok = true;
@@ -351,8 +350,8 @@ struct QkvOp : OpBase {
     norm_into(c, x, sbf(sm, o_win), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     return ok;
   }
-  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
-    if (ok && (int)threadIdx.x < n) out[u0 + threadIdx.x] = f2bf(res[threadIdx.x]);
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok, int t) const {
+    if (ok && t < n) out[u0 + t] = f2bf(res[t]);
   }
   __device__ __forceinline__ void finish(Smem&, bool) const {}
 };
@@ -367,18 +366,18 @@ struct OProjOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int) const { return false; }
   __device__ __forceinline__ void load_dependent(Smem&) const {}
-  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem&) const {
-    bulk_g2s(stage, w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), bar, pol);
+  template <class Fn>
+  __device__ __forceinline__ void copies(int, int u0, int n, const int*, Fn&& f) const {
+    f(w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), 0u);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     copy_vec(sbf(sm, o_ctx), Kc, sm.x0);
     return true;
   }
-  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
-    if (!ok || (int)threadIdx.x >= n) return;
-    const int u = u0 + threadIdx.x;
-    const float v = res[threadIdx.x];
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok, int t) const {
+    if (!ok || t >= n) return;
+    const int u = u0 + t;
+    const float v = res[t];
     if (c.world == 1) {
       out[u] = v;
     } else {
@@ -415,14 +414,14 @@ struct RouterMlpOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int) const { return false; }
   __device__ __forceinline__ void load_dependent(Smem&) const {}
-  __device__ __forceinline__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem&) const {
+  template <class Fn>
+  __device__ __forceinline__ void copies(int s, int u0, int n, const int*, Fn&& f) const {
     const uint32_t bytes = (uint32_t)(n * c.H * 2);
     if (s == 0) {
-      bulk_g2s(stage, router_w + (size_t)u0 * c.H, bytes, bar, pol);
+      f(router_w + (size_t)u0 * c.H, bytes, 0u);
     } else {
-      bulk_g2s(stage, gate + (size_t)u0 * c.H, bytes, bar, pol);
-      bulk_g2s(stage + bytes, up + (size_t)u0 * c.H, bytes, bar, pol);
+      f(gate + (size_t)u0 * c.H, bytes, 0u);
+      f(up + (size_t)u0 * c.H, bytes, bytes);
     }
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
@@ -515,8 +514,7 @@ struct RouterMlpOp : OpBase {
     }
     return ok;
   }
-  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
-    const int t = threadIdx.x;
+  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok, int t) const {
     if (s == 0) {
       if (ok && t < n) router_logits[u0 + t] = rbf(res[t]);
       // right after this CTA's last router tile (identical test on every thread):
@@ -635,16 +633,16 @@ struct MoeUpOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int s) const { return s == 1; }
   __device__ __forceinline__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
-  __device__ __forceinline__ void issue(int s, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem& sm) const {
+  template <class Fn>
+  __device__ __forceinline__ void copies(int s, int u0, int n, const int* ids, Fn&& f) const {
     if (s == 0) {
-      bulk_g2s(stage, mlp_down + (size_t)u0 * I, (uint32_t)(n * I * 2), bar, pol);
+      f(mlp_down + (size_t)u0 * I, (uint32_t)(n * I * 2), 0u);
     } else {
       const int k = u0 / F, f0 = u0 % F;
-      const size_t e = (size_t)sm.ints[kSmemExp + k];
+      const size_t e = (size_t)ids[k];
       const uint32_t bytes = (uint32_t)(n * c.H * 2);
-      bulk_g2s(stage, gate_up + ((e * 2 + 0) * F + f0) * c.H, bytes, bar, pol);
-      bulk_g2s(stage + bytes, gate_up + ((e * 2 + 1) * F + f0) * c.H, bytes, bar, pol);
+      f(gate_up + ((e * 2 + 0) * F + f0) * c.H, bytes, 0u);
+      f(gate_up + ((e * 2 + 1) * F + f0) * c.H, bytes, bytes);
     }
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
@@ -653,8 +651,7 @@ struct MoeUpOp : OpBase {
     if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
     return true;
   }
-  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok) const {
-    const int t = threadIdx.x;
+  __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok, int t) const {
     if (!ok || t >= n) return;
     if (s == 0) {
       mlp_out[u0 + t] = res[t];
@@ -680,20 +677,19 @@ struct MoeDownOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int) const { return true; }
   __device__ __forceinline__ void load_dependent(Smem& sm) const { load_expert_ids(top_idx, topk, sm); }
-  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem& sm) const {
+  template <class Fn>
+  __device__ __forceinline__ void copies(int, int u0, int n, const int* ids, Fn&& f) const {
     const uint32_t bytes = (uint32_t)(n * F * 2);
     for (int k = 0; k < topk; ++k) {
-      const size_t e = (size_t)sm.ints[kSmemExp + k];
-      bulk_g2s(stage + (size_t)k * bytes, down + (e * c.H + u0) * F, bytes, bar, pol);
+      const size_t e = (size_t)ids[k];
+      f(down + (e * c.H + u0) * F, bytes, (uint32_t)k * bytes);
     }
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     copy_vec(sbf(sm, o_act), topk * F, sm.x0);
     return true;
   }
-  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok) const {
-    const int t = threadIdx.x;
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok, int t) const {
     if (!ok || t >= n) return;
     const int u = u0 + t;
     if (c.world == 1) {
@@ -735,9 +731,9 @@ struct LmHeadOp : OpBase {
 
   __device__ __forceinline__ bool seg_dependent(int) const { return false; }
   __device__ __forceinline__ void load_dependent(Smem&) const {}
-  __device__ __forceinline__ void issue(int, int u0, int n, unsigned char* stage, uint64_t* bar, uint64_t pol,
-                        const Smem&) const {
-    bulk_g2s(stage, embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), bar, pol);
+  template <class Fn>
+  __device__ __forceinline__ void copies(int, int u0, int n, const int*, Fn&& f) const {
+    f(embed + (size_t)(vbegin + u0) * c.H, (uint32_t)(n * c.H * 2), 0u);
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     Vec x;
@@ -751,8 +747,7 @@ struct LmHeadOp : OpBase {
     named_bar(kBarReduce, kConsumerThreads);
     return ok;
   }
-  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem& sm, bool ok) const {
-    const int t = threadIdx.x;
+  __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem& sm, bool ok, int t) const {
     if (!ok || t >= n) return;
     const int u = u0 + t;
     float v = rbf(res[t]);  // einsum output is bf16 (model.py:381-382)

@@ -13,6 +13,7 @@
 #include <cmath>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <map>
 #include <mutex>
@@ -1068,42 +1069,67 @@ extern "C" int g4_model_profile(g4_model* m, void* stream, int steps, float* ms_
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_model_profile before finalize");
   G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  int rc = prepare_all(m);
+  if (rc) return rc;
+  // One step of per-operator launches with an event after each, captured into a graph
+  // (on a private stream: the caller's may be the legacy default stream) and replayed:
+  // the class times are device time between the events, with no host launch gaps.
   const int nl = (int)m->L.size();
   const int per_step = 6 * nl + 1;
-  std::vector<cudaEvent_t> ev((size_t)per_step * steps + 1);
+  std::vector<cudaEvent_t> ev((size_t)per_step + 1);
   for (auto& e : ev) G4_CUDA(cudaEventCreate(&e), G4_ERR_CUDA);
-  int rc = G4_OK;
-  size_t k = 0;
-  G4_CUDA(cudaEventRecord(ev[k++], st), G4_ERR_CUDA);
-  for (int s = 0; s < steps && !rc; ++s) {
+  cudaStream_t cap = nullptr;
+  cudaGraph_t g = nullptr;
+  cudaGraphExec_t gx = nullptr;
+  if (cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking) != cudaSuccess) {
+    rc = fail(G4_ERR_CUDA, "g4_model_profile: stream create failed");
+  } else if (cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal) != cudaSuccess) {
+    rc = fail(G4_ERR_LAUNCH, "g4_model_profile: begin capture failed");
+  } else {
+    // an event record node (a plain record inside a capture only orders streams)
+    auto mark = [cap](cudaEvent_t e) { cudaEventRecordWithFlags(e, cap, cudaEventRecordExternal); };
+    size_t k = 0;
+    mark(ev[k++]);
     for (int i = 0; i < nl && !rc; ++i) {
-      if (!rc) rc = launch_gemv(m->k1[i], m->nsm, st);
-      cudaEventRecord(ev[k++], st);
-      if (!rc) rc = launch_attention(m->k2[i], st);
-      cudaEventRecord(ev[k++], st);
-      if (!rc) rc = launch_gemv(m->k3[i], m->nsm, st);
-      cudaEventRecord(ev[k++], st);
-      if (!rc) rc = launch_gemv(m->k4[i], m->nsm, st);
-      cudaEventRecord(ev[k++], st);
-      if (!rc) rc = launch_gemv(m->k5[i], m->nsm, st);
-      cudaEventRecord(ev[k++], st);
-      if (!rc) rc = launch_gemv(m->k6[i], m->nsm, st);
-      cudaEventRecord(ev[k++], st);
+      if (!rc) rc = launch_gemv(m->k1[i], m->nsm, cap);
+      mark(ev[k++]);
+      if (!rc) rc = launch_attention(m->k2[i], cap);
+      mark(ev[k++]);
+      if (!rc) rc = launch_gemv(m->k3[i], m->nsm, cap);
+      mark(ev[k++]);
+      if (!rc) rc = launch_gemv(m->k4[i], m->nsm, cap);
+      mark(ev[k++]);
+      if (!rc) rc = launch_gemv(m->k5[i], m->nsm, cap);
+      mark(ev[k++]);
+      if (!rc) rc = launch_gemv(m->k6[i], m->nsm, cap);
+      mark(ev[k++]);
     }
-    if (!rc) rc = launch_gemv(m->lm, m->nsm, st);
-    cudaEventRecord(ev[k++], st);
+    if (!rc) rc = launch_gemv(m->lm, m->nsm, cap);
+    mark(ev[k++]);
+    const cudaError_t e = cudaStreamEndCapture(cap, &g);
+    if (!rc && e != cudaSuccess) rc = fail(G4_ERR_LAUNCH, "g4_model_profile: capture: %s", cudaGetErrorString(e));
+    if (!rc && cudaGraphInstantiate(&gx, g, 0) != cudaSuccess)
+      rc = fail(G4_ERR_LAUNCH, "g4_model_profile: graph instantiate failed");
   }
-  cudaStreamSynchronize(st);
   for (int c = 0; c < nclass; ++c) ms_out[c] = 0.f;
-  if (!rc) {
-    for (size_t j = 1; j < k; ++j) {
+  for (int s = 0; s < steps && !rc; ++s) {
+    if (cudaGraphLaunch(gx, st) != cudaSuccess || cudaStreamSynchronize(st) != cudaSuccess) {
+      rc = fail(G4_ERR_LAUNCH, "g4_model_profile: replay failed");
+      break;
+    }
+    for (int j = 1; j <= per_step; ++j) {
       float ms = 0.f;
-      cudaEventElapsedTime(&ms, ev[j - 1], ev[j]);
-      const size_t in_step = (j - 1) % per_step;
-      const int cls = in_step == (size_t)per_step - 1 ? 6 : (int)(in_step % 6);
-      ms_out[cls] += ms;
+      if (cudaEventElapsedTime(&ms, ev[j - 1], ev[j]) != cudaSuccess) {
+        rc = fail(G4_ERR_CUDA, "g4_model_profile: event timing unavailable");
+        break;
+      }
+      const int in_step = j - 1;
+      ms_out[in_step == per_step - 1 ? 6 : in_step % 6] += ms;
     }
   }
+  if (gx) cudaGraphExecDestroy(gx);
+  if (g) cudaGraphDestroy(g);
+  if (cap) cudaStreamDestroy(cap);
   for (auto& e : ev) cudaEventDestroy(e);
   return rc;
 }

@@ -173,6 +173,19 @@ __device__ __forceinline__ const int2* step_ranges(const StepProgram& P, const S
   return reinterpret_cast<const int2*>(sm.stages + (size_t)P.stages * kStageBytes);
 }
 
+// The program's matrix-product phases in order (attention phases carry no tiles):
+// index i -> (layer, kind).
+__device__ __forceinline__ void gemv_phase_of(int i, int nlayers, int& l, int& kind) {
+  if (i == 5 * nlayers) {
+    l = nlayers;
+    kind = 6;  // LM head
+    return;
+  }
+  l = i / 5;
+  const int r = i - 5 * l;
+  kind = r == 0 ? 0 : r + 1;  // 0 qkv, 2 o_proj, 3 router+MLP, 4 MLP down+experts up, 5 experts down
+}
+
 // Producer lane: every weight tile of one operator owned by this CTA.
 template <class Op>
 __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepProgram& P, Smem& sm, RingPos& rp,
@@ -201,19 +214,6 @@ __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepPr
     }
   }
   return true;
-}
-
-// The program's matrix-product phases in order (attention phases carry no tiles):
-// index i -> (layer, kind).
-__device__ __forceinline__ void gemv_phase_of(int i, int nlayers, int& l, int& kind) {
-  if (i == 5 * nlayers) {
-    l = nlayers;
-    kind = 6;  // LM head
-    return;
-  }
-  l = i / 5;
-  const int r = i - 5 * l;
-  kind = r == 0 ? 0 : r + 1;  // 0 qkv, 2 o_proj, 3 router+MLP, 4 MLP down+experts up, 5 experts down
 }
 
 __device__ __forceinline__ const OpBase* producer_op(const StepProgram& P, int l, int kind) {
@@ -391,6 +391,7 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   bool ok = ps.live;
   if (ps.live) {
     stage_activations(ob.ac, ob.nac, sm.stg);
+    if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 1);
     wait_constants(P, sm, ps);
     if (kind == kKindRouterMlp && threadIdx.x == 0) {
       const int2 r0 = step_ranges(P, sm)[(l * 5 + 2) * kRangeSlots];
@@ -398,6 +399,7 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
       sm.ints[kSmemRouterMine] = r0.y - r0.x;
     }
     named_bar(kBarConsumers, kConsumerThreads);
+    if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 2);
     switch (kind) {
       case kKindQkv: ok = reinterpret_cast<const QkvOp*>(sm.opc)->prologue(sm); break;
       case kKindOProj: ok = reinterpret_cast<const OProjOp*>(sm.opc)->prologue(sm); break;
@@ -414,14 +416,14 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   const int gi = kind == kKindLm ? 5 * P.nlayers : l * 5 + (kind == kKindQkv ? 0 : kind - 1);
   const int2* rng = step_ranges(P, sm) + gi * kRangeSlots;
   consume_segments<CPLM>(ob, sm, ps.rp, ps.wp, P.stages, ok && ps.live, status, h,
-                         [&](int s, int u0, int n, const Res& r, bool eok) {
+                         [&](int s, int u0, int n, const Res& r, bool eok, int t) {
                            switch (kind) {
-                             case kKindQkv: reinterpret_cast<const QkvOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
-                             case kKindOProj: reinterpret_cast<const OProjOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
-                             case kKindRouterMlp: reinterpret_cast<const RouterMlpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
-                             case kKindMoeUp: reinterpret_cast<const MoeUpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
-                             case kKindMoeDown: reinterpret_cast<const MoeDownOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
-                             default: reinterpret_cast<const LmHeadOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok); break;
+                             case kKindQkv: reinterpret_cast<const QkvOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
+                             case kKindOProj: reinterpret_cast<const OProjOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
+                             case kKindRouterMlp: reinterpret_cast<const RouterMlpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
+                             case kKindMoeUp: reinterpret_cast<const MoeUpOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
+                             case kKindMoeDown: reinterpret_cast<const MoeDownOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
+                             default: reinterpret_cast<const LmHeadOp*>(sm.opc)->epilogue(s, u0, n, r, sm, eok, t); break;
                            }
                          },
                          rng);
