@@ -54,9 +54,10 @@ struct AttnArgs {
 };
 
 __host__ __device__ __forceinline__ int attn_smem_bytes(int g, int d) {
-  // acc [g][d] + lane-group stats [64][g] x 2 + merge scales [g][kAttnMaxSplit] + misc
-  // + the normalised query heads q_s [g][d] (bf16)
-  return g * d * 4 + 2 * 64 * g * 4 + g * kAttnMaxSplit * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2;
+  // acc [g][d] + lane-group stats [64][g] x 2 + misc + the normalised query heads
+  // q_s [g][d] (bf16) + the new key and value kn_s / vn_s [d] (bf16) + the RoPE
+  // table [d] (fp32 cos | sin)
+  return g * d * 4 + 2 * 64 * g * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2 + 2 * d * 2 + d * 4;
 }
 
 // One work item (KV head hk, split sp) of decode attention, run by the kAttnThreads
@@ -71,6 +72,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   constexpr int KPW = 32 / LK;                // lane groups per warp
   constexpr int CPL = (D / 8) / LK;           // 16-byte chunks per lane of a key row
   constexpr int NGRP = kAttnWarps * KPW;      // lane groups per CTA
+  constexpr int KB = 4;                       // keys per lane group in flight
   // heads kept in registers at once: at most 4, so that the item fits the step
   // kernel's register budget next to everything else (more heads = one more pass
   // over the keys, which then come from L2)
@@ -78,21 +80,23 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   float* acc_s = reinterpret_cast<float*>(smem);                     // [G][D]
   float* gm = acc_s + G * D;                                         // [NGRP][G]
   float* gl = gm + 64 * G;                                           // [NGRP][G]
-  float* scale_s = gl + 64 * G;                                      // [G][kAttnMaxSplit]
-  float* ml = scale_s + G * kAttnMaxSplit;                           // M[G], L[G]
+  float* ml = gl + 64 * G;                                           // M[G], L[G]
   int* flag = reinterpret_cast<int*>(ml + 2 * kAttnMaxG);
   bf16_t* q_s = reinterpret_cast<bf16_t*>(flag + 16);                // [G][D]
+  bf16_t* kn_s = q_s + G * D;                                        // [D] new key
+  bf16_t* vn_s = kn_s + D;                                           // [D] new value
+  float* rope_s = reinterpret_cast<float*>(vn_s + D);                // [D/2] cos | [D/2] sin
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // norm weights, RoPE frequencies of this lane
-  float wq[PER], wk[PER], fr[PER];
+  // norm weights of this lane
+  float wq[PER], wk[PER];
 #pragma unroll
   for (int i = 0; i < PER; ++i) {
     const int e = lane + 32 * i;
     wq[i] = bf2f(a.q_norm[e]);
     wk[i] = bf2f(a.k_norm[e]);
-    fr[i] = a.inv_freq[e < D / 2 ? e : e - D / 2];
   }
+  const float fr = (int)threadIdx.x < D / 2 ? a.inv_freq[threadIdx.x] : 0.f;
   const int pos = a.pos_fixed >= 0 ? a.pos_fixed : ldcg_i(a.ctrl + G4_CTRL_POS);
   if (pos < 0 || pos >= a.max_len) {  // never index the cache out of bounds
     if (threadIdx.x == 0 && hk == 0 && sp == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
@@ -116,7 +120,47 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   const bf16_t* kraw = a.qkv + (size_t)a.n_kv * G * D;
   const bf16_t* vraw = a.k_eq_v ? kraw : kraw + (size_t)a.n_kv * D;
 
-  // ---- 1. q heads (and the new k/v if this split holds pos): one warp per vector
+  // ---- 0. with all heads in one pass and registers to spare (G <= 4, G * CPL <= 4),
+  // the first KB keys of every lane group go in flight now, under step 1: the cached
+  // rows do not depend on it (only key `pos`, written below, does; it is patched from
+  // shared memory before use)
+  constexpr bool kEarly = G <= 4 && G * CPL <= 4;
+  const int gi_lane = lane / LK, li = lane % LK;
+  const int grp = warp * KPW + gi_lane;
+  const bf16_t* kbase = a.cache_k + (size_t)hk * D;
+  const bf16_t* vbase = a.cache_v + (size_t)hk * D;
+  const int jstart = warp * KPW;  // warp-uniform
+  uint4 kr[KB][CPL], vr[KB][CPL];
+  auto load_keys = [&](int jw) {
+#pragma unroll
+    for (int m = 0; m < KB; ++m) {
+      const int j = jw + gi_lane + m * NGRP;
+#pragma unroll
+      for (int c = 0; c < CPL; ++c) {
+        if (j < n) {
+          kr[m][c] = ldcg_u4(kbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
+          vr[m][c] = ldcg_u4(vbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
+        } else {
+          kr[m][c] = make_uint4(0, 0, 0, 0);
+          vr[m][c] = make_uint4(0, 0, 0, 0);
+        }
+      }
+    }
+  };
+  if (kEarly) load_keys(jstart);
+
+  // ---- 1. RoPE table of this position (cos / sin of pos * inv_freq, rounded to bf16
+  // as the reference does, model.py:76-78): one sincosf per thread, shared by every
+  // vector below.  Then the q heads (and the new k/v if this split holds pos): one
+  // warp per vector.
+  static_assert(D / 2 <= kAttnThreads, "one RoPE frequency per thread");
+  if ((int)threadIdx.x < D / 2) {
+    float sn, cs;
+    sincosf((float)pos * fr, &sn, &cs);
+    rope_s[threadIdx.x] = rbf(cs);
+    rope_s[D / 2 + threadIdx.x] = rbf(sn);
+  }
+  named_bar(bar, kAttnThreads);
   const bool has_new = (pos >= k0 && pos < k1);
   const int nvec = G + (has_new ? 2 : 0);
   for (int vi = warp; vi < nvec; vi += kAttnWarps) {  // warp-uniform
@@ -143,10 +187,10 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
       float out[PER];
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
-        float sn, cs;
-        sincosf((float)pos * fr[i], &sn, &cs);
+        const int f = (lane + 32 * i) % (D / 2);
+        const float cs = rope_s[f], sn = rope_s[D / 2 + f];
         const float rot = i < PER / 2 ? -v[i + PER / 2] : v[i - PER / 2];
-        out[i] = rbf(rbf(v[i] * rbf(cs)) + rbf(rot * rbf(sn)));
+        out[i] = rbf(rbf(v[i] * cs) + rbf(rot * sn));
       }
 #pragma unroll
       for (int i = 0; i < PER; ++i) v[i] = out[i];
@@ -156,8 +200,13 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
       for (int i = 0; i < PER; ++i) q_s[vi * D + lane + 32 * i] = f2bf(v[i]);
     } else {
       bf16_t* dst = (vi == G ? a.cache_k : a.cache_v) + (size_t)pos * row_stride + (size_t)hk * D;
+      bf16_t* cpy = vi == G ? kn_s : vn_s;
 #pragma unroll
-      for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(v[i]);
+      for (int i = 0; i < PER; ++i) {
+        const bf16_t b = f2bf(v[i]);
+        dst[lane + 32 * i] = b;
+        cpy[lane + 32 * i] = b;
+      }
     }
   }
   for (int i = threadIdx.x; i < G * D; i += kAttnThreads) acc_s[i] = 0.f;
@@ -166,10 +215,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 3);
 
   // ---- 2. online softmax per lane group over its keys
-  const int gi_lane = lane / LK, li = lane % LK;
-  const int grp = warp * KPW + gi_lane;
-  const bf16_t* kbase = a.cache_k + (size_t)hk * D;
-  const bf16_t* vbase = a.cache_v + (size_t)hk * D;
+  const int jnew = has_new ? pos - k0 : -1;  // index of the new key in this slice
 #pragma unroll 1
   for (int h0 = 0; h0 < G; h0 += HG) {
     uint4 qr[HG][CPL];
@@ -189,29 +235,25 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     // warp runs the same iterations, so the shuffles in group_sum always see a full
     // warp.  Lane group gi_lane takes keys jw + gi_lane + m*NGRP.
 #pragma unroll 1
-    for (int jw = warp * KPW; jw < n; jw += NGRP * 4) {
+    for (int jw = jstart; jw < n; jw += NGRP * KB) {
+      if (!kEarly || jw != jstart || h0 != 0) load_keys(jw);  // else already in flight
       const int j0 = jw + gi_lane;
-      uint4 kr[4][CPL], vr[4][CPL];
 #pragma unroll
-      for (int m = 0; m < 4; ++m) {
-        const int j = j0 + m * NGRP;
+      for (int m = 0; m < KB; ++m) {
+        if (j0 + m * NGRP == jnew) {
 #pragma unroll
-        for (int c = 0; c < CPL; ++c) {
-          if (j < n) {
-            kr[m][c] = ldcg_u4(kbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
-            vr[m][c] = ldcg_u4(vbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
-          } else {
-            kr[m][c] = make_uint4(0, 0, 0, 0);
-            vr[m][c] = make_uint4(0, 0, 0, 0);
+          for (int c = 0; c < CPL; ++c) {
+            kr[m][c] = reinterpret_cast<const uint4*>(kn_s)[li + c * LK];
+            vr[m][c] = reinterpret_cast<const uint4*>(vn_s)[li + c * LK];
           }
         }
       }
 #pragma unroll
       for (int h = 0; h < HG; ++h) {
-        float sc[4];
+        float sc[KB];
         float mx = m_run[h];
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < KB; ++m) {
           float s = 0.f;
 #pragma unroll
           for (int c = 0; c < CPL; ++c) s = dot8(kr[m][c], qr[h][c], s);
@@ -225,7 +267,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
 #pragma unroll
         for (int e = 0; e < CPL * 8; ++e) acc[h][e] *= corr;
 #pragma unroll
-        for (int m = 0; m < 4; ++m) {
+        for (int m = 0; m < KB; ++m) {
           const float p = sc[m] == -INFINITY ? 0.f : expf(sc[m] - mx);
           l_run[h] += p;
 #pragma unroll
@@ -281,6 +323,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
       for (int h = 0; h < HG; ++h)
 #pragma unroll
         for (int e = 0; e < CPL * 8; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
+#pragma unroll 1
     for (int q = 0; q < kAttnWarps; ++q) {
       if (warp == q && gi_lane == 0) {
 #pragma unroll
@@ -293,13 +336,14 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   }
 
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
-  // ---- 4. partials, then the last active CTA of this KV head merges them
+  // ---- 4. partials, then the last active CTA of this KV head merges them.  The
+  // acq_rel counter update (after the block barrier) publishes this CTA's partials
+  // and, for the last CTA, acquires every other CTA's.
   float* pbase = a.part + ((size_t)hk * a.nsplit + sp) * G * (D + 2);
   for (int i = threadIdx.x; i < G * (D + 2); i += kAttnThreads) {
     const int h = i / (D + 2), e = i % (D + 2);
     pbase[i] = e == 0 ? ml[h] : (e == 1 ? ml[kAttnMaxG + h] : acc_s[h * D + e - 2]);
   }
-  __threadfence();
   named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) {
     const int old = atomic_add_acq_rel_gpu(a.counters + hk, 1);
@@ -310,38 +354,60 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   const bool merge = *flag != 0;
   named_bar(bar, kAttnThreads);  // every thread has read the flag before it is reused
   if (!merge) return;
-  __threadfence();
+  // One pass over the partials: each thread takes elements i = tid + 256 k of the
+  // [G][D] context and, SB splits at a time (all their loads in flight together),
+  // folds (m, l, acc) into a running max-rescaled sum in split order.
+  constexpr int NE = (G * D + kAttnThreads - 1) / kAttnThreads;
+  constexpr int SB = NE <= 2 ? 16 : (NE >= 16 ? 1 : 16 / NE);  // <= 96 values in flight
   const float* hbase = a.part + (size_t)hk * a.nsplit * G * (D + 2);
-  for (int h = warp; h < G; h += kAttnWarps) {  // warp-uniform
-    float M = -INFINITY;
-    for (int s2 = lane; s2 < n_active; s2 += 32) M = fmaxf(M, ldcg_f(hbase + ((size_t)s2 * G + h) * (D + 2)));
-    M = warp_max(M);
-    float L = 0.f;
-    for (int s2 = lane; s2 < n_active; s2 += 32) {
-      const float* p = hbase + ((size_t)s2 * G + h) * (D + 2);
-      const float f = expf(ldcg_f(p) - M);
-      scale_s[h * kAttnMaxSplit + s2] = f;
-      L += ldcg_f(p + 1) * f;
-    }
-    L = warp_sum(L);
-    if (lane == 0) ml[h] = L;
+  float M[NE], L[NE], O[NE];
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    M[k] = -INFINITY;
+    L[k] = 0.f;
+    O[k] = 0.f;
   }
-  named_bar(bar, kAttnThreads);
-  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) {
-    const int h = i / D, e = i % D;
-    const float* src = hbase + (size_t)h * (D + 2) + 2 + e;
-    const size_t sstride = (size_t)G * (D + 2);
-    float o = 0.f;
-    int s2 = 0;
-    for (; s2 + 4 <= n_active; s2 += 4) {
-      float v[4];
+#pragma unroll 1
+  for (int s0 = 0; s0 < n_active; s0 += SB) {
+    float mv[NE][SB], lv[NE][SB], av[NE][SB];
 #pragma unroll
-      for (int u = 0; u < 4; ++u) v[u] = ldcg_f(src + (s2 + u) * sstride);
+    for (int k = 0; k < NE; ++k) {
+      const int i = threadIdx.x + kAttnThreads * k;
+      const int h = i / D, e = i % D;
 #pragma unroll
-      for (int u = 0; u < 4; ++u) o = fmaf(v[u], scale_s[h * kAttnMaxSplit + s2 + u], o);
+      for (int q = 0; q < SB; ++q) {
+        mv[k][q] = -INFINITY;
+        lv[k][q] = 0.f;
+        av[k][q] = 0.f;
+        if (i < G * D && s0 + q < n_active) {
+          const float* p = hbase + ((size_t)(s0 + q) * G + h) * (D + 2);
+          mv[k][q] = ldcg_f(p);
+          lv[k][q] = ldcg_f(p + 1);
+          av[k][q] = ldcg_f(p + 2 + e);
+        }
+      }
     }
-    for (; s2 < n_active; ++s2) o = fmaf(ldcg_f(src + s2 * sstride), scale_s[h * kAttnMaxSplit + s2], o);
-    a.ctx[((size_t)hk * G + h) * D + e] = f2bf(o / ml[h]);
+#pragma unroll
+    for (int k = 0; k < NE; ++k) {
+      float mb = M[k];
+#pragma unroll
+      for (int q = 0; q < SB; ++q) mb = fmaxf(mb, mv[k][q]);
+      const float cf = M[k] == -INFINITY ? 0.f : expf(M[k] - mb);
+      L[k] *= cf;
+      O[k] *= cf;
+#pragma unroll
+      for (int q = 0; q < SB; ++q) {
+        const float f = mv[k][q] == -INFINITY ? 0.f : expf(mv[k][q] - mb);
+        L[k] = fmaf(lv[k][q], f, L[k]);
+        O[k] = fmaf(av[k][q], f, O[k]);
+      }
+      M[k] = mb;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    const int i = threadIdx.x + kAttnThreads * k;
+    if (i < G * D) a.ctx[((size_t)hk * G + i / D) * D + i % D] = f2bf(O[k] / L[k]);
   }
   if (threadIdx.x == 0) {
     atomicExch(a.counters + hk, 0);
