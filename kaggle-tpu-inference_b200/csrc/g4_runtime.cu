@@ -262,6 +262,21 @@ static float host_bf16_round(float f) {
   return r;
 }
 
+// Partition weight of a router row (see the router+MLP operator's plan): with
+// `per_tile` router rows per ring tile, the router takes R = ceil(E / per_tile) CTAs
+// and a weight w gives each of them one tile when per_tile * row * w equals the MLP
+// bytes per remaining CTA.
+static int router_row_weight(int E, int I_local, int H, int nsm) {
+  const long long row = 2LL * H;
+  const int per_tile = (int)(kStageBytes / row);
+  if (per_tile < 1) return 1;
+  const int R = (E + per_tile - 1) / per_tile;
+  if (R >= nsm) return 1;
+  const double mlp_per_cta = (double)I_local * 2 * row / (nsm - R);
+  const int w = (int)(mlp_per_cta / ((double)per_tile * row) + 0.5);
+  return w < 1 ? 1 : w;
+}
+
 static int pick_nsplit(int n_kv, int max_live, int nsm) {
   int need = (max_live + kAttnMaxChunk - 1) / kAttnMaxChunk;
   int want = nsm / n_kv;
@@ -880,9 +895,11 @@ extern "C" int g4_model_finalize(g4_model* m) {
     r.ctrl = m->ctrl;
     r.nseg = 2;
     r.trace_id = i * 8 + 3;
-    // router rows weigh 3x in the partition: the CTA that completes them also runs
-    // the top-k selection, so the router CTAs take fewer MLP rows
-    r.seg[0] = SegDesc{m->E, 1, H, 0, 3};
+    // The CTA completing the router logits also runs the top-k selection, and the
+    // experts' weights wait for it: router rows get CTAs of their own, one tile of
+    // rows each, by weighing a router row so that one tile of them costs what an MLP
+    // CTA streams (the MLP rows then spread over the other CTAs).
+    r.seg[0] = SegDesc{m->E, 1, H, 0, router_row_weight(m->E, m->I_local, H, m->nsm)};
     r.seg[1] = SegDesc{m->I_local, 2, H, 0};
     r.xsel[1] = 1;  // router rows: x0 (router input); MLP gate|up: x1 (MLP input)
     r.xbytes[0] = H * 2;
@@ -896,6 +913,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
       if (m->world == 1) r.o_o = sg.activation(m->o_out, H * 4);
       r.o_x = sg.activation(m->xres, H * 2);
     }
+    r.stgbytes = std::max(r.stgbytes, kRouterScratchBytes);  // top-k scratch
     r.xres = m->xres;
     r.resmid = m->resmid;
     r.h2 = m->h2;
@@ -1454,6 +1472,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
     Stager sg(&r);
     r.o_wrs = sg.constant(router_scale, H * 2);
   }
+  r.stgbytes = std::max(r.stgbytes, kRouterScratchBytes);  // top-k scratch
   r.block_mode = 1;
   r.block_x = static_cast<const bf16_t*>(x);
   r.h2 = reinterpret_cast<bf16_t*>(s + o_h2);

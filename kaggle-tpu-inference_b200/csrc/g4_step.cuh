@@ -189,7 +189,7 @@ __device__ __forceinline__ void gemv_phase_of(int i, int nlayers, int& l, int& k
 // Producer lane: every weight tile of one operator owned by this CTA.
 template <class Op>
 __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepProgram& P, Smem& sm, RingPos& rp,
-                                           uint64_t pol, int seq, const int2* rng) {
+                                           uint64_t pol, int seq, const int2* rng, int& ids_layer) {
   int* status = P.ctrl + G4_CTRL_STATUS;
   bool dep_loaded = false;
   for (int s = 0; s < op.nseg; ++s) {
@@ -198,13 +198,16 @@ __device__ __forceinline__ bool produce_op(const Op& op, int layer, const StepPr
     ue = rng[s].y;
     if (ub >= ue) continue;
     if (op.seg_dependent(s) && !dep_loaded) {
-      const int want = seq + 1;
-      if (!spin_until(P.sync + kSyncRouter + layer, [want](int v) { return v == want; }, status,
-                      ldcg_i(P.ctrl + G4_CTRL_TIMEOUT_US))) {
-        sm.ints[kSmemDead] = 1;
-        return false;
+      if (ids_layer != layer) {  // experts-down reuses the ids experts-up loaded
+        const int want = seq + 1;
+        if (!spin_until(P.sync + kSyncRouter + layer, [want](int v) { return v == want; }, status,
+                        ldcg_i(P.ctrl + G4_CTRL_TIMEOUT_US))) {
+          sm.ints[kSmemDead] = 1;
+          return false;
+        }
+        op.load_dependent(sm);
+        ids_layer = layer;
       }
-      op.load_dependent(sm);
       dep_loaded = true;
     }
     for (int u = ub; u < ue;) {
@@ -263,6 +266,7 @@ static __device__ __noinline__ void produce_step(const StepProgram& P, Smem sm, 
   RingPos rp;
   const int nops = 5 * P.nlayers + 1;
   fetch_plan(P, sm, 0);
+  int ids_layer = -1;  // layer whose expert ids are in Smem::ints[kSmemExp..]
   bool ok = true;
   for (int i = 0; i < nops && ok; ++i) {
     if (!mbar_wait(&sm.pbar[1], i & 1, status)) {
@@ -275,12 +279,12 @@ static __device__ __noinline__ void produce_step(const StepProgram& P, Smem sm, 
     const unsigned char* slot = sm.popc + (i & 1) * kOpCopyBytes;
     const int2* rng = step_ranges(P, sm) + i * kRangeSlots;
     switch (kind) {
-      case 0: ok = produce_op(*reinterpret_cast<const QkvOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
-      case 2: ok = produce_op(*reinterpret_cast<const OProjOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
-      case 3: ok = produce_op(*reinterpret_cast<const RouterMlpOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
-      case 4: ok = produce_op(*reinterpret_cast<const MoeUpOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
-      case 5: ok = produce_op(*reinterpret_cast<const MoeDownOp*>(slot), l, P, sm, rp, pol, seq, rng); break;
-      default: ok = produce_op(*reinterpret_cast<const LmHeadOp*>(slot), l < P.nlayers ? l : P.nlayers - 1, P, sm, rp, pol, seq, rng); break;
+      case 0: ok = produce_op(*reinterpret_cast<const QkvOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      case 2: ok = produce_op(*reinterpret_cast<const OProjOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      case 3: ok = produce_op(*reinterpret_cast<const RouterMlpOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      case 4: ok = produce_op(*reinterpret_cast<const MoeUpOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      case 5: ok = produce_op(*reinterpret_cast<const MoeDownOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      default: ok = produce_op(*reinterpret_cast<const LmHeadOp*>(slot), l < P.nlayers ? l : P.nlayers - 1, P, sm, rp, pol, seq, rng, ids_layer); break;
     }
   }
   producer_exit(sm);
@@ -320,18 +324,18 @@ __device__ __forceinline__ void wait_constants(const StepProgram& P, Smem& sm, P
     sm.ints[kSmemDead] = 1;
 }
 
-// End of operator ps.phase: all of this CTA's stores done -> issue the next
+// End of operator ps.phase: all of this CTA's stores done -> arrive -> issue the next
 // operator's constant copies (the staging area is free; an empty list still
-// completes the barrier phase the next operator waits for) -> arrive.
+// completes the barrier phase the next operator waits for).
 __device__ __forceinline__ void phase_end(const StepProgram& P, Smem& sm, PhaseState& ps, const OpBase* next) {
   named_bar(kBarConsumers, kConsumerThreads);
   if (threadIdx.x == 0) {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic reads -> async writes
+    // release: this CTA's stores (ordered before by the barrier above) become
+    // visible before the arrival; the arrival goes first, the copies are local
+    red_release_gpu_add(P.sync + kSyncBarrier, 1);
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");  // generic accesses -> async writes
     if (next) issue_copies(next->cc, next->ncc, sm.stg, &sm.pbar[0]);
     else issue_copies(nullptr, 0, sm.stg, &sm.pbar[0]);
-    // release: this CTA's stores (ordered before by the barrier above) become
-    // visible before the arrival
-    red_release_gpu_add(P.sync + kSyncBarrier, 1);
   }
   ++ps.phase;
 }
