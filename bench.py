@@ -47,8 +47,10 @@ METRIC = "decode tok/s @32K ctx, bs=1"
 FALLBACK_HBM_GBS = 6650.0
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the step
-# kernel, keyed by (world, layers); filled from an ncu capture of the step kernel.
-NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {}
+# kernel, keyed by (world, layers): one full-size config-4 launch (the 37th, position 36)
+# captured by ncu, summarised in profiles/step_kernel_launches_config4.md -- 7.41 GB read
+# + 18.0 MB written against 7.41 GB of algorithmic bytes at that position.
+NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {(1, 30): 7.41e9 + 18.04e6}
 
 # DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each kernel
 # class, from the ncu capture summarised in profiles/decode_layer_ncu_full_small.md
@@ -71,7 +73,7 @@ def parse_args():
     ap.add_argument("--global-head-dim", type=int, default=256)
     ap.add_argument("--seed", type=int, default=3)
     ap.add_argument("--profile-steps", type=int, default=4)
-    ap.add_argument("--cpu-steps", type=int, default=1)
+    ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
@@ -234,7 +236,7 @@ def run_reference(args, cfg, rank, world, workload):
     if rank != 0:
         return 0
     steps = max(1, min(args.steps, args.cpu_steps))
-    warm = 1 if args.warmup > 0 else 0
+    warm = min(args.warmup, 3)  # the CPU step is ~1.5 s: at most 3 warm-up steps
     value, cores = cpu_decode_sample(cfg, args.max_len, steps, warm)
     sample = (f"{steps} timed full-size decode step(s) after {warm} warm-up at position 32+, "
               f"max_len {args.max_len}, CPU restatement of the reference forward (oracle/)")

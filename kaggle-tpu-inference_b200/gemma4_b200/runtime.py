@@ -23,6 +23,23 @@ from .config import TextConfig
 from .model import Mesh, local_cache_shapes
 
 
+HANDLE_BYTES = 64  # one CUDA IPC memory handle
+
+
+def exchange_handles(mine: bytes, world: int, group=None) -> bytes:
+    """Every rank's exchange-buffer handle, concatenated in rank order (the layout
+    ``g4_comm_open`` expects), swapped through the torch.distributed process group."""
+    import torch.distributed as dist
+
+    if len(mine) != HANDLE_BYTES:
+        raise ValueError(f"an IPC handle is {HANDLE_BYTES} bytes, got {len(mine)}")
+    allh: list = [None] * world
+    dist.all_gather_object(allh, mine, group=group)
+    if any(h is None or len(h) != HANDLE_BYTES for h in allh):
+        raise RuntimeError("a rank sent no valid IPC handle")
+    return b"".join(allh)
+
+
 class Comm:
     def __init__(self, mesh: Mesh, hidden: int, group=None):
         L = N.lib()
@@ -33,12 +50,10 @@ class Comm:
         if mesh.world > 1:
             import torch.distributed as dist
 
-            buf = ctypes.create_string_buffer(64)
+            buf = ctypes.create_string_buffer(HANDLE_BYTES)
             N.check(L.g4_comm_get_handle(self.handle, buf), "g4_comm_get_handle")
-            mine = bytes(buf.raw)
-            allh: list = [None] * mesh.world
-            dist.all_gather_object(allh, mine, group=group)
-            N.check(L.g4_comm_open(self.handle, b"".join(allh)), "g4_comm_open")
+            allh = exchange_handles(bytes(buf.raw), mesh.world, group)
+            N.check(L.g4_comm_open(self.handle, allh), "g4_comm_open")
             dist.barrier(group=group)
 
     def close(self):
