@@ -165,7 +165,9 @@ int g4_model_destroy(g4_model* model);
  *   gate_up      bf16[E,2,F/world,H] (this rank's F slice), down bf16[E,H,F/world]
  *   out          bf16[H]            summed expert output (identical on every rank)
  *   top_idx      int32[K], top_w fp32[K]  (outputs, may be NULL)
- *   scratch_ctl  int32[G4_CTRL_WORDS] control block (STEP used as the exchange epoch) */
+ *   scratch_ctl  int32[G4_CTRL_WORDS] control block (STEP used as the exchange epoch)
+ * x, out, router_proj, router_scale, gate_up and down must be 16-byte aligned
+ * (G4_ERR_ARG otherwise). */
 int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* comm,
                  const void* x, const void* router_proj, const void* router_scale,
                  const void* per_expert_scale, const void* gate_up, const void* down,

@@ -1413,8 +1413,10 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   if (!valid_cfg(cfg) || !x || !router_proj || !router_scale || !per_expert_scale || !gate_up ||
       !down || !out || !control)
     return fail(G4_ERR_ARG, "g4_moe_block: null argument");
-  if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
-    return fail(G4_ERR_ARG, "g4_moe_block: x and out must be 16-byte aligned");
+  for (const void* p : {x, static_cast<const void*>(out), router_proj, router_scale, gate_up, down})
+    if (reinterpret_cast<uintptr_t>(p) % 16)  // read by 16-byte TMA bulk copies
+      return fail(G4_ERR_ARG, "g4_moe_block: x, out, router_proj, router_scale, gate_up and down "
+                              "must be 16-byte aligned");
   if (world < 1 || world > kMaxWorld || rank < 0 || rank >= world)
     return fail(G4_ERR_ARG, "g4_moe_block: bad rank/world");
   if (world > 1 && (!comm || !comm->open || comm->world != world || comm->rank != rank))
