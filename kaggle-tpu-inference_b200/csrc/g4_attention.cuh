@@ -358,7 +358,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   // [G][D] context and, SB splits at a time (all their loads in flight together),
   // folds (m, l, acc) into a running max-rescaled sum in split order.
   constexpr int NE = (G * D + kAttnThreads - 1) / kAttnThreads;
-  constexpr int SB = NE <= 2 ? 16 : (NE >= 16 ? 1 : 16 / NE);  // <= 96 values in flight
+  constexpr int SB = NE <= 2 ? 16 : (NE >= 32 ? 1 : 32 / NE);  // <= 96 values in flight
   const float* hbase = a.part + (size_t)hk * a.nsplit * G * (D + 2);
   float M[NE], L[NE], O[NE];
 #pragma unroll
