@@ -936,8 +936,11 @@ extern "C" int g4_model_finalize(g4_model* m) {
     u.ctrl = m->ctrl;
     u.nseg = 2;
     u.trace_id = i * 8 + 4;
-    u.seg[0] = SegDesc{H, 1, m->I_local, 0};
-    u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local};
+    // dense MLP-down rows cost 6/5 of an expert row's bytes in the partition: their tiles
+    // (10 rows of 4224 B for config 4) give two warps two rows each, so those CTAs
+    // stream slower per byte (measured ~27 vs ~33 KB/us)
+    u.seg[0] = SegDesc{H, 1, m->I_local, 0, 6};
+    u.seg[1] = SegDesc{m->topk * m->F_local, 2, H, m->F_local, 5};
     u.xsel[0] = 1;  // MLP down: x1 (activation); experts gate|up: x0 (MoE input)
     u.xbytes[0] = H * 2;
     u.xbytes[1] = m->I_local * 2;
