@@ -53,11 +53,18 @@ struct AttnArgs {
   int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
 
+// Heads per pass (at most 4) and whether the warps' partial sums are merged through
+// per-warp shared-memory slots (one barrier) rather than warp by warp (a barrier each):
+// when the slots take at most 32 KB.
+__host__ __device__ __forceinline__ int attn_heads_per_pass(int g) { return g > 4 ? 4 : g; }
+__host__ __device__ __forceinline__ bool attn_slot_merge(int g, int d) { return attn_heads_per_pass(g) * d <= 1024; }
+
 __host__ __device__ __forceinline__ int attn_smem_bytes(int g, int d) {
   // acc [g][d] + lane-group stats [64][g] x 2 + misc + the normalised query heads
   // q_s [g][d] (bf16) + the new key and value kn_s / vn_s [d] (bf16) + the RoPE
-  // table [d] (fp32 cos | sin)
-  return g * d * 4 + 2 * 64 * g * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2 + 2 * d * 2 + d * 4;
+  // table [d] (fp32 cos | sin) + the merge slots [warps][heads per pass][d] (fp32)
+  return g * d * 4 + 2 * 64 * g * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2 + 2 * d * 2 + d * 4 +
+         (attn_slot_merge(g, d) ? kAttnWarps * attn_heads_per_pass(g) * d * 4 : 0);
 }
 
 // One work item (KV head hk, split sp) of decode attention, run by the kAttnThreads
@@ -86,6 +93,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   bf16_t* kn_s = q_s + G * D;                                        // [D] new key
   bf16_t* vn_s = kn_s + D;                                           // [D] new value
   float* rope_s = reinterpret_cast<float*>(vn_s + D);                // [D/2] cos | [D/2] sin
+  float* mslot = rope_s + D;                                         // [warps][HG][D] (slot merge)
+  constexpr bool kSlotMerge = HG * D <= 1024;
+  static_assert(kSlotMerge == (HG * D <= 1024), "same rule as attn_slot_merge");
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   // norm weights of this lane
@@ -323,15 +333,39 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
       for (int h = 0; h < HG; ++h)
 #pragma unroll
         for (int e = 0; e < CPL * 8; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
-#pragma unroll 1
-    for (int q = 0; q < kAttnWarps; ++q) {
-      if (warp == q && gi_lane == 0) {
+    if (kSlotMerge) {
+      // every warp stores its sums in its own slot; then each thread adds the slots of
+      // its elements in warp order, from 0 -- the same additions, in the same order, as
+      // the warp-by-warp loop below, with one barrier instead of one per warp
+      if (gi_lane == 0) {
 #pragma unroll
         for (int h = 0; h < HG; ++h)
 #pragma unroll
-          for (int e = 0; e < CPL * 8; ++e) acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)] += acc[h][e];
+          for (int c = 0; c < CPL; ++c) {
+            float4* dst = reinterpret_cast<float4*>(mslot + (warp * HG + h) * D + (li + c * LK) * 8);
+            dst[0] = make_float4(acc[h][c * 8 + 0], acc[h][c * 8 + 1], acc[h][c * 8 + 2], acc[h][c * 8 + 3]);
+            dst[1] = make_float4(acc[h][c * 8 + 4], acc[h][c * 8 + 5], acc[h][c * 8 + 6], acc[h][c * 8 + 7]);
+          }
       }
       named_bar(bar, kAttnThreads);
+      for (int i = threadIdx.x; i < HG * D; i += kAttnThreads) {
+        float v = 0.f;
+#pragma unroll
+        for (int q = 0; q < kAttnWarps; ++q) v += mslot[q * HG * D + i];
+        acc_s[h0 * D + i] = v;
+      }
+      named_bar(bar, kAttnThreads);
+    } else {
+#pragma unroll 1
+      for (int q = 0; q < kAttnWarps; ++q) {
+        if (warp == q && gi_lane == 0) {
+#pragma unroll
+          for (int h = 0; h < HG; ++h)
+#pragma unroll
+            for (int e = 0; e < CPL * 8; ++e) acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)] += acc[h][e];
+        }
+        named_bar(bar, kAttnThreads);
+      }
     }
   }
 
