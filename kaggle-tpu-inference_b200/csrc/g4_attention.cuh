@@ -107,6 +107,18 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     wk[i] = bf2f(a.k_norm[e]);
   }
   const float fr = (int)threadIdx.x < D / 2 ? a.inv_freq[threadIdx.x] : 0.f;
+  // this warp's first vector of step 1 (q head `warp`, or the raw k / v) does not depend
+  // on the position: its loads go out now, with the position's
+  const bf16_t* qraw = a.qkv;
+  const bf16_t* kraw = a.qkv + (size_t)a.n_kv * G * D;
+  const bf16_t* vraw = a.k_eq_v ? kraw : kraw + (size_t)a.n_kv * D;
+  const bf16_t* src0 = warp < G ? qraw + ((size_t)hk * G + warp) * D
+                                : (warp == G ? kraw + (size_t)hk * D : vraw + (size_t)hk * D);
+  float pre[PER];
+  if (warp < G + 2) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) pre[i] = bf2f(ldcg_bf(src0 + lane + 32 * i));
+  }
   const int pos = a.pos_fixed >= 0 ? a.pos_fixed : ldcg_i(a.ctrl + G4_CTRL_POS);
   if (pos < 0 || pos >= a.max_len) {  // never index the cache out of bounds
     if (threadIdx.x == 0 && hk == 0 && sp == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
@@ -126,9 +138,6 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     n = kAttnMaxChunk;
   }
   const size_t row_stride = (size_t)a.n_kv * D;
-  const bf16_t* qraw = a.qkv;
-  const bf16_t* kraw = a.qkv + (size_t)a.n_kv * G * D;
-  const bf16_t* vraw = a.k_eq_v ? kraw : kraw + (size_t)a.n_kv * D;
 
   // ---- 0. with all heads in one pass and registers to spare (G <= 4, G * CPL <= 4),
   // the first KB keys of every lane group go in flight now, under step 1: the cached
@@ -181,7 +190,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     float ss = 0.f;
 #pragma unroll
     for (int i = 0; i < PER; ++i) {
-      v[i] = bf2f(ldcg_bf(src + lane + 32 * i));
+      v[i] = vi == warp ? pre[i] : bf2f(ldcg_bf(src + lane + 32 * i));  // first vector: loaded at entry
       ss += v[i] * v[i];
     }
     ss = warp_sum(ss);
