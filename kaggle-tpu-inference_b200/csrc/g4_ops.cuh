@@ -543,6 +543,9 @@ struct RouterMlpOp : OpBase {
   // thread), then each probability's rank among all E (ties -> lower expert index,
   // like a stable top-k), the top-k weights summed in rank order.
   __device__ __forceinline__ void router_done(int mine, Smem& sm) const {
+    const int t = threadIdx.x;
+    // the expert scale is a weight: its load goes out before the counter round trip
+    const float scale = t < E ? bf2f(pes[t]) : 0.f;
     named_bar(kBarReduce, kConsumerThreads);
     if (threadIdx.x == 0) {
       int last = 0;
@@ -557,13 +560,11 @@ struct RouterMlpOp : OpBase {
     const bool last = sm.ints[kSmemLast] != 0;
     named_bar(kBarReduce, kConsumerThreads);  // the flag slot is reused by later code
     if (!last) return;
-    const int t = threadIdx.x;
     float* pv = reinterpret_cast<float*>(sm.stg);  // [E]
     float* top_p = pv + kConsumerThreads;           // [topk] selected probabilities, rank order
-    float l = -INFINITY, scale = 0.f;
+    float l = -INFINITY;
     if (t < E) {
       l = ldcg_f(router_logits + t);
-      scale = bf2f(pes[t]);
       pv[t] = l;
     }
     named_bar(kBarReduce, kConsumerThreads);
