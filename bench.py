@@ -1,8 +1,8 @@
 #!/usr/bin/env python3
-"""Decode benchmark of the B200 Gemma-4 26B-A4B path (BASELINE.json metric / config 4).
+"""Decode benchmark of the B200 Gemma-4 26B-A4B path (headline metric: benchmark config 4).
 
 Workload (config 4): the 26B-A4B-shaped model with seeded random bf16 weights N(0,0.02)
-(seed 3; global head_dim 256 as BASELINE states), batch-1 greedy decode with a
+(seed 3; global head_dim 256 as the benchmark configuration states), batch-1 greedy decode with a
 32,768-token resident KV cache, a 32-token random prompt, then decode steps.  A step
 is one decoded token; the timed steps continue the same sequence (positions
 32+W .. 32+W+K), so the default W=16, K=752 covers exactly config 4's 768 tokens.
@@ -265,7 +265,7 @@ def main() -> int:
     cfg = make_config(global_head_dim=args.global_head_dim, num_hidden_layers=args.layers,
                       num_experts=args.experts, vocab_size=args.vocab)
     workload = {
-        "workload": "BASELINE config 4: 26B-A4B-shaped random model (seed 3), bs=1 greedy decode, "
+        "workload": "benchmark config 4: 26B-A4B-shaped random model (seed 3), bs=1 greedy decode, "
                     "32K resident KV cache, 32-token prompt",
         "model": "gemma-4-26B-A4B-shape (random init)", "global_head_dim": args.global_head_dim,
         "max_len": args.max_len, "prompt_len": args.prompt_len, "global_batch": 1,

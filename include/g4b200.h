@@ -190,14 +190,18 @@ int g4_attention_decode(const void* qkv_raw, const void* q_norm, const void* k_n
 
 /* g4_attention_decode_noalloc: the same computation and arguments as
  * g4_attention_decode, for callers that must not allocate device memory during the call
- * -- e.g. code recording its stream into a CUDA graph, servers that reserve their whole
- * memory budget at start-up, or hosts whose own allocator owns the GPU.  No counterpart
- * in the reference (its JAX runtime owns all device memory).  Scratch lives in a fixed
- * 4 MiB device array built into the library (kept on every GPU the library is loaded on
- * until exit); shapes whose split-KV partials exceed it fail with G4_ERR_SHAPE.  The
- * first call on a device looks the array's address up (cudaGetSymbolAddress) with that
- * device current; make that first call before any stream capture.  Every call shares
- * the one array: calls that overlap on the GPU (different streams, no ordering) race. */
+ * -- servers that reserve their whole memory budget at start-up, hosts whose own caching
+ * allocator owns the GPU, loops that cannot take an allocation's synchronisation.  No
+ * counterpart in the reference (its JAX runtime owns all device memory).  Scratch lives
+ * in a fixed 4 MiB device array built into the library (kept on every GPU the library is
+ * loaded on until exit); shapes whose split-KV partials exceed it fail with
+ * G4_ERR_SHAPE.  It calls no cudaMalloc/cudaFree: each call enqueues one small set-up
+ * kernel (zeroes the merge counters and status word, writes the RoPE table, passed by
+ * value) and the attention kernel on `stream`.  The first call on a device looks the
+ * array's address up (cudaGetSymbolAddress) with that device current; make that first
+ * call before any stream capture.  Every call shares the one array: calls that overlap
+ * on the GPU (different streams, no ordering) race.  Kernel-side status bits are not
+ * reported (the return code covers argument checks and launches only). */
 int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_norm, const void* k_norm,
                                 void* cache_k, void* cache_v, int max_len, int n_q_heads,
                                 int n_kv_heads, int head_dim, int k_eq_v, int pos, int window,

@@ -1444,17 +1444,11 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
                o_z = take(256);
   char* s = block_scratch(off);
   if (!s) return fail(G4_ERR_NOMEM, "g4_moe_block: scratch allocation failed");
-  g4_comm* cm = comm;
-  g4_comm* tmp = nullptr;
-  if (!cm) {
-    int rc = g4_comm_create(dev, 0, 1, H, &tmp);
-    if (rc) return rc;
-    cm = tmp;
-  }
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   Common c{};
   c.counters = reinterpret_cast<int*>(s + kBlockMoeCounters);
-  for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = cm->peer[p];
+  // world 1 never touches an exchange buffer: no communicator is needed
+  for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = world > 1 ? comm->peer[p] : nullptr;
   c.rank = rank;
   c.world = world;
   c.xpayload = 2 * H;
@@ -1544,28 +1538,49 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
                                static_cast<bf16_t*>(out));
     if (e != cudaSuccess) rc = fail(G4_ERR_LAUNCH, "reduce launch: %s", cudaGetErrorString(e));
   }
-  if (tmp) {
-    cudaStreamSynchronize(st);
-    g4_comm_destroy(tmp);
-  }
   return rc;
 }
 
 // ------------------------------------------------------------------ allocation-free attention
-// Some callers cannot allocate device memory when they call into the library: code that
-// runs while its stream is being recorded into a CUDA graph (an allocation there breaks
-// the recording), servers that reserve their whole memory budget at start-up and must
-// not grow afterwards, and hosts whose own allocator owns the device and forbids other
-// allocations.  g4_attention_decode allocates its scratch (split-KV partials and merge
-// counters) on first use; g4_attention_decode_noalloc computes exactly the same thing but
-// keeps that scratch in the fixed device array below, which the library carries in every
-// GPU it is loaded on until the process exits.
+// Some callers cannot allocate device memory when they call into the library: servers
+// that reserve their whole memory budget at start-up and must not grow afterwards, hosts
+// whose own caching allocator owns the device and forbids allocations behind its back,
+// and latency-critical loops that cannot take the device-wide synchronisation a
+// cudaMalloc/cudaFree may imply.  g4_attention_decode allocates its scratch (split-KV
+// partials and merge counters) on first use; g4_attention_decode_noalloc computes exactly
+// the same thing but keeps that scratch in the fixed device array below, which the
+// library carries in every GPU it is loaded on until the process exits.
 //
-// Layout of the array: [0, 256) merge counters (one per KV head, zero between calls),
-// [256, 512) control block (status word), [512, 1536) RoPE table, [2048, end) partials.
+// Layout of the array (byte offsets): merge counters, one int per KV head, zero between
+// calls; the attention control block (its status word is cleared per call and not read
+// back: kernel-side status bits are not reported by this entry point); the RoPE inverse
+// frequencies; the split-KV partials.
 constexpr size_t kNoAllocScratchBytes = (size_t)4 << 20;  // 4 MiB per device
-constexpr size_t kNoAllocPartOffset = 2048;
+constexpr size_t kNoAllocCounters = 0;                     // int[kBlockMaxKv]
+constexpr size_t kNoAllocCtrl = 256;                       // int[G4_CTRL_WORDS]
+constexpr size_t kNoAllocInvFreq = 1024;                   // float[kAttnMaxD / 2]
+constexpr size_t kNoAllocPartOffset = 2048;                // partials to the end
+static_assert(kNoAllocCtrl >= kNoAllocCounters + kBlockMaxKv * 4 &&
+                  kNoAllocInvFreq >= kNoAllocCtrl + G4_CTRL_WORDS * 4 &&
+                  kNoAllocPartOffset >= kNoAllocInvFreq + kAttnMaxD / 2 * 4,
+              "allocation-free scratch regions overlap");
 static __device__ __align__(256) unsigned char g4_noalloc_scratch[kNoAllocScratchBytes];
+
+// Per-call reset of the shared array, with the RoPE table passed by value as a kernel
+// parameter (copied at launch): no host buffer has to outlive the call.
+struct NoAllocSetup {
+  float inv_freq[kAttnMaxD / 2];
+  int n_inv;
+};
+__global__ void noalloc_setup_kernel(const __grid_constant__ NoAllocSetup p, unsigned char* s) {
+  int* counters = reinterpret_cast<int*>(s + kNoAllocCounters);
+  int* ctrl = reinterpret_cast<int*>(s + kNoAllocCtrl);
+  float* inv = reinterpret_cast<float*>(s + kNoAllocInvFreq);
+  const int t = threadIdx.x;
+  if (t < kBlockMaxKv) counters[t] = 0;
+  if (t < G4_CTRL_WORDS) ctrl[t] = 0;
+  for (int i = t; i < p.n_inv; i += blockDim.x) inv[i] = p.inv_freq[i];
+}
 
 namespace {
 constexpr int kNoAllocMaxDevices = 64;
@@ -1620,12 +1635,13 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   int rc = noalloc_scratch(dev, &s);
   if (rc) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  // The array keeps the previous call's contents: zero the counters and status word.
-  G4_CUDA(cudaMemsetAsync(s, 0, 512, st), G4_ERR_CUDA);
-  float tab[kAttnMaxD / 2];  // host table on the stack: no host allocation either
-  rope_inv_freq(head_dim, theta, partial_rotary, tab);
-  G4_CUDA(cudaMemcpyAsync(s + 1024, tab, sizeof(float) * (head_dim / 2), cudaMemcpyHostToDevice, st),
-          G4_ERR_CUDA);
+  // The array keeps the previous call's contents: the counters and the status word are
+  // zeroed and this call's RoPE table written, by one small kernel on the same stream.
+  NoAllocSetup setup;
+  setup.n_inv = head_dim / 2;
+  rope_inv_freq(head_dim, theta, partial_rotary, setup.inv_freq);
+  noalloc_setup_kernel<<<1, 256, 0, st>>>(setup, s);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   AttnArgs a{};
   a.qkv = static_cast<const bf16_t*>(qkv_raw);
   a.q_norm = static_cast<const bf16_t*>(q_norm);
@@ -1633,9 +1649,9 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   a.cache_k = static_cast<bf16_t*>(cache_k);
   a.cache_v = static_cast<bf16_t*>(cache_v);
   a.ctx = static_cast<bf16_t*>(ctx);
-  a.counters = reinterpret_cast<int*>(s);
-  a.ctrl = reinterpret_cast<int*>(s + 256);
-  a.inv_freq = reinterpret_cast<const float*>(s + 1024);
+  a.counters = reinterpret_cast<int*>(s + kNoAllocCounters);
+  a.ctrl = reinterpret_cast<int*>(s + kNoAllocCtrl);
+  a.inv_freq = reinterpret_cast<const float*>(s + kNoAllocInvFreq);
   a.part = reinterpret_cast<float*>(s + kNoAllocPartOffset);
   a.pos_fixed = pos;
   a.n_kv = n_kv_heads;

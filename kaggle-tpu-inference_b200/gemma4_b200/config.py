@@ -113,7 +113,7 @@ def interleaved_layer_types(n_layers: int, period: int = 6) -> tuple[str, ...]:
 
 
 def make_config(**kw) -> TextConfig:
-    """Build a config from keyword overrides of the 26B-A4B shape."""
+    """Build a config from keyword overrides of the 26B-A4B shape (benchmark config 4)."""
     base = dict(
         hidden_size=2816,
         num_hidden_layers=30,
@@ -146,12 +146,12 @@ def make_config(**kw) -> TextConfig:
 
 
 def gemma4_26b_a4b(global_head_dim: int = 256) -> TextConfig:
-    """BASELINE config 4 (global_head_dim 256); 512 is the real checkpoint's value."""
+    """benchmark config 4 (global_head_dim 256); 512 is the real checkpoint's value."""
     return make_config(global_head_dim=global_head_dim)
 
 
 def tiny_parity_config() -> TextConfig:
-    """the CPU-runnable tiny random model."""
+    """benchmark config 1: the CPU-runnable tiny random model."""
     return make_config(
         hidden_size=256,
         num_hidden_layers=4,

@@ -3,7 +3,7 @@
   hf_parity_tiny.npz  logits of HuggingFace transformers on the reference's own parity
                       model (gemma4_tpu tests/test_parity.py:29-74; see tests/hf_tiny.py):
                       24-token prefill logits and the decode-position logits.
-  oracle_config1.npz  BASELINE config 1 (tiny random model, seed 0 weights N(0,0.02),
+  oracle_config1.npz  benchmark config 1 (tiny random model, seed 0 weights N(0,0.02),
                       128 prompt ids ~U[0,4096) from numpy seed 0, 32 greedy tokens) run
                       token by token through the bf16-faithful oracle: generated ids,
                       the top-2 margin per generated position, and the full logits of

@@ -1,9 +1,9 @@
 """Block-level parity of the CUDA kernels with the CPU oracle, through the C ABI.
 
-* decode attention: sliding layer 16 q / 8 KV heads, d 256, window
+* decode attention (benchmark config 3): sliding layer 16 q / 8 KV heads, d 256, window
   1024, cache 32768; full k==v layer 16 q / 2 KV heads, d 256 (and the real 512), cache
   32768 fully live; Q/K/V N(0,1), seed 2.
-* MoE block: hidden 2816, 128 experts top-8, moe_intermediate 704,
+* MoE block (benchmark config 2): hidden 2816, 128 experts top-8, moe_intermediate 704,
   weights N(0, 0.02), x N(0, 1), seed 1, world 1.
 
 Tolerances: the kernels reproduce every bf16 rounding point of the reference except

@@ -56,7 +56,7 @@ def _compare(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step")
 
 @pytest.mark.parametrize("engine", ["step", "ops"])
 def test_tiny_config1_teacher_forced_and_greedy(engine):
-    """128-token prompt, 32 greedy tokens."""
+    """benchmark config 1: 128-token prompt, 32 greedy tokens."""
     from golden.make_golden import CONFIG1_NEW, config1_inputs
 
     cfg, params, prompt = config1_inputs()

@@ -11,10 +11,10 @@ from gemma4_b200.weights import (active_params_per_token, checkpoint_key_map, pa
 
 
 def test_bench_model_accounting_matches_baseline():
-    # BASELINE.md: 2 x active_params_per_token = 7.399 GB (global d 256) / 7.644 GB (d 512)
+    # 2 x active_params_per_token = 7.399 GB (global d 256) / 7.644 GB (d 512)
     assert abs(2 * active_params_per_token(gemma4_26b_a4b(256)) / 1e9 - 7.399) < 0.001
     assert abs(2 * active_params_per_token(gemma4_26b_a4b(512)) / 1e9 - 7.644) < 0.001
-    # README.md:113: 47.0 GiB of bf16 weights for the real shape
+    # reference README.md:113: 47.0 GiB of bf16 weights for the real shape
     assert abs(param_bytes(gemma4_26b_a4b(512)) / 2 ** 30 - 47.00) < 0.01
 
 

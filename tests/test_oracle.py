@@ -5,7 +5,7 @@
   corr > 0.999, top-1 > 0.9, decode corr > 0.999), live and through the committed
   golden logits;
 * the reference's "sparse decode equals dense prefill" check (test_parity.py:127-151);
-* BASELINE config 1 golden vectors (regression pin of the bf16-faithful oracle).
+* benchmark config 1 golden vectors (regression pin of the bf16-faithful oracle).
 """
 
 import os
@@ -47,7 +47,7 @@ def test_oracle_matches_transformers(hf, router_input):
     dl, _ = o.decode(cache, int(ids[0, seq - 1]), seq - 1, 32)
     dcorr = _corr(dl, ref[seq - 1])
     assert corr > 0.999 and top1 > 0.9 and dcorr > 0.999, (corr, top1, dcorr)
-    # tighter than the reference's own bar: it reports corr 0.99997 (README.md:12-14)
+    # tighter than the reference's own bar: it reports corr 0.99997 (reference README.md:12-14)
     assert corr > 0.9999 and dcorr > 0.9999
 
 

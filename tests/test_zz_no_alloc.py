@@ -1,8 +1,9 @@
 """The allocation-free attention entry point agrees with the allocating one.
 
 g4_attention_decode_noalloc exists for callers that cannot allocate device memory while
-they call the library (a stream being recorded into a CUDA graph, a server that reserved
-its whole memory budget at start-up, a host whose allocator owns the GPU).  It keeps its
+they call the library (a server that reserved its whole memory budget at start-up, a host
+whose caching allocator owns the GPU, a loop that cannot take an allocation's
+synchronisation).  It keeps its
 scratch in a fixed array inside the library, shared by all calls, so this test makes two
 calls in a row -- the second one must not see leftovers of the first -- and compares both
 with g4_attention_decode on the same inputs.  It lives in its own file, collected last.
