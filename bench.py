@@ -46,19 +46,12 @@ sys.path.insert(0, os.path.join(ROOT, "kaggle-tpu-inference_b200"))
 METRIC = "decode tok/s @32K ctx, bs=1"
 FALLBACK_HBM_GBS = 6650.0
 
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of the step
-# kernel, keyed by (world, layers): one full-size config-4 launch (the 37th, position 36)
-# captured by ncu, summarised in profiles/step_kernel_launches_config4.md -- 7.41 GB read
-# + 18.0 MB written against 7.41 GB of algorithmic bytes at that position.
-NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {(1, 30): 7.41e9 + 18.04e6}
-
-# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) per launch of each kernel
-# class, from the ncu capture summarised in profiles/decode_layer_ncu_full_small.md
-# (profiling case with 32 experts: per-layer bytes equal the full model's, except the
-# router rows, 0.54 MB more with 128 experts, added to router_mlp_up).
-NCU_TRAFFIC_BYTES_PER_LAUNCH: dict = {
-    "qkv": 46.28e6, "o_proj": 23.12e6, "router_mlp_up": 24.66e6,
-    "mlp_down_experts_up": 76.54e6, "experts_down": 31.78e6,
+# DRAM traffic (dram__bytes_read.sum + dram__bytes_write.sum) of one full-size launch of
+# the step kernel, keyed by (world, layers), as measured by ncu (launch-list capture of
+# this bench, one metric pass) on the build named beside it; re-captured when the kernel
+# changes.  None where no capture exists (reported as null).
+NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {
+    (1, 30): (7.41e9 + 18.04e6, "step kernel of commit 4c55f17, config 4, launch at position 36"),
 }
 
 
@@ -254,6 +247,41 @@ def run_reference(args, cfg, rank, world, workload):
 
 
 # ----------------------------------------------------------------------------- GPU arm
+def tokens_check(generated, prompt, cfg, args, world, rank, local, dev):
+    """N > 1: the timed run's generated tokens must be identical on every rank; rank 0
+    also replays the same prompt and step count with the same model at world 1 on its
+    own GPU and reports how long a prefix of the sequence agrees (greedy decoding at a
+    top-2 near-tie may go either way when the partial sums are added in another order)."""
+    import torch
+    import torch.distributed as dist
+
+    allt = [torch.empty_like(generated) for _ in range(world)]
+    dist.all_gather(allt, generated)
+    same = all(torch.equal(t, allt[0]) for t in allt)
+    out = {"ranks_identical": same, "tokens": int(generated.numel())}
+    if rank == 0:
+        from gemma4_b200.engine import Engine
+        from gemma4_b200.model import Mesh
+
+        one = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=Mesh(0, 1, local),
+                     engine=args.engine)
+        m1 = one.model
+        m1.reset(prompt)
+        m1.step(len(prompt) + args.warmup + args.steps)
+        torch.cuda.synchronize(dev)
+        m1.check_status()
+        ref = m1.tokens_out[len(prompt):len(prompt) + generated.numel()].cpu()
+        got = generated.cpu()
+        diff = (ref != got).nonzero()
+        out["world1_equal_prefix"] = int(diff[0, 0]) if len(diff) else int(got.numel())
+        out["world1_identical"] = not len(diff)
+        m1.close()
+        del one, m1
+        torch.cuda.empty_cache()
+    dist.barrier()
+    return out
+
+
 def main() -> int:
     args = parse_args()
     world = int(os.environ.get("WORLD_SIZE", args.gpus))
@@ -328,6 +356,9 @@ def main() -> int:
         ms = float(t.item())
     value = args.steps / (ms / 1000.0)
     pos_avg = len(prompt) + args.warmup + args.steps // 2
+    n_gen = args.warmup + args.steps + 1  # tokens generated after the prompt
+    generated = m.tokens_out[len(prompt):len(prompt) + n_gen].clone()
+    tokens_match = tokens_check(generated, prompt, cfg, args, world, rank, local, dev) if world > 1 else None
 
     # ---- per-kernel-class timing of the per-op kernels (event-separated steps)
     prof = m.profile(args.profile_steps)
@@ -346,7 +377,8 @@ def main() -> int:
         achieved = rank_bytes / (launch_ms / 1000.0) / 1e9
         roofline = {"bound": "hbm", "kernel": "step_kernel", "achieved": achieved, "peak": peak,
                     "unit": "GB/s", "frac": achieved / peak, "peak_kind": peak_kind,
-                    "traffic": NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH.get((world, args.layers)),
+                    "traffic": (NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH.get((world, args.layers)) or (None,))[0],
+                    "traffic_source": (NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH.get((world, args.layers)) or (None, None))[1],
                     "algorithmic_bytes_per_launch": rank_bytes, "mean_launch_ms": launch_ms,
                     "time_share": 1.0}
     else:
@@ -357,7 +389,7 @@ def main() -> int:
         achieved = dom_bytes / (dom_ms / 1000.0) / 1e9
         roofline = {"bound": "hbm", "kernel": dom, "achieved": achieved, "peak": peak, "unit": "GB/s",
                     "frac": achieved / peak, "peak_kind": peak_kind,
-                    "traffic": NCU_TRAFFIC_BYTES_PER_LAUNCH.get(dom),
+                    "traffic": None,
                     "algorithmic_bytes_per_launch": dom_bytes, "mean_launch_ms": dom_ms,
                     "time_share": prof[dom] / total_ms}
     step_roof = {"achieved_aggregate_gbs": sb * value / 1e9, "peak_aggregate_gbs": peak * world,
@@ -397,7 +429,7 @@ def main() -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
             "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
-            "cpu_baseline": cpu,
+            "cpu_baseline": cpu, "tokens_match": tokens_match,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

@@ -55,6 +55,16 @@ extern "C" {
 #define G4_CTRL_STATUS 3       /* G4_STATUS_* bits, sticky until the host clears    */
 #define G4_CTRL_TIMEOUT_US 4   /* bound of every cross-GPU wait, microseconds       */
 #define G4_CTRL_WRITE_LOGITS 5 /* nonzero: each step stores its fp32 logits shard   */
+/* Sampling (model.py:414-424): with TEMPERATURE > 0 (fp32 bits) each step replaces the
+ * greedy token by a draw from top_k(logits / t, TOP_K) -> softmax -> top-p (TOP_P, fp32
+ * bits) -> renormalised, with a Philox-4x32-10 uniform keyed by SEED_HI:SEED_LO and the
+ * position (0 for the step that consumes the last forced token, as the reference folds
+ * 0 into the prefill key; the consumed position for later steps).  TOP_K <= 128. */
+#define G4_CTRL_TEMPERATURE 6
+#define G4_CTRL_TOP_P 7
+#define G4_CTRL_TOP_K 8
+#define G4_CTRL_SEED_LO 9
+#define G4_CTRL_SEED_HI 10
 #define G4_CTRL_WORDS 16
 
 /* Model hyper-parameters; mirrors TextConfig (gemma4_tpu/config.py:11-49). */

@@ -36,8 +36,8 @@ namespace g4 {
 
 constexpr int kMaxHidden = 4096;
 constexpr int kBarReduce = 2;      // named barrier id for prologue block reductions
-constexpr int kSites = 3;          // exchange sites: attention out, FFN out, argmax
-constexpr int kSiteAttn = 0, kSiteFfn = 1, kSiteArgmax = 2;
+constexpr int kSites = 4;          // exchange sites: attention out, FFN out, argmax, sampling
+constexpr int kSiteAttn = 0, kSiteFfn = 1, kSiteArgmax = 2, kSiteSample = 3;
 constexpr int kXFlagBytes = kSites * 2 * kMaxWorld * 128;
 // Smem::ints slots
 constexpr int kSmemRouterEnd = 32;  // end of this CTA's router units (0: none)
@@ -733,7 +733,9 @@ struct LmHeadOp : OpBase {
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;
     bv[threadIdx.x] = -INFINITY;
     bi[threadIdx.x] = 0x7fffffff;
-    sm.ints[kSmemWriteLogits] = ldcg_i(ctrl + G4_CTRL_WRITE_LOGITS);
+    // the sampler (temperature > 0) reads the logits this step writes
+    sm.ints[kSmemWriteLogits] = ldcg_i(ctrl + G4_CTRL_WRITE_LOGITS) != 0 ||
+                                __int_as_float(ldcg_i(ctrl + G4_CTRL_TEMPERATURE)) > 0.f;
     named_bar(kBarReduce, kConsumerThreads);
     return ok;
   }

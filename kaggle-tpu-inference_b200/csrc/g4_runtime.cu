@@ -22,6 +22,7 @@
 
 #include "g4_attention.cuh"
 #include "g4_ops.cuh"
+#include "g4_sample.cuh"
 #include "g4_step.cuh"
 
 using namespace g4;
@@ -313,8 +314,8 @@ struct g4_model {
   // library scratch
   char* scratch = nullptr;
   bf16_t *xres, *resmid, *h2, *qkv_raw, *ctx, *mlp_act, *moe_act, *moe_out;
-  float *o_out, *mlp_out, *router_logits, *top_w, *attn_part, *cand_v;
-  int *top_idx, *attn_cnt, *cand_i, *counters;
+  float *o_out, *mlp_out, *router_logits, *top_w, *attn_part, *cand_v, *samp_v;
+  int *top_idx, *attn_cnt, *cand_i, *counters, *samp_i;
   bool finalized = false;
   // plans
   std::vector<QkvOp> k1;
@@ -324,6 +325,8 @@ struct g4_model {
   std::vector<MoeUpOp> k5;
   std::vector<MoeDownOp> k6;
   LmHeadOp lm{};
+  SampleArgs sampler{};  // temperature > 0: replaces the greedy token after the LM head
+  int sample_ctas = 0;
   // persistent step kernel
   int engine = G4_ENGINE_STEP_KERNEL;
   StepProgram prog{};
@@ -789,6 +792,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
   const size_t o_cv = take((size_t)m->nsm * 4), o_ci = take((size_t)m->nsm * 4);
   const size_t o_cnt = take(kNumCounters * 4);
   const size_t o_sync = take(kNumSyncWords * 4);
+  const size_t o_sv = take((size_t)kSampleMaxCtas * kSampleMaxK * 4), o_si = take((size_t)kSampleMaxCtas * kSampleMaxK * 4);
   if (cudaMalloc(&m->scratch, off) != cudaSuccess)
     return fail(G4_ERR_NOMEM, "scratch cudaMalloc(%zu) failed", off);
   cudaMemset(m->scratch, 0, off);
@@ -812,6 +816,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
   m->cand_i = (int*)(s + o_ci);
   m->counters = (int*)(s + o_cnt);
   m->sync = (int*)(s + o_sync);
+  m->samp_v = (float*)(s + o_sv);
+  m->samp_i = (int*)(s + o_si);
 
   // ---- plans
   const g4_config& c = m->cfg;
@@ -1003,6 +1009,21 @@ extern "C" int g4_model_finalize(g4_model* m) {
     lm.max_len = m->max_len;
     lm.softcap = c.final_logit_softcapping;
   }
+  {
+    SampleArgs& sa = m->sampler;
+    sa = SampleArgs{};
+    sa.logits = m->logits;
+    sa.V_local = m->V_local;
+    sa.vbegin = m->vbegin;
+    sa.max_len = m->max_len;
+    sa.ctrl = m->ctrl;
+    sa.tokens_out = m->tokens_out;
+    sa.cand_v = m->samp_v;
+    sa.cand_i = m->samp_i;
+    sa.c = make_common(m, nl - 1);
+    m->sample_ctas = (m->V_local + kSampleChunk - 1) / kSampleChunk;
+    if (m->sample_ctas > kSampleMaxCtas) return fail(G4_ERR_SHAPE, "vocab slice too large for the sampler");
+  }
   // RoPE tables live in a small device buffer shared by all layers of a type.
   {
     const int dsl = c.head_dim, dfu = c.global_head_dim;
@@ -1022,6 +1043,27 @@ extern "C" int g4_model_finalize(g4_model* m) {
   return G4_OK;
 }
 
+// Dynamic shared memory of the sampler: one sorted chunk, or the merge of every CTA's
+// candidates (K <= kSampleMaxK each), whichever is larger.
+static int sample_smem(const g4_model* m) {
+  int n = 1;
+  while (n < m->sample_ctas * kSampleMaxK) n <<= 1;
+  return std::max(kSampleChunk * 8, n * 8);
+}
+
+static int prepare_sampler(const g4_model* m) {
+  G4_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sample_smem(m)),
+          G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+static int launch_sampler(const g4_model* m, cudaStream_t st) {
+  cudaError_t e = launch_pdl(sample_kernel, dim3(m->sample_ctas), dim3(kSampleThreads), sample_smem(m), st,
+                             m->sampler);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "sampler launch: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
 template <class Op>
 static int prepare_op(const Op& op) {
   const int smem = gemv_smem_bytes(smem_aux_bytes(SmemSizes{op.xbytes[0], op.xbytes[1], op.stgbytes}), kStages);
@@ -1035,8 +1077,9 @@ static int prepare_op(const Op& op) {
 }
 
 static int prepare_all(g4_model* m) {
-  if (m->engine == G4_ENGINE_STEP_KERNEL) return prepare_step(m);
   int rc;
+  if ((rc = prepare_sampler(m))) return rc;
+  if (m->engine == G4_ENGINE_STEP_KERNEL) return prepare_step(m);
   for (size_t i = 0; i < m->L.size(); ++i) {
     if ((rc = prepare_op(m->k1[i])) || (rc = prepare_op(m->k3[i])) || (rc = prepare_op(m->k4[i])) ||
         (rc = prepare_op(m->k5[i])) || (rc = prepare_op(m->k6[i])))
@@ -1047,9 +1090,12 @@ static int prepare_all(g4_model* m) {
 }
 
 static int enqueue_step(g4_model* m, cudaStream_t st) {
-  if (m->engine == G4_ENGINE_STEP_KERNEL) return launch_step(m, st);
-  const int nl = (int)m->L.size();
   int rc;
+  if (m->engine == G4_ENGINE_STEP_KERNEL) {
+    if ((rc = launch_step(m, st))) return rc;
+    return launch_sampler(m, st);
+  }
+  const int nl = (int)m->L.size();
   for (int i = 0; i < nl; ++i) {
     if ((rc = launch_gemv(m->k1[i], m->nsm, st))) return rc;
     if ((rc = launch_attention(m->k2[i], st))) return rc;
@@ -1058,7 +1104,8 @@ static int enqueue_step(g4_model* m, cudaStream_t st) {
     if ((rc = launch_gemv(m->k5[i], m->nsm, st))) return rc;
     if ((rc = launch_gemv(m->k6[i], m->nsm, st))) return rc;
   }
-  return launch_gemv(m->lm, m->nsm, st);
+  if ((rc = launch_gemv(m->lm, m->nsm, st))) return rc;
+  return launch_sampler(m, st);
 }
 
 extern "C" int g4_model_host_tokens(g4_model* m, int** host_ptr) {
@@ -1073,6 +1120,7 @@ extern "C" int g4_model_host_tokens(g4_model* m, int** host_ptr) {
     int* dptr = nullptr;
     G4_CUDA(cudaHostGetDevicePointer((void**)&dptr, m->tokens_host, 0), G4_ERR_CUDA);
     m->lm.tokens_host = dptr;
+    m->sampler.tokens_host = dptr;
     m->prog_dirty = true;
   }
   *host_ptr = m->tokens_host;
@@ -1179,7 +1227,8 @@ extern "C" int g4_trace_read(void* host_dst, long long bytes) {
 
 extern "C" int g4_model_kernel_count(const g4_model* m) {
   if (!m) return 0;
-  return m->engine == G4_ENGINE_STEP_KERNEL ? 1 : 6 * (int)m->L.size() + 1;
+  // + the sampler, which returns at once unless control[TEMPERATURE] > 0
+  return m->engine == G4_ENGINE_STEP_KERNEL ? 2 : 6 * (int)m->L.size() + 2;
 }
 
 extern "C" int g4_model_set_engine(g4_model* m, int engine) {
@@ -1197,10 +1246,8 @@ extern "C" int g4_step(g4_model* m, void* stream) {
   if (!m) return fail(G4_ERR_ARG, "g4_step: null model");
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_step before g4_model_finalize");
   G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
-  if (m->engine == G4_ENGINE_STEP_KERNEL) {
-    int rc = prepare_step(m);
-    if (rc) return rc;
-  }
+  int rc = prepare_all(m);
+  if (rc) return rc;
   return enqueue_step(m, static_cast<cudaStream_t>(stream));
 }
 

@@ -28,7 +28,9 @@ G4_STATUS_BAD_TOKEN = 0x4
 G4_STATUS_POS_OVERFLOW = 0x8
 
 CTRL_POS, CTRL_STEP, CTRL_FORCED_LEN, CTRL_STATUS, CTRL_TIMEOUT_US, CTRL_WRITE_LOGITS = range(6)
+CTRL_TEMPERATURE, CTRL_TOP_P, CTRL_TOP_K, CTRL_SEED_LO, CTRL_SEED_HI = range(6, 11)
 CTRL_WORDS = 16
+SAMPLE_MAX_TOP_K = 128
 
 EXPORTS = (
     "g4_version", "g4_strerror", "g4_last_error",

@@ -31,6 +31,19 @@ from .weights import active_params_per_token, load_params, param_bytes, rank_sha
 PREFILL_BUCKET = 256
 
 
+def _seed_of(key) -> int:
+    """The sampling seed of a step fn's ``key`` argument (an int, a 1-element tensor or
+    array, or None = 0); the reference passes a JAX PRNG key built from the seed."""
+    if key is None:
+        return 0
+    try:
+        return int(key)
+    except (TypeError, ValueError):
+        import numpy as np
+
+        return int(np.asarray(key).ravel()[-1])
+
+
 def _round_up(x: int, m: int) -> int:
     return max(m, ((x + m - 1) // m) * m)
 
@@ -51,6 +64,8 @@ class Engine:
         mesh: Mesh | None = None,
         engine: str = "step",
     ):
+        if not 1 <= top_k <= 128:
+            raise ValueError(f"top_k must be in [1, 128] on the B200 sampler, got {top_k}")
         if batch != 1:
             raise NotImplementedError("the B200 decode path runs batch 1 (engine.py:167 fills row 0)")
         self.model_dir = model_dir
@@ -90,10 +105,9 @@ class Engine:
         """Callable with the reference's jitted-step signature (engine.py:60, 74)."""
 
         def fn(params, tokens, cache, pos, key=None, temperature=0.0, top_p=1.0):
-            del params, cache, key, top_p
-            if float(temperature) > 0.0:
-                raise NotImplementedError("stochastic sampling is not on the B200 path yet")
+            del params, cache
             m = self.model
+            m.set_sampling(float(temperature), float(top_p), self.top_k, _seed_of(key))
             if n_steps is not None:  # prefill: tokens [1, T], pos = prompt length
                 plen = int(pos)
                 m.reset(tokens[0, :plen].tolist())
@@ -126,6 +140,7 @@ class Engine:
         out = {}
         m = self.model
         t0 = time.perf_counter()
+        m.set_sampling(0.0, 1.0, self.top_k, 0)
         m.reset([0, 0, 0, 0])
         m.step(1, use_graph=False)   # first launch configures the kernels
         m.capture()
@@ -160,14 +175,12 @@ class Engine:
         p_len = len(prompt_ids)
         if self.max_len - p_len < 1:
             raise ValueError(f"prompt({p_len}) fills the resident context ({self.max_len})")
-        if float(temperature) > 0.0:
-            raise NotImplementedError(
-                "stochastic sampling (temperature > 0) is not on the B200 path yet; use temperature=0")
         max_new_tokens = allowed_output_tokens(max_new_tokens, p_len, self.max_len)
         bucket = min(_round_up(p_len, PREFILL_BUCKET), self.max_len)
         m = self.model
         host = m.tokens_host
 
+        m.set_sampling(float(temperature), float(top_p), self.top_k, int(seed))
         t_start = time.perf_counter()
         m.reset(prompt_ids)
         m.step(p_len)

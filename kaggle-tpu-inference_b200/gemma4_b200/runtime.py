@@ -62,6 +62,11 @@ class Comm:
             self.handle = ctypes.c_void_p()
 
 
+def _i32(v: int) -> int:
+    """An unsigned 32-bit value as the int32 with the same bits."""
+    return v - (1 << 32) if v >= (1 << 31) else v
+
+
 class DecodeModel:
     """Per-rank native model.  ``shard``: native tensor name -> CUDA tensor."""
 
@@ -132,6 +137,19 @@ class DecodeModel:
 
     def set_write_logits(self, on: bool):
         self.ctrl[N.CTRL_WRITE_LOGITS] = 1 if on else 0
+
+    def set_sampling(self, temperature: float = 0.0, top_p: float = 1.0, top_k: int = 64,
+                     seed: int = 0):
+        """Sampling parameters of the following steps (model.py:414-424).  temperature
+        <= 0 is greedy; otherwise each step draws from top_k(logits / t) with the top-p
+        mask, keyed by (seed, position) -- see include/g4b200.h G4_CTRL_TEMPERATURE."""
+        if not 1 <= int(top_k) <= N.SAMPLE_MAX_TOP_K:
+            raise ValueError(f"top_k must be in [1, {N.SAMPLE_MAX_TOP_K}], got {top_k}")
+        f = torch.tensor([float(temperature), float(top_p)], dtype=torch.float32).view(torch.int32)
+        s64 = int(seed) & (2 ** 64 - 1)
+        words = torch.tensor([int(f[0]), int(f[1]), int(top_k),
+                              _i32(s64 & 0xFFFFFFFF), _i32(s64 >> 32)], dtype=torch.int32)
+        self.ctrl[N.CTRL_TEMPERATURE:N.CTRL_SEED_HI + 1].copy_(words)
 
     def step(self, n: int = 1, use_graph: bool = True):
         """Enqueue ``n`` decode steps on the current stream (asynchronous)."""

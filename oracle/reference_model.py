@@ -336,3 +336,68 @@ class Oracle:
 def sample_greedy(logits: torch.Tensor) -> int:
     """Greedy branch of model.py:414-424 (first index of the maximum)."""
     return int(torch.argmax(logits))
+
+
+# ----------------------------------------------------------------------------- sampling
+def philox4x32_10(ctr, key):
+    """Philox-4x32 with 10 rounds (Salmon, Moraes, Dror, Shaw, SC 2011) on Python ints:
+    multipliers 0xD2511F53 / 0xCD9E8D57, key increments 0x9E3779B9 / 0xBB67AE85.  The
+    counter-based generator the device sampler documents (keyed by the seed, counter =
+    (position, 0, 0, 0))."""
+    c0, c1, c2, c3 = (int(v) & 0xFFFFFFFF for v in ctr)
+    k0, k1 = (int(v) & 0xFFFFFFFF for v in key)
+    for _ in range(10):
+        p0, p1 = 0xD2511F53 * c0, 0xCD9E8D57 * c2
+        c0, c1, c2, c3 = ((p1 >> 32) ^ c1 ^ k0) & 0xFFFFFFFF, p1 & 0xFFFFFFFF, \
+            ((p0 >> 32) ^ c3 ^ k1) & 0xFFFFFFFF, p0 & 0xFFFFFFFF
+        k0, k1 = (k0 + 0x9E3779B9) & 0xFFFFFFFF, (k1 + 0xBB67AE85) & 0xFFFFFFFF
+    return c0, c1, c2, c3
+
+
+def philox_uniform(seed: int, position: int) -> np.float32:
+    """Uniform in [0, 1) of (seed, position): the top 24 bits of the first output word."""
+    s = int(seed) & (2 ** 64 - 1)
+    c = philox4x32_10((position, 0, 0, 0), (s & 0xFFFFFFFF, s >> 32))
+    return np.float32(c[0] >> 8) * np.float32(1.0 / 16777216.0)
+
+
+def sampling_distribution(logits: torch.Tensor, temperature: float, top_k: int, top_p: float):
+    """model.py:414-424 up to the categorical draw, in fp32 with sequential sums:
+    top_k(logits / t) (ties to the lower index, like lax.top_k), softmax, the top-p mask
+    (cumsum - p) < top_p.  Returns (token ids, unnormalised kept probabilities, their sum)."""
+    t = np.float32(max(float(temperature), 1e-6))
+    v = (logits.float().numpy().astype(np.float32) / t).astype(np.float32)
+    order = np.lexsort((np.arange(v.size), -v))[:top_k]  # value desc, index asc
+    vals = v[order]
+    mx = vals[0]
+    e = np.exp((vals - mx).astype(np.float32)).astype(np.float32)
+    total = np.float32(0.0)
+    for x in e:
+        total = np.float32(total + x)
+    probs, csum, kept = [], np.float32(0.0), np.float32(0.0)
+    for x in e:
+        p = np.float32(x / total)
+        csum = np.float32(csum + p)
+        if np.float32(csum - p) < np.float32(top_p):
+            probs.append(p)
+            kept = np.float32(kept + p)
+        else:
+            break
+    if not probs:
+        probs, kept = [np.float32(e[0] / total)], np.float32(e[0] / total)
+    return order[:len(probs)], np.array(probs, np.float32), kept
+
+
+def sample_token(logits: torch.Tensor, temperature: float, top_k: int, top_p: float, u: float) -> int:
+    """The token model.py:414-424 draws when its categorical sample is the inverse CDF of
+    the renormalised kept probabilities at ``u`` (greedy for temperature <= 0)."""
+    if temperature <= 0.0:
+        return int(torch.argmax(logits))
+    ids, probs, kept = sampling_distribution(logits, temperature, top_k, top_p)
+    target = np.float32(np.float32(u) * kept)
+    acc = np.float32(0.0)
+    for i, p in zip(ids, probs):
+        acc = np.float32(acc + p)
+        if target < acc:
+            return int(i)
+    return int(ids[-1])

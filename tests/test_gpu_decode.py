@@ -5,7 +5,11 @@ position compares logits of identical inputs.  Pass bar (north star): logits cor
 >= 0.9999 at every position and identical argmax wherever the oracle's top-2 margin
 exceeds 2 bf16 ulps of the top logit (with the std-0.02 random weights the bf16
 logits are small and exact ties are common; tied positions are reported, not failed).
+Every comparison prints one ``PARITY`` line with the worst correlation and the bf16
+max-abs / max-rel error of the logits (max |gpu - oracle|, and that over max |oracle|).
 """
+
+import os
 
 import numpy as np
 import pytest
@@ -39,17 +43,31 @@ def _run_gpu(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step")
     return torch.stack(logits).cpu(), ids, host
 
 
-def _compare(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step"):
+def decided_mask(ref):
+    """Positions whose oracle top-2 margin exceeds 2 bf16 ulps of the top logit."""
+    top2 = torch.topk(ref, 2, dim=-1).values
+    margin = top2[..., 0] - top2[..., 1]
+    return margin > 2 * top2[..., 0].abs().clamp_min(1e-30) * 2.0 ** -7
+
+
+def parity_report(name, lg, ref):
+    """Worst per-position correlation, bf16 max-abs / max-rel error; printed and returned."""
+    worst = min(corr(lg[i], ref[i]) for i in range(len(ref)))
+    max_abs = float((lg.float() - ref.float()).abs().max())
+    max_rel = max_abs / float(ref.float().abs().max())
+    print(f"PARITY {name}: positions {len(ref)}, worst corr {worst:.7f}, max_abs {max_abs:.3e}, "
+          f"max_rel {max_rel:.3e}")
+    return worst, max_abs, max_rel
+
+
+def _compare(cfg, params, prompt, n_new, max_len, use_graph=True, engine="step", name="decode"):
     lg, ids, host = _run_gpu(cfg, params, prompt, n_new, max_len, use_graph, engine)
     assert ids == host, "mapped host token mirror disagrees with the device ring"
     o = Oracle(cfg, params, mode="bf16")
     ref, ref_ids = o.greedy_generate(prompt, n_new, max_len, teacher=ids)
     assert lg.shape == ref.shape
-    worst = min(corr(lg[i], ref[i]) for i in range(len(ref)))
-    top2 = torch.topk(ref, 2, dim=-1).values
-    margin = top2[:, 0] - top2[:, 1]
-    ulp = top2[:, 0].abs().clamp_min(1e-30) * 2.0 ** -7
-    decided = margin > 2 * ulp
+    worst, _, max_rel = parity_report(name, lg, ref)
+    decided = decided_mask(ref)
     agree = lg.argmax(-1) == ref.argmax(-1)
     return worst, agree, decided, ids, ref_ids
 
@@ -60,13 +78,21 @@ def test_tiny_config1_teacher_forced_and_greedy(engine):
     from golden.make_golden import CONFIG1_NEW, config1_inputs
 
     cfg, params, prompt = config1_inputs()
-    worst, agree, decided, ids, _ = _compare(cfg, params, prompt, CONFIG1_NEW, 160, engine=engine)
+    worst, agree, decided, ids, _ = _compare(cfg, params, prompt, CONFIG1_NEW, 160, engine=engine,
+                                             name=f"config1[{engine}]")
     assert worst >= 0.9999, worst
     assert bool(agree[decided].all()), (agree.logical_not() & decided).nonzero()
-    golden = np.load("tests/golden/oracle_config1.npz")
-    same = (np.array(ids) == golden["ids"]).mean()
-    print(f"config1 [{engine}]: worst corr {worst:.6f}, decided {int(decided.sum())}/{len(decided)}, "
-          f"free-running ids equal to golden: {same:.3f}")
+    # free-running greedy ids equal the oracle's own free-running sequence (golden) up to
+    # the first generated position whose top-2 margin is within 2 bf16 ulps (a tie there
+    # may go either way); the teacher-forced oracle logits equal the golden run's up to
+    # the first differing token, so their margins decide
+    golden = np.load(os.path.join(os.path.dirname(__file__), "golden", "oracle_config1.npz"))
+    gen_decided = decided[len(prompt) - 1:].tolist()
+    upto = gen_decided.index(False) if False in gen_decided else CONFIG1_NEW
+    assert ids[:upto] == golden["ids"][:upto].tolist(), (ids, golden["ids"].tolist())
+    print(f"config1 [{engine}]: free-running ids equal to the golden sequence over "
+          f"{upto}/{CONFIG1_NEW} positions ({'no' if upto == CONFIG1_NEW else 'first'} undecided "
+          f"position{'' if upto == CONFIG1_NEW else ' at ' + str(upto)})")
 
 
 @pytest.mark.parametrize("engine", ["step", "ops"])
@@ -130,7 +156,7 @@ def test_real_layer_shapes_two_layers():
                       vocab_size=16384)
     params = random_params(cfg, 3)
     prompt = [int(t) for t in torch.randint(0, cfg.vocab_size, (6,), generator=torch.Generator().manual_seed(3))]
-    worst, agree, decided, _, _ = _compare(cfg, params, prompt, 4, 64)
+    worst, agree, decided, _, _ = _compare(cfg, params, prompt, 4, 64, name="two_layer_real_shapes")
     assert worst >= 0.9999, worst
     assert bool(agree[decided].all())
 
@@ -155,6 +181,10 @@ def test_engine_generate_protocol():
     assert cut == toks[: toks.index(stop) + 1]
     with pytest.raises(ValueError):
         list(eng.generate(list(range(96)), 4, temperature=0.0))
+    # every generated token (the prefill's and each decode step's) is the oracle's
+    # argmax given the same history, wherever the oracle's top-2 margin is decided
     o = Oracle(cfg, params, mode="bf16")
-    ref, _ = o.greedy_generate(prompt, 12, 96, teacher=toks)
-    assert corr(ref[-1], ref[-1]) == 1.0
+    ref, ref_ids = o.greedy_generate(prompt, 12, 96, teacher=toks)
+    dec = decided_mask(ref[len(prompt) - 1:])
+    assert len(ref_ids) == len(toks) == 12
+    assert all(a == b for a, b, d in zip(toks, ref_ids, dec.tolist()) if d), (toks, ref_ids)
