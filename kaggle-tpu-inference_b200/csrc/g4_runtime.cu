@@ -20,17 +20,12 @@
 #include <string>
 #include <vector>
 
-#include "g4_attention.cuh"
-#include "g4_ops.cuh"
-#include "g4_sample.cuh"
-#include "g4_step.cuh"
-
-using namespace g4;
+#include "g4_internal.h"
 
 // ------------------------------------------------------------------ errors
 static thread_local std::string g_last_error;
 
-static int fail(int code, const char* fmt, ...) {
+int g4_fail(int code, const char* fmt, ...) {
   char buf[512];
   va_list ap;
   va_start(ap, fmt);
@@ -39,14 +34,6 @@ static int fail(int code, const char* fmt, ...) {
   g_last_error = buf;
   return code;
 }
-
-#define G4_CUDA(call, code)                                                              \
-  do {                                                                                   \
-    cudaError_t e_ = (call);                                                             \
-    if (e_ != cudaSuccess)                                                               \
-      return fail(code, "%s failed: %s (%s:%d)", #call, cudaGetErrorString(e_), __FILE__, \
-                  __LINE__);                                                             \
-  } while (0)
 
 extern "C" const char* g4_version(void) { return "g4b200 0.1 sm_100a"; }
 
@@ -65,16 +52,6 @@ extern "C" const char* g4_strerror(int code) {
 }
 
 extern "C" const char* g4_last_error(void) { return g_last_error.c_str(); }
-
-// ------------------------------------------------------------------ communicator
-struct g4_comm {
-  int device = 0, rank = 0, world = 1, hidden = 0;
-  size_t bytes = 0;
-  char* local = nullptr;
-  char* peer[kMaxWorld] = {};
-  bool mapped[kMaxWorld] = {};
-  bool open = false;
-};
 
 static size_t comm_bytes(int hidden) {
   return (size_t)kXFlagBytes + (size_t)kSites * 2 * kMaxWorld * (2 * (size_t)hidden) * 4;
@@ -136,23 +113,6 @@ extern "C" int g4_comm_destroy(g4_comm* c) {
   if (c->local) cudaFree(c->local);
   delete c;
   return G4_OK;
-}
-
-// ------------------------------------------------------------------ launch helper
-template <class Kernel, class... Args>
-static cudaError_t launch_pdl(Kernel k, dim3 grid, dim3 block, size_t smem, cudaStream_t st,
-                              Args... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = st;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, k, args...);
 }
 
 template <class Op, int CPLM>
@@ -246,14 +206,14 @@ static int launch_attention(const AttnArgs& a, cudaStream_t st) {
   return G4_OK;
 }
 
-static void rope_inv_freq(int d, double theta, double partial, float* out) {
+void g4_rope_inv_freq(int d, double theta, double partial, float* out) {
   // model.py:54-61: fp64 inverse frequencies for the rotated pairs, zero (NoPE) tail
   const int nrot = (int)(partial * d / 2);
   for (int i = 0; i < d / 2; ++i)
     out[i] = i < nrot ? (float)(1.0 / std::pow(theta, (double)(2 * i) / (double)d)) : 0.0f;
 }
 
-static float host_bf16_round(float f) {
+float g4_host_bf16_round(float f) {
   uint32_t u;
   memcpy(&u, &f, 4);
   u += 0x7fffu + ((u >> 16) & 1u);
@@ -286,60 +246,6 @@ static int pick_nsplit(int n_kv, int max_live, int nsm) {
   if (ns > kAttnMaxSplit) ns = kAttnMaxSplit;
   return ns;
 }
-
-// ------------------------------------------------------------------ model
-struct LayerDev {
-  bool full = false;
-  int d = 0, n_kv = 0, g = 0, rows_q = 0, rows_k = 0, rows_v = 0, k_eq_v = 0, nsplit = 1;
-  bf16_t *qkv = nullptr, *o = nullptr, *gate = nullptr, *up = nullptr, *down = nullptr;
-  bf16_t *router = nullptr, *router_scale = nullptr, *pes = nullptr, *exp_gu = nullptr,
-         *exp_down = nullptr;
-  bf16_t *n_in = nullptr, *n_post_attn = nullptr, *n_pre_ff = nullptr, *n_post_ff = nullptr,
-         *n_pre_ff2 = nullptr, *n_post_ff1 = nullptr, *n_post_ff2 = nullptr;
-  bf16_t *q_norm = nullptr, *k_norm = nullptr, *scalar = nullptr;
-  bf16_t *cache_k = nullptr, *cache_v = nullptr;
-};
-
-struct g4_model {
-  g4_config cfg{};
-  std::vector<unsigned char> is_full;
-  int rank = 0, world = 1, max_len = 0, device = 0, nsm = 148;
-  int H = 0, I_local = 0, F_local = 0, V_local = 0, vbegin = 0, E = 0, topk = 0;
-  std::vector<LayerDev> L;
-  bf16_t *embed = nullptr, *final_norm = nullptr;
-  int *ctrl = nullptr, *tokens_in = nullptr, *tokens_out = nullptr;
-  float* logits = nullptr;
-  g4_comm* comm = nullptr;
-  g4_comm* own_comm = nullptr;  // world == 1 without an attached communicator
-  // library scratch
-  char* scratch = nullptr;
-  bf16_t *xres, *resmid, *h2, *qkv_raw, *ctx, *mlp_act, *moe_act, *moe_out;
-  float *o_out, *mlp_out, *router_logits, *top_w, *attn_part, *cand_v, *samp_v;
-  int *top_idx, *attn_cnt, *cand_i, *counters, *samp_i;
-  bool finalized = false;
-  // plans
-  std::vector<QkvOp> k1;
-  std::vector<AttnArgs> k2;
-  std::vector<OProjOp> k3;
-  std::vector<RouterMlpOp> k4;
-  std::vector<MoeUpOp> k5;
-  std::vector<MoeDownOp> k6;
-  LmHeadOp lm{};
-  SampleArgs sampler{};  // temperature > 0: replaces the greedy token after the LM head
-  int sample_ctas = 0;
-  // persistent step kernel
-  int engine = G4_ENGINE_STEP_KERNEL;
-  StepProgram prog{};
-  int step_cplm = 0;
-  const void* step_kernel = nullptr;
-  char* prog_mem = nullptr;  // device copies of the operator plans
-  bool prog_dirty = true;    // host plans changed since the last upload
-  int* sync = nullptr;       // kNumSyncWords (library scratch)
-  float* rope_tab = nullptr;
-  int* tokens_host = nullptr;  // mapped pinned mirror of tokens_out (g4_model_host_tokens)
-  cudaGraph_t graph = nullptr;
-  cudaGraphExec_t gexec = nullptr;
-};
 
 static bool valid_cfg(const g4_config* c) {
   return c && c->hidden_size > 0 && c->num_hidden_layers > 0 && c->num_attention_heads > 0 &&
@@ -822,7 +728,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
   // ---- plans
   const g4_config& c = m->cfg;
   const int nl = (int)m->L.size();
-  const float hinv = host_bf16_round(std::pow((float)H, -0.5f));
+  const float hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
   m->k1.resize(nl);
   m->k2.resize(nl);
   m->k3.resize(nl);
@@ -854,7 +760,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     a.tokens_out = m->tokens_out;
     a.vocab = c.vocab_size;
     a.max_len = m->max_len;
-    a.embed_scale = host_bf16_round(std::sqrt((float)H));
+    a.embed_scale = g4_host_bf16_round(std::sqrt((float)H));
 
     AttnArgs& t = m->k2[i];
     t = AttnArgs{};
@@ -1028,8 +934,8 @@ extern "C" int g4_model_finalize(g4_model* m) {
   {
     const int dsl = c.head_dim, dfu = c.global_head_dim;
     std::vector<float> tab(dsl / 2 + dfu / 2);
-    rope_inv_freq(dsl, c.rope_theta_sliding, 1.0, tab.data());
-    rope_inv_freq(dfu, c.rope_theta_full, c.rope_partial_rotary_factor_full, tab.data() + dsl / 2);
+    g4_rope_inv_freq(dsl, c.rope_theta_sliding, 1.0, tab.data());
+    g4_rope_inv_freq(dfu, c.rope_theta_full, c.rope_partial_rotary_factor_full, tab.data() + dsl / 2);
     float* dev = nullptr;
     if (cudaMalloc(&dev, tab.size() * 4) != cudaSuccess) return fail(G4_ERR_NOMEM, "rope table");
     cudaMemcpy(dev, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice);
@@ -1051,13 +957,13 @@ static int sample_smem(const g4_model* m) {
   return std::max(kSampleChunk * 8, n * 8);
 }
 
-static int prepare_sampler(const g4_model* m) {
+int g4_prepare_sampler(const g4_model* m) {
   G4_CUDA(cudaFuncSetAttribute(sample_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, sample_smem(m)),
           G4_ERR_LAUNCH);
   return G4_OK;
 }
 
-static int launch_sampler(const g4_model* m, cudaStream_t st) {
+int g4_launch_sampler(const g4_model* m, cudaStream_t st) {
   cudaError_t e = launch_pdl(sample_kernel, dim3(m->sample_ctas), dim3(kSampleThreads), sample_smem(m), st,
                              m->sampler);
   if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "sampler launch: %s", cudaGetErrorString(e));
@@ -1078,7 +984,7 @@ static int prepare_op(const Op& op) {
 
 static int prepare_all(g4_model* m) {
   int rc;
-  if ((rc = prepare_sampler(m))) return rc;
+  if ((rc = g4_prepare_sampler(m))) return rc;
   if (m->engine == G4_ENGINE_STEP_KERNEL) return prepare_step(m);
   for (size_t i = 0; i < m->L.size(); ++i) {
     if ((rc = prepare_op(m->k1[i])) || (rc = prepare_op(m->k3[i])) || (rc = prepare_op(m->k4[i])) ||
@@ -1093,7 +999,7 @@ static int enqueue_step(g4_model* m, cudaStream_t st) {
   int rc;
   if (m->engine == G4_ENGINE_STEP_KERNEL) {
     if ((rc = launch_step(m, st))) return rc;
-    return launch_sampler(m, st);
+    return g4_launch_sampler(m, st);
   }
   const int nl = (int)m->L.size();
   for (int i = 0; i < nl; ++i) {
@@ -1105,7 +1011,7 @@ static int enqueue_step(g4_model* m, cudaStream_t st) {
     if ((rc = launch_gemv(m->k6[i], m->nsm, st))) return rc;
   }
   if ((rc = launch_gemv(m->lm, m->nsm, st))) return rc;
-  return launch_sampler(m, st);
+  return g4_launch_sampler(m, st);
 }
 
 extern "C" int g4_model_host_tokens(g4_model* m, int** host_ptr) {
@@ -1329,6 +1235,7 @@ extern "C" int g4_model_destroy(g4_model* m) {
   cudaSetDevice(m->device);
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   if (m->graph) cudaGraphDestroy(m->graph);
+  g4_prefill_release(m);
   if (m->rope_tab) cudaFree(m->rope_tab);
   if (m->prog_mem) cudaFree(m->prog_mem);
   if (m->tokens_host) cudaFreeHost(m->tokens_host);
@@ -1413,7 +1320,7 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   float* inv = reinterpret_cast<float*>(s + kBlockInvFreq);
   a.part = reinterpret_cast<float*>(s + kBlockPartOffset);
   std::vector<float> tab(head_dim / 2);
-  rope_inv_freq(head_dim, theta, partial_rotary, tab.data());
+  g4_rope_inv_freq(head_dim, theta, partial_rotary, tab.data());
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   G4_CUDA(cudaMemcpyAsync(inv, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st), G4_ERR_CUDA);
   G4_CUDA(cudaStreamSynchronize(st), G4_ERR_CUDA);
@@ -1529,7 +1436,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   r.top_w = tw;
   r.E = E;
   r.topk = K;
-  r.hinv = host_bf16_round(std::pow((float)H, -0.5f));
+  r.hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
 
   MoeUpOp u{};
   u.trace_id = -1;
@@ -1686,7 +1593,7 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   // zeroed and this call's RoPE table written, by one small kernel on the same stream.
   NoAllocSetup setup;
   setup.n_inv = head_dim / 2;
-  rope_inv_freq(head_dim, theta, partial_rotary, setup.inv_freq);
+  g4_rope_inv_freq(head_dim, theta, partial_rotary, setup.inv_freq);
   noalloc_setup_kernel<<<1, 256, 0, st>>>(setup, s);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   AttnArgs a{};
