@@ -275,6 +275,17 @@ def tokens_check(generated, prompt, cfg, args, world, rank, local, dev):
         diff = (ref != got).nonzero()
         out["world1_equal_prefix"] = int(diff[0, 0]) if len(diff) else int(got.numel())
         out["world1_identical"] = not len(diff)
+        if len(diff):
+            # the world-1 logits of the step that produced the first differing token: its
+            # top-2 margin in bf16 ulps of the top logit (<= ~2: a tie that either order of
+            # the partial sums may break differently)
+            j = int(diff[0, 0])
+            m1.reset(prompt, write_logits=True)
+            m1.step(len(prompt) + j)
+            torch.cuda.synchronize(dev)
+            top2 = torch.topk(m1.logits.float(), 2).values.cpu()
+            ulp = float(top2[0].abs()) * 2.0 ** -7
+            out["divergence_top2_margin_ulps"] = float(top2[0] - top2[1]) / max(ulp, 1e-30)
         m1.close()
         del one, m1
         torch.cuda.empty_cache()

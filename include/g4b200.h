@@ -151,6 +151,26 @@ int g4_model_kernel_count(const g4_model* model); /* kernels launched per step *
 #define G4_ENGINE_STEP_KERNEL 0
 #define G4_ENGINE_OP_KERNELS 1
 int g4_model_set_engine(g4_model* model, int engine);
+/* g4_prefill: the prompt tokens_in[0, n_tokens) through the whole model on the tensor
+ * cores -- the reference's jitted prefill step (engine.py:57-69: model.forward with
+ * dense_moe=True and last_index = n_tokens - 1, model.py:333-386) -- in chunks of at most
+ * `chunk` tokens (0: 4096; rounded up to a multiple of 128; a chunk attends to the cache
+ * rows of all earlier chunks).  Writes K/V cache rows [0, n_tokens) of every layer, the
+ * fp32 logits of position n_tokens - 1 ("logits"), tokens_out[n_tokens] (greedy, or the
+ * sample when control[TEMPERATURE] > 0) and sets control[POS] = n_tokens, so the next
+ * g4_step continues the sequence.  The caller sets control[FORCED_LEN] = n_tokens (the
+ * prompt).  Allocates a workspace on first use (grown for a larger chunk; freed by
+ * g4_model_destroy).  world > 1: G4_ERR_SHAPE (tensor-parallel prefill is not built;
+ * consume the prompt with g4_step instead). */
+int g4_prefill(g4_model* model, int n_tokens, int chunk, void* stream);
+/* g4_gemm_bf16: C[M, N] = A[M, K] . B[N, K]^T on the tensor cores (tcgen05, TMEM accumulator,
+ * TMA-fed), bf16 operands with row strides lda / ldb (elements, multiples of 8; 16-byte
+ * aligned bases), fp32 accumulation, C in fp32 (c_f32 != 0) or rounded to bf16, row stride
+ * ldc.  The GEMM every prefill contraction runs on (the jnp.einsum calls of model.py
+ * inside the jitted prefill step, engine.py:57-69).  status: optional int* (device) that
+ * receives G4_STATUS_MBAR_TIMEOUT if a bounded wait gives up. */
+int g4_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M, int N,
+                 int K, int c_f32, int* status, void* stream);
 /* Mapped pinned host mirror (int32[max_len+1]) of tokens_out, written by each step's
  * last kernel; lets the host read token i after step i's event without a copy that
  * would queue behind later steps (engine.py:196-200 lookahead read).  Call after

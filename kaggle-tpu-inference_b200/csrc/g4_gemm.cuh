@@ -55,6 +55,8 @@ struct GemmArgs {
   int band;              // 0 none; 1 scores (rows = queries, cols = keys); 2 P.V (K = keys)
   int q_pos0, key_pos0;  // absolute positions of row 0 / of column or K index 0
   int window;            // sliding window (0: causal only)
+  int a_row0, a_col0;    // constant coordinate offsets of A and B (e.g. the first key row)
+  int b_row0, b_col0;
   int* status;           // error bits (bounded waits)
 };
 
@@ -228,9 +230,9 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   if (warp == 0) {
     if (lane == 0 && has_k) {
-      const int arow = z * a.za_row + m0, acol0 = z * a.za_col;
+      const int arow = a.a_row0 + z * a.za_row + m0, acol0 = a.a_col0 + z * a.za_col;
       const int zb = z / a.zb_div;
-      const int brow = zb * a.zb_row + n0, bcol0 = zb * a.zb_col;
+      const int brow = a.b_row0 + zb * a.zb_row + n0, bcol0 = a.b_col0 + zb * a.zb_col;
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
         const int s = i % STAGES;
         if (i >= STAGES && !gemm_wait(&empty[s], ((i / STAGES) - 1) & 1, a.status, abort)) break;

@@ -1,0 +1,732 @@
+// Prompt prefill on the tensor cores: the reference's jitted prefill step
+// (gemma4_tpu/engine.py:57-69), i.e. model.forward over the prompt with dense_moe=True and
+// last_index = prompt_len - 1 (model.py:333-386), then the first token's sample.
+//
+// The prompt runs in chunks of up to `chunk` tokens through all layers (a chunk attends to
+// the cache rows of every earlier chunk, so the result does not depend on the chunking).
+// Every contraction is one tcgen05 GEMM (g4_gemm.cuh); the vector work between them --
+// RMSNorms, RoPE, cache writes, the masked softmax, GELU gating, router softmax / top-k,
+// the MLP || MoE combine -- is a row-parallel kernel here, with the reference's rounding
+// points (every einsum output rounded to bf16 after fp32 accumulation, fp32 norms and
+// softmax, bf16 probabilities, bf16 elementwise products):
+//
+//   x = embed[tok] * bf16(sqrt(H))                                   model.py:356-357
+//   per layer:  xn = rms(x)*w_in; qkv = xn Wqkv^T                     :299, :197-199
+//               q = rope(rms(q)*q_norm) ; k -> cache, v = rms(v) -> cache   :198-206
+//               S_h = q_h K^T (bf16), band mask, fp32 softmax -> P_h (bf16)  :208-211
+//               ctx_h = P_h V ; o = ctx Wo^T                          :212-213
+//               x += rms(o)*w_pa ; MLP: down(gelu(gate)*up)           :300-310, :218-221
+//               router: softmax, top-k, renorm, x per_expert_scale    :224-232
+//               dense MoE: act[t,e,f] = gelu(g)*u*w[t,e] over ALL experts (w = 0 off
+//               the top-k) ; out = sum_{e,f} act * down  (ONE GEMM, 3-D B)   :241-250
+//               x = (x + rms(rms(mlp)*pf1 + rms(moe)*pf2)*pf) * layer_scalar  :312-322
+//   last row:   rms(x)*norm ; logits = x E^T (bf16) ; softcap ; argmax / sample  :373-385
+//
+// Tensor-parallel prefill (world > 1) is not built: g4_prefill returns G4_ERR_SHAPE and
+// the caller consumes the prompt with decode steps instead.
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <map>
+#include <mutex>
+
+#include "g4_gemm.cuh"
+#include "g4_internal.h"
+
+namespace {
+
+constexpr int kRowThreads = 256;
+constexpr int kMaxRowElems = kMaxHidden / kRowThreads;  // per-thread elements of a hidden row
+
+// ------------------------------------------------------------------ row helpers
+// Sum of v over the block (kRowThreads threads), fixed order, identical on every thread.
+__device__ __forceinline__ float row_sum(float v, float* red) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  v = warp_sum(v);
+  __syncthreads();  // earlier users of red are done
+  if (lane == 0) red[warp] = v;
+  __syncthreads();
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < kRowThreads / 32; ++i) s += red[i];
+  return s;
+}
+
+// Elements h = threadIdx.x + 256 i of a bf16 row into registers (0 beyond n).
+__device__ __forceinline__ void load_row(const bf16_t* src, int n, float (&v)[kMaxRowElems]) {
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    v[i] = h < n ? bf2f(src[h]) : 0.f;
+  }
+}
+
+// 1 / sqrt(mean(v^2) + eps) of a register row (model.py:42-47, fp32).
+__device__ __forceinline__ float row_rms(const float (&v)[kMaxRowElems], int n, float eps, float* red) {
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) ss += v[i] * v[i];
+  return 1.0f / sqrtf(row_sum(ss, red) / (float)n + eps);
+}
+
+// ------------------------------------------------------------------ kernels
+// x[t] = bf16(embed[token] * scale) for the chunk's tokens (model.py:356-357).
+__global__ void pf_embed(const int* tokens, const bf16_t* embed, bf16_t* x, int H, int V, float scale, int* ctrl) {
+  const int t = blockIdx.x;
+  int tok = tokens[t];
+  if (tok < 0 || tok >= V) {
+    if (threadIdx.x == 0) atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_BAD_TOKEN);
+    tok = 0;
+  }
+  for (int h = threadIdx.x; h < H; h += blockDim.x)
+    x[(size_t)t * H + h] = f2bf(bf2f(embed[(size_t)tok * H + h]) * scale);
+}
+
+// out[t] = bf16(rms(x[t]) * w)
+__global__ void pf_rmsnorm(const bf16_t* x, const bf16_t* w, bf16_t* out, int H, float eps) {
+  __shared__ float red[32];
+  const size_t row = (size_t)blockIdx.x * H;
+  float v[kMaxRowElems];
+  load_row(x + row, H, v);
+  const float r = row_rms(v, H, eps, red);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    if (h < H) out[row + h] = f2bf((v[i] * r) * bf2f(w[h]));
+  }
+}
+
+// q heads: rope(bf16(rms(q) * q_norm)) -> q buffer [T, nq * d]; k: the same with k_norm
+// -> cache_k[pos]; v: bf16(rms(v_raw)) (k_raw on k==v layers) -> cache_v[pos]
+// (model.py:197-206).  One warp per (token, vector); D / 32 elements per lane.
+template <int D>
+__global__ void pf_qk_rope(const bf16_t* qkv, int rows, bf16_t* qbuf, const bf16_t* q_norm, const bf16_t* k_norm,
+                           bf16_t* cache_k, bf16_t* cache_v, const float* inv_freq, int nq, int n_kv, int k_eq_v,
+                           int pos0, int M, float eps) {
+  constexpr int PER = D / 32;
+  const int lane = threadIdx.x & 31;
+  const int gw = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int nvec = nq + 2 * n_kv;
+  if (gw >= M * nvec) return;
+  const int t = gw / nvec, vi = gw % nvec;
+  const int pos = pos0 + t;
+  const bf16_t* row = qkv + (size_t)t * rows;
+  const bf16_t* src;
+  int kind;  // 0 q, 1 k, 2 v
+  if (vi < nq) {
+    src = row + (size_t)vi * D;
+    kind = 0;
+  } else if (vi < nq + n_kv) {
+    src = row + (size_t)nq * D + (size_t)(vi - nq) * D;
+    kind = 1;
+  } else {
+    const int h = vi - nq - n_kv;
+    src = k_eq_v ? row + (size_t)nq * D + (size_t)h * D : row + (size_t)(nq + n_kv) * D + (size_t)h * D;
+    kind = 2;
+  }
+  float v[PER];
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    v[i] = bf2f(src[lane + 32 * i]);
+    ss += v[i] * v[i];
+  }
+  ss = warp_sum(ss);
+  const float r = 1.0f / sqrtf(ss / (float)D + eps);
+#pragma unroll
+  for (int i = 0; i < PER; ++i) {
+    float o = v[i] * r;
+    if (kind == 0) o = o * bf2f(q_norm[lane + 32 * i]);
+    else if (kind == 1) o = o * bf2f(k_norm[lane + 32 * i]);
+    v[i] = rbf(o);
+  }
+  if (kind < 2) {  // rotate-half RoPE with bf16-rounded cos / sin (model.py:64-78)
+    float out[PER];
+#pragma unroll
+    for (int i = 0; i < PER; ++i) {
+      const int f = (lane + 32 * i) % (D / 2);
+      float sn, cs;
+      sincosf((float)pos * inv_freq[f], &sn, &cs);
+      const float rot = i < PER / 2 ? -v[i + PER / 2] : v[i - PER / 2];
+      out[i] = rbf(rbf(v[i] * rbf(cs)) + rbf(rot * rbf(sn)));
+    }
+#pragma unroll
+    for (int i = 0; i < PER; ++i) v[i] = out[i];
+  }
+  bf16_t* dst;
+  if (kind == 0) dst = qbuf + (size_t)t * nq * D + (size_t)vi * D;
+  else if (kind == 1) dst = cache_k + ((size_t)pos * n_kv + (vi - nq)) * D;
+  else dst = cache_v + ((size_t)pos * n_kv + (vi - nq - n_kv)) * D;
+#pragma unroll
+  for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = f2bf(v[i]);
+}
+
+// Vt[h][j][key - lo] = cache_v[key][h][j] for keys [lo, lo + span): V transposed so that
+// the P.V product reads it K-major.  32 x 32 tiles through shared memory.
+__global__ void pf_vtrans(const bf16_t* cache_v, bf16_t* vt, int lo, int span, int n_kv, int d, int ld) {
+  __shared__ bf16_t tile[32][34];
+  const int h = blockIdx.z;
+  const int k0 = blockIdx.x * 32, j0 = blockIdx.y * 32;
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int key = k0 + r, j = j0 + threadIdx.x;
+    tile[r][threadIdx.x] = key < span ? cache_v[((size_t)(lo + key) * n_kv + h) * d + j] : (bf16_t)0;
+  }
+  __syncthreads();
+  for (int r = threadIdx.y; r < 32; r += blockDim.y) {
+    const int j = j0 + r, key = k0 + threadIdx.x;
+    if (key < span) vt[((size_t)h * d + j) * ld + key] = tile[threadIdx.x][r];
+  }
+}
+
+// Masked softmax of one score row in place (model.py:209-211): keys at key_pos0 + j valid
+// for query q = q_pos0 + m when key <= q and (window == 0 or key > q - window); fp32 softmax
+// of the bf16 scores over the valid keys (a masked key's exp(-1e30 - max) is exactly 0),
+// probabilities rounded to bf16; every column the P.V product reads for this row's tile
+// ([j0, j1), the same band arithmetic as gemm_tile_range) gets a value, zero if masked.
+__global__ void pf_softmax(bf16_t* sp, int M, int ld, int span, int q_pos0, int key_pos0, int window) {
+  __shared__ float red[32];
+  const int h = blockIdx.x / M, m = blockIdx.x % M;
+  bf16_t* row = sp + ((size_t)h * M + m) * ld;
+  const int q = q_pos0 + m;
+  const int m0 = (m / kGemmBM) * kGemmBM;
+  const int qlo = q_pos0 + m0, qhi = q_pos0 + min(m0 + kGemmBM, M) - 1;
+  const int jlo = max((window > 0 ? qlo - window + 1 : 0) - key_pos0, 0);
+  const int jhi = min(qhi - key_pos0 + 1, span);
+  const int j0 = (jlo / kGemmBK) * kGemmBK, j1 = min((jhi + kGemmBK - 1) / kGemmBK * kGemmBK, span);
+  const int vlo = max((window > 0 ? q - window + 1 : 0) - key_pos0, 0), vhi = min(q - key_pos0 + 1, span);
+  float mx = -INFINITY;
+  for (int j = vlo + threadIdx.x; j < vhi; j += blockDim.x) mx = fmaxf(mx, bf2f(row[j]));
+  mx = warp_max(mx);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = mx;
+  __syncthreads();
+  mx = -INFINITY;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) mx = fmaxf(mx, red[i]);
+  float s = 0.f;
+  for (int j = vlo + threadIdx.x; j < vhi; j += blockDim.x) s += expf(bf2f(row[j]) - mx);
+  s = row_sum(s, red);
+  for (int j = j0 + threadIdx.x; j < j1; j += blockDim.x) {
+    const float p = (j >= vlo && j < vhi) ? expf(bf2f(row[j]) - mx) / s : 0.f;
+    row[j] = f2bf(p);
+  }
+}
+
+// After attention (model.py:300-316, one row per CTA): x = x + rms(o) * w_pa (the residual,
+// in place); mlp_in = rms(x) * w_pff; h2 = rms(x) * w_pff2 (the MoE input); router input
+// rin = rms(h2) * router.scale * bf16(H^-1/2), each product rounded to bf16 (:225-226).
+__global__ void pf_post_attn(const bf16_t* o, bf16_t* x, const bf16_t* w_pa, const bf16_t* w_pff,
+                             const bf16_t* w_pff2, const bf16_t* rscale, bf16_t* mlp_in, bf16_t* h2, bf16_t* rin,
+                             int H, float eps, float hinv) {
+  __shared__ float red[32];
+  const size_t row = (size_t)blockIdx.x * H;
+  float v[kMaxRowElems], t[kMaxRowElems];
+  load_row(o + row, H, v);
+  const float r = row_rms(v, H, eps, red);
+  load_row(x + row, H, t);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    t[i] = h < H ? rbf(t[i] + rbf((v[i] * r) * bf2f(w_pa[h]))) : 0.f;
+    if (h < H) x[row + h] = f2bf(t[i]);
+  }
+  const float r2 = row_rms(t, H, eps, red);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    if (h < H) {
+      mlp_in[row + h] = f2bf((t[i] * r2) * bf2f(w_pff[h]));
+      v[i] = rbf((t[i] * r2) * bf2f(w_pff2[h]));
+      h2[row + h] = f2bf(v[i]);
+    } else {
+      v[i] = 0.f;
+    }
+  }
+  const float r3 = row_rms(v, H, eps, red);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    if (h < H) rin[row + h] = f2bf(rbf(rbf(v[i] * r3) * bf2f(rscale[h])) * hinv);
+  }
+}
+
+// act = bf16(bf16(gelu(gate)) * up) (model.py:221)
+__global__ void pf_gelu_mul(const bf16_t* gate, const bf16_t* up, bf16_t* act, size_t n) {
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x)
+    act[i] = f2bf(rbf(gelu_tanh(bf2f(gate[i]))) * bf2f(up[i]));
+}
+
+// Router of one token (model.py:227-232): fp32 softmax of the bf16 logits, top-k by
+// probability (ties to the lower expert), renormalised, times per_expert_scale -> the
+// dense per-expert weight row (0 off the top-k, the one-hot einsum of :243-245).
+// Expert e on thread e; sums in expert / rank order (the decode router's arithmetic).
+__global__ void pf_router(const bf16_t* logits, const bf16_t* pes, float* wfull, int E, int K) {
+  __shared__ float pv[256];
+  __shared__ float top_p[kMaxTopK];
+  const int t = threadIdx.x;
+  const bf16_t* lrow = logits + (size_t)blockIdx.x * E;
+  const float l = t < E ? bf2f(lrow[t]) : -INFINITY;
+  if (t < E) pv[t] = l;
+  __syncthreads();
+  float mx = -INFINITY;
+  for (int j = 0; j < E; ++j) mx = fmaxf(mx, pv[j]);
+  const float ex = t < E ? expf(l - mx) : 0.f;
+  __syncthreads();
+  if (t < E) pv[t] = ex;
+  __syncthreads();
+  float sum = 0.f;
+  for (int j = 0; j < E; ++j) sum += pv[j];
+  const float p = ex / sum;
+  __syncthreads();
+  if (t < E) pv[t] = p;
+  __syncthreads();
+  int rank = 0;
+  for (int j = 0; j < E; ++j) {
+    const float q = pv[j];
+    rank += (q > p || (q == p && j < t)) ? 1 : 0;
+  }
+  const bool sel = t < E && rank < K;
+  if (sel) top_p[rank] = p;
+  __syncthreads();
+  if (t < E) {
+    float w = 0.f;
+    if (sel) {
+      float wsum = 0.f;
+      for (int k = 0; k < K; ++k) wsum += top_p[k];
+      w = (p / wsum) * bf2f(pes[t]);
+    }
+    wfull[(size_t)blockIdx.x * E + t] = w;
+  }
+}
+
+// Dense-MoE activation (model.py:246-248): act[t, e, f] = bf16(bf16(bf16(gelu(g)) * u) *
+// bf16(w[t, e])) with g, u = gu[t, e, 0 / 1, f]; zero for experts off the top-k.
+__global__ void pf_moe_act(const bf16_t* gu, const float* wfull, bf16_t* act, int M, int E, int F) {
+  const size_t n = (size_t)M * E * F;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t t = i / ((size_t)E * F);
+    const int e = (int)((i / F) % E), f = (int)(i % F);
+    const float w = wfull[t * E + e];
+    const bf16_t* g = gu + t * (size_t)E * 2 * F + (size_t)e * 2 * F;
+    act[i] = w == 0.f ? (bf16_t)0 : f2bf(rbf(rbf(rbf(gelu_tanh(bf2f(g[f]))) * bf2f(g[F + f])) * rbf(w)));
+  }
+}
+
+// Layer output (model.py:312-322, one row per CTA): h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2,
+// h = rms(h1 + h2)*pf, x = (resid + h) * layer_scalar.
+__global__ void pf_combine(const bf16_t* mlp, const bf16_t* moe, bf16_t* x, const bf16_t* pf1, const bf16_t* pf2,
+                           const bf16_t* pf, const bf16_t* scalar, int H, float eps) {
+  __shared__ float red[32];
+  const size_t row = (size_t)blockIdx.x * H;
+  float a[kMaxRowElems], b[kMaxRowElems];
+  load_row(mlp + row, H, a);
+  load_row(moe + row, H, b);
+  const float r1 = row_rms(a, H, eps, red), r2 = row_rms(b, H, eps, red);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    a[i] = h < H ? rbf(rbf((a[i] * r1) * bf2f(pf1[h])) + rbf((b[i] * r2) * bf2f(pf2[h]))) : 0.f;
+  }
+  const float r3 = row_rms(a, H, eps, red);
+  const float sc = bf2f(scalar[0]);
+#pragma unroll
+  for (int i = 0; i < kMaxRowElems; ++i) {
+    const int h = threadIdx.x + kRowThreads * i;
+    if (h < H) x[row + h] = f2bf(rbf(rbf(bf2f(x[row + h]) + rbf((a[i] * r3) * bf2f(pf[h]))) * sc));
+  }
+}
+
+// LM-head epilogue of the prompt's last position (model.py:381-385 + the greedy branch of
+// :414-424): softcapped fp32 logits of this rank's vocab slice, first index of the maximum
+// -> tokens_out[n]; POS = n.  One CTA.
+__global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegin, float softcap, int* tokens_out,
+                               int* tokens_host, int* ctrl, int n) {
+  __shared__ float bv[32];
+  __shared__ int bi[32];
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int u = threadIdx.x; u < V; u += blockDim.x) {
+    float v = bf2f(lg[u]);
+    if (softcap > 0.f) v = tanhf(v / softcap) * softcap;
+    logits[u] = v;
+    if (v > best) {  // increasing u per thread: ties keep the lower index
+      best = v;
+      bidx = u;
+    }
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bidx, o);
+    if (ov > best || (ov == best && oi < bidx)) {
+      best = ov;
+      bidx = oi;
+    }
+  }
+  if ((threadIdx.x & 31) == 0) {
+    bv[threadIdx.x >> 5] = best;
+    bi[threadIdx.x >> 5] = bidx;
+  }
+  __syncthreads();
+  if (threadIdx.x != 0) return;
+  for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+    if (bv[w] > best || (bv[w] == best && bi[w] < bidx)) {
+      best = bv[w];
+      bidx = bi[w];
+    }
+  const int token = bidx == 0x7fffffff ? 0 : vbegin + bidx;
+  tokens_out[n] = token;
+  if (tokens_host) tokens_host[n] = token;
+  ctrl[G4_CTRL_POS] = n;
+}
+
+// ------------------------------------------------------------------ tensor maps
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// A K-major bf16 matrix [rows, inner] (row stride `ld` elements) read in boxes of 64
+// elements x box_rows rows with 128-byte swizzle; out-of-range elements read as zero.
+int make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t ld, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (ld * 2) % 16)
+    return fail(G4_ERR_ARG, "tensor map: base or row stride not 16-byte aligned");
+  const cuuint64_t dims[2] = {inner, rows};
+  const cuuint64_t strides[1] = {ld * 2};
+  const cuuint32_t box[2] = {(cuuint32_t)kGemmBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled (2-D) failed: %d", (int)r);
+  return G4_OK;
+}
+
+// A bf16 tensor [slabs, rows, inner] read in boxes of 64 x box_rows x 1.
+int make_map_3d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t slabs, uint32_t box_rows) {
+  auto fn = encode_fn();
+  if (!fn) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  if ((reinterpret_cast<uintptr_t>(base) & 15) || (inner * 2) % 16)
+    return fail(G4_ERR_ARG, "tensor map: base or row stride not 16-byte aligned");
+  const cuuint64_t dims[3] = {inner, rows, slabs};
+  const cuuint64_t strides[2] = {inner * 2, inner * rows * 2};
+  const cuuint32_t box[3] = {(cuuint32_t)kGemmBK, box_rows, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(G4_ERR_CUDA, "cuTensorMapEncodeTiled (3-D) failed: %d", (int)r);
+  return G4_OK;
+}
+
+// ------------------------------------------------------------------ GEMM launches
+struct Operand {
+  const void* p;
+  uint64_t inner, rows, ld;  // 2-D [rows, inner], row stride ld (elements)
+  uint64_t slabs = 0;        // > 0: 3-D [slabs, rows, inner], dense
+};
+
+int gemm_prepare(int bn) {
+  static std::mutex mu;
+  static std::map<std::pair<int, int>, bool> done;
+  int dev = 0;
+  cudaGetDevice(&dev);
+  std::lock_guard<std::mutex> lock(mu);
+  if (done[{dev, bn}]) return G4_OK;
+  const void* k = bn == 256 ? reinterpret_cast<const void*>(gemm_kernel<256>)
+                            : reinterpret_cast<const void*>(gemm_kernel<128>);
+  G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(bn)), G4_ERR_LAUNCH);
+  done[{dev, bn}] = true;
+  return G4_OK;
+}
+
+// C[z] (M x N) = A[z] (M x K) . B[z] (N x K)^T; `g` carries the shape, output and offsets.
+int gemm(const Operand& A, const Operand& B, GemmArgs g, int Z, cudaStream_t st) {
+  if (g.M <= 0 || g.N <= 0 || g.K <= 0 || Z <= 0) return G4_OK;
+  if (!g.zb_div) g.zb_div = 1;
+  const int bn = g.N <= 128 ? 128 : 256;
+  int rc = gemm_prepare(bn);
+  if (rc) return rc;
+  GemmParams P;
+  memset(&P, 0, sizeof(P));
+  if ((rc = make_map_2d(&P.ta, A.p, A.inner, A.rows, A.ld, kGemmBM))) return rc;
+  if (B.slabs) rc = make_map_3d(&P.tb, B.p, B.inner, B.rows, B.slabs, bn);
+  else rc = make_map_2d(&P.tb, B.p, B.inner, B.rows, B.ld, bn);
+  if (rc) return rc;
+  P.a = g;
+  const dim3 grid((g.N + bn - 1) / bn, (g.M + kGemmBM - 1) / kGemmBM, Z);
+  if (bn == 256)
+    gemm_kernel<256><<<grid, kGemmThreads, gemm_smem_bytes(256), st>>>(P);
+  else
+    gemm_kernel<128><<<grid, kGemmThreads, gemm_smem_bytes(128), st>>>(P);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+GemmArgs plain(int M, int N, int K, void* C, long long ldc, int* status) {
+  GemmArgs g{};
+  g.M = M;
+  g.N = N;
+  g.K = K;
+  g.C = C;
+  g.ldc = ldc;
+  g.zb_div = 1;
+  g.status = status;
+  return g;
+}
+
+size_t up256(size_t b) { return (b + 255) / 256 * 256; }
+
+}  // namespace
+
+// ------------------------------------------------------------------ workspace
+struct PrefillWs {
+  int chunk = 0, ks = 0;  // tokens per chunk; padded key capacity (row stride of scores)
+  char* base = nullptr;
+  bf16_t *x, *xn, *qkv, *q, *sp, *vt, *ctx, *o, *mlp_in, *h2, *rin, *gate, *up, *act, *mlp_out, *rlog, *gu, *mact,
+      *moe_out, *xf, *lmlog;
+  float* wfull;
+};
+
+void g4_prefill_release(g4_model* m) {
+  if (!m || !m->prefill) return;
+  if (m->prefill->base) cudaFree(m->prefill->base);
+  delete m->prefill;
+  m->prefill = nullptr;
+}
+
+static int prefill_workspace(g4_model* m, int chunk) {
+  if (m->prefill && m->prefill->chunk >= chunk) return G4_OK;
+  g4_prefill_release(m);
+  const int H = m->H, E = m->E, F = m->F_local, I = m->I_local;
+  size_t rmax = 0, qmax = 0, nqmax = 0, vtmax = 0;
+  for (const LayerDev& l : m->L) {
+    rmax = std::max(rmax, (size_t)(l.rows_q + l.rows_k + l.rows_v));
+    qmax = std::max(qmax, (size_t)l.rows_q);
+    nqmax = std::max(nqmax, (size_t)(l.n_kv * l.g));
+    vtmax = std::max(vtmax, (size_t)l.n_kv * l.d);
+  }
+  const size_t ks = ((size_t)m->max_len + 63) / 64 * 64;
+  const size_t C = chunk;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += up256(bytes);
+    return o;
+  };
+  const size_t o_x = take(C * H * 2), o_xn = take(C * H * 2), o_qkv = take(C * rmax * 2), o_q = take(C * qmax * 2),
+               o_sp = take(nqmax * C * ks * 2), o_vt = take(vtmax * ks * 2), o_ctx = take(C * qmax * 2),
+               o_o = take(C * H * 2), o_mi = take(C * H * 2), o_h2 = take(C * H * 2), o_rin = take(C * H * 2),
+               o_g = take(C * I * 2), o_u = take(C * I * 2), o_a = take(C * I * 2), o_mo = take(C * H * 2),
+               o_rl = take(C * E * 2), o_wf = take(C * E * 4), o_gu = take(C * (size_t)E * 2 * F * 2),
+               o_ma = take(C * (size_t)E * F * 2), o_moe = take(C * H * 2), o_xf = take((size_t)H * 2),
+               o_lm = take((size_t)m->V_local * 2);
+  PrefillWs* w = new PrefillWs();
+  if (cudaMalloc(&w->base, off) != cudaSuccess) {
+    delete w;
+    return fail(G4_ERR_NOMEM, "prefill workspace cudaMalloc(%zu) failed", off);
+  }
+  char* b = w->base;
+  w->chunk = chunk;
+  w->ks = (int)ks;
+  w->x = (bf16_t*)(b + o_x);
+  w->xn = (bf16_t*)(b + o_xn);
+  w->qkv = (bf16_t*)(b + o_qkv);
+  w->q = (bf16_t*)(b + o_q);
+  w->sp = (bf16_t*)(b + o_sp);
+  w->vt = (bf16_t*)(b + o_vt);
+  w->ctx = (bf16_t*)(b + o_ctx);
+  w->o = (bf16_t*)(b + o_o);
+  w->mlp_in = (bf16_t*)(b + o_mi);
+  w->h2 = (bf16_t*)(b + o_h2);
+  w->rin = (bf16_t*)(b + o_rin);
+  w->gate = (bf16_t*)(b + o_g);
+  w->up = (bf16_t*)(b + o_u);
+  w->act = (bf16_t*)(b + o_a);
+  w->mlp_out = (bf16_t*)(b + o_mo);
+  w->rlog = (bf16_t*)(b + o_rl);
+  w->wfull = (float*)(b + o_wf);
+  w->gu = (bf16_t*)(b + o_gu);
+  w->mact = (bf16_t*)(b + o_ma);
+  w->moe_out = (bf16_t*)(b + o_moe);
+  w->xf = (bf16_t*)(b + o_xf);
+  w->lmlog = (bf16_t*)(b + o_lm);
+  m->prefill = w;
+  return G4_OK;
+}
+
+static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, const float* inv, int pos0, int M, float eps,
+                          cudaStream_t st) {
+  const int nq = l.n_kv * l.g, rows = l.rows_q + l.rows_k + l.rows_v;
+  const long long warps = (long long)M * (nq + 2 * l.n_kv);
+  const dim3 grid((unsigned)((warps + 7) / 8));
+#define G4_QK(D)                                                                                              \
+  pf_qk_rope<D><<<grid, 256, 0, st>>>(qkv, rows, q, l.q_norm, l.k_norm, l.cache_k, l.cache_v, inv, nq, l.n_kv, \
+                                      l.k_eq_v, pos0, M, eps)
+  switch (l.d) {
+    case 64: G4_QK(64); break;
+    case 128: G4_QK(128); break;
+    case 256: G4_QK(256); break;
+    case 512: G4_QK(512); break;
+    default: return fail(G4_ERR_SHAPE, "prefill: head_dim %d", l.d);
+  }
+#undef G4_QK
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+// One chunk of `M` prompt tokens at positions [c0, c0 + M) through every layer.
+static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, cudaStream_t st) {
+  PrefillWs& w = *m->prefill;
+  const g4_config& c = m->cfg;
+  const int H = m->H, E = m->E, F = m->F_local, I = m->I_local, K = m->topk;
+  const float eps = c.rms_norm_eps;
+  int* status = m->ctrl + G4_CTRL_STATUS;
+  int rc;
+  pf_embed<<<M, 256, 0, st>>>(m->tokens_in + c0, m->embed, w.x, H, c.vocab_size,
+                              g4_host_bf16_round(std::sqrt((float)H)), m->ctrl);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  const float hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
+  for (size_t li = 0; li < m->L.size(); ++li) {
+    const LayerDev& l = m->L[li];
+    const AttnArgs& aa = m->k2[li];
+    const int nq = l.n_kv * l.g, d = l.d, R = l.rows_q + l.rows_k + l.rows_v;
+    // ---- attention (model.py:195-213)
+    pf_rmsnorm<<<M, kRowThreads, 0, st>>>(w.x, l.n_in, w.xn, H, eps);
+    if ((rc = gemm({w.xn, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.qkv, (uint64_t)H, (uint64_t)R, (uint64_t)H},
+                   plain(M, R, H, w.qkv, R, status), 1, st)))
+      return rc;
+    if ((rc = launch_qk_rope(l, w.qkv, w.q, aa.inv_freq, c0, M, eps, st))) return rc;
+    const int window = l.full ? 0 : c.sliding_window;
+    const int lo = window > 0 ? std::max(0, c0 - window + 1) : 0, span = c0 + M - lo;
+    {  // scores S_h = q_h . K^T, one z per query head (its KV head: z / g)
+      GemmArgs g = plain(M, span, d, w.sp, w.ks, status);
+      g.za_col = d;
+      g.zb_div = l.g;
+      g.zb_col = d;
+      g.b_row0 = lo;
+      g.zc_row = M;
+      g.band = 1;
+      g.q_pos0 = c0;
+      g.key_pos0 = lo;
+      g.window = window;
+      if ((rc = gemm({w.q, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
+                     {l.cache_k, (uint64_t)l.n_kv * d, (uint64_t)m->max_len, (uint64_t)l.n_kv * d}, g, nq, st)))
+        return rc;
+    }
+    pf_softmax<<<nq * M, 256, 0, st>>>(w.sp, M, w.ks, span, c0, lo, window);
+    pf_vtrans<<<dim3((span + 31) / 32, d / 32, l.n_kv), dim3(32, 8), 0, st>>>(l.cache_v, w.vt, lo, span, l.n_kv, d,
+                                                                              w.ks);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    {  // ctx_h = P_h . V (V^T rows per KV head)
+      GemmArgs g = plain(M, d, span, w.ctx, (long long)nq * d, status);
+      g.za_row = M;
+      g.zb_div = l.g;
+      g.zb_row = d;
+      g.zc_col = d;
+      g.band = 2;
+      g.q_pos0 = c0;
+      g.key_pos0 = lo;
+      g.window = window;
+      if ((rc = gemm({w.sp, (uint64_t)span, (uint64_t)nq * M, (uint64_t)w.ks},
+                     {w.vt, (uint64_t)span, (uint64_t)l.n_kv * d, (uint64_t)w.ks}, g, nq, st)))
+        return rc;
+    }
+    if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
+                   {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(M, H, nq * d, w.o, H, status), 1,
+                   st)))
+      return rc;
+    pf_post_attn<<<M, kRowThreads, 0, st>>>(w.o, w.x, l.n_post_attn, l.n_pre_ff, l.n_pre_ff2, l.router_scale,
+                                             w.mlp_in, w.h2, w.rin, H, eps, hinv);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    // ---- dense MLP (model.py:218-221)
+    if ((rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.gate, (uint64_t)H, (uint64_t)I, (uint64_t)H},
+                   plain(M, I, H, w.gate, I, status), 1, st)))
+      return rc;
+    if ((rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.up, (uint64_t)H, (uint64_t)I, (uint64_t)H},
+                   plain(M, I, H, w.up, I, status), 1, st)))
+      return rc;
+    pf_gelu_mul<<<std::min(4096, (M * I + 255) / 256), 256, 0, st>>>(w.gate, w.up, w.act, (size_t)M * I);
+    if ((rc = gemm({w.act, (uint64_t)I, (uint64_t)M, (uint64_t)I}, {l.down, (uint64_t)I, (uint64_t)H, (uint64_t)I},
+                   plain(M, H, I, w.mlp_out, H, status), 1, st)))
+      return rc;
+    // ---- router + dense MoE over all experts (model.py:224-250)
+    if ((rc = gemm({w.rin, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.router, (uint64_t)H, (uint64_t)E, (uint64_t)H},
+                   plain(M, E, H, w.rlog, E, status), 1, st)))
+      return rc;
+    pf_router<<<M, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
+    if ((rc = gemm({w.h2, (uint64_t)H, (uint64_t)M, (uint64_t)H},
+                   {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H},
+                   plain(M, E * 2 * F, H, w.gu, (long long)E * 2 * F, status), 1, st)))
+      return rc;
+    pf_moe_act<<<std::min(8192, (int)(((size_t)M * E * F + 255) / 256)), 256, 0, st>>>(w.gu, w.wfull, w.mact, M, E,
+                                                                                       F);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    {  // sum over (expert, f) in one GEMM: B = down [E, H, F] as 3-D (f, h, e)
+      const int kpe = (F + kGemmBK - 1) / kGemmBK;
+      GemmArgs g = plain(M, H, E * kpe * kGemmBK, w.moe_out, H, status);
+      g.b_kpe = kpe;
+      g.a_slab = F;
+      Operand B{l.exp_down, (uint64_t)F, (uint64_t)H, (uint64_t)F};
+      B.slabs = E;
+      if ((rc = gemm({w.mact, (uint64_t)E * F, (uint64_t)M, (uint64_t)E * F}, B, g, 1, st))) return rc;
+    }
+    pf_combine<<<M, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
+                                           l.scalar, H, eps);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  }
+  if (last) {  // final norm, LM head of the last prompt position (last_index, model.py:372-385)
+    pf_rmsnorm<<<1, kRowThreads, 0, st>>>(w.x + (size_t)(M - 1) * H, m->final_norm, w.xf, H, eps);
+    if ((rc = gemm({w.xf, (uint64_t)H, 1, (uint64_t)H},
+                   {m->embed + (size_t)m->vbegin * H, (uint64_t)H, (uint64_t)m->V_local, (uint64_t)H},
+                   plain(1, m->V_local, H, w.lmlog, m->V_local, status), 1, st)))
+      return rc;
+    pf_lm_epilogue<<<1, 1024, 0, st>>>(w.lmlog, m->logits, m->V_local, m->vbegin, c.final_logit_softcapping,
+                                       m->tokens_out, m->lm.tokens_host, m->ctrl, n_total);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  }
+  return G4_OK;
+}
+
+extern "C" int g4_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M,
+                            int N, int K, int c_f32, int* status, void* stream) {
+  if (!A || !B || !C) return fail(G4_ERR_ARG, "g4_gemm_bf16: null pointer");
+  if (M < 1 || N < 1 || K < 1 || lda < K || ldb < K || ldc < N)
+    return fail(G4_ERR_ARG, "g4_gemm_bf16: bad shape %d x %d x %d", M, N, K);
+  GemmArgs g = plain(M, N, K, C, ldc, status);
+  g.c_f32 = c_f32 ? 1 : 0;
+  return gemm({A, (uint64_t)K, (uint64_t)M, (uint64_t)lda}, {B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb}, g, 1,
+              static_cast<cudaStream_t>(stream));
+}
+
+extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, void* stream) {
+  if (!m) return fail(G4_ERR_ARG, "g4_prefill: null model");
+  if (!m->finalized) return fail(G4_ERR_STATE, "g4_prefill before g4_model_finalize");
+  if (m->world != 1) return fail(G4_ERR_SHAPE, "g4_prefill: tensor-parallel prefill is not built (world %d)", m->world);
+  if (n_tokens < 1 || n_tokens > m->max_len)
+    return fail(G4_ERR_ARG, "g4_prefill: %d tokens outside [1, %d]", n_tokens, m->max_len);
+  if (chunk <= 0) chunk = 4096;
+  chunk = std::min(chunk, n_tokens);
+  chunk = (chunk + kGemmBM - 1) / kGemmBM * kGemmBM;
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  int rc = prefill_workspace(m, chunk);
+  if (rc) return rc;
+  if ((rc = g4_prepare_sampler(m))) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  for (int c0 = 0; c0 < n_tokens; c0 += chunk) {
+    const int M = std::min(chunk, n_tokens - c0);
+    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, st))) return rc;
+  }
+  return g4_launch_sampler(m, st);  // temperature > 0: replaces the greedy first token
+}

@@ -107,7 +107,8 @@ __host__ __device__ __forceinline__ float sample_uniform(uint64_t seed, uint32_t
 
 __device__ __forceinline__ float ctrl_float(const int* ctrl, int word) { return __int_as_float(ldcg_i(ctrl + word)); }
 
-__global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __grid_constant__ SampleArgs a) {
+// (internal linkage: every translation unit that includes this header launches its own copy)
+static __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __grid_constant__ SampleArgs a) {
   extern __shared__ __align__(16) unsigned char sample_smem[];
   pdl_wait();
   const float temp = ctrl_float(a.ctrl, G4_CTRL_TEMPERATURE);

@@ -39,7 +39,7 @@ EXPORTS = (
     "g4_step", "g4_graph_capture", "g4_graph_launch", "g4_model_status",
     "g4_model_kernel_count", "g4_model_host_tokens", "g4_model_profile", "g4_model_destroy",
     "g4_moe_block", "g4_attention_decode", "g4_trace_read", "g4_attention_decode_noalloc",
-    "g4_model_set_engine",
+    "g4_model_set_engine", "g4_prefill", "g4_gemm_bf16",
 )
 
 ENGINE_STEP_KERNEL = 0  # one persistent kernel per decode step (default)
@@ -111,6 +111,9 @@ def lib() -> ctypes.CDLL:
     L.g4_model_status.argtypes = [c_void_p, c_void_p, POINTER(c_int)]
     L.g4_model_kernel_count.argtypes = [c_void_p]
     L.g4_model_set_engine.argtypes = [c_void_p, c_int]
+    L.g4_prefill.argtypes = [c_void_p, c_int, c_int, c_void_p]
+    L.g4_gemm_bf16.argtypes = [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
+                               c_int, c_int, c_void_p, c_void_p]
     L.g4_model_host_tokens.argtypes = [c_void_p, POINTER(POINTER(c_int))]
     L.g4_model_profile.argtypes = [c_void_p, c_void_p, c_int, POINTER(c_float), c_int]
     L.g4_model_destroy.argtypes = [c_void_p]

@@ -63,6 +63,8 @@ class Engine:
         random_std: float = 0.02,
         mesh: Mesh | None = None,
         engine: str = "step",
+        prefill: bool = True,
+        prefill_chunk: int = 0,
     ):
         if not 1 <= top_k <= 128:
             raise ValueError(f"top_k must be in [1, 128] on the B200 sampler, got {top_k}")
@@ -73,6 +75,8 @@ class Engine:
         self.max_len = max_len
         self.batch = batch
         self.top_k = top_k
+        self.use_prefill = prefill
+        self.prefill_chunk = prefill_chunk
         self.mesh = mesh or make_mesh()
         self.n_devices = self.mesh.world
         self.device = torch.device("cuda", self.mesh.device)
@@ -111,7 +115,7 @@ class Engine:
             if n_steps is not None:  # prefill: tokens [1, T], pos = prompt length
                 plen = int(pos)
                 m.reset(tokens[0, :plen].tolist())
-                m.step(plen)
+                self._consume_prompt(plen)
                 out_pos = plen
             else:                    # decode: token [1, 1] already in tokens_out at pos
                 out_pos = int(pos) + 1
@@ -128,6 +132,12 @@ class Engine:
         return self._step_fn(None)
 
     # ---------------------------------------------------------------- helpers
+    def _consume_prompt(self, n: int):
+        """The prompt through the model: one tensor-core prefill (engine.py:57-69) when
+        the library has it for this model (world 1), else ``n`` decode steps."""
+        if not (self.use_prefill and self.model.prefill(n, self.prefill_chunk)):
+            self.model.step(n)
+
     def reset_cache(self):
         for t in self.model.cache_k + self.model.cache_v:
             t.zero_()
@@ -183,7 +193,7 @@ class Engine:
         m.set_sampling(float(temperature), float(top_p), self.top_k, int(seed))
         t_start = time.perf_counter()
         m.reset(prompt_ids)
-        m.step(p_len)
+        self._consume_prompt(p_len)
         torch.cuda.current_stream(self.device).synchronize()
         m.check_status()
         first = int(host[p_len])

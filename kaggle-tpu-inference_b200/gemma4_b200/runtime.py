@@ -164,6 +164,17 @@ class DecodeModel:
                 for _ in range(n):
                     N.check(L.g4_step(self.handle, st), "g4_step")
 
+    def prefill(self, n_tokens: int, chunk: int = 0):
+        """Consume the first ``n_tokens`` forced tokens in one tensor-core pass per chunk
+        (``g4_prefill``): cache rows [0, n), tokens_out[n] and POS = n, like ``n`` steps.
+        Returns False (nothing enqueued) where the library has no prefill for this model
+        (tensor parallel), so the caller consumes the prompt with decode steps."""
+        if self.mesh.world > 1:
+            return False
+        with torch.cuda.device(self.device):
+            N.check(N.lib().g4_prefill(self.handle, int(n_tokens), int(chunk), N.stream_handle()), "g4_prefill")
+        return True
+
     def capture(self):
         with torch.cuda.device(self.device):
             N.check(N.lib().g4_graph_capture(self.handle, N.stream_handle()), "g4_graph_capture")
