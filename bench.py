@@ -69,6 +69,8 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--prefill-tokens", type=int, default=4096,
+                    help="benchmark config 5 prompt length for the prefill (TTFT) leg; 0 skips it")
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
     # profiling knobs (smaller models for ncu captures); defaults are config 4
     ap.add_argument("--layers", type=int, default=30)
@@ -244,6 +246,66 @@ def run_reference(args, cfg, rank, world, workload):
     }
     print(json.dumps(line), flush=True)
     return 0
+
+
+# ----------------------------------------------------------------------------- prefill
+def prefill_flops(cfg, T, dense):
+    """FLOPs of one prefill of T tokens as run (world 1): projections, attention over the
+    causal / sliding band, router, the MoE over all experts (dense) or the top-k (routed),
+    and the last position's LM head."""
+    H, E, F, I, K = (cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size, cfg.intermediate_size,
+                     cfg.top_k_experts)
+    tot = 0.0
+    for lt in cfg.layer_types:
+        d, kv = cfg.head_dim_for(lt), cfg.kv_heads_for(lt)
+        nq = cfg.num_attention_heads
+        rows = nq * d + kv * d * (1 if cfg.k_eq_v_for(lt) else 2)
+        keys = T / 2 if lt == "full_attention" else min(cfg.sliding_window, T / 2)  # mean live keys
+        moe = (E if dense else K) * 3 * F * H
+        tot += 2.0 * T * (H * rows + nq * d * H + 3 * H * I + H * E + moe) + 4.0 * T * keys * d * nq
+    return tot + 2.0 * H * cfg.vocab_size
+
+
+def prefill_leg(eng, cfg, args, dev):
+    """Benchmark config 5's prefill: a prompt of --prefill-tokens random ids (seed 4)
+    through g4_prefill (tcgen05 GEMMs), timed with CUDA events (best of 2 after one
+    warm-up) in both MoE modes; TTFT ms and tensor-core throughput against the measured
+    bf16 peak.  Weights are the bench model's (values do not change the timing)."""
+    import torch
+
+    T = min(args.prefill_tokens, args.max_len - 1)
+    g = torch.Generator().manual_seed(4)
+    prompt = torch.randint(0, cfg.vocab_size, (T,), generator=g).tolist()
+    m = eng.model
+    out = {"tokens": T, "workload": "benchmark config 5 prefill (one prompt, world 1)"}
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            peak = float(json.load(f)["bf16_tflops"])
+        peak_kind = "measured"
+    except (OSError, KeyError, ValueError):
+        peak, peak_kind = 1590.0, "fallback"
+    for dense in (False, True):
+        times = []
+        for rep in range(3):
+            m.reset(prompt)
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            m.prefill(T, 0, dense_moe=dense)
+            e1.record()
+            torch.cuda.synchronize(dev)
+            if rep:
+                times.append(e0.elapsed_time(e1))
+        m.check_status()
+        ms = min(times)
+        key = "dense_moe" if dense else "routed_moe"
+        fl = prefill_flops(cfg, T, dense)
+        out[key] = {"ttft_ms": ms, "tflops_as_run": fl / ms / 1e9, "flops_as_run": fl,
+                    "useful_tflops": prefill_flops(cfg, T, False) / ms / 1e9,
+                    "frac_of_bf16_peak": fl / ms / 1e9 / peak}
+    out["bf16_peak_tflops"] = peak
+    out["peak_kind"] = peak_kind
+    return out
 
 
 # ----------------------------------------------------------------------------- GPU arm
@@ -422,6 +484,8 @@ def main() -> int:
                "d2h_bytes_per_step": 4, "ttft_ms": 1000 * evs[0]["ttft"], "tokens": len(evs),
                "path": "Engine.generate (temperature 0), wall clock call -> last token"}
 
+    prefill = prefill_leg(eng, cfg, args, dev) if args.prefill_tokens > 0 and world == 1 else None
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         try:
@@ -440,7 +504,7 @@ def main() -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
             "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
-            "cpu_baseline": cpu, "tokens_match": tokens_match,
+            "cpu_baseline": cpu, "tokens_match": tokens_match, "prefill": prefill,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

@@ -108,6 +108,13 @@ const char* g4_last_error(void);
 int g4_comm_create(int device, int rank, int world, int hidden_size, g4_comm** out);
 int g4_comm_get_handle(const g4_comm* comm, void* handle_out /* 64 bytes, host */);
 int g4_comm_open(g4_comm* comm, const void* handles /* world*64 bytes, host */);
+/* g4_comm_open_local: the same for `n` ranks owned by ONE process, one device each (the
+ * reference's single-process engine over every device, model.py:159-161 make_mesh):
+ * comms[r] is rank r's communicator (created with world = n on its own device); peer
+ * access is enabled between the devices and every rank addresses the others' exchange
+ * buffers directly (no IPC handles).  The ranks' steps must then be launched so that they
+ * run concurrently (one stream per device; each device's graph launched in turn). */
+int g4_comm_open_local(g4_comm* const* comms, int n);
 int g4_comm_destroy(g4_comm* comm);
 
 /* ---------------------------------------------------------------- model
@@ -161,8 +168,14 @@ int g4_model_set_engine(g4_model* model, int engine);
  * g4_step continues the sequence.  The caller sets control[FORCED_LEN] = n_tokens (the
  * prompt).  Allocates a workspace on first use (grown for a larger chunk; freed by
  * g4_model_destroy).  world > 1: G4_ERR_SHAPE (tensor-parallel prefill is not built;
- * consume the prompt with g4_step instead). */
-int g4_prefill(g4_model* model, int n_tokens, int chunk, void* stream);
+ * consume the prompt with g4_step instead).
+ * flags: 0 computes the MoE over the routed (token, expert) pairs only, as grouped GEMMs:
+ * an expert off a token's top-k has routing weight 0 in the reference's dense einsum
+ * (model.py:241-250), so its terms are exactly zero and the result is the dense one up to
+ * the fp32 summation order; G4_PREFILL_DENSE_MOE runs the dense all-expert computation as
+ * written (all 128 experts per token, 16x the MoE FLOPs at top-8). */
+#define G4_PREFILL_DENSE_MOE 0x1
+int g4_prefill(g4_model* model, int n_tokens, int chunk, int flags, void* stream);
 /* g4_gemm_bf16: C[M, N] = A[M, K] . B[N, K]^T on the tensor cores (tcgen05, TMEM accumulator,
  * TMA-fed), bf16 operands with row strides lda / ldb (elements, multiples of 8; 16-byte
  * aligned bases), fp32 accumulation, C in fp32 (c_f32 != 0) or rounded to bf16, row stride

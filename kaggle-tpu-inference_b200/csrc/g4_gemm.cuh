@@ -57,6 +57,10 @@ struct GemmArgs {
   int window;            // sliding window (0: causal only)
   int a_row0, a_col0;    // constant coordinate offsets of A and B (e.g. the first key row)
   int b_row0, b_col0;
+  int ksplit;            // > 1: split-K; grid.z = Z * ksplit, split s writes its fp32 partial
+  long long split_stride;  //   sum to C + s * split_stride (elements; C is fp32 then)
+  const int* z_rows;     // grouped GEMM: entry z owns A / C rows [z_rows[z], z_rows[z+1]) and
+                         //   its M is their count (za_row / zc_row then unused); else null
   int* status;           // error bits (bounded waits)
 };
 
@@ -158,17 +162,18 @@ __device__ __forceinline__ bool gemm_wait(uint64_t* bar, uint32_t parity, int* s
 }
 
 // The k-block range [kb0, kb1) of tile (m0, n0), and whether the tile is computed at all.
-__device__ __forceinline__ bool gemm_tile_range(const GemmArgs& a, int m0, int n0, int bn, int& kb0, int& kb1) {
+__device__ __forceinline__ bool gemm_tile_range(const GemmArgs& a, int M, int m0, int n0, int bn, int& kb0,
+                                                int& kb1) {
   const int nkb = (a.K + kGemmBK - 1) / kGemmBK;
   kb0 = 0;
   kb1 = nkb;
   if (a.band == 1) {  // scores: row q sees keys (q - window, q]
-    const int qlo = a.q_pos0 + m0, qhi = a.q_pos0 + min(m0 + kGemmBM, a.M) - 1;
+    const int qlo = a.q_pos0 + m0, qhi = a.q_pos0 + min(m0 + kGemmBM, M) - 1;
     const int klo = a.key_pos0 + n0, khi = a.key_pos0 + min(n0 + bn, a.N) - 1;
     if (klo > qhi) return false;
     if (a.window > 0 && khi <= qlo - a.window) return false;
   } else if (a.band == 2) {  // P.V: K index j is the key at key_pos0 + j
-    const int qlo = a.q_pos0 + m0, qhi = a.q_pos0 + min(m0 + kGemmBM, a.M) - 1;
+    const int qlo = a.q_pos0 + m0, qhi = a.q_pos0 + min(m0 + kGemmBM, M) - 1;
     int jlo = (a.window > 0 ? qlo - a.window + 1 : 0) - a.key_pos0;
     int jhi = qhi - a.key_pos0 + 1;
     jlo = max(jlo, 0);
@@ -199,9 +204,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   const GemmArgs& a = P.a;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * BN, z = blockIdx.z;
+  const int m0 = blockIdx.y * kGemmBM, n0 = blockIdx.x * BN;
+  const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  const int z = blockIdx.z / ks, split = blockIdx.z % ks;
+  int M = a.M, arow_base = a.a_row0 + z * a.za_row;
+  long long crow_base = (long long)z * a.zc_row;
+  if (a.z_rows) {  // grouped: this entry's rows
+    const int r0 = __ldg(a.z_rows + z), r1 = __ldg(a.z_rows + z + 1);
+    M = r1 - r0;
+    arow_base = a.a_row0 + r0;
+    crow_base = r0;
+  }
+  if (m0 >= M) return;  // uniform over the CTA
   int kb0, kb1;
-  if (!gemm_tile_range(a, m0, n0, BN, kb0, kb1)) return;  // uniform over the CTA
+  if (!gemm_tile_range(a, M, m0, n0, BN, kb0, kb1)) return;
+  if (ks > 1) {  // this split's share of the k-blocks (an empty share writes zeros)
+    const int per = (kb1 - kb0 + ks - 1) / ks;
+    const int s0 = kb0 + split * per;
+    kb1 = min(kb1, s0 + per);
+    kb0 = min(s0, kb1);
+  }
   const bool has_k = kb1 > kb0;
 
   if (threadIdx.x == 0) {
@@ -230,7 +252,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
 
   if (warp == 0) {
     if (lane == 0 && has_k) {
-      const int arow = a.a_row0 + z * a.za_row + m0, acol0 = a.a_col0 + z * a.za_col;
+      const int arow = arow_base + m0, acol0 = a.a_col0 + z * a.za_col;
       const int zb = z / a.zb_div;
       const int brow = a.b_row0 + zb * a.zb_row + n0, bcol0 = a.b_col0 + zb * a.zb_col;
       for (int kb = kb0, i = 0; kb < kb1; ++kb, ++i) {
@@ -278,9 +300,11 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
     if (has_k && lane == 0) ready = gemm_wait(accum, 0, a.status, abort) ? 1 : 0;
     ready = __shfl_sync(0xffffffffu, ready, 0);
     tc_fence_after();
-    const bool row_ok = row < a.M;
-    const long long crow = (long long)z * a.zc_row + row;
+    const bool row_ok = row < M;
+    const long long crow = crow_base + row;
     const long long ccol0 = (long long)z * a.zc_col + n0;
+    const bool out_f32 = a.c_f32 || ks > 1;
+    void* cbase = ks > 1 ? static_cast<void*>(static_cast<float*>(a.C) + split * a.split_stride) : a.C;
 #pragma unroll 1
     for (int c0 = 0; c0 < BN; c0 += 32) {
       uint32_t r[32];
@@ -292,8 +316,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
       }
       if (!row_ok || n0 + c0 >= a.N || !ready) continue;
       const int ncols = min(32, a.N - (n0 + c0));
-      if (a.c_f32) {
-        float* dst = reinterpret_cast<float*>(a.C) + crow * a.ldc + ccol0 + c0;
+      if (out_f32) {
+        float* dst = reinterpret_cast<float*>(cbase) + crow * a.ldc + ccol0 + c0;
         if (ncols == 32 && (((uintptr_t)dst) & 15) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 4)
@@ -302,7 +326,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
           for (int i = 0; i < ncols; ++i) dst[i] = __uint_as_float(r[i]);
         }
       } else {
-        bf16_t* dst = reinterpret_cast<bf16_t*>(a.C) + crow * a.ldc + ccol0 + c0;
+        bf16_t* dst = reinterpret_cast<bf16_t*>(cbase) + crow * a.ldc + ccol0 + c0;
         if (ncols == 32 && (((uintptr_t)dst) & 15) == 0) {
 #pragma unroll
           for (int i = 0; i < 32; i += 8) {

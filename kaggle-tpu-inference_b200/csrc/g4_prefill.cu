@@ -313,6 +313,111 @@ __global__ void pf_moe_act(const bf16_t* gu, const float* wfull, bf16_t* act, in
   }
 }
 
+// ---- routed MoE: the dense einsums of model.py:241-250 restricted to the (token, expert)
+// pairs with a nonzero routing weight.  An expert off a token's top-k has weight 0, so its
+// activation is exactly 0 and its products add exactly 0 to the dense sum: computing only
+// the routed pairs gives the dense result, up to the fp32 summation order of the down
+// projection (per expert, then the experts in increasing order).
+// Rows of the grouped buffers: expert e owns rows [z_rows[e], z_rows[e+1]), its tokens in
+// increasing order (a stable counting sort, independent of scheduling).
+
+// counts[e] = number of tokens routed to expert e (one CTA per expert).
+__global__ void pf_route_count(const float* wfull, int M, int E, int* counts) {
+  __shared__ float red[32];
+  const int e = blockIdx.x;
+  int c = 0;
+  for (int t = threadIdx.x; t < M; t += blockDim.x) c += wfull[(size_t)t * E + e] != 0.f ? 1 : 0;
+  const float s = row_sum((float)c, red);
+  if (threadIdx.x == 0) counts[e] = (int)s;
+}
+
+// z_rows = exclusive prefix of counts (z_rows[E] = routed pairs).
+__global__ void pf_route_scan(const int* counts, int E, int* z_rows) {
+  if (threadIdx.x != 0) return;
+  int acc = 0;
+  for (int e = 0; e < E; ++e) {
+    z_rows[e] = acc;
+    acc += counts[e];
+  }
+  z_rows[E] = acc;
+}
+
+// Row of every routed (token, expert) pair: tokens of expert e in increasing order from
+// z_rows[e]; rowmap[t][e] = that row or -1 (one CTA per expert, ordered block scan).
+__global__ void pf_route_assign(const float* wfull, int M, int E, const int* z_rows, int* gather_tok,
+                                float* gather_w, int* rowmap) {
+  __shared__ int wcount[kRowThreads / 32];
+  const int e = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int base = z_rows[e];
+  for (int t0 = 0; t0 < M; t0 += blockDim.x) {
+    const int t = t0 + threadIdx.x;
+    const float wv = t < M ? wfull[(size_t)t * E + e] : 0.f;
+    const bool member = wv != 0.f;
+    const unsigned bal = __ballot_sync(0xffffffffu, member);
+    if (lane == 0) wcount[warp] = __popc(bal);
+    __syncthreads();
+    int before = 0, total = 0;
+    for (int i = 0; i < (int)(blockDim.x >> 5); ++i) {
+      if (i < warp) before += wcount[i];
+      total += wcount[i];
+    }
+    if (t < M) {
+      if (member) {
+        const int r = base + before + __popc(bal & ((1u << lane) - 1u));
+        gather_tok[r] = t;
+        gather_w[r] = wv;
+        rowmap[(size_t)t * E + e] = r;
+      } else {
+        rowmap[(size_t)t * E + e] = -1;
+      }
+    }
+    base += total;
+    __syncthreads();  // wcount is rewritten by the next chunk
+  }
+}
+
+// hg[r] = h2[gather_tok[r]] for the routed rows (one CTA per possible row).
+__global__ void pf_gather_rows(const bf16_t* h2, const int* gather_tok, const int* z_rows, int E, int H, bf16_t* hg) {
+  const int r = blockIdx.x;
+  if (r >= z_rows[E]) return;
+  const uint4* src = reinterpret_cast<const uint4*>(h2 + (size_t)gather_tok[r] * H);
+  uint4* dst = reinterpret_cast<uint4*>(hg + (size_t)r * H);
+  for (int i = threadIdx.x; i < H / 8; i += blockDim.x) dst[i] = src[i];
+}
+
+// act[r, f] = bf16(bf16(bf16(gelu(g)) * u) * bf16(w_r)) of the routed rows (model.py:246-248).
+__global__ void pf_routed_act(const bf16_t* gug, const float* gather_w, const int* z_rows, int E, int F,
+                              bf16_t* act) {
+  const size_t n = (size_t)z_rows[E] * F;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = i / F;
+    const int f = (int)(i % F);
+    const bf16_t* g = gug + r * 2 * F;
+    act[i] = f2bf(rbf(rbf(rbf(gelu_tanh(bf2f(g[f]))) * bf2f(g[F + f])) * rbf(gather_w[r])));
+  }
+}
+
+// moe[t] = bf16(sum over t's experts in increasing order of the fp32 down outputs).
+__global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, int H, bf16_t* moe) {
+  __shared__ int rows[kMaxTopK * 2];
+  __shared__ int nrows;
+  const int t = blockIdx.x;
+  if (threadIdx.x == 0) {
+    int n = 0;
+    for (int e = 0; e < E && n < kMaxTopK * 2; ++e) {
+      const int r = rowmap[(size_t)t * E + e];
+      if (r >= 0) rows[n++] = r;
+    }
+    nrows = n;
+  }
+  __syncthreads();
+  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+    float acc = 0.f;
+    for (int i = 0; i < nrows; ++i) acc += outg[(size_t)rows[i] * H + h];
+    moe[(size_t)t * H + h] = f2bf(acc);
+  }
+}
+
 // Layer output (model.py:312-322, one row per CTA): h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2,
 // h = rms(h1 + h2)*pf, x = (resid + h) * layer_scalar.
 __global__ void pf_combine(const bf16_t* mlp, const bf16_t* moe, bf16_t* x, const bf16_t* pf1, const bf16_t* pf2,
@@ -451,13 +556,53 @@ int gemm_prepare(int bn) {
   return G4_OK;
 }
 
+// out[m, n] = sum over the splits of part[s][m][n] (fixed order), as fp32 or bf16.
+__global__ void pf_split_reduce(const float* part, int S, int M, int N, void* out, long long ldc, int out_f32) {
+  const size_t n = (size_t)M * N;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (size_t)gridDim.x * blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < S; ++s) acc += part[(size_t)s * n + i];
+    const size_t r = i / N, c = i % N;
+    if (out_f32) static_cast<float*>(out)[r * ldc + c] = acc;
+    else static_cast<bf16_t*>(out)[r * ldc + c] = f2bf(acc);
+  }
+}
+
+// Split-K scratch: fp32 partial sums of GEMMs whose tiles alone cannot fill the GPU
+// (few output tiles: short prompts, narrow outputs).  Set by the prefill for its calls.
+struct SplitBuf {
+  float* p = nullptr;
+  size_t elems = 0;
+};
+
 // C[z] (M x N) = A[z] (M x K) . B[z] (N x K)^T; `g` carries the shape, output and offsets.
-int gemm(const Operand& A, const Operand& B, GemmArgs g, int Z, cudaStream_t st) {
+// A plain (un-batched, un-banded) GEMM with fewer output tiles than SMs is split along K
+// into fp32 partials in `sb` and summed by pf_split_reduce.
+int gemm(const Operand& A, const Operand& B, GemmArgs g, int Z, cudaStream_t st, SplitBuf sb = SplitBuf{}) {
   if (g.M <= 0 || g.N <= 0 || g.K <= 0 || Z <= 0) return G4_OK;
   if (!g.zb_div) g.zb_div = 1;
   const int bn = g.N <= 128 ? 128 : 256;
   int rc = gemm_prepare(bn);
   if (rc) return rc;
+  int nsm = 148, dev = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&nsm, cudaDevAttrMultiProcessorCount, dev);
+  const long long tiles = (long long)((g.N + bn - 1) / bn) * ((g.M + kGemmBM - 1) / kGemmBM) * Z;
+  const int nkb = g.b_kpe > 0 ? g.K / kGemmBK : (g.K + kGemmBK - 1) / kGemmBK;
+  int S = 1;
+  if (sb.p && Z == 1 && !g.band && !g.z_rows && tiles < nsm && g.ldc == g.N) {
+    S = (int)std::min<long long>((2LL * nsm + tiles - 1) / tiles, nkb / 2);
+    S = (int)std::min<long long>(S, (long long)(sb.elems / ((size_t)g.M * g.N)));
+  }
+  void* out = g.C;
+  const int out_f32 = g.c_f32;
+  if (S >= 2) {
+    g.ksplit = S;
+    g.split_stride = (long long)g.M * g.N;
+    g.C = sb.p;
+  } else {
+    S = 1;
+  }
   GemmParams P;
   memset(&P, 0, sizeof(P));
   if ((rc = make_map_2d(&P.ta, A.p, A.inner, A.rows, A.ld, kGemmBM))) return rc;
@@ -465,12 +610,18 @@ int gemm(const Operand& A, const Operand& B, GemmArgs g, int Z, cudaStream_t st)
   else rc = make_map_2d(&P.tb, B.p, B.inner, B.rows, B.ld, bn);
   if (rc) return rc;
   P.a = g;
-  const dim3 grid((g.N + bn - 1) / bn, (g.M + kGemmBM - 1) / kGemmBM, Z);
+  const dim3 grid((g.N + bn - 1) / bn, (g.M + kGemmBM - 1) / kGemmBM, Z * S);
   if (bn == 256)
     gemm_kernel<256><<<grid, kGemmThreads, gemm_smem_bytes(256), st>>>(P);
   else
     gemm_kernel<128><<<grid, kGemmThreads, gemm_smem_bytes(128), st>>>(P);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  if (S > 1) {
+    const size_t n = (size_t)g.M * g.N;
+    pf_split_reduce<<<(unsigned)std::min<size_t>(4096, (n + 255) / 256), 256, 0, st>>>(sb.p, S, g.M, g.N, out,
+                                                                                       g.ldc, out_f32);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  }
   return G4_OK;
 }
 
@@ -497,7 +648,15 @@ struct PrefillWs {
   bf16_t *x, *xn, *qkv, *q, *sp, *vt, *ctx, *o, *mlp_in, *h2, *rin, *gate, *up, *act, *mlp_out, *rlog, *gu, *mact,
       *moe_out, *xf, *lmlog;
   float* wfull;
+  float* split;  // split-K partial sums
+  size_t split_elems;
+  // routed MoE: per-expert row ranges, the routed rows' token / weight, token x expert row map
+  int *counts, *z_rows, *gather_tok, *rowmap;
+  float *gather_w, *outg;
+  bf16_t *hg, *gug, *actg;
 };
+
+constexpr size_t kSplitElems = (size_t)16 << 20;  // 64 MB of fp32 split-K partials
 
 void g4_prefill_release(g4_model* m) {
   if (!m || !m->prefill) return;
@@ -531,7 +690,11 @@ static int prefill_workspace(g4_model* m, int chunk) {
                o_g = take(C * I * 2), o_u = take(C * I * 2), o_a = take(C * I * 2), o_mo = take(C * H * 2),
                o_rl = take(C * E * 2), o_wf = take(C * E * 4), o_gu = take(C * (size_t)E * 2 * F * 2),
                o_ma = take(C * (size_t)E * F * 2), o_moe = take(C * H * 2), o_xf = take((size_t)H * 2),
-               o_lm = take((size_t)m->V_local * 2);
+               o_lm = take((size_t)m->V_local * 2), o_split = take(kSplitElems * 4);
+  const size_t CK = C * (size_t)m->topk;
+  const size_t o_cnt = take((size_t)E * 4), o_zr = take((size_t)(E + 1) * 4), o_gt = take(CK * 4),
+               o_rm = take(C * (size_t)E * 4), o_gw = take(CK * 4), o_og = take(CK * H * 4), o_hg = take(CK * H * 2),
+               o_gug = take(CK * 2 * F * 2), o_ag = take(CK * F * 2);
   PrefillWs* w = new PrefillWs();
   if (cudaMalloc(&w->base, off) != cudaSuccess) {
     delete w;
@@ -562,6 +725,17 @@ static int prefill_workspace(g4_model* m, int chunk) {
   w->moe_out = (bf16_t*)(b + o_moe);
   w->xf = (bf16_t*)(b + o_xf);
   w->lmlog = (bf16_t*)(b + o_lm);
+  w->split = (float*)(b + o_split);
+  w->split_elems = kSplitElems;
+  w->counts = (int*)(b + o_cnt);
+  w->z_rows = (int*)(b + o_zr);
+  w->gather_tok = (int*)(b + o_gt);
+  w->rowmap = (int*)(b + o_rm);
+  w->gather_w = (float*)(b + o_gw);
+  w->outg = (float*)(b + o_og);
+  w->hg = (bf16_t*)(b + o_hg);
+  w->gug = (bf16_t*)(b + o_gug);
+  w->actg = (bf16_t*)(b + o_ag);
   m->prefill = w;
   return G4_OK;
 }
@@ -586,9 +760,48 @@ static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, const
   return G4_OK;
 }
 
-// One chunk of `M` prompt tokens at positions [c0, c0 + M) through every layer.
-static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, cudaStream_t st) {
+// Routed MoE of the chunk's M tokens (see pf_route_count): routing tables, the gathered
+// MoE inputs, one grouped GEMM per projection (entry e = expert e: its rows, its weights),
+// the activation, and the per-token sum of the routed experts' outputs.
+static int routed_moe(g4_model* m, const LayerDev& l, int M, cudaStream_t st) {
   PrefillWs& w = *m->prefill;
+  const int H = m->H, E = m->E, F = m->F_local, MK = M * m->topk;
+  int* status = m->ctrl + G4_CTRL_STATUS;
+  int rc;
+  pf_route_count<<<E, kRowThreads, 0, st>>>(w.wfull, M, E, w.counts);
+  pf_route_scan<<<1, 32, 0, st>>>(w.counts, E, w.z_rows);
+  pf_route_assign<<<E, kRowThreads, 0, st>>>(w.wfull, M, E, w.z_rows, w.gather_tok, w.gather_w, w.rowmap);
+  pf_gather_rows<<<MK, 128, 0, st>>>(w.h2, w.gather_tok, w.z_rows, E, H, w.hg);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  {  // gate|up of every routed row: entry e reads expert e's [2F, H] rows
+    GemmArgs g = plain(M, 2 * F, H, w.gug, 2 * F, status);
+    g.zb_row = 2 * F;
+    g.z_rows = w.z_rows;
+    if ((rc = gemm({w.hg, (uint64_t)H, (uint64_t)MK, (uint64_t)H},
+                   {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H}, g, E, st)))
+      return rc;
+  }
+  pf_routed_act<<<std::min(8192, (MK * F + 255) / 256), 256, 0, st>>>(w.gug, w.gather_w, w.z_rows, E, F, w.actg);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  {  // down of every routed row (fp32): entry e reads expert e's [H, F] rows
+    GemmArgs g = plain(M, H, F, w.outg, H, status);
+    g.c_f32 = 1;
+    g.zb_row = H;
+    g.z_rows = w.z_rows;
+    if ((rc = gemm({w.actg, (uint64_t)F, (uint64_t)MK, (uint64_t)F},
+                   {l.exp_down, (uint64_t)F, (uint64_t)E * H, (uint64_t)F}, g, E, st)))
+      return rc;
+  }
+  pf_routed_combine<<<M, 256, 0, st>>>(w.outg, w.rowmap, E, H, w.moe_out);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  return G4_OK;
+}
+
+// One chunk of `M` prompt tokens at positions [c0, c0 + M) through every layer; `dense`
+// runs the MoE over all experts (the reference's prefill as written), else routed.
+static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, bool dense, cudaStream_t st) {
+  PrefillWs& w = *m->prefill;
+  const SplitBuf sb{w.split, w.split_elems};
   const g4_config& c = m->cfg;
   const int H = m->H, E = m->E, F = m->F_local, I = m->I_local, K = m->topk;
   const float eps = c.rms_norm_eps;
@@ -605,7 +818,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, cud
     // ---- attention (model.py:195-213)
     pf_rmsnorm<<<M, kRowThreads, 0, st>>>(w.x, l.n_in, w.xn, H, eps);
     if ((rc = gemm({w.xn, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.qkv, (uint64_t)H, (uint64_t)R, (uint64_t)H},
-                   plain(M, R, H, w.qkv, R, status), 1, st)))
+                   plain(M, R, H, w.qkv, R, status), 1, st, sb)))
       return rc;
     if ((rc = launch_qk_rope(l, w.qkv, w.q, aa.inv_freq, c0, M, eps, st))) return rc;
     const int window = l.full ? 0 : c.sliding_window;
@@ -645,42 +858,47 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, cud
     }
     if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
                    {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(M, H, nq * d, w.o, H, status), 1,
-                   st)))
+                   st, sb)))
       return rc;
     pf_post_attn<<<M, kRowThreads, 0, st>>>(w.o, w.x, l.n_post_attn, l.n_pre_ff, l.n_pre_ff2, l.router_scale,
                                              w.mlp_in, w.h2, w.rin, H, eps, hinv);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
     // ---- dense MLP (model.py:218-221)
     if ((rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.gate, (uint64_t)H, (uint64_t)I, (uint64_t)H},
-                   plain(M, I, H, w.gate, I, status), 1, st)))
+                   plain(M, I, H, w.gate, I, status), 1, st, sb)))
       return rc;
     if ((rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.up, (uint64_t)H, (uint64_t)I, (uint64_t)H},
-                   plain(M, I, H, w.up, I, status), 1, st)))
+                   plain(M, I, H, w.up, I, status), 1, st, sb)))
       return rc;
     pf_gelu_mul<<<std::min(4096, (M * I + 255) / 256), 256, 0, st>>>(w.gate, w.up, w.act, (size_t)M * I);
     if ((rc = gemm({w.act, (uint64_t)I, (uint64_t)M, (uint64_t)I}, {l.down, (uint64_t)I, (uint64_t)H, (uint64_t)I},
-                   plain(M, H, I, w.mlp_out, H, status), 1, st)))
+                   plain(M, H, I, w.mlp_out, H, status), 1, st, sb)))
       return rc;
     // ---- router + dense MoE over all experts (model.py:224-250)
     if ((rc = gemm({w.rin, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.router, (uint64_t)H, (uint64_t)E, (uint64_t)H},
-                   plain(M, E, H, w.rlog, E, status), 1, st)))
+                   plain(M, E, H, w.rlog, E, status), 1, st, sb)))
       return rc;
     pf_router<<<M, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
-    if ((rc = gemm({w.h2, (uint64_t)H, (uint64_t)M, (uint64_t)H},
-                   {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H},
-                   plain(M, E * 2 * F, H, w.gu, (long long)E * 2 * F, status), 1, st)))
+    if (!dense) {  // the same sum over the routed (token, expert) pairs only
+      if ((rc = routed_moe(m, l, M, st))) return rc;
+    } else if ((rc = gemm({w.h2, (uint64_t)H, (uint64_t)M, (uint64_t)H},
+                          {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H},
+                          plain(M, E * 2 * F, H, w.gu, (long long)E * 2 * F, status), 1, st, sb))) {
       return rc;
-    pf_moe_act<<<std::min(8192, (int)(((size_t)M * E * F + 255) / 256)), 256, 0, st>>>(w.gu, w.wfull, w.mact, M, E,
-                                                                                       F);
-    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
-    {  // sum over (expert, f) in one GEMM: B = down [E, H, F] as 3-D (f, h, e)
+    }
+    if (dense) {
+      pf_moe_act<<<std::min(8192, (int)(((size_t)M * E * F + 255) / 256)), 256, 0, st>>>(w.gu, w.wfull, w.mact, M,
+                                                                                         E, F);
+      G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    }
+    if (dense) {  // sum over (expert, f) in one GEMM: B = down [E, H, F] as 3-D (f, h, e)
       const int kpe = (F + kGemmBK - 1) / kGemmBK;
       GemmArgs g = plain(M, H, E * kpe * kGemmBK, w.moe_out, H, status);
       g.b_kpe = kpe;
       g.a_slab = F;
       Operand B{l.exp_down, (uint64_t)F, (uint64_t)H, (uint64_t)F};
       B.slabs = E;
-      if ((rc = gemm({w.mact, (uint64_t)E * F, (uint64_t)M, (uint64_t)E * F}, B, g, 1, st))) return rc;
+      if ((rc = gemm({w.mact, (uint64_t)E * F, (uint64_t)M, (uint64_t)E * F}, B, g, 1, st, sb))) return rc;
     }
     pf_combine<<<M, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
                                            l.scalar, H, eps);
@@ -690,7 +908,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, cud
     pf_rmsnorm<<<1, kRowThreads, 0, st>>>(w.x + (size_t)(M - 1) * H, m->final_norm, w.xf, H, eps);
     if ((rc = gemm({w.xf, (uint64_t)H, 1, (uint64_t)H},
                    {m->embed + (size_t)m->vbegin * H, (uint64_t)H, (uint64_t)m->V_local, (uint64_t)H},
-                   plain(1, m->V_local, H, w.lmlog, m->V_local, status), 1, st)))
+                   plain(1, m->V_local, H, w.lmlog, m->V_local, status), 1, st, sb)))
       return rc;
     pf_lm_epilogue<<<1, 1024, 0, st>>>(w.lmlog, m->logits, m->V_local, m->vbegin, c.final_logit_softcapping,
                                        m->tokens_out, m->lm.tokens_host, m->ctrl, n_total);
@@ -710,8 +928,9 @@ extern "C" int g4_gemm_bf16(const void* A, long long lda, const void* B, long lo
               static_cast<cudaStream_t>(stream));
 }
 
-extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, void* stream) {
+extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, int flags, void* stream) {
   if (!m) return fail(G4_ERR_ARG, "g4_prefill: null model");
+  if (flags & ~G4_PREFILL_DENSE_MOE) return fail(G4_ERR_ARG, "g4_prefill: unknown flags 0x%x", flags);
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_prefill before g4_model_finalize");
   if (m->world != 1) return fail(G4_ERR_SHAPE, "g4_prefill: tensor-parallel prefill is not built (world %d)", m->world);
   if (n_tokens < 1 || n_tokens > m->max_len)
@@ -726,7 +945,8 @@ extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, void* stream) {
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   for (int c0 = 0; c0 < n_tokens; c0 += chunk) {
     const int M = std::min(chunk, n_tokens - c0);
-    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, st))) return rc;
+    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, (flags & G4_PREFILL_DENSE_MOE) != 0, st)))
+      return rc;
   }
   return g4_launch_sampler(m, st);  // temperature > 0: replaces the greedy first token
 }

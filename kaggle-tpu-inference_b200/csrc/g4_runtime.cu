@@ -105,6 +105,36 @@ extern "C" int g4_comm_open(g4_comm* c, const void* handles) {
   return G4_OK;
 }
 
+extern "C" int g4_comm_open_local(g4_comm* const* comms, int n) {
+  if (!comms || n < 1 || n > kMaxWorld) return fail(G4_ERR_ARG, "g4_comm_open_local: bad communicator list");
+  for (int r = 0; r < n; ++r) {
+    const g4_comm* c = comms[r];
+    if (!c || c->world != n || c->rank != r || c->hidden != comms[0]->hidden)
+      return fail(G4_ERR_ARG, "g4_comm_open_local: communicator %d is not rank %d of world %d", r, r, n);
+    for (int q = 0; q < r; ++q)
+      if (comms[q]->device == c->device)
+        return fail(G4_ERR_ARG, "g4_comm_open_local: ranks %d and %d share device %d", q, r, c->device);
+  }
+  for (int r = 0; r < n; ++r) {
+    g4_comm* c = comms[r];
+    G4_CUDA(cudaSetDevice(c->device), G4_ERR_CUDA);
+    for (int p = 0; p < n; ++p) {
+      if (p == r) continue;
+      int can = 0;
+      G4_CUDA(cudaDeviceCanAccessPeer(&can, c->device, comms[p]->device), G4_ERR_CUDA);
+      if (!can) return fail(G4_ERR_CUDA, "device %d cannot access device %d", c->device, comms[p]->device);
+      const cudaError_t e = cudaDeviceEnablePeerAccess(comms[p]->device, 0);
+      if (e == cudaErrorPeerAccessAlreadyEnabled) cudaGetLastError();  // clear the sticky-free error
+      else if (e != cudaSuccess)
+        return fail(G4_ERR_CUDA, "cudaDeviceEnablePeerAccess(%d -> %d): %s", c->device, comms[p]->device,
+                    cudaGetErrorString(e));
+      c->peer[p] = comms[p]->local;  // same process: the peer's own allocation, no IPC mapping
+    }
+    c->open = true;
+  }
+  return G4_OK;
+}
+
 extern "C" int g4_comm_destroy(g4_comm* c) {
   if (!c) return G4_OK;
   cudaSetDevice(c->device);

@@ -31,6 +31,7 @@ CTRL_POS, CTRL_STEP, CTRL_FORCED_LEN, CTRL_STATUS, CTRL_TIMEOUT_US, CTRL_WRITE_L
 CTRL_TEMPERATURE, CTRL_TOP_P, CTRL_TOP_K, CTRL_SEED_LO, CTRL_SEED_HI = range(6, 11)
 CTRL_WORDS = 16
 SAMPLE_MAX_TOP_K = 128
+PREFILL_DENSE_MOE = 0x1
 
 EXPORTS = (
     "g4_version", "g4_strerror", "g4_last_error",
@@ -39,7 +40,7 @@ EXPORTS = (
     "g4_step", "g4_graph_capture", "g4_graph_launch", "g4_model_status",
     "g4_model_kernel_count", "g4_model_host_tokens", "g4_model_profile", "g4_model_destroy",
     "g4_moe_block", "g4_attention_decode", "g4_trace_read", "g4_attention_decode_noalloc",
-    "g4_model_set_engine", "g4_prefill", "g4_gemm_bf16",
+    "g4_model_set_engine", "g4_prefill", "g4_gemm_bf16", "g4_comm_open_local",
 )
 
 ENGINE_STEP_KERNEL = 0  # one persistent kernel per decode step (default)
@@ -100,6 +101,7 @@ def lib() -> ctypes.CDLL:
     L.g4_comm_get_handle.argtypes = [c_void_p, c_char_p]
     L.g4_comm_open.argtypes = [c_void_p, c_char_p]
     L.g4_comm_destroy.argtypes = [c_void_p]
+    L.g4_comm_open_local.argtypes = [POINTER(c_void_p), c_int]
     L.g4_model_create.argtypes = [POINTER(G4Config), c_char_p, c_int, c_int, c_int, c_int,
                                   POINTER(c_void_p)]
     L.g4_model_set_tensor.argtypes = [c_void_p, c_char_p, c_void_p, c_longlong]
@@ -111,7 +113,7 @@ def lib() -> ctypes.CDLL:
     L.g4_model_status.argtypes = [c_void_p, c_void_p, POINTER(c_int)]
     L.g4_model_kernel_count.argtypes = [c_void_p]
     L.g4_model_set_engine.argtypes = [c_void_p, c_int]
-    L.g4_prefill.argtypes = [c_void_p, c_int, c_int, c_void_p]
+    L.g4_prefill.argtypes = [c_void_p, c_int, c_int, c_int, c_void_p]
     L.g4_gemm_bf16.argtypes = [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
                                c_int, c_int, c_void_p, c_void_p]
     L.g4_model_host_tokens.argtypes = [c_void_p, POINTER(POINTER(c_int))]

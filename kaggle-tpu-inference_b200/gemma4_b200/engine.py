@@ -6,16 +6,27 @@ Same constructor, attributes and generator protocol as gemma4_tpu/engine.py:25-2
 yielding ``prefill`` then ``decode`` events, ``reset_cache()``, ``prefill_fn(t)``,
 ``decode_fn()`` and ``_put``.
 
-What changes underneath: each rank owns one GPU (``torchrun`` for tensor parallelism,
-rank/world from torch.distributed or the launcher env); the step is one captured CUDA
-graph of the C-ABI kernels, replayed per token; a prompt is consumed by the same step
-as forced tokens; tokens never leave the device between steps and the host reads
-token i from a mapped pinned mirror once step i's event has completed, ``lookahead``
-steps behind the dispatch, like the reference's lookahead-3 loop (engine.py:192-221).
+Devices: like the reference (``make_mesh`` over every device, model.py:159-161) an Engine
+in a plain process owns every visible GPU as one tensor-parallel rank each, from one
+host thread: the ranks' communicators address each other's exchange buffers directly
+(``g4_comm_open_local``) and every step is launched on all devices in turn (the launches
+are asynchronous, so the devices run the step together).  Under ``torchrun`` (an
+initialised process group or RANK/WORLD_SIZE in the environment) each process owns its
+own rank instead and the communicator handles travel over the process group.  An
+explicit ``mesh`` (one rank) or ``devices`` list overrides both.
+
+What changes underneath: the decode step is one captured CUDA graph of the C-ABI
+kernels per device, replayed per token; a prompt goes through the tensor-core prefill
+(``g4_prefill``, engine.py:57-69) on one device, or through forced decode steps under
+tensor parallelism; tokens never leave the device between steps and the host reads
+token i from rank 0's mapped pinned mirror once step i's event has completed,
+``lookahead`` steps behind the dispatch, like the reference's lookahead-3 loop
+(engine.py:192-221).  ``temperature > 0`` samples on the device (model.py:414-424).
 """
 
 from __future__ import annotations
 
+import os
 import time
 from collections import deque
 from typing import Iterator
@@ -48,6 +59,26 @@ def _round_up(x: int, m: int) -> int:
     return max(m, ((x + m - 1) // m) * m)
 
 
+def _local_meshes(mesh: Mesh | None, devices) -> list[Mesh]:
+    """The ranks this process owns: an explicit mesh; else the torchrun rank; else one
+    rank per listed (or visible) device."""
+    if mesh is not None:
+        return [mesh]
+    launched = False
+    try:
+        import torch.distributed as dist
+
+        launched = dist.is_available() and dist.is_initialized()
+    except ImportError:  # pragma: no cover
+        pass
+    if devices is None and (launched or int(os.environ.get("WORLD_SIZE", "1")) > 1):
+        return [make_mesh()]
+    if devices is None:
+        devices = list(range(max(1, torch.cuda.device_count())))
+    devices = list(devices)
+    return [Mesh(r, len(devices), d) for r, d in enumerate(devices)]
+
+
 class Engine:
     def __init__(
         self,
@@ -62,6 +93,7 @@ class Engine:
         random_seed: int | None = None,
         random_std: float = 0.02,
         mesh: Mesh | None = None,
+        devices=None,
         engine: str = "step",
         prefill: bool = True,
         prefill_chunk: int = 0,
@@ -77,24 +109,40 @@ class Engine:
         self.top_k = top_k
         self.use_prefill = prefill
         self.prefill_chunk = prefill_chunk
-        self.mesh = mesh or make_mesh()
+        self.meshes = _local_meshes(mesh, devices)
+        self.mesh = self.meshes[0]
         self.n_devices = self.mesh.world
         self.device = torch.device("cuda", self.mesh.device)
         torch.cuda.set_device(self.device)
 
         t0 = time.time()
-        if random_seed is not None:
-            shard = random_rank_shard(self.cfg, random_seed, self.mesh, self.device, random_std)
-        else:
-            canon = params if params is not None else load_params(self.cfg, model_dir, progress)
-            shard = rank_shard(self.cfg, canon.__getitem__, self.mesh, self.device)
-            del canon
-        torch.cuda.synchronize(self.device)
+        shards = []
+        for ms in self.meshes:
+            dev = torch.device("cuda", ms.device)
+            with torch.cuda.device(dev):
+                if random_seed is not None:
+                    shards.append(random_rank_shard(self.cfg, random_seed, ms, dev, random_std))
+                elif params is not None:  # canonical tensors in host memory (tests, conversions)
+                    shards.append(rank_shard(self.cfg, params.__getitem__, ms, dev))
+                else:  # this rank's slices straight from the checkpoint's memory maps
+                    shards.append(load_params(self.cfg, model_dir, ms, progress, dev))
+                torch.cuda.synchronize(dev)
         self.load_seconds = time.time() - t0
 
-        self.comm = Comm(self.mesh, self.cfg.hidden_size) if self.mesh.world > 1 else None
-        self.model = DecodeModel(self.cfg, shard, self.mesh, max_len, self.comm, engine=engine)
-        self.params = shard
+        H = self.cfg.hidden_size
+        if self.mesh.world == 1:
+            self.comms = [None]
+        elif len(self.meshes) == self.mesh.world:  # every rank in this process
+            self.comms = Comm.local_group(self.meshes, H)
+        else:  # one rank of a torchrun job
+            self.comms = [Comm(self.mesh, H)]
+        self.comm = self.comms[0]
+        self.models = []
+        for ms, shard, comm in zip(self.meshes, shards, self.comms):
+            with torch.cuda.device(ms.device):
+                self.models.append(DecodeModel(self.cfg, shard, ms, max_len, comm, engine=engine))
+        self.model = self.models[0]
+        self.params = shards[0]
         self.param_bytes = param_bytes(self.cfg)
         self.cache_bytes = cache_bytes(self.cfg, batch, max_len)
         self.active_params = active_params_per_token(self.cfg)
@@ -104,23 +152,38 @@ class Engine:
     def cache(self) -> dict:
         return {"k": self.model.cache_k, "v": self.model.cache_v}
 
+    def _all(self, fn):
+        """fn(model) on every rank this process owns, each with its device current."""
+        for m in self.models:
+            with torch.cuda.device(m.device):
+                fn(m)
+
+    def _sync(self):
+        for m in self.models:
+            torch.cuda.current_stream(m.device).synchronize()
+
+    def _check(self):
+        for m in self.models:
+            m.check_status()
+
     # ---------------------------------------------------------------- step fns
     def _step_fn(self, n_steps: int | None):
         """Callable with the reference's jitted-step signature (engine.py:60, 74)."""
 
         def fn(params, tokens, cache, pos, key=None, temperature=0.0, top_p=1.0):
             del params, cache
-            m = self.model
-            m.set_sampling(float(temperature), float(top_p), self.top_k, _seed_of(key))
+            seed = _seed_of(key)
+            self._all(lambda m: m.set_sampling(float(temperature), float(top_p), self.top_k, seed))
             if n_steps is not None:  # prefill: tokens [1, T], pos = prompt length
                 plen = int(pos)
-                m.reset(tokens[0, :plen].tolist())
+                ids = tokens[0, :plen].tolist()
+                self._all(lambda m: m.reset(ids))
                 self._consume_prompt(plen)
                 out_pos = plen
             else:                    # decode: token [1, 1] already in tokens_out at pos
                 out_pos = int(pos) + 1
-                m.step(1)
-            tok = m.tokens_out[out_pos:out_pos + 1].reshape(1, 1)
+                self._all(lambda m: m.step(1))
+            tok = self.model.tokens_out[out_pos:out_pos + 1].reshape(1, 1)
             return tok, self.cache, out_pos
 
         return fn
@@ -135,38 +198,43 @@ class Engine:
     def _consume_prompt(self, n: int):
         """The prompt through the model: one tensor-core prefill (engine.py:57-69) when
         the library has it for this model (world 1), else ``n`` decode steps."""
-        if not (self.use_prefill and self.model.prefill(n, self.prefill_chunk)):
-            self.model.step(n)
+        if not (self.use_prefill and len(self.models) == 1 and self.model.prefill(n, self.prefill_chunk)):
+            self._all(lambda m: m.step(n))
 
     def reset_cache(self):
-        for t in self.model.cache_k + self.model.cache_v:
-            t.zero_()
+        for m in self.models:
+            for t in m.cache_k + m.cache_v:
+                t.zero_()
 
     def _put(self, value, dtype=torch.int32):
         return torch.as_tensor(value, dtype=dtype, device=self.device)
 
     def compile_all(self, bucket: int = PREFILL_BUCKET) -> dict[str, float]:
-        """Capture the step graph, warm it up and time blocking decode steps."""
+        """Capture the step graphs, warm them up and time blocking decode steps."""
         out = {}
-        m = self.model
         t0 = time.perf_counter()
-        m.set_sampling(0.0, 1.0, self.top_k, 0)
-        m.reset([0, 0, 0, 0])
-        m.step(1, use_graph=False)   # first launch configures the kernels
-        m.capture()
-        torch.cuda.synchronize(self.device)
+
+        def first(m):
+            m.set_sampling(0.0, 1.0, self.top_k, 0)
+            m.reset([0, 0, 0, 0])
+            m.step(1, use_graph=False)   # first launch configures the kernels
+
+        self._all(first)
+        self._all(lambda m: m.capture())
+        self._sync()
         out["prefill_compile_s"] = time.perf_counter() - t0
         t0 = time.perf_counter()
-        m.step(3)
-        torch.cuda.synchronize(self.device)
+        self._all(lambda m: m.step(3))
+        self._sync()
         out["decode_compile_s"] = time.perf_counter() - t0
         n = 8
         t0 = time.perf_counter()
-        m.step(n)
-        torch.cuda.synchronize(self.device)
+        for _ in range(n):
+            self._all(lambda m: m.step(1))
+        self._sync()
         self.decode_step_seconds = (time.perf_counter() - t0) / n
         out["decode_step_s"] = self.decode_step_seconds
-        m.check_status()
+        self._check()
         return out
 
     # ---------------------------------------------------------------- generation
@@ -187,15 +255,16 @@ class Engine:
             raise ValueError(f"prompt({p_len}) fills the resident context ({self.max_len})")
         max_new_tokens = allowed_output_tokens(max_new_tokens, p_len, self.max_len)
         bucket = min(_round_up(p_len, PREFILL_BUCKET), self.max_len)
-        m = self.model
-        host = m.tokens_host
+        lead = self.model
+        host = lead.tokens_host
+        ids = list(prompt_ids)
 
-        m.set_sampling(float(temperature), float(top_p), self.top_k, int(seed))
+        self._all(lambda m: m.set_sampling(float(temperature), float(top_p), self.top_k, int(seed)))
         t_start = time.perf_counter()
-        m.reset(prompt_ids)
+        self._all(lambda m: m.reset(ids))
         self._consume_prompt(p_len)
-        torch.cuda.current_stream(self.device).synchronize()
-        m.check_status()
+        self._sync()
+        self._check()
         first = int(host[p_len])
         ttft = time.perf_counter() - t_start
         yield {"kind": "prefill", "token": first, "ttft": ttft, "prompt_tokens": p_len,
@@ -222,9 +291,10 @@ class Engine:
                     return
 
         for _ in range(max_new_tokens - 1):
-            m.step(1)
-            ev = torch.cuda.Event()
-            ev.record()
+            self._all(lambda m: m.step(1))
+            with torch.cuda.device(lead.device):
+                ev = torch.cuda.Event()
+                ev.record()
             pos += 1
             pending.append((ev, pos))
             yield from drain(lookahead)
@@ -232,5 +302,5 @@ class Engine:
                 break
         if not stopped:
             yield from drain(0)
-        torch.cuda.current_stream(self.device).synchronize()
-        m.check_status()
+        self._sync()
+        self._check()

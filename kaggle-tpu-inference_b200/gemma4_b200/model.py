@@ -132,16 +132,16 @@ def shard_slice(n: int, mesh: Mesh) -> slice:
 
 
 def shard_param(t, spec: tuple, mesh: Mesh):
-    """Slice one canonical tensor to this rank's shard along its "tp" axis."""
+    """Slice one canonical tensor (torch or numpy) to this rank's shard along its "tp" axis."""
     for ax, s in enumerate(spec):
         if s == "tp":
-            idx = [slice(None)] * t.dim()
+            idx = [slice(None)] * len(t.shape)
             idx[ax] = shard_slice(t.shape[ax], mesh)
             return t[tuple(idx)]
     return t
 
 
-def pack_layer_attention(cfg: TextConfig, i: int, get, mesh: Mesh):
+def pack_layer_attention(cfg: TextConfig, i: int, get, mesh: Mesh, presharded: bool = False):
     """(qkv [rows, H], o_proj [H, q rows]) of layer i for this rank."""
     import torch
 
@@ -149,13 +149,15 @@ def pack_layer_attention(cfg: TextConfig, i: int, get, mesh: Mesh):
     p = f"layers.{i}."
     specs = param_specs(cfg)
     h = cfg.hidden_size
-    q = shard_param(get(p + "q_proj"), specs[p + "q_proj"], mesh)
-    k = shard_param(get(p + "k_proj"), specs[p + "k_proj"], mesh)
-    parts = [q.reshape(-1, h), k.reshape(-1, h)]
+
+    def take(name):
+        t = get(p + name)
+        return t if presharded else shard_param(t, specs[p + name], mesh)
+
+    parts = [take("q_proj").reshape(-1, h), take("k_proj").reshape(-1, h)]
     if not cfg.k_eq_v_for(lt):
-        parts.append(shard_param(get(p + "v_proj"), specs[p + "v_proj"], mesh).reshape(-1, h))
-    o = shard_param(get(p + "o_proj"), specs[p + "o_proj"], mesh)
-    return torch.cat(parts, 0).contiguous(), o.reshape(h, -1).contiguous()
+        parts.append(take("v_proj").reshape(-1, h))
+    return torch.cat(parts, 0).contiguous(), take("o_proj").reshape(h, -1).contiguous()
 
 
 REPLICATED_LAYER_FIELDS = (
@@ -168,20 +170,23 @@ SHARDED_LAYER_FIELDS = ("mlp.gate_proj", "mlp.up_proj", "mlp.down_proj",
                         "experts.gate_up_proj", "experts.down_proj")
 
 
-def pack_rank_shard(cfg: TextConfig, get, mesh: Mesh, layers=None):
-    """Yield (native tensor name, tensor) for this rank; ``get(flat_name)`` -> canonical."""
+def pack_rank_shard(cfg: TextConfig, get, mesh: Mesh, layers=None, presharded: bool = False):
+    """Yield (native tensor name, tensor) for this rank.  ``get(flat_name)`` returns the
+    canonical tensor, or with ``presharded`` this rank's slice of it along its
+    ``param_specs`` axis (a loader that reads only the rank's bytes)."""
     specs = param_specs(cfg)
     yield "embed", get("embed")
     yield "norm", get("norm")
     for i in (range(cfg.num_hidden_layers) if layers is None else layers):
         p = f"layers.{i}."
-        qkv, o = pack_layer_attention(cfg, i, get, mesh)
+        qkv, o = pack_layer_attention(cfg, i, get, mesh, presharded)
         yield p + "qkv", qkv
         yield p + "o_proj", o
         for f in REPLICATED_LAYER_FIELDS:
             yield p + f, get(p + f)
         for f in SHARDED_LAYER_FIELDS:
-            yield p + f, shard_param(get(p + f), specs[p + f], mesh).contiguous()
+            t = get(p + f)
+            yield p + f, (t if presharded else shard_param(t, specs[p + f], mesh)).contiguous()
 
 
 # ----------------------------------------------------------------------------- KV cache

@@ -41,13 +41,13 @@ def exchange_handles(mine: bytes, world: int, group=None) -> bytes:
 
 
 class Comm:
-    def __init__(self, mesh: Mesh, hidden: int, group=None):
+    def __init__(self, mesh: Mesh, hidden: int, group=None, _local: bool = False):
         L = N.lib()
         self.mesh = mesh
         self.handle = ctypes.c_void_p()
         N.check(L.g4_comm_create(mesh.device, mesh.rank, mesh.world, hidden, ctypes.byref(self.handle)),
                 "g4_comm_create")
-        if mesh.world > 1:
+        if mesh.world > 1 and not _local:
             import torch.distributed as dist
 
             buf = ctypes.create_string_buffer(HANDLE_BYTES)
@@ -55,6 +55,16 @@ class Comm:
             allh = exchange_handles(bytes(buf.raw), mesh.world, group)
             N.check(L.g4_comm_open(self.handle, allh), "g4_comm_open")
             dist.barrier(group=group)
+
+    @classmethod
+    def local_group(cls, meshes, hidden: int) -> list:
+        """One communicator per device for ranks owned by this process (one device each):
+        created on their devices and opened together with direct peer addressing
+        (``g4_comm_open_local``), no IPC handles and no process group."""
+        comms = [cls(m, hidden, _local=True) for m in meshes]
+        arr = (ctypes.c_void_p * len(comms))(*[c.handle.value for c in comms])
+        N.check(N.lib().g4_comm_open_local(arr, len(comms)), "g4_comm_open_local")
+        return comms
 
     def close(self):
         if self.handle:
@@ -164,15 +174,19 @@ class DecodeModel:
                 for _ in range(n):
                     N.check(L.g4_step(self.handle, st), "g4_step")
 
-    def prefill(self, n_tokens: int, chunk: int = 0):
+    def prefill(self, n_tokens: int, chunk: int = 0, dense_moe: bool = False):
         """Consume the first ``n_tokens`` forced tokens in one tensor-core pass per chunk
         (``g4_prefill``): cache rows [0, n), tokens_out[n] and POS = n, like ``n`` steps.
-        Returns False (nothing enqueued) where the library has no prefill for this model
-        (tensor parallel), so the caller consumes the prompt with decode steps."""
+        ``dense_moe`` runs the reference's all-expert MoE as written instead of the routed
+        pairs (same result up to fp32 summation order).  Returns False (nothing enqueued)
+        where the library has no prefill for this model (tensor parallel), so the caller
+        consumes the prompt with decode steps."""
         if self.mesh.world > 1:
             return False
+        flags = N.PREFILL_DENSE_MOE if dense_moe else 0
         with torch.cuda.device(self.device):
-            N.check(N.lib().g4_prefill(self.handle, int(n_tokens), int(chunk), N.stream_handle()), "g4_prefill")
+            N.check(N.lib().g4_prefill(self.handle, int(n_tokens), int(chunk), flags, N.stream_handle()),
+                    "g4_prefill")
         return True
 
     def capture(self):

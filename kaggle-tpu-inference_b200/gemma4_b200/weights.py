@@ -1,12 +1,13 @@
 """Weights: HF checkpoint names -> flat names -> per-rank device shards.
 
-Mirrors the reference loader's contract (gemma4_tpu/weights.py): the same checkpoint
-key map (weights.py:30-58), reshape to the canonical ``param_shapes`` (:61-67),
-``params_from_arrays`` as the test entry point (:70-83), streaming ``load_params``
-from safetensors with the index file (:86-135) and the accounting helpers
-``param_bytes`` / ``active_params_per_token`` (:138-159).  Instead of
-``jax.device_put(NamedSharding)`` each rank packs its own shard into the tensors the
-C ABI consumes (``model.pack_rank_shard``) directly on its GPU.
+Keeps the reference loader's contract (gemma4_tpu/weights.py): the checkpoint key map
+(weights.py:30-58), canonical ``param_shapes`` (:61-67), ``params_from_arrays`` as the
+test entry point (:70-83), ``load_params`` from a safetensors directory (:86-135) with
+its FileNotFoundError / KeyError, and the accounting helpers ``param_bytes`` /
+``active_params_per_token`` (:138-159).  Underneath, a rank never materialises the
+model: each tensor is memory-mapped from the checkpoint, its rank slice is cut in the
+canonical shape and only that slice is copied to the GPU, where ``pack_rank_shard``
+lays it out for the C ABI.
 
 ``random_params`` is the seeded synthetic-weight generator used for the random
 26B-A4B-shaped benchmark model: every flat name draws N(0, std) from its own
@@ -18,6 +19,7 @@ from __future__ import annotations
 
 import glob
 import json
+import math
 import os
 import zlib
 from typing import Callable, Iterable
@@ -45,84 +47,149 @@ def checkpoint_key_map(cfg: TextConfig, prefix: str = "model.language_model.") -
     return out
 
 
-def reshape_param(cfg: TextConfig, flat_name: str, t):
-    """Reshape a checkpoint tensor to its canonical shape (reference weights.py:61-67)."""
-    target = param_shapes(cfg)[flat_name]
-    if tuple(t.shape) == target:
+def as_canonical(cfg: TextConfig, flat_name: str, t):
+    """View a checkpoint array (numpy or torch) in the canonical ``param_shapes`` shape.
+
+    HF stores the projections 2-D (``q_proj`` as [kv*g*d, H], ``o_proj`` as [H, kv*g*d],
+    ``experts.gate_up_proj`` as [E, 2*F, H]); the canonical shapes split those axes in
+    the same row-major order, so the conversion is a reshape (reference weights.py:61-67).
+    """
+    want = tuple(param_shapes(cfg)[flat_name])
+    have = tuple(t.shape)
+    if have == want:
         return t
-    n = 1
-    for s in target:
-        n *= s
-    if t.numel() != n:
-        raise ValueError(f"{flat_name}: checkpoint shape {tuple(t.shape)} != expected {target}")
-    return t.reshape(target)
+    if math.prod(have) != math.prod(want):
+        raise ValueError(f"{flat_name}: {math.prod(have)} elements in the checkpoint ({have}), "
+                         f"the model needs {want}")
+    return t.reshape(want)
 
 
 def params_from_arrays(cfg: TextConfig, get: Callable, names: Iterable[str],
                        prefix: str = "model.language_model.") -> dict:
-    """Canonical torch tensors (bf16, CPU) from any ``name -> array`` accessor.
-
-    Same selection rules as the reference (weights.py:70-83): unknown names and
-    duplicates are skipped.  Arrays may be numpy arrays or torch tensors.
-    """
+    """Canonical bf16 CPU tensors from a ``checkpoint name -> array`` accessor: the test
+    entry point of the reference loader (weights.py:70-83).  Names outside the key map,
+    names of parameters the config has no use for, and repeats are ignored."""
     import numpy as np
     import torch
 
-    shapes = param_shapes(cfg)
-    key_map = checkpoint_key_map(cfg, prefix)
+    wanted = set(param_shapes(cfg))
+    to_flat = checkpoint_key_map(cfg, prefix)
     out: dict = {}
-    for ck in names:
-        flat = key_map.get(ck)
-        if flat is None or flat not in shapes or flat in out:
+    for name in names:
+        flat = to_flat.get(name)
+        if flat not in wanted or flat in out:
             continue
-        a = get(ck)
-        t = a if isinstance(a, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(a))
-        out[flat] = reshape_param(cfg, flat, t.detach().to(torch.bfloat16).contiguous())
+        arr = get(name)
+        t = arr if isinstance(arr, torch.Tensor) else torch.from_numpy(np.ascontiguousarray(arr))
+        out[flat] = as_canonical(cfg, flat, t.detach().to(torch.bfloat16)).contiguous()
     return out
 
 
-def load_params(cfg: TextConfig, model_dir: str, progress=None) -> dict:
-    """Stream an HF safetensors checkpoint into canonical CPU bf16 tensors.
+# ----------------------------------------------------------------------------- checkpoint
+_ST_DTYPES = {"BF16": ("<u2", "bf16"), "F16": ("<f2", "f16"), "F32": ("<f4", "f32")}
 
-    Raises ``FileNotFoundError`` without safetensors and ``KeyError`` listing missing
-    parameters, like the reference (weights.py:97-98, 132-134).
+
+class SafetensorsDir:
+    """The tensors of an HF safetensors checkpoint directory, as read-only memory maps.
+
+    The safetensors layout is an 8-byte little-endian header length, a JSON header
+    mapping each tensor name to {dtype, shape, data_offsets} and the raw row-major data;
+    parsing it directly lets a rank map a tensor and copy only the bytes of its own
+    shard (the pages a slice touches), never the whole 47 GB model.  With
+    ``model.safetensors.index.json`` only the files it names are opened; without it
+    every ``*.safetensors`` file's header is read.
     """
-    from safetensors import safe_open
 
-    shapes = param_shapes(cfg)
-    key_map = checkpoint_key_map(cfg)
-    files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))
-    if not files:
-        raise FileNotFoundError(f"no safetensors under {model_dir}")
-    index_path = os.path.join(model_dir, "model.safetensors.index.json")
-    if os.path.exists(index_path):
-        with open(index_path) as f:
-            weight_map = json.load(f)["weight_map"]
-        by_file: dict[str, list[str]] = {}
-        for ck in key_map:
-            if ck in weight_map:
-                by_file.setdefault(os.path.join(model_dir, weight_map[ck]), []).append(ck)
-    else:
-        by_file = {f: list(key_map) for f in files}
-    params: dict = {}
-    done, total = 0, len(shapes)
-    for path, keys in by_file.items():
-        with safe_open(path, framework="pt", device="cpu") as f:
-            have = set(f.keys())
-            for ck in keys:
-                flat = key_map[ck]
-                if ck not in have or flat not in shapes:
+    def __init__(self, model_dir: str):
+        self.model_dir = model_dir
+        files = sorted(glob.glob(os.path.join(model_dir, "*.safetensors")))
+        if not files:
+            raise FileNotFoundError(f"{model_dir}: no *.safetensors checkpoint files")
+        index = os.path.join(model_dir, "model.safetensors.index.json")
+        if os.path.exists(index):
+            with open(index) as f:
+                names = sorted(set(json.load(f)["weight_map"].values()))
+            files = [os.path.join(model_dir, n) for n in names]
+        self.entries: dict[str, tuple] = {}  # name -> (path, dtype, shape, byte offset, nbytes)
+        for path in files:
+            with open(path, "rb") as f:
+                n = int.from_bytes(f.read(8), "little")
+                header = json.loads(f.read(n))
+            base = 8 + n
+            for name, meta in header.items():
+                if name == "__metadata__":
                     continue
-                import torch
+                lo, hi = meta["data_offsets"]
+                self.entries[name] = (path, meta["dtype"], tuple(meta["shape"]), base + lo, hi - lo)
 
-                params[flat] = reshape_param(cfg, flat, f.get_tensor(ck).to(torch.bfloat16))
-                done += 1
-                if progress:
-                    progress(done, total, flat)
-    missing = sorted(set(shapes) - set(params))
-    if missing:
-        raise KeyError(f"missing {len(missing)} params, e.g. {missing[:5]}")
-    return params
+    def __contains__(self, name: str) -> bool:
+        return name in self.entries
+
+    def array(self, name: str):
+        """(numpy memmap of the tensor in its stored shape, dtype tag); bf16 is uint16."""
+        import numpy as np
+
+        path, dtype, shape, off, nbytes = self.entries[name]
+        if dtype not in _ST_DTYPES:
+            raise ValueError(f"{name}: unsupported checkpoint dtype {dtype}")
+        npdt, tag = _ST_DTYPES[dtype]
+        count = nbytes // np.dtype(npdt).itemsize
+        mm = np.memmap(path, dtype=npdt, mode="r", offset=off, shape=(count,))
+        return mm.reshape(shape) if shape else mm.reshape(()), tag
+
+
+def _to_bf16_tensor(a, tag: str, device):
+    """A slice of a checkpoint memmap as a bf16 tensor on ``device``: only the slice's
+    pages are read; the result never aliases the (read-only) file mapping."""
+    import numpy as np
+    import torch
+
+    a = np.ascontiguousarray(a)
+    if not a.flags.writeable:  # an unsliced mapping: copy once (the host-to-device copy
+        a = np.array(a)        # would otherwise read it in place, but a CPU result may not)
+    if tag == "bf16":
+        t = torch.from_numpy(a.view(np.int16)).view(torch.bfloat16)
+    else:
+        t = torch.from_numpy(a).to(torch.bfloat16)
+    return t.to(device)
+
+
+def load_params(cfg: TextConfig, model_dir: str, mesh: Mesh | None = None, progress=None, device=None) -> dict:
+    """This rank's packed parameter shard (native tensor name -> tensor on ``device``)
+    from an HF safetensors checkpoint -- the reference's ``load_params`` (weights.py:86-135)
+    for one rank of the ``tp`` mesh.
+
+    Every parameter is mapped, viewed in its canonical shape, sliced along its
+    ``param_specs`` axis for this rank, and only that slice is copied to the GPU, so a
+    rank reads its own ~1/world of the expert and projection bytes.  Raises
+    FileNotFoundError without checkpoint files and KeyError naming the parameters the
+    checkpoint lacks (before anything is copied).
+    """
+    import torch
+
+    from .model import param_specs, shard_param
+
+    mesh = mesh or Mesh()
+    device = device if device is not None else torch.device("cuda", mesh.device)
+    ckpt = SafetensorsDir(model_dir)
+    to_ckpt = {flat: name for name, flat in checkpoint_key_map(cfg).items()}
+    shapes, specs = param_shapes(cfg), param_specs(cfg)
+    absent = [flat for flat in shapes if to_ckpt.get(flat) not in ckpt]
+    if absent:
+        raise KeyError(f"{model_dir}: the checkpoint lacks {len(absent)} of the model's {len(shapes)} "
+                       f"parameters, first {absent[:5]}")
+    done = [0]
+
+    def shard_of(flat: str):
+        arr, tag = ckpt.array(to_ckpt[flat])
+        part = shard_param(as_canonical(cfg, flat, arr), specs[flat], mesh)
+        t = _to_bf16_tensor(part, tag, device)
+        done[0] += 1
+        if progress:
+            progress(done[0], len(shapes), flat)
+        return t
+
+    return {name: t.contiguous() for name, t in pack_rank_shard(cfg, shard_of, mesh, presharded=True)}
 
 
 def param_bytes(cfg: TextConfig) -> int:

@@ -56,3 +56,39 @@ def test_real_shapes_tensor_parallel(world):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_moe_block_sharded(world):
     _run(world, "moe_block")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_single_process_engine_owns_all_devices(world):
+    """One process drives `world` GPUs (the reference's single-process engine over every
+    device): in-process communicators with direct peer addressing, each step launched on
+    every device from one host thread.  Greedy tokens follow the oracle where decided and
+    equal the single-GPU engine's up to the first undecided position; sampling with a seed
+    is reproducible."""
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
+    from gemma4_b200.config import tiny_parity_config
+    from gemma4_b200.engine import Engine
+    from gemma4_b200.model import Mesh
+    from gemma4_b200.weights import random_params
+    from oracle.reference_model import Oracle
+    from test_gpu_decode import decided_mask
+
+    cfg = tiny_parity_config()
+    params = random_params(cfg, 0)
+    eng = Engine(None, max_len=96, cfg=cfg, params=params, devices=list(range(world)))
+    assert eng.n_devices == world and len(eng.models) == world
+    eng.compile_all()
+    prompt = list(range(5, 25))
+    a = [e["token"] for e in eng.generate(prompt, 10, temperature=0.0, stop_ids=())]
+    s1 = [e["token"] for e in eng.generate(prompt, 10, seed=3, stop_ids=())]
+    s2 = [e["token"] for e in eng.generate(prompt, 10, seed=3, stop_ids=())]
+    del eng
+    one = Engine(None, max_len=96, cfg=cfg, params=params, mesh=Mesh(0, 1, 0))
+    b = [e["token"] for e in one.generate(prompt, 10, temperature=0.0, stop_ids=())]
+    ref, ref_ids = Oracle(cfg, params, mode="bf16").greedy_generate(prompt, 10, 96, teacher=a)
+    dec = decided_mask(ref[len(prompt) - 1:]).tolist()
+    assert all(x == y for x, y, d in zip(a, ref_ids, dec) if d), (a, ref_ids)
+    upto = dec.index(False) if False in dec else len(dec)
+    assert a[:upto] == b[:upto], (a, b)
+    assert s1 == s2

@@ -25,12 +25,13 @@ pytestmark = pytest.mark.gpu
 DEV = torch.device("cuda", 0)
 
 
-def _prefill_case(cfg, params, prompt, max_len, chunk, n_dec, name):
+def _prefill_case(cfg, params, prompt, max_len, chunk, n_dec, name, dense=False):
     shard = rank_shard(cfg, params.__getitem__, Mesh(0, 1, 0), DEV)
     m = DecodeModel(cfg, shard, Mesh(0, 1, 0), max_len)
     p = len(prompt)
     m.reset(prompt, write_logits=True)
-    assert m.prefill(p, chunk)
+    assert m.prefill(p, chunk, dense_moe=dense)
+    name = f"{name} {'dense' if dense else 'routed'} MoE"
     torch.cuda.synchronize()
     m.check_status()
     assert int(m.ctrl[0]) == p
@@ -72,24 +73,36 @@ def _prefill_case(cfg, params, prompt, max_len, chunk, n_dec, name):
         assert bool((got.argmax(-1) == refs.argmax(-1))[d].all())
 
 
+@pytest.mark.parametrize("dense", [False, True])
 @pytest.mark.parametrize("chunk", [0, 128])
-def test_prefill_tiny_config1(chunk):
+def test_prefill_tiny_config1(chunk, dense):
     """config 1: 128-token prompt (one chunk) and a 300-token prompt in 128-token chunks
-    (sliding window 64: later chunks attend across the chunk boundary)."""
+    (sliding window 64: later chunks attend across the chunk boundary); routed and dense
+    (all-expert) MoE."""
     cfg = tiny_parity_config()
     params = random_params(cfg, 0)
     n = 128 if chunk == 0 else 300
     prompt = torch.randint(0, cfg.vocab_size, (n,), generator=torch.Generator().manual_seed(9)).tolist()
-    _prefill_case(cfg, params, prompt, 512, chunk, 4, f"config1 T={n} chunk={chunk or 'all'}")
+    _prefill_case(cfg, params, prompt, 512, chunk, 4, f"config1 T={n} chunk={chunk or 'all'}", dense)
 
 
-def test_prefill_real_layer_shapes():
-    """26B-A4B per-layer shapes, 2 layers [sliding, full], 16 experts top-8 (the dense
-    all-expert MoE), vocab 16384, 256-token prompt."""
+@pytest.mark.parametrize("dense", [False, True])
+def test_prefill_real_layer_shapes(dense):
+    """26B-A4B per-layer shapes, 2 layers [sliding, full], 16 experts top-8, vocab 16384,
+    256-token prompt, routed and dense (all-expert) MoE."""
     cfg = make_config(num_hidden_layers=2, layer_types=(SLIDING, FULL), num_experts=16, vocab_size=16384)
     params = random_params(cfg, 3)
     prompt = torch.randint(0, cfg.vocab_size, (256,), generator=torch.Generator().manual_seed(4)).tolist()
-    _prefill_case(cfg, params, prompt, 1536, 0, 2, "real_shapes_2_layers T=256")
+    _prefill_case(cfg, params, prompt, 1536, 0, 2, "real_shapes_2_layers T=256", dense)
+
+
+def test_prefill_128_experts_short_prompt():
+    """128 experts top-8 (the full model's router and expert count), 40-token prompt:
+    short prompts use the split-K path of the narrow projections."""
+    cfg = make_config(num_hidden_layers=2, layer_types=(SLIDING, FULL), vocab_size=32768)
+    params = random_params(cfg, 6)
+    prompt = torch.randint(0, cfg.vocab_size, (40,), generator=torch.Generator().manual_seed(6)).tolist()
+    _prefill_case(cfg, params, prompt, 256, 0, 2, "128_experts T=40")
 
 
 def test_prefill_real_shapes_long_chunks_and_d512():
