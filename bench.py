@@ -69,6 +69,7 @@ def parse_args():
     ap.add_argument("--cpu-steps", type=int, default=8)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-blocks", action="store_true", help="skip the config 2 / 3 block legs")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="benchmark config 5 prompt length for the prefill (TTFT) leg; 0 skips it")
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
@@ -308,6 +309,90 @@ def prefill_leg(eng, cfg, args, dev):
     return out
 
 
+# ----------------------------------------------------------------------------- blocks
+def block_legs(args, dev, reps=20):
+    """Benchmark configs 2 and 3 through their C-ABI block entry points, world 1: the MoE
+    block (router + top-8 experts, hidden 2816, 128 experts, F 704, seed 1) and decode
+    attention over a 32,768-row cache (sliding: 16 q / 8 KV heads, window 1024; full k==v:
+    16 q / 2 KV heads, 32,768 live keys), d 256, at the last position.  Each call is timed
+    alone with CUDA events after a 256 MB write that flushes L2; achieved GB/s = the
+    call's algorithmic bytes / mean time, against the measured HBM copy peak."""
+    import ctypes
+
+    import torch
+
+    from gemma4_b200 import _native as N
+    from gemma4_b200.config import make_config
+    from gemma4_b200.weights import random_param
+
+    peak, peak_kind = peaks()
+    L = N.lib()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    st = N.stream_handle()
+
+    def timed(call):
+        ts = []
+        for _ in range(reps + 2):
+            flush.fill_(1)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            call()
+            e1.record()
+            torch.cuda.synchronize(dev)
+            ts.append(e0.elapsed_time(e1))
+        return sum(ts[2:]) / reps  # ms, after 2 warm-up calls
+
+    out = {"l2_policy": "256 MB L2 flush before each timed call", "peak_gbs": peak, "peak_kind": peak_kind}
+    # ---- config 2: MoE block
+    cfg = make_config(num_hidden_layers=1, layer_types=("sliding_attention",))
+    names = ("router.proj", "router.scale", "router.per_expert_scale", "experts.gate_up_proj", "experts.down_proj")
+    w = {n: random_param(cfg, "layers.0." + n, 1, device=dev) for n in names}
+    g = torch.Generator(device=dev).manual_seed(1)
+    xs = [torch.randn(cfg.hidden_size, device=dev, generator=g).to(torch.bfloat16) for _ in range(reps + 2)]
+    o = torch.empty(cfg.hidden_size, dtype=torch.bfloat16, device=dev)
+    ctrl = torch.zeros(N.CTRL_WORDS, dtype=torch.int32, device=dev)
+    ccfg = N.G4Config.from_text_config(cfg)
+    it = iter(range(10 ** 9))
+
+    def moe():
+        x = xs[next(it) % len(xs)]  # a new token each call: new experts, no L2 reuse
+        N.check(L.g4_moe_block(ctypes.byref(ccfg), 0, 1, None, N.ptr(x), N.ptr(w["router.proj"]),
+                               N.ptr(w["router.scale"]), N.ptr(w["router.per_expert_scale"]),
+                               N.ptr(w["experts.gate_up_proj"]), N.ptr(w["experts.down_proj"]), N.ptr(o), None,
+                               None, N.ptr(ctrl), st), "g4_moe_block")
+
+    ms = timed(moe)
+    H, E, F, K = cfg.hidden_size, cfg.num_experts, cfg.moe_intermediate_size, cfg.top_k_experts
+    b = 2 * (E * H + K * 3 * F * H)
+    out["moe_block_config2"] = {"us": 1000 * ms, "algorithmic_bytes": b, "achieved_gbs": b / ms / 1e6,
+                                "frac": b / ms / 1e6 / peak, "kernels": 3}
+    del w, xs
+    # ---- config 3: decode attention at position 32767
+    max_len, d = 32768, 256
+    for name, nq, nkv, window, theta, partial, kv_eq in (("attention_sliding_config3", 16, 8, 1024, 1e4, 1.0, 0),
+                                                          ("attention_full_kv_config3", 16, 2, 0, 1e6, 0.25, 1)):
+        rows = nq * d + nkv * d * (1 if kv_eq else 2)
+        qkv = torch.randn(rows, device=dev, generator=g).to(torch.bfloat16)
+        qn = torch.ones(d, dtype=torch.bfloat16, device=dev)
+        ck = torch.randn(max_len, nkv, d, device=dev, generator=g).to(torch.bfloat16)
+        cv = torch.randn(max_len, nkv, d, device=dev, generator=g).to(torch.bfloat16)
+        ctx = torch.empty(nq * d, dtype=torch.bfloat16, device=dev)
+        pos = max_len - 1
+
+        def attn():
+            N.check(L.g4_attention_decode(N.ptr(qkv), N.ptr(qn), N.ptr(qn), N.ptr(ck), N.ptr(cv), max_len, nq, nkv,
+                                          d, kv_eq, pos, window, theta, partial, 1e-6, N.ptr(ctx), st),
+                    "g4_attention_decode")
+
+        ms = timed(attn)
+        live = min(window, pos + 1) if window else pos + 1
+        b = 2 * 2 * live * nkv * d + 2 * rows + 2 * nq * d  # K and V rows read, q|k|v in, ctx out
+        out[name] = {"us": 1000 * ms, "live_keys": live, "algorithmic_bytes": b, "achieved_gbs": b / ms / 1e6,
+                     "frac": b / ms / 1e6 / peak}
+        del ck, cv
+    return out
+
+
 # ----------------------------------------------------------------------------- GPU arm
 def tokens_check(generated, prompt, cfg, args, world, rank, local, dev):
     """N > 1: the timed run's generated tokens must be identical on every rank; rank 0
@@ -485,6 +570,7 @@ def main() -> int:
                "path": "Engine.generate (temperature 0), wall clock call -> last token"}
 
     prefill = prefill_leg(eng, cfg, args, dev) if args.prefill_tokens > 0 and world == 1 else None
+    blocks = block_legs(args, dev) if world == 1 and not args.no_blocks else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -504,7 +590,7 @@ def main() -> int:
             "scaling": "strong", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
             "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
-            "cpu_baseline": cpu, "tokens_match": tokens_match, "prefill": prefill,
+            "cpu_baseline": cpu, "tokens_match": tokens_match, "prefill": prefill, "blocks": blocks,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

@@ -91,7 +91,18 @@ def main():
     from gemma4_b200.model import Mesh
 
     cfg = make_config(num_hidden_layers=args.layers)
-    eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=3, mesh=Mesh(0, 1, 0), engine=args.engine)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank, local = int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:  # under torchrun: every rank traces its own GPU, rank 0 prints
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=3, mesh=Mesh(rank, world, local),
+                 engine=args.engine)
     eng.compile_all()
     m = eng.model
     prompt = list(range(100, 132))
@@ -103,8 +114,14 @@ def main():
     m.check_status()
     buf = np.zeros((TRACE_LAUNCHES, TRACE_CTAS, TRACE_EVENTS), np.uint64)
     N.check(N.lib().g4_trace_read(buf.ctypes.data, buf.nbytes), "g4_trace_read")
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+        if rank != 0:
+            return 0
     ncta, span, st = phase_stats(buf, args.layers)
-    print(f"engine {args.engine}, {args.layers} layers, {ncta} CTAs traced, step span {span:.1f} us")
+    print(f"engine {args.engine}, {args.layers} layers, world {world} (rank 0 shown), {ncta} CTAs traced, "
+          f"step span {span:.1f} us")
     cols = ["start-skew", "stage", "const+bar", "compute", "first-tile", "tiles", "straggle", "gap", "span"]
     print("kind   " + " ".join(f"{c:>10s}" for c in cols))
     for k in KINDS:
