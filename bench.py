@@ -70,6 +70,8 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-blocks", action="store_true", help="skip the config 2 / 3 block legs")
+    ap.add_argument("--long-context-steps", type=int, default=20,
+                    help="steps timed at the end of the 32K cache (all keys live); 0 skips")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="benchmark config 5 prompt length for the prefill (TTFT) leg; 0 skips it")
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
@@ -518,6 +520,38 @@ def main() -> int:
     generated = m.tokens_out[len(prompt):len(prompt) + n_gen].clone()
     tokens_match = tokens_check(generated, prompt, cfg, args, world, rank, local, dev) if world > 1 else None
 
+    # ---- the same steps with 32K live keys: decode at the end of the resident cache, where
+    # every full layer attends to the whole cache and every sliding layer to its full window
+    # (the reference's decode cost at any position; here the worst case)
+    long_ctx = None
+    if args.long_context_steps > 0:
+        n_long = args.long_context_steps
+        p0 = args.max_len - n_long - 1
+        m.reset(prompt)
+        m.ctrl[0] = p0  # positions p0.. read tokens_out (their values do not change the time)
+        m.step(2)
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        m.step(n_long - 2)
+        e1.record()
+        barrier()
+        m.check_status()
+        lms = e0.elapsed_time(e1)
+        if world > 1:
+            t = torch.tensor([lms], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            lms = float(t.item())
+        lpos = p0 + n_long // 2
+        lb = sum(class_bytes(cfg, world, lpos).values())
+        lval = (n_long - 2) / (lms / 1000.0)
+        long_ctx = {"position": lpos, "live_keys_full_layers": lpos + 1, "value": lval, "unit": "tok/s",
+                    "ms_per_step": lms / (n_long - 2), "bytes_per_launch_rank": lb,
+                    "achieved_gbs_rank": lb / (lms / (n_long - 2) / 1000.0) / 1e9}
+        long_ctx["frac"] = long_ctx["achieved_gbs_rank"] / peaks()[0]
+        m.reset(prompt)  # back to the start of the cache for the per-kernel profile below
+        m.step(len(prompt))
+
     # ---- per-kernel-class timing of the per-op kernels (event-separated steps)
     prof = m.profile(args.profile_steps)
     barrier()
@@ -591,6 +625,7 @@ def main() -> int:
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
             "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
             "cpu_baseline": cpu, "tokens_match": tokens_match, "prefill": prefill, "blocks": blocks,
+            "long_context": long_ctx,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

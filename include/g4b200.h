@@ -104,7 +104,9 @@ const char* g4_last_error(void);
  * 64-byte IPC handles from g4_comm_get_handle (any host transport) and pass all of
  * them, in rank order, to g4_comm_open, which maps every peer buffer for direct
  * NVLink stores.  Replaces the implicit GSPMD collectives (model.py:303, 310, 316,
- * 381-382). */
+ * 381-382).  The exchange flags count the steps of the control block they serve
+ * (control[STEP] is the epoch): a communicator serves one model, or one caller's
+ * control block for g4_moe_block; a new model needs a new communicator. */
 int g4_comm_create(int device, int rank, int world, int hidden_size, g4_comm** out);
 int g4_comm_get_handle(const g4_comm* comm, void* handle_out /* 64 bytes, host */);
 int g4_comm_open(g4_comm* comm, const void* handles /* world*64 bytes, host */);

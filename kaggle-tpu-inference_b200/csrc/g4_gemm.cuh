@@ -61,6 +61,7 @@ struct GemmArgs {
   long long split_stride;  //   sum to C + s * split_stride (elements; C is fp32 then)
   const int* z_rows;     // grouped GEMM: entry z owns A / C rows [z_rows[z], z_rows[z+1]) and
                          //   its M is their count (za_row / zc_row then unused); else null
+  int nz;                // batch entries (the persistent kernel walks n_tiles x m_tiles x nz x ksplit)
   int* status;           // error bits (bounded waits)
 };
 
@@ -356,6 +357,235 @@ __global__ void __launch_bounds__(kGemmThreads, 1) gemm_kernel(const __grid_cons
   if (warp == 1) {
     tc_fence_after();
     asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(BN) : "memory");
+  }
+}
+
+// ------------------------------------------------------------------ persistent variant
+// Tile t of the launch (n fastest, then m, then batch entry z and split s) and whether it
+// is computed; every role walks the same sequence and skips the same tiles.
+struct GemmTile {
+  int n0, m0, z, split, M, kb0, kb1;
+  int arow_base;
+  long long crow_base;
+};
+
+template <int BN>
+__device__ __forceinline__ bool gemm_tile(const GemmArgs& a, int t, int n_tn, int n_tm, int ks, GemmTile& T) {
+  T.n0 = (t % n_tn) * BN;
+  const int r = t / n_tn;
+  T.m0 = (r % n_tm) * kGemmBM;
+  const int zs = r / n_tm;
+  T.z = zs / ks;
+  T.split = zs % ks;
+  T.M = a.M;
+  T.arow_base = a.a_row0 + T.z * a.za_row;
+  T.crow_base = (long long)T.z * a.zc_row;
+  if (a.z_rows) {
+    const int r0 = __ldg(a.z_rows + T.z), r1 = __ldg(a.z_rows + T.z + 1);
+    T.M = r1 - r0;
+    T.arow_base = a.a_row0 + r0;
+    T.crow_base = r0;
+  }
+  if (T.m0 >= T.M) return false;
+  if (!gemm_tile_range(a, T.M, T.m0, T.n0, BN, T.kb0, T.kb1)) return false;
+  if (ks > 1) {
+    const int per = (T.kb1 - T.kb0 + ks - 1) / ks;
+    const int s0 = T.kb0 + T.split * per;
+    T.kb1 = min(T.kb1, s0 + per);
+    T.kb0 = min(s0, T.kb1);
+  }
+  return true;
+}
+
+// One persistent CTA per SM walks tiles blockIdx.x, blockIdx.x + gridDim.x, ...  The TMA
+// ring runs across tile boundaries, and TMEM holds TWO accumulators (2 x BN columns): the
+// MMA lane fills one while the epilogue warps drain the other, so the epilogue of a tile
+// overlaps the main loop of the next (acc_full / acc_empty mbarriers per buffer).
+template <int BN>
+__global__ void __launch_bounds__(kGemmThreads, 1) gemm_persistent_kernel(const __grid_constant__ GemmParams P) {
+  constexpr int STAGES = BN >= 256 ? 4 : 6;
+  constexpr int BSTAGE = BN * kGemmBK * 2;
+  constexpr uint32_t STAGE_TX = kGemmAStage + BSTAGE;
+  extern __shared__ unsigned char gemm_smem_raw[];
+  unsigned char* smem =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(gemm_smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* sa = smem;
+  unsigned char* sb = smem + STAGES * kGemmAStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(sb + STAGES * BSTAGE);
+  uint64_t* empty = full + STAGES;
+  uint64_t* acc_full = empty + STAGES;  // [2]
+  uint64_t* acc_empty = acc_full + 2;   // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(acc_empty + 2);
+  volatile int* abort = reinterpret_cast<volatile int*>(tmem_slot + 1);
+  volatile int* issued = abort + 1;
+  volatile int* consumed = abort + 2;
+
+  const GemmArgs& a = P.a;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int ks = a.ksplit > 1 ? a.ksplit : 1;
+  const int n_tn = (a.N + BN - 1) / BN, n_tm = (a.M + kGemmBM - 1) / kGemmBM;
+  const int ntiles = n_tn * n_tm * (a.nz > 0 ? a.nz : 1) * ks;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 4);  // one arrival per epilogue warp
+    }
+    *abort = 0;
+    *issued = 0;
+    *consumed = 0;
+    mbar_init_fence();
+    tma_prefetch_desc(&P.ta);
+    tma_prefetch_desc(&P.tb);
+  }
+  if (warp == 1) {  // TMEM: two BN-column fp32 accumulators
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(tmem_slot)),
+                 "r"(2 * BN)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int i = 0;  // k-blocks issued by this CTA (ring position)
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        GemmTile T;
+        if (!gemm_tile<BN>(a, t, n_tn, n_tm, ks, T)) continue;
+        const int acol0 = a.a_col0 + T.z * a.za_col;
+        const int zb = T.z / a.zb_div;
+        const int brow = a.b_row0 + zb * a.zb_row + T.n0, bcol0 = a.b_col0 + zb * a.zb_col;
+        const int arow = T.arow_base + T.m0;
+        for (int kb = T.kb0; kb < T.kb1; ++kb, ++i) {
+          const int s = i % STAGES;
+          if (i >= STAGES && !gemm_wait(&empty[s], ((i / STAGES) - 1) & 1, a.status, abort)) break;
+          mbar_arrive_expect_tx(&full[s], STAGE_TX);
+          if (a.b_kpe > 0) {
+            const int slab = kb / a.b_kpe, kin = (kb % a.b_kpe) * kGemmBK;
+            tma_load_2d(sa + s * kGemmAStage, &P.ta, acol0 + slab * a.a_slab + kin, arow, &full[s]);
+            tma_load_3d(sb + s * BSTAGE, &P.tb, kin, brow, slab, &full[s]);
+          } else {
+            tma_load_2d(sa + s * kGemmAStage, &P.ta, acol0 + kb * kGemmBK, arow, &full[s]);
+            tma_load_2d(sb + s * BSTAGE, &P.tb, bcol0 + kb * kGemmBK, brow, &full[s]);
+          }
+          *issued = i + 1;
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16(kGemmBM, BN);
+      int i = 0, it = 0;  // k-blocks consumed, tiles accumulated
+      for (int t = blockIdx.x; t < ntiles && !*abort; t += gridDim.x) {
+        GemmTile T;
+        if (!gemm_tile<BN>(a, t, n_tn, n_tm, ks, T)) continue;
+        const int b = it & 1, use = it >> 1;
+        ++it;
+        if (use > 0 && !gemm_wait(&acc_empty[b], (use - 1) & 1, a.status, abort)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + (uint32_t)(b * BN);
+        bool ok = true;
+        for (int kb = T.kb0; kb < T.kb1; ++kb, ++i) {
+          const int s = i % STAGES;
+          if (!gemm_wait(&full[s], (i / STAGES) & 1, a.status, abort)) {
+            ok = false;
+            break;
+          }
+          *consumed = i + 1;
+          tc_fence_after();
+          const uint32_t a_addr = smem_addr(sa + s * kGemmAStage), b_addr = smem_addr(sb + s * BSTAGE);
+#pragma unroll
+          for (int kk = 0; kk < kGemmBK / 16; ++kk)
+            umma_bf16(acc, umma_desc_sw128(a_addr + kk * 32), umma_desc_sw128(b_addr + kk * 32), idesc,
+                      (kb > T.kb0 || kk > 0) ? 1u : 0u);
+          umma_commit(&empty[s]);
+        }
+        umma_commit(&acc_full[b]);  // this tile's MMAs (or none) are complete
+        if (!ok) break;
+      }
+    }
+  } else {
+    // ---------------------------------------------------------------- epilogue
+    const int q = warp & 3;
+    int it = 0;
+    for (int t = blockIdx.x; t < ntiles; t += gridDim.x) {
+      GemmTile T;
+      if (!gemm_tile<BN>(a, t, n_tn, n_tm, ks, T)) continue;
+      const int b = it & 1, use = it >> 1;
+      ++it;
+      const bool has_k = T.kb1 > T.kb0;
+      int ready = 1;
+      if (lane == 0) ready = gemm_wait(&acc_full[b], use & 1, a.status, abort) ? 1 : 0;
+      ready = __shfl_sync(0xffffffffu, ready, 0);
+      if (!ready) break;
+      tc_fence_after();
+      const int row = T.m0 + q * 32 + lane;
+      const bool row_ok = row < T.M;
+      const long long crow = T.crow_base + row;
+      const long long ccol0 = (long long)T.z * a.zc_col + T.n0;
+      const bool out_f32 = a.c_f32 || ks > 1;
+      void* cbase = ks > 1 ? static_cast<void*>(static_cast<float*>(a.C) + T.split * a.split_stride) : a.C;
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 32) {
+        uint32_t r[32];
+        if (has_k) {
+          tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + (uint32_t)(b * BN + c0), r);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) r[i] = 0u;
+        }
+        if (!row_ok || T.n0 + c0 >= a.N) continue;
+        const int ncols = min(32, a.N - (T.n0 + c0));
+        if (out_f32) {
+          float* dst = reinterpret_cast<float*>(cbase) + crow * a.ldc + ccol0 + c0;
+          if (ncols == 32 && (((uintptr_t)dst) & 15) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 4)
+              *reinterpret_cast<uint4*>(dst + i) = make_uint4(r[i], r[i + 1], r[i + 2], r[i + 3]);
+          } else {
+            for (int i = 0; i < ncols; ++i) dst[i] = __uint_as_float(r[i]);
+          }
+        } else {
+          bf16_t* dst = reinterpret_cast<bf16_t*>(cbase) + crow * a.ldc + ccol0 + c0;
+          if (ncols == 32 && (((uintptr_t)dst) & 15) == 0) {
+#pragma unroll
+            for (int i = 0; i < 32; i += 8) {
+              uint4 u;
+              u.x = (uint32_t)f2bf(__uint_as_float(r[i])) | ((uint32_t)f2bf(__uint_as_float(r[i + 1])) << 16);
+              u.y = (uint32_t)f2bf(__uint_as_float(r[i + 2])) | ((uint32_t)f2bf(__uint_as_float(r[i + 3])) << 16);
+              u.z = (uint32_t)f2bf(__uint_as_float(r[i + 4])) | ((uint32_t)f2bf(__uint_as_float(r[i + 5])) << 16);
+              u.w = (uint32_t)f2bf(__uint_as_float(r[i + 6])) | ((uint32_t)f2bf(__uint_as_float(r[i + 7])) << 16);
+              *reinterpret_cast<uint4*>(dst + i) = u;
+            }
+          } else {
+            for (int i = 0; i < ncols; ++i) dst[i] = f2bf(__uint_as_float(r[i]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[b]);  // this warp's quadrant of buffer b is read
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (threadIdx.x == 0 && *abort) {
+    for (int i = *consumed; i < *issued; ++i) {
+      const uint64_t t0 = globaltimer_ns();
+      while (!mbar_try_wait(&full[i % STAGES], (i / STAGES) & 1) && globaltimer_ns() - t0 < kLocalTimeoutNs) {
+      }
+    }
+  }
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem), "r"(2 * BN) : "memory");
   }
 }
 

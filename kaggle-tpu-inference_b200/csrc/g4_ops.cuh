@@ -54,6 +54,7 @@ struct Common {
   int* counters;
   char* xbase[kMaxWorld];  // exchange buffer of every rank, mapped in this process
   int rank, world;
+  int nsig;                // CTAs per rank that signal each all-reduce use (its producers)
   int xpayload;            // floats per exchange slot
   int H;
   int layer, nlayers;
@@ -73,31 +74,56 @@ __device__ __forceinline__ int site_use(const int* ctrl, const Common& c, int si
   return site == kSiteArgmax ? step : step * c.nlayers + layer;
 }
 
-// All consumer threads: make this CTA's peer stores visible, then the last CTA of the
-// grid publishes flag value use+1 to every rank.
-__device__ __forceinline__ void xchg_signal(const Common& c, int site, int use, int counter_id) {
+// Arrival counter of (site, parity) in `peer`'s exchange buffer: a 64-bit word that every
+// signalling CTA of every rank increments once per use of that site and parity, so use u
+// of the site is complete when it reaches ((u >> 1) + 1) * nsig * world (monotonic: it is
+// never reset while the communicator serves its model).
+__device__ __forceinline__ unsigned long long* xcount(const Common& c, int peer, int site, int parity) {
+  return reinterpret_cast<unsigned long long*>(xflag(c, peer, site, parity, 0));
+}
+__device__ __forceinline__ unsigned long long xcount_target(const Common& c, int use) {
+  return (unsigned long long)((use >> 1) + 1) * (unsigned long long)c.nsig * (unsigned long long)c.world;
+}
+
+// All consumer threads: make this CTA's peer stores visible (system-scope fence per
+// thread), then thread 0 counts this CTA in on every rank with one release reduction
+// each -- no grid-wide counter and no last-CTA hop on the critical path.
+__device__ __forceinline__ void xchg_signal(const Common& c, int site, int use, int /*counter_id*/) {
   __threadfence_system();
   named_bar(kBarReduce, kConsumerThreads);
   if (threadIdx.x == 0) {
-    int* cnt = c.counters + counter_id;
-    int old = atomic_add_acq_rel_gpu(cnt, 1);
-    if (old == (int)gridDim.x - 1) {
-      __threadfence_system();
-      for (int p = 0; p < c.world; ++p) st_release_sys(xflag(c, p, site, use & 1, c.rank), use + 1);
-      atomicExch(cnt, 0);
+    for (int p = 0; p < c.world; ++p) {
+      unsigned long long* cnt = xcount(c, p, site, use & 1);
+      asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(cnt), "l"(1ull) : "memory");
     }
   }
 }
 
-// Thread 0 waits for every rank's flag of (site, use); result broadcast to consumers.
-__device__ __forceinline__ bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
-  if (threadIdx.x == 0) {
-    int ok = 1;
-    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
-    for (int src = 0; src < c.world && ok; ++src)
-      ok = wait_flag_geq(xflag(c, c.rank, site, use & 1, src), use + 1, tmo, ctrl + G4_CTRL_STATUS);
-    sm.ints[kSmemOk] = ok;
+// Wait (bounded) until the local arrival counter of (site, use) reaches its target.
+__device__ __forceinline__ bool xchg_arrived(int* ctrl, const Common& c, int site, int use) {
+  const unsigned long long* cnt = xcount(c, c.rank, site, use & 1);
+  const unsigned long long target = xcount_target(c, use);
+  auto load = [cnt]() {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(cnt) : "memory");
+    return v;
+  };
+  if (load() >= target) return true;
+  const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
+  const uint64_t limit = static_cast<uint64_t>(tmo > 0 ? tmo : 1000000) * 1000ull;
+  const uint64_t t0 = globaltimer_ns();
+  while (load() < target) {
+    if (globaltimer_ns() - t0 > limit) {
+      atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_PEER_TIMEOUT);
+      return false;
+    }
   }
+  return true;
+}
+
+// Thread 0 waits for every rank's contributions to (site, use); broadcast to consumers.
+__device__ __forceinline__ bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
+  if (threadIdx.x == 0) sm.ints[kSmemOk] = xchg_arrived(ctrl, c, site, use) ? 1 : 0;
   named_bar(kBarReduce, kConsumerThreads);
   return sm.ints[kSmemOk] != 0;
 }

@@ -549,11 +549,25 @@ int gemm_prepare(int bn) {
   cudaGetDevice(&dev);
   std::lock_guard<std::mutex> lock(mu);
   if (done[{dev, bn}]) return G4_OK;
-  const void* k = bn == 256 ? reinterpret_cast<const void*>(gemm_kernel<256>)
-                            : reinterpret_cast<const void*>(gemm_kernel<128>);
-  G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(bn)), G4_ERR_LAUNCH);
+  const void* ks[2] = {bn == 256 ? reinterpret_cast<const void*>(gemm_kernel<256>)
+                                 : reinterpret_cast<const void*>(gemm_kernel<128>),
+                       bn == 256 ? reinterpret_cast<const void*>(gemm_persistent_kernel<256>)
+                                 : reinterpret_cast<const void*>(gemm_persistent_kernel<128>)};
+  for (const void* k : ks)
+    G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, gemm_smem_bytes(bn)),
+            G4_ERR_LAUNCH);
   done[{dev, bn}] = true;
   return G4_OK;
+}
+
+// The persistent GEMM (one CTA per SM, double-buffered TMEM accumulators) is the default;
+// G4_GEMM_TILES=1 launches one CTA per output tile instead (kept for A/B measurement).
+bool gemm_tiles_mode() {
+  static const bool v = [] {
+    const char* e = getenv("G4_GEMM_TILES");
+    return e && e[0] == '1';
+  }();
+  return v;
 }
 
 // out[m, n] = sum over the splits of part[s][m][n] (fixed order), as fp32 or bf16.
@@ -609,12 +623,22 @@ int gemm(const Operand& A, const Operand& B, GemmArgs g, int Z, cudaStream_t st,
   if (B.slabs) rc = make_map_3d(&P.tb, B.p, B.inner, B.rows, B.slabs, bn);
   else rc = make_map_2d(&P.tb, B.p, B.inner, B.rows, B.ld, bn);
   if (rc) return rc;
+  g.nz = Z;
   P.a = g;
-  const dim3 grid((g.N + bn - 1) / bn, (g.M + kGemmBM - 1) / kGemmBM, Z * S);
-  if (bn == 256)
-    gemm_kernel<256><<<grid, kGemmThreads, gemm_smem_bytes(256), st>>>(P);
-  else
-    gemm_kernel<128><<<grid, kGemmThreads, gemm_smem_bytes(128), st>>>(P);
+  if (gemm_tiles_mode()) {
+    const dim3 grid((g.N + bn - 1) / bn, (g.M + kGemmBM - 1) / kGemmBM, Z * S);
+    if (bn == 256)
+      gemm_kernel<256><<<grid, kGemmThreads, gemm_smem_bytes(256), st>>>(P);
+    else
+      gemm_kernel<128><<<grid, kGemmThreads, gemm_smem_bytes(128), st>>>(P);
+  } else {
+    const long long all = (long long)((g.N + bn - 1) / bn) * ((g.M + kGemmBM - 1) / kGemmBM) * Z * S;
+    const dim3 grid((unsigned)std::min<long long>(all, nsm));
+    if (bn == 256)
+      gemm_persistent_kernel<256><<<grid, kGemmThreads, gemm_smem_bytes(256), st>>>(P);
+    else
+      gemm_persistent_kernel<128><<<grid, kGemmThreads, gemm_smem_bytes(128), st>>>(P);
+  }
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   if (S > 1) {
     const size_t n = (size_t)g.M * g.N;

@@ -455,6 +455,7 @@ static Common make_common(const g4_model* m, int layer) {
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = m->comm ? m->comm->peer[p] : nullptr;
   c.rank = m->rank;
   c.world = m->world;
+  c.nsig = m->nsm;  // every matrix-product launch (step kernel or per-op kernel) has nsm CTAs
   c.xpayload = 2 * m->H;
   c.H = m->H;
   c.layer = layer;
@@ -1316,6 +1317,14 @@ char* block_scratch(size_t bytes) {
 }
 }  // namespace
 
+struct RopeTable {
+  float v[kAttnMaxD / 2];
+  int n;
+};
+__global__ void rope_table_kernel(const __grid_constant__ RopeTable p, float* dst) {
+  for (int i = threadIdx.x; i < p.n; i += blockDim.x) dst[i] = p.v[i];
+}
+
 extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, const void* k_norm,
                                    void* cache_k, void* cache_v, int max_len, int n_q_heads,
                                    int n_kv_heads, int head_dim, int k_eq_v, int pos, int window,
@@ -1349,11 +1358,13 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   a.ctrl = reinterpret_cast<int*>(s + kBlockCtrl);
   float* inv = reinterpret_cast<float*>(s + kBlockInvFreq);
   a.part = reinterpret_cast<float*>(s + kBlockPartOffset);
-  std::vector<float> tab(head_dim / 2);
-  g4_rope_inv_freq(head_dim, theta, partial_rotary, tab.data());
+  // the RoPE table travels by value as a kernel parameter (no host copy, no stream sync)
+  RopeTable tab;
+  tab.n = head_dim / 2;
+  g4_rope_inv_freq(head_dim, theta, partial_rotary, tab.v);
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  G4_CUDA(cudaMemcpyAsync(inv, tab.data(), tab.size() * 4, cudaMemcpyHostToDevice, st), G4_ERR_CUDA);
-  G4_CUDA(cudaStreamSynchronize(st), G4_ERR_CUDA);
+  rope_table_kernel<<<1, 256, 0, st>>>(tab, inv);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   a.inv_freq = inv;
   a.pos_fixed = pos;
   a.n_kv = n_kv_heads;
@@ -1375,13 +1386,7 @@ __global__ void moe_block_reduce_kernel(Common c, int* ctrl, bf16_t* out) {
   pdl_wait();
   __shared__ int ok;
   const int use = site_use(ctrl, c, kSiteFfn, c.layer);
-  if (threadIdx.x == 0) {
-    int good = 1;
-    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
-    for (int src = 0; src < c.world && good; ++src)
-      good = wait_flag_geq(xflag(c, c.rank, kSiteFfn, use & 1, src), use + 1, tmo, ctrl + G4_CTRL_STATUS);
-    ok = good;
-  }
+  if (threadIdx.x == 0) ok = xchg_arrived(ctrl, c, kSiteFfn, use) ? 1 : 0;  // every rank's down CTAs
   __syncthreads();
   if (!ok) return;
   for (int h = threadIdx.x; h < c.H; h += blockDim.x) {
@@ -1435,6 +1440,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = world > 1 ? comm->peer[p] : nullptr;
   c.rank = rank;
   c.world = world;
+  c.nsig = nsm;  // the down-projection kernel's CTAs signal the all-reduce
   c.xpayload = 2 * H;
   c.H = H;
   c.layer = 0;

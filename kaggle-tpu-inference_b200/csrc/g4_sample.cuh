@@ -146,7 +146,7 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __g
   int n = 1;
   while (n < (int)gridDim.x * K) n <<= 1;
   float* mv = reinterpret_cast<float*>(sample_smem);
-  int* mi = reinterpret_cast<int*>(sample_smem + n * 4);
+  int* mi = reinterpret_cast<int*>(sample_smem + n * 4);  // (re-carved for the world merge)
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int b = i / K, k = i % K;
     const bool live = i < (int)gridDim.x * K;
@@ -182,6 +182,10 @@ static __global__ void __launch_bounds__(kSampleThreads) sample_kernel(const __g
     if (!ok) return;  // the greedy token stays; the status bit reports the timeout
     n = 1;
     while (n < a.c.world * K) n <<= 1;
+    // re-carve the value / index arrays for the new length (this rank's K best already
+    // sit in the exchange slots, so the old arrays are no longer read)
+    mv = reinterpret_cast<float*>(sample_smem);
+    mi = reinterpret_cast<int*>(sample_smem + n * 4);
     for (int i = threadIdx.x; i < n; i += blockDim.x) {
       const int src = i / K, k = i % K;
       const bool live = i < a.c.world * K;

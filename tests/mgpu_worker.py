@@ -43,14 +43,17 @@ def corr(a, b) -> float:
     return float(np.corrcoef(a.double().numpy().ravel(), b.double().numpy().ravel())[0, 1])
 
 
-def decode_run(cfg, params_dev, mesh, prompt, n_new, max_len, engine, comm=None):
-    """(logits of this rank's vocab slice [steps, V/W], generated ids) of one decode run."""
+def decode_run(cfg, params_dev, mesh, prompt, n_new, max_len, engine, comm=None, sampling=None):
+    """(logits of this rank's vocab slice [steps, V/W], generated ids) of one decode run;
+    ``sampling`` = (temperature, top_p, top_k, seed) draws on the device instead of argmax."""
     from gemma4_b200.runtime import DecodeModel
     from gemma4_b200.weights import rank_shard
 
     dev = torch.device("cuda", mesh.device)
     shard = rank_shard(cfg, params_dev.__getitem__, mesh, dev)
     m = DecodeModel(cfg, shard, mesh, max_len, comm, engine=engine)
+    if sampling:
+        m.set_sampling(*sampling)
     m.reset(prompt, write_logits=True)
     out = []
     for _ in range(len(prompt) + n_new - 1):
@@ -79,7 +82,28 @@ def case_decode(cfg, seed, prompt, n_new, max_len, engine):
     dist.all_gather(rings, ring)
     parts = [torch.empty_like(logits) for _ in range(world)]
     dist.all_gather(parts, logits)
+    # the same decode sampling on the device (temperature 1, top-p 0.9, top-k 64): every rank
+    # merges all ranks' candidates, so the draws must match the restatement on full logits
+    samp = (1.0, 0.9, 64, 4242)
+    comm.close()  # a communicator's flags count one model's steps: a new model gets a new one
+    comm = Comm(mesh, cfg.hidden_size)
+    slog, sring = decode_run(cfg, params_dev, mesh, prompt, n_new, max_len, engine, comm, sampling=samp)
+    srings = [torch.empty_like(sring) for _ in range(world)]
+    dist.all_gather(srings, sring)
+    sparts = [torch.empty_like(slog) for _ in range(world)]
+    dist.all_gather(sparts, slog)
     comm.close()
+    if dist.get_rank() == 0:
+        from oracle.reference_model import philox_uniform, sample_token
+
+        for r in range(1, world):
+            assert torch.equal(srings[r], srings[0]), f"rank {r} sampled ring differs from rank 0"
+        sfull = torch.cat(sparts, dim=-1).cpu()
+        p = len(prompt)
+        for pos in range(p - 1, p + n_new - 1):
+            u = philox_uniform(samp[3], 0 if pos == p - 1 else pos)
+            want = sample_token(sfull[pos], samp[0], samp[2], samp[1], u)
+            assert int(srings[0][pos + 1]) == want, (pos, int(srings[0][pos + 1]), want)
     msg = None
     if rank == 0:
         for r in range(1, world):
