@@ -70,6 +70,7 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-blocks", action="store_true", help="skip the config 2 / 3 block legs")
+    ap.add_argument("--prefill-only", action="store_true", help="profiling: run only the prefill leg")
     ap.add_argument("--long-context-steps", type=int, default=20,
                     help="steps timed at the end of the 32K cache (all keys live); 0 skips")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
@@ -483,6 +484,12 @@ def main() -> int:
     mesh = Mesh(rank, world, local)
     eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh,
                  engine=args.engine)
+    if args.prefill_only:  # profiling case: the prefill leg alone, one JSON line
+        line = {"metric": "prefill TTFT ms", "config": workload,
+                "prefill": prefill_leg(eng, cfg, args, dev) if world == 1 else None}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
     eng.compile_all()
     m = eng.model
     prompt = prompt_ids(cfg, args.prompt_len, args.seed)

@@ -178,6 +178,23 @@ int g4_model_set_engine(g4_model* model, int engine);
  * written (all 128 experts per token, 16x the MoE FLOPs at top-8). */
 #define G4_PREFILL_DENSE_MOE 0x1
 int g4_prefill(g4_model* model, int n_tokens, int chunk, int flags, void* stream);
+/* Batched decode: `batch` sequences decoded together (the forward over a [B, 1] token batch
+ * with a per-sequence cache, model.py:333-386 / 174-185; benchmark config 5's batch-8
+ * decode).  World 1, greedy.
+ * g4_batch_reserve: allocates a KV cache of ctx_len positions per sequence and layer and
+ *   the per-sequence control blocks (replaces any earlier reservation).
+ * g4_batch_prefill: sequence `seq`'s prompt, tokens_in[0, n_tokens), through g4_prefill's
+ *   tensor-core path into its cache; its first generated token goes to the sequence's
+ *   next-input slot (and to *token_out, device, if not NULL); its position becomes n.
+ * g4_batch_step: one token of every sequence: each projection as a tensor-core GEMM of the
+ *   B rows, the routed MoE over the B x top-k pairs, attention per sequence over its own
+ *   cache; writes every sequence's argmax as its next input (and to tokens_out[B] /
+ *   logits_out[B, vocab], device, if not NULL) and advances the positions.
+ * g4_batch_status: synchronises and ORs the sequences' status words (G4_ERR_TIMEOUT if set). */
+int g4_batch_reserve(g4_model* model, int batch, int ctx_len);
+int g4_batch_prefill(g4_model* model, int seq, int n_tokens, int* token_out, void* stream);
+int g4_batch_step(g4_model* model, int* tokens_out, float* logits_out, void* stream);
+int g4_batch_status(g4_model* model, void* stream, int* status_out);
 /* g4_gemm_bf16: C[M, N] = A[M, K] . B[N, K]^T on the tensor cores (tcgen05, TMEM accumulator,
  * TMA-fed), bf16 operands with row strides lda / ldb (elements, multiples of 8; 16-byte
  * aligned bases), fp32 accumulation, C in fp32 (c_f32 != 0) or rounded to bf16, row stride

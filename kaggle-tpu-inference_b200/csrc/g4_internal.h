@@ -57,6 +57,7 @@ inline cudaError_t launch_pdl(Kernel k, dim3 grid, dim3 block, size_t smem, cuda
 }
 
 struct PrefillWs;  // g4_prefill.cu
+struct BatchWs;    // g4_prefill.cu
 
 // ------------------------------------------------------------------ model
 struct LayerDev {
@@ -111,6 +112,7 @@ struct g4_model {
   cudaGraph_t graph = nullptr;
   cudaGraphExec_t gexec = nullptr;
   PrefillWs* prefill = nullptr;  // prefill workspace (g4_prefill), allocated on first use
+  BatchWs* batch = nullptr;      // batched decoder (g4_batch_reserve)
 };
 
 // Launch the sampler after a step's (or the prefill's) LM head (g4_runtime.cu).
@@ -118,6 +120,10 @@ int g4_launch_sampler(const g4_model* m, cudaStream_t st);
 int g4_prepare_sampler(const g4_model* m);
 // Free the prefill workspace (g4_prefill.cu).
 void g4_prefill_release(g4_model* m);
+// Free the batched decoder's caches and buffers (g4_prefill.cu).
+void g4_batch_release(g4_model* m);
+// Launch one decode-attention item grid (g4_runtime.cu).
+int g4_launch_attention(const AttnArgs& a, cudaStream_t st);
 // model.py:54-61: fp64 inverse frequencies of the rotated pairs, zero (NoPE) tail.
 void g4_rope_inv_freq(int d, double theta, double partial, float* out);
 float g4_host_bf16_round(float f);

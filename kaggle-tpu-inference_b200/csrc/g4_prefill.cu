@@ -442,13 +442,21 @@ __global__ void pf_combine(const bf16_t* mlp, const bf16_t* moe, bf16_t* x, cons
   }
 }
 
-// LM-head epilogue of the prompt's last position (model.py:381-385 + the greedy branch of
-// :414-424): softcapped fp32 logits of this rank's vocab slice, first index of the maximum
-// -> tokens_out[n]; POS = n.  One CTA.
-__global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegin, float softcap, int* tokens_out,
-                               int* tokens_host, int* ctrl, int n) {
+// LM-head epilogue of a row (model.py:381-385 + the greedy branch of :414-424):
+// softcapped fp32 logits of this rank's vocab slice, first index of the maximum ->
+// tok_out[out_index]; control POS = n.  One CTA per row: row r reads lg + r * V, writes
+// logits + r * V, tok_out[out_index + r] and ctrl + r * ctrl_stride (n + r * n_stride).
+__global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegin, float softcap, int* tok_out,
+                               int out_index, int* tokens_host, int* ctrl, int n, int ctrl_stride = 0,
+                               int n_stride = 0) {
   __shared__ float bv[32];
   __shared__ int bi[32];
+  const int row = blockIdx.x;
+  lg += (size_t)row * V;
+  logits += (size_t)row * V;
+  ctrl += (size_t)row * ctrl_stride;
+  out_index += row;
+  if (n >= 0) n += row * n_stride;
   float best = -INFINITY;
   int bidx = 0x7fffffff;
   for (int u = threadIdx.x; u < V; u += blockDim.x) {
@@ -481,9 +489,9 @@ __global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegi
       bidx = bi[w];
     }
   const int token = bidx == 0x7fffffff ? 0 : vbegin + bidx;
-  tokens_out[n] = token;
-  if (tokens_host) tokens_host[n] = token;
-  ctrl[G4_CTRL_POS] = n;
+  tok_out[out_index] = token;
+  if (tokens_host) tokens_host[out_index] = token;
+  ctrl[G4_CTRL_POS] = n >= 0 ? n : ctrl[G4_CTRL_POS] + 1;  // n < 0: a decode step advances
 }
 
 // ------------------------------------------------------------------ tensor maps
@@ -764,14 +772,14 @@ static int prefill_workspace(g4_model* m, int chunk) {
   return G4_OK;
 }
 
-static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, const float* inv, int pos0, int M, float eps,
-                          cudaStream_t st) {
+static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, bf16_t* ck, bf16_t* cv, const float* inv,
+                          int pos0, int M, float eps, cudaStream_t st) {
   const int nq = l.n_kv * l.g, rows = l.rows_q + l.rows_k + l.rows_v;
   const long long warps = (long long)M * (nq + 2 * l.n_kv);
   const dim3 grid((unsigned)((warps + 7) / 8));
-#define G4_QK(D)                                                                                              \
-  pf_qk_rope<D><<<grid, 256, 0, st>>>(qkv, rows, q, l.q_norm, l.k_norm, l.cache_k, l.cache_v, inv, nq, l.n_kv, \
-                                      l.k_eq_v, pos0, M, eps)
+#define G4_QK(D)                                                                                          \
+  pf_qk_rope<D><<<grid, 256, 0, st>>>(qkv, rows, q, l.q_norm, l.k_norm, ck, cv, inv, nq, l.n_kv, l.k_eq_v, \
+                                      pos0, M, eps)
   switch (l.d) {
     case 64: G4_QK(64); break;
     case 128: G4_QK(128); break;
@@ -821,18 +829,33 @@ static int routed_moe(g4_model* m, const LayerDev& l, int M, cudaStream_t st) {
   return G4_OK;
 }
 
+// Where a prefill reads its tokens and writes its caches and first token: the model's own
+// sequence, or one sequence of the batched decoder.
+struct PfTarget {
+  const int* tokens;                   // prompt tokens [n]
+  bf16_t* const* ck;                   // per layer: K / V cache [cache_len, kv, d]
+  bf16_t* const* cv;
+  int cache_len;
+  int* tok_out;                        // the first generated token goes to tok_out[out_index]
+  int out_index;
+  int* tok_host;                       // optional mapped host mirror of tok_out
+  int* ctrl;                           // control block (POS = n, STATUS)
+  float* logits;                       // fp32 softcapped logits of the last position
+};
+
 // One chunk of `M` prompt tokens at positions [c0, c0 + M) through every layer; `dense`
 // runs the MoE over all experts (the reference's prefill as written), else routed.
-static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, bool dense, cudaStream_t st) {
+static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, bool dense, cudaStream_t st,
+                         const PfTarget& tg) {
   PrefillWs& w = *m->prefill;
   const SplitBuf sb{w.split, w.split_elems};
   const g4_config& c = m->cfg;
   const int H = m->H, E = m->E, F = m->F_local, I = m->I_local, K = m->topk;
   const float eps = c.rms_norm_eps;
-  int* status = m->ctrl + G4_CTRL_STATUS;
+  int* status = tg.ctrl + G4_CTRL_STATUS;
   int rc;
-  pf_embed<<<M, 256, 0, st>>>(m->tokens_in + c0, m->embed, w.x, H, c.vocab_size,
-                              g4_host_bf16_round(std::sqrt((float)H)), m->ctrl);
+  pf_embed<<<M, 256, 0, st>>>(tg.tokens + c0, m->embed, w.x, H, c.vocab_size,
+                              g4_host_bf16_round(std::sqrt((float)H)), tg.ctrl);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   const float hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
   for (size_t li = 0; li < m->L.size(); ++li) {
@@ -844,7 +867,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
     if ((rc = gemm({w.xn, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.qkv, (uint64_t)H, (uint64_t)R, (uint64_t)H},
                    plain(M, R, H, w.qkv, R, status), 1, st, sb)))
       return rc;
-    if ((rc = launch_qk_rope(l, w.qkv, w.q, aa.inv_freq, c0, M, eps, st))) return rc;
+    if ((rc = launch_qk_rope(l, w.qkv, w.q, tg.ck[li], tg.cv[li], aa.inv_freq, c0, M, eps, st))) return rc;
     const int window = l.full ? 0 : c.sliding_window;
     const int lo = window > 0 ? std::max(0, c0 - window + 1) : 0, span = c0 + M - lo;
     {  // scores S_h = q_h . K^T, one z per query head (its KV head: z / g)
@@ -859,11 +882,12 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
       g.key_pos0 = lo;
       g.window = window;
       if ((rc = gemm({w.q, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
-                     {l.cache_k, (uint64_t)l.n_kv * d, (uint64_t)m->max_len, (uint64_t)l.n_kv * d}, g, nq, st)))
+                     {tg.ck[li], (uint64_t)l.n_kv * d, (uint64_t)tg.cache_len, (uint64_t)l.n_kv * d}, g, nq,
+                     st)))
         return rc;
     }
     pf_softmax<<<nq * M, 256, 0, st>>>(w.sp, M, w.ks, span, c0, lo, window);
-    pf_vtrans<<<dim3((span + 31) / 32, d / 32, l.n_kv), dim3(32, 8), 0, st>>>(l.cache_v, w.vt, lo, span, l.n_kv, d,
+    pf_vtrans<<<dim3((span + 31) / 32, d / 32, l.n_kv), dim3(32, 8), 0, st>>>(tg.cv[li], w.vt, lo, span, l.n_kv, d,
                                                                               w.ks);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
     {  // ctx_h = P_h . V (V^T rows per KV head)
@@ -934,11 +958,32 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
                    {m->embed + (size_t)m->vbegin * H, (uint64_t)H, (uint64_t)m->V_local, (uint64_t)H},
                    plain(1, m->V_local, H, w.lmlog, m->V_local, status), 1, st, sb)))
       return rc;
-    pf_lm_epilogue<<<1, 1024, 0, st>>>(w.lmlog, m->logits, m->V_local, m->vbegin, c.final_logit_softcapping,
-                                       m->tokens_out, m->lm.tokens_host, m->ctrl, n_total);
+    pf_lm_epilogue<<<1, 1024, 0, st>>>(w.lmlog, tg.logits, m->V_local, m->vbegin, c.final_logit_softcapping,
+                                       tg.tok_out, tg.out_index, tg.tok_host, tg.ctrl, n_total);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   }
   return G4_OK;
+}
+
+// The model's own sequence as a prefill target.
+static PfTarget model_target(g4_model* m, std::vector<bf16_t*>& ck, std::vector<bf16_t*>& cv, int n) {
+  ck.clear();
+  cv.clear();
+  for (const LayerDev& l : m->L) {
+    ck.push_back(l.cache_k);
+    cv.push_back(l.cache_v);
+  }
+  PfTarget t{};
+  t.tokens = m->tokens_in;
+  t.ck = ck.data();
+  t.cv = cv.data();
+  t.cache_len = m->max_len;
+  t.tok_out = m->tokens_out;
+  t.out_index = n;
+  t.tok_host = m->lm.tokens_host;
+  t.ctrl = m->ctrl;
+  t.logits = m->logits;
+  return t;
 }
 
 extern "C" int g4_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M,
@@ -967,10 +1012,217 @@ extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, int flags, void*
   if (rc) return rc;
   if ((rc = g4_prepare_sampler(m))) return rc;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<bf16_t*> ck, cv;
+  const PfTarget tg = model_target(m, ck, cv, n_tokens);
   for (int c0 = 0; c0 < n_tokens; c0 += chunk) {
     const int M = std::min(chunk, n_tokens - c0);
-    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, (flags & G4_PREFILL_DENSE_MOE) != 0, st)))
+    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, (flags & G4_PREFILL_DENSE_MOE) != 0, st, tg)))
       return rc;
   }
   return g4_launch_sampler(m, st);  // temperature > 0: replaces the greedy first token
+}
+
+// ------------------------------------------------------------------ batched decode
+// B sequences decoded together (benchmark config 5's batch-8 decode; the reference's
+// forward takes [B, T] inputs, model.py:333-386, and its cache has a batch axis,
+// model.py:174-185).  Each sequence has its own KV cache [ctx, kv, d] per layer and its
+// own control block (position, status); one step runs every projection as a tensor-core
+// GEMM with M = B (split-K: the step is weight-streaming bound), the routed MoE as grouped
+// GEMMs over the B x top-k pairs (each selected expert's weights read once for all the
+// sequences that picked it), and attention per sequence with the decode attention kernel.
+struct BatchWs {
+  int B = 0, ctx = 0;
+  char* mem = nullptr;
+  std::vector<bf16_t*> ck, cv;  // per layer: sequence 0's cache; sequence b at + b * ctx * kv * d
+  int* ctrl = nullptr;          // [B][G4_CTRL_WORDS]
+  int* tokens = nullptr;        // [B] next input token of each sequence
+  float* logits = nullptr;      // [B, V_local] fp32 softcapped logits of the last step
+  bf16_t* xf = nullptr;         // [B, H]
+  bf16_t* lmlog = nullptr;      // [B, V_local]
+};
+
+void g4_batch_release(g4_model* m) {
+  if (!m || !m->batch) return;
+  if (m->batch->mem) cudaFree(m->batch->mem);
+  delete m->batch;
+  m->batch = nullptr;
+}
+
+extern "C" int g4_batch_reserve(g4_model* m, int batch, int ctx_len) {
+  if (!m || !m->finalized) return fail(G4_ERR_STATE, "g4_batch_reserve: model not finalized");
+  if (m->world != 1) return fail(G4_ERR_SHAPE, "g4_batch_reserve: batched decode runs at world 1");
+  if (batch < 1 || batch > 64 || ctx_len < 1 || ctx_len > m->max_len)
+    return fail(G4_ERR_ARG, "g4_batch_reserve: batch %d (1..64), context %d (1..%d)", batch, ctx_len, m->max_len);
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  g4_batch_release(m);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    const size_t o = off;
+    off += up256(bytes);
+    return o;
+  };
+  std::vector<size_t> ok, ov;
+  for (const LayerDev& l : m->L) {
+    const size_t per = (size_t)batch * ctx_len * l.n_kv * l.d * 2;
+    ok.push_back(take(per));
+    ov.push_back(take(per));
+  }
+  const size_t o_ctrl = take((size_t)batch * G4_CTRL_WORDS * 4), o_tok = take((size_t)batch * 4),
+               o_lg = take((size_t)batch * m->V_local * 4), o_xf = take((size_t)batch * m->H * 2),
+               o_lm = take((size_t)batch * m->V_local * 2);
+  BatchWs* w = new BatchWs();
+  if (cudaMalloc(&w->mem, off) != cudaSuccess) {
+    delete w;
+    return fail(G4_ERR_NOMEM, "g4_batch_reserve: cudaMalloc(%zu) failed", off);
+  }
+  G4_CUDA(cudaMemset(w->mem, 0, off), G4_ERR_CUDA);
+  w->B = batch;
+  w->ctx = ctx_len;
+  for (size_t i = 0; i < m->L.size(); ++i) {
+    w->ck.push_back(reinterpret_cast<bf16_t*>(w->mem + ok[i]));
+    w->cv.push_back(reinterpret_cast<bf16_t*>(w->mem + ov[i]));
+  }
+  w->ctrl = reinterpret_cast<int*>(w->mem + o_ctrl);
+  w->tokens = reinterpret_cast<int*>(w->mem + o_tok);
+  w->logits = reinterpret_cast<float*>(w->mem + o_lg);
+  w->xf = reinterpret_cast<bf16_t*>(w->mem + o_xf);
+  w->lmlog = reinterpret_cast<bf16_t*>(w->mem + o_lm);
+  std::vector<int> ctrl((size_t)batch * G4_CTRL_WORDS, 0);
+  for (int b = 0; b < batch; ++b) ctrl[(size_t)b * G4_CTRL_WORDS + G4_CTRL_TIMEOUT_US] = 2000000;
+  G4_CUDA(cudaMemcpy(w->ctrl, ctrl.data(), ctrl.size() * 4, cudaMemcpyHostToDevice), G4_ERR_CUDA);
+  m->batch = w;
+  return G4_OK;
+}
+
+// Sequence `seq`'s cache pointers.
+static void batch_caches(const g4_model* m, int seq, std::vector<bf16_t*>& ck, std::vector<bf16_t*>& cv) {
+  const BatchWs& w = *m->batch;
+  ck.clear();
+  cv.clear();
+  for (size_t i = 0; i < m->L.size(); ++i) {
+    const size_t per = (size_t)w.ctx * m->L[i].n_kv * m->L[i].d;
+    ck.push_back(w.ck[i] + (size_t)seq * per);
+    cv.push_back(w.cv[i] + (size_t)seq * per);
+  }
+}
+
+extern "C" int g4_batch_prefill(g4_model* m, int seq, int n_tokens, int* token_out, void* stream) {
+  if (!m || !m->batch) return fail(G4_ERR_STATE, "g4_batch_prefill before g4_batch_reserve");
+  BatchWs& bw = *m->batch;
+  if (seq < 0 || seq >= bw.B || n_tokens < 1 || n_tokens >= bw.ctx)
+    return fail(G4_ERR_ARG, "g4_batch_prefill: sequence %d of %d, %d tokens (context %d)", seq, bw.B, n_tokens, bw.ctx);
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  const int chunk = std::min(4096, (n_tokens + kGemmBM - 1) / kGemmBM * kGemmBM);
+  int rc = prefill_workspace(m, std::max(chunk, m->prefill ? m->prefill->chunk : 0));
+  if (rc) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  std::vector<bf16_t*> ck, cv;
+  batch_caches(m, seq, ck, cv);
+  PfTarget tg{};
+  tg.tokens = m->tokens_in;  // the prompt, as for g4_prefill
+  tg.ck = ck.data();
+  tg.cv = cv.data();
+  tg.cache_len = bw.ctx;
+  tg.tok_out = bw.tokens;
+  tg.out_index = seq;
+  tg.ctrl = bw.ctrl + (size_t)seq * G4_CTRL_WORDS;
+  tg.logits = bw.logits + (size_t)seq * m->V_local;
+  for (int c0 = 0; c0 < n_tokens; c0 += chunk) {
+    const int M = std::min(chunk, n_tokens - c0);
+    if ((rc = prefill_chunk(m, c0, M, c0 + M == n_tokens, n_tokens, false, st, tg))) return rc;
+  }
+  if (token_out) G4_CUDA(cudaMemcpyAsync(token_out, bw.tokens + seq, 4, cudaMemcpyDeviceToDevice, st), G4_ERR_CUDA);
+  return G4_OK;
+}
+
+extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, void* stream) {
+  if (!m || !m->batch) return fail(G4_ERR_STATE, "g4_batch_step before g4_batch_reserve");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  BatchWs& bw = *m->batch;
+  const int B = bw.B;
+  int rc = prefill_workspace(m, std::max(kGemmBM, m->prefill ? m->prefill->chunk : 0));
+  if (rc) return rc;
+  PrefillWs& w = *m->prefill;
+  const SplitBuf sb{w.split, w.split_elems};
+  const g4_config& c = m->cfg;
+  const int H = m->H, E = m->E, F = m->F_local, I = m->I_local, K = m->topk;
+  const float eps = c.rms_norm_eps;
+  int* status = bw.ctrl + G4_CTRL_STATUS;  // sequence 0's status word collects GEMM timeouts
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  pf_embed<<<B, 256, 0, st>>>(bw.tokens, m->embed, w.x, H, c.vocab_size, g4_host_bf16_round(std::sqrt((float)H)),
+                              bw.ctrl);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  const float hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
+  std::vector<bf16_t*> ck, cv;
+  for (size_t li = 0; li < m->L.size(); ++li) {
+    const LayerDev& l = m->L[li];
+    const int nq = l.n_kv * l.g, d = l.d, R = l.rows_q + l.rows_k + l.rows_v;
+    pf_rmsnorm<<<B, kRowThreads, 0, st>>>(w.x, l.n_in, w.xn, H, eps);
+    if ((rc = gemm({w.xn, (uint64_t)H, (uint64_t)B, (uint64_t)H}, {l.qkv, (uint64_t)H, (uint64_t)R, (uint64_t)H},
+                   plain(B, R, H, w.qkv, R, status), 1, st, sb)))
+      return rc;
+    for (int b = 0; b < B; ++b) {  // q/k norm, RoPE, cache write and attention of sequence b
+      batch_caches(m, b, ck, cv);
+      AttnArgs a = m->k2[li];
+      a.qkv = w.qkv + (size_t)b * R;
+      a.cache_k = ck[li];
+      a.cache_v = cv[li];
+      a.ctx = w.ctx + (size_t)b * nq * d;
+      a.ctrl = bw.ctrl + (size_t)b * G4_CTRL_WORDS;
+      a.pos_fixed = -1;
+      a.max_len = bw.ctx;
+      a.trace_id = -1;
+      if ((rc = g4_launch_attention(a, st))) return rc;
+    }
+    if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)B, (uint64_t)nq * d},
+                   {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(B, H, nq * d, w.o, H, status), 1,
+                   st, sb)))
+      return rc;
+    pf_post_attn<<<B, kRowThreads, 0, st>>>(w.o, w.x, l.n_post_attn, l.n_pre_ff, l.n_pre_ff2, l.router_scale,
+                                             w.mlp_in, w.h2, w.rin, H, eps, hinv);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    if ((rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)B, (uint64_t)H}, {l.gate, (uint64_t)H, (uint64_t)I, (uint64_t)H},
+                   plain(B, I, H, w.gate, I, status), 1, st, sb)) ||
+        (rc = gemm({w.mlp_in, (uint64_t)H, (uint64_t)B, (uint64_t)H}, {l.up, (uint64_t)H, (uint64_t)I, (uint64_t)H},
+                   plain(B, I, H, w.up, I, status), 1, st, sb)))
+      return rc;
+    pf_gelu_mul<<<std::min(4096, (B * I + 255) / 256), 256, 0, st>>>(w.gate, w.up, w.act, (size_t)B * I);
+    if ((rc = gemm({w.act, (uint64_t)I, (uint64_t)B, (uint64_t)I}, {l.down, (uint64_t)I, (uint64_t)H, (uint64_t)I},
+                   plain(B, H, I, w.mlp_out, H, status), 1, st, sb)) ||
+        (rc = gemm({w.rin, (uint64_t)H, (uint64_t)B, (uint64_t)H}, {l.router, (uint64_t)H, (uint64_t)E, (uint64_t)H},
+                   plain(B, E, H, w.rlog, E, status), 1, st, sb)))
+      return rc;
+    pf_router<<<B, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
+    if ((rc = routed_moe(m, l, B, st))) return rc;
+    pf_combine<<<B, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
+                                           l.scalar, H, eps);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  }
+  pf_rmsnorm<<<B, kRowThreads, 0, st>>>(w.x, m->final_norm, bw.xf, H, eps);
+  if ((rc = gemm({bw.xf, (uint64_t)H, (uint64_t)B, (uint64_t)H},
+                 {m->embed + (size_t)m->vbegin * H, (uint64_t)H, (uint64_t)m->V_local, (uint64_t)H},
+                 plain(B, m->V_local, H, bw.lmlog, m->V_local, status), 1, st, sb)))
+    return rc;
+  // every row: softcapped logits, argmax -> the sequence's next token, position + 1
+  pf_lm_epilogue<<<B, 1024, 0, st>>>(bw.lmlog, bw.logits, m->V_local, m->vbegin, c.final_logit_softcapping, bw.tokens,
+                                     0, nullptr, bw.ctrl, -1, G4_CTRL_WORDS, 0);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  if (tokens_out) G4_CUDA(cudaMemcpyAsync(tokens_out, bw.tokens, (size_t)B * 4, cudaMemcpyDeviceToDevice, st), G4_ERR_CUDA);
+  if (logits_out)
+    G4_CUDA(cudaMemcpyAsync(logits_out, bw.logits, (size_t)B * m->V_local * 4, cudaMemcpyDeviceToDevice, st),
+            G4_ERR_CUDA);
+  return G4_OK;
+}
+
+extern "C" int g4_batch_status(g4_model* m, void* stream, int* status_out) {
+  if (!m || !m->batch) return fail(G4_ERR_STATE, "g4_batch_status before g4_batch_reserve");
+  G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
+  G4_CUDA(cudaStreamSynchronize(static_cast<cudaStream_t>(stream)), G4_ERR_CUDA);
+  std::vector<int> ctrl((size_t)m->batch->B * G4_CTRL_WORDS);
+  G4_CUDA(cudaMemcpy(ctrl.data(), m->batch->ctrl, ctrl.size() * 4, cudaMemcpyDeviceToHost), G4_ERR_CUDA);
+  int st = 0;
+  for (int b = 0; b < m->batch->B; ++b) st |= ctrl[(size_t)b * G4_CTRL_WORDS + G4_CTRL_STATUS];
+  if (status_out) *status_out = st;
+  if (st) return fail(G4_ERR_TIMEOUT, "batched decode status word 0x%x", st);
+  return G4_OK;
 }

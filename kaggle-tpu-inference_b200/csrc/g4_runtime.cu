@@ -235,6 +235,7 @@ static int launch_attention(const AttnArgs& a, cudaStream_t st) {
   if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(e));
   return G4_OK;
 }
+int g4_launch_attention(const AttnArgs& a, cudaStream_t st) { return launch_attention(a, st); }
 
 void g4_rope_inv_freq(int d, double theta, double partial, float* out) {
   // model.py:54-61: fp64 inverse frequencies for the rotated pairs, zero (NoPE) tail
@@ -1267,6 +1268,7 @@ extern "C" int g4_model_destroy(g4_model* m) {
   if (m->gexec) cudaGraphExecDestroy(m->gexec);
   if (m->graph) cudaGraphDestroy(m->graph);
   g4_prefill_release(m);
+  g4_batch_release(m);
   if (m->rope_tab) cudaFree(m->rope_tab);
   if (m->prog_mem) cudaFree(m->prog_mem);
   if (m->tokens_host) cudaFreeHost(m->tokens_host);

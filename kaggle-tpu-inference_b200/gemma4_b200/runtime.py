@@ -227,3 +227,51 @@ class DecodeModel:
             self.close()
         except Exception:
             pass
+
+
+class BatchDecoder:
+    """``batch`` sequences decoded together on one rank's model (``g4_batch_*``): each has
+    its own KV cache of ``ctx_len`` positions; prompts go through the tensor-core prefill,
+    every step decodes one greedy token of every sequence (benchmark config 5's batch-8
+    decode; the reference forward's batch axis, model.py:333-386)."""
+
+    def __init__(self, model: DecodeModel, batch: int, ctx_len: int):
+        self.model, self.batch, self.ctx_len = model, batch, ctx_len
+        dev = model.device
+        with torch.cuda.device(dev):
+            N.check(N.lib().g4_batch_reserve(model.handle, batch, ctx_len), "g4_batch_reserve")
+        self.tokens = torch.zeros(batch, dtype=torch.int32, device=dev)
+        self.logits = torch.zeros(batch, model.v_local, dtype=torch.float32, device=dev)
+        self.positions = [0] * batch
+
+    def prefill(self, seq: int, prompt_ids) -> None:
+        """Sequence ``seq``'s prompt into its cache; its first token becomes its next input."""
+        m = self.model
+        p = len(prompt_ids)
+        if not 1 <= p < self.ctx_len:
+            raise ValueError(f"prompt length {p} outside [1, {self.ctx_len})")
+        with torch.cuda.device(m.device):
+            m.tokens_in[:p].copy_(torch.as_tensor(list(prompt_ids), dtype=torch.int32))
+            N.check(N.lib().g4_batch_prefill(m.handle, seq, p, N.ptr(self.tokens[seq:seq + 1]), N.stream_handle()),
+                    "g4_batch_prefill")
+        self.positions[seq] = p
+
+    def step(self, write_logits: bool = False) -> torch.Tensor:
+        """One token of every sequence (asynchronous); returns the device tensor of the
+        B tokens just produced (valid after the stream reaches this point)."""
+        m = self.model
+        if max(self.positions) + 1 >= self.ctx_len:
+            raise ValueError("a sequence would pass the end of its cache")
+        with torch.cuda.device(m.device):
+            N.check(N.lib().g4_batch_step(m.handle, N.ptr(self.tokens),
+                                          N.ptr(self.logits) if write_logits else None, N.stream_handle()),
+                    "g4_batch_step")
+        self.positions = [p + 1 for p in self.positions]
+        return self.tokens
+
+    def check_status(self):
+        st = ctypes.c_int(0)
+        with torch.cuda.device(self.model.device):
+            rc = N.lib().g4_batch_status(self.model.handle, N.stream_handle(), ctypes.byref(st))
+        if rc != N.G4_OK:
+            raise N.G4Error(rc, "batched decode", f"status word 0x{st.value:x}")
