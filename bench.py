@@ -71,6 +71,7 @@ def parse_args():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-blocks", action="store_true", help="skip the config 2 / 3 block legs")
     ap.add_argument("--prefill-only", action="store_true", help="profiling: run only the prefill leg")
+    ap.add_argument("--blocks-only", action="store_true", help="profiling: run only the block legs")
     ap.add_argument("--long-context-steps", type=int, default=20,
                     help="steps timed at the end of the 32K cache (all keys live); 0 skips")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
@@ -482,6 +483,11 @@ def main() -> int:
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     mesh = Mesh(rank, world, local)
+    if args.blocks_only:  # profiling case: the config 2 / 3 block legs alone, one JSON line
+        if rank == 0:
+            print(json.dumps({"metric": "block kernels", "blocks": block_legs(args, dev, reps=args.steps)}),
+                  flush=True)
+        return 0
     eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh,
                  engine=args.engine)
     if args.prefill_only:  # profiling case: the prefill leg alone, one JSON line
