@@ -1,42 +1,65 @@
 // Split-KV decode attention for one query token (reference: gemma4_tpu/model.py:195-213).
 //
-// Grid = n_kv (local KV heads) x nsplit.  The live key span of KV head h --
-// (pos-window, pos] for sliding layers, [0, pos] for full layers, instead of the
-// reference's masked pass over the whole max_len cache (masked entries contribute
-// exp(-1e30 - max) = 0 there, so skipping them is exact) -- is cut into
-// n_active <= nsplit slices of at least kAttnMinKeys keys; CTAs past n_active exit
-// at once.  Per active CTA:
-//   1. q_norm RMSNorm + RoPE of the g query heads of KV head h (bf16 rounding points
-//      of model.py:198 / 70-78); the CTA whose slice holds `pos` also normalises,
-//      RoPEs and writes k (and v = rms(v_raw), or rms(k_raw) for k==v layers) into
-//      the cache (model.py:200-206).
-//   2. every group of LK lanes owns a strided set of keys and runs an online softmax
-//      over them: scores s = bf16(q.k) (scale 1.0, rounded like the reference einsum),
-//      running max / mass, and acc += exp(s - m) v in fp32 registers; K and V of a
-//      batch of keys are loaded together.
-//   3. the lane groups are merged in a fixed order (butterfly within a warp, then warp
-//      by warp through shared memory) into (m, l, acc[g][d]), which goes to the
-//      partial buffer; the last CTA of head h (atomic counter) merges the n_active
-//      partials in split order with max-rescaling and rounds the context to bf16.
-//      Every sum has a fixed order: results are bitwise reproducible.
-// Difference from the reference: it rounds the normalised probabilities to bf16
-// before P.V; here P.V uses fp32 weights and the context is rounded once -- closer
-// to exact arithmetic, within the tolerance the parity tests state.
+// Work items are (KV head hk, split sp), n_kv x nsplit of them.  The live key span of
+// KV head h -- (pos-window, pos] for sliding layers, [0, pos] for full layers, instead of
+// the reference's masked pass over the whole max_len cache (masked entries contribute
+// exp(-1e30 - max) = 0 there, so skipping them is exact) -- is cut into n_active <=
+// nsplit slices of at least kAttnMinKeys keys; items past n_active do nothing.
+//
+// Keys stream through a ring of shared-memory stages.  A producer lane issues TMA tiled
+// loads of KPS keys of K and of V per stage (2-D tensor maps over the cache viewed as
+// [max_len, n_kv*d], 128-byte swizzle, boxes of 64 elements x KPS rows, L2 evict-first:
+// the cache is read once per token); a full / empty mbarrier pair guards each stage.  The
+// persistent step kernel feeds its one ring with these tiles too: layer l's attention
+// tiles are issued right after layer l's qkv weights, so they stream in under the qkv
+// phase.  The standalone kernel has a ring of its own (kAttnStages deep).
+//
+// Per item, the 8 consumer warps:
+//   1. q_norm RMSNorm + RoPE of the g query heads (bf16 rounding points of model.py:198
+//      and 70-78); the item whose slice holds `pos` also normalises, RoPEs and writes k
+//      (and v = rms(v_raw), or rms(k_raw) for k==v layers) into the cache
+//      (model.py:200-206) and keeps both in shared memory;
+//   2. per stage, on the tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate):
+//        S^T [KPS keys x 8 heads] = K . Q^T: warp w contracts its own 16-dim groups
+//          (w, w+8, ...) and leaves the partial in shared memory; after one barrier every
+//          warp adds the partials in warp order (the same bits in every warp), rounds
+//          the scores to bf16 as the reference einsum does, and updates the online
+//          softmax (running max m, mass l);
+//        O^T [16 dims x 8 heads] += V^T . P^T for the warp's own dim groups, with
+//          P = exp(s - m) rounded to bf16.  The reference rounds the normalised
+//          probabilities to bf16 before P.V; here the normalisation 1/l is applied once
+//          at the end, in fp32.
+//      The summed scores land in each thread exactly as its P^T operand fragment (keys
+//      2c, 2c+1, 2c+8, 2c+9 of head lane/4), so no transposes are needed.  The cache row
+//      at `pos` is never read from the stage: the ldmatrix row address of that key
+//      points at the shared copy of the new key / value, and keys past the slice point
+//      at a zero row (the stage holds stale or zero-filled rows there).
+//   3. (m, l, O) of the item go to the partial buffer; the last CTA of head h (atomic
+//      counter) merges the n_active partials in split order with max-rescaling and
+//      rounds the context to bf16.
+// Every sum has a fixed order: results are bitwise reproducible, and the step kernel
+// and the standalone kernel (same items, same stages) compute identical bits.
 #pragma once
+
+#include <cuda.h>
 
 #include "g4_common.cuh"
 
 namespace g4 {
 
-constexpr int kAttnThreads = 256;
+constexpr int kAttnThreads = 256;                      // consumer threads (8 warps)
 constexpr int kAttnWarps = kAttnThreads / 32;
-constexpr int kAttnMaxChunk = 1024;  // keys per CTA
-constexpr int kAttnMinKeys = 32;     // keys per CTA before another split is used
-constexpr int kAttnMaxG = 8;         // query heads per KV head handled by one CTA
+constexpr int kAttnKernelThreads = kAttnThreads + 32;  // + the producer warp (standalone kernel)
+constexpr int kAttnStages = 4;                         // ring depth of the standalone kernel
+constexpr int kAttnMaxChunk = 1024;  // keys per item the host's split aims to stay under
+constexpr int kAttnMinKeys = 32;     // keys per item before another split is used
+constexpr int kAttnMaxG = 8;         // query heads per KV head: one 8-column MMA tile
 constexpr int kAttnMaxD = 512;
 constexpr int kAttnMaxSplit = 256;
 
 struct AttnArgs {
+  CUtensorMap tmk;         // cache_k as [max_len, n_kv*d] bf16, box 64 x attn_kps(d), 128-byte swizzle
+  CUtensorMap tmv;         // cache_v, the same
   const bf16_t* qkv;       // q [n_kv*g*d] | k [n_kv*d] | v [n_kv*d] (v absent if k_eq_v)
   const bf16_t* q_norm;    // [d]
   const bf16_t* k_norm;    // [d]
@@ -53,51 +76,189 @@ struct AttnArgs {
   int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
 
-// Heads per pass (at most 4) and whether the warps' partial sums are merged through
-// per-warp shared-memory slots (one barrier) rather than warp by warp (a barrier each):
-// when the slots take at most 32 KB.
-__host__ __device__ __forceinline__ int attn_heads_per_pass(int g) { return g > 4 ? 4 : g; }
-__host__ __device__ __forceinline__ bool attn_slot_merge(int g, int d) { return attn_heads_per_pass(g) * d <= 1024; }
+// Keys per stage (a multiple of 16), bytes of a stage (K boxes then V boxes, d/64 of
+// each, KPS rows of 128 bytes per box) and the head stride of the score partials.
+__host__ __device__ __forceinline__ int attn_kps(int d) { return d > 256 ? 16 : 32; }
+__host__ __device__ __forceinline__ int attn_stage_bytes(int d) { return 4 * d * attn_kps(d); }
+__host__ __device__ __forceinline__ int attn_hs(int d) { return attn_kps(d) + 8; }
 
+// Scratch of one item (byte offsets from a 16-byte aligned base): the normalised query
+// heads q [8][d] bf16 (rows past g zero), the new key and value [d] bf16 each, a 16-byte
+// zero row, the RoPE table [d] fp32 (cos | sin), the score partials
+// [2][8 warps][8 heads][hs] fp32 (double-buffered by stage) and a flag word.
+struct AttnSmem {
+  int q, kn, vn, zero, rope, part, flag, bytes;
+};
+__host__ __device__ __forceinline__ AttnSmem attn_smem_layout(int d) {
+  AttnSmem s;
+  s.q = 0;
+  s.kn = s.q + 8 * d * 2;
+  s.vn = s.kn + d * 2;
+  s.zero = s.vn + d * 2;
+  s.rope = s.zero + 16;
+  s.part = s.rope + d * 4;
+  s.flag = s.part + 2 * kAttnWarps * 8 * attn_hs(d) * 4;
+  s.bytes = s.flag + 64;
+  return s;
+}
 __host__ __device__ __forceinline__ int attn_smem_bytes(int g, int d) {
-  // acc [g][d] + lane-group stats [64][g] x 2 + misc + the normalised query heads
-  // q_s [g][d] (bf16) + the new key and value kn_s / vn_s [d] (bf16) + the RoPE
-  // table [d] (fp32 cos | sin) + the merge slots [warps][heads per pass][d] (fp32)
-  return g * d * 4 + 2 * 64 * g * 4 + 2 * kAttnMaxG * 4 + 64 + g * d * 2 + 2 * d * 2 + d * 4 +
-         (attn_slot_merge(g, d) ? kAttnWarps * attn_heads_per_pass(g) * d * 4 : 0);
+  (void)g;
+  return attn_smem_layout(d).bytes;
+}
+// Standalone kernel: alignment slack, the ring, the scratch, 2 x kAttnStages mbarriers
+// and 4 ints (dead flag, stages issued, producer done).
+__host__ __device__ __forceinline__ int attn_kernel_smem_bytes(int d) {
+  return 1024 + kAttnStages * attn_stage_bytes(d) + ((attn_smem_layout(d).bytes + 15) & ~15) +
+         2 * kAttnStages * 8 + 16;
+}
+
+// A ring of stages guarded by full (one producer arrival + bytes) / empty (one arrival
+// per consumer warp) mbarriers.
+struct AttnRing {
+  uint64_t* full;
+  uint64_t* empty;
+  unsigned char* stages;
+  int stride;  // bytes from one stage to the next (a multiple of 1024)
+  int n;       // stages
+};
+
+// Keys [k0, k1) of split `sp` when the query sits at `pos`, and the number of splits
+// that hold keys; false when split sp holds none.  Producer and consumers both use it.
+__host__ __device__ __forceinline__ bool attn_span(int pos, int window, int nsplit, int sp, int& k0, int& k1,
+                                                   int& n_active) {
+  const int start = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
+  const int nlive = pos - start + 1;
+  int chunk = (nlive + nsplit - 1) / nsplit;
+  if (chunk < kAttnMinKeys) chunk = kAttnMinKeys;
+  n_active = (nlive + chunk - 1) / chunk;
+  if (sp >= n_active) return false;
+  k0 = start + sp * chunk;
+  k1 = pos + 1 < k0 + chunk ? pos + 1 : k0 + chunk;
+  return true;
+}
+
+__device__ __forceinline__ int attn_pos(const AttnArgs* a) {
+  return a->pos_fixed >= 0 ? a->pos_fixed : ldcg_i(a->ctrl + G4_CTRL_POS);
+}
+
+// ------------------------------------------------------------------ warp-level MMA pieces
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr)
+               : "memory");
+}
+// d += a . b for one m16n8k16 tile (A row-major 16x16, B column-major 16x8, bf16 in,
+// fp32 accumulate).
+__device__ __forceinline__ void mma_16816(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+      "{%0, %1, %2, %3};"
+      : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// Two fp32 values -> bf16x2 (round to nearest even), `lo` in the low half.
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+  uint32_t r;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
+  return r;
+}
+
+// 2-D TMA tile load with an L2 cache policy (no multicast).
+__device__ __forceinline__ void attn_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
+                                              uint64_t pol) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%3, %4}], [%2], %5;" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(smem_addr(bar)), "r"(x), "r"(y), "l"(pol)
+      : "memory");
+}
+
+// Bounded wait for a stage to be released; sets *dead and a status bit on timeout (or
+// returns at once when the consumers already died).
+__device__ __forceinline__ bool ring_wait_free(uint64_t* empty, uint32_t parity, volatile int* dead, int* status) {
+  if (mbar_try_wait(empty, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  while (!mbar_try_wait(empty, parity)) {
+    if (*dead) return false;
+    if (globaltimer_ns() - t0 > kLocalTimeoutNs) {
+      atomicOr(status, G4_STATUS_MBAR_TIMEOUT);
+      *dead = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+// Producer lane: the stages of this CTA's items (it0, it0 + step, ...) into `ring`, in
+// the order the consumers take them.  `a` lives in global or kernel-parameter memory
+// (the TMA reads its tensor maps there).  `issued` (optional) tracks the stages issued
+// for a drain after a failure.  Returns false after setting *dead when a stage never
+// became free.
+__device__ __forceinline__ bool attn_produce(const AttnArgs* a, int it0, int step, const AttnRing& ring, RingPos& rp,
+                                             volatile int* dead, int* status, int* issued) {
+  const int d = a->d, nsplit = a->nsplit, kps = attn_kps(d), nbox = d >> 6;
+  const int pos = attn_pos(a);
+  if (pos < 0 || pos >= a->max_len) return true;  // the consumers skip the layer and report it
+  const uint64_t pol = l2_evict_first_policy();
+  const uint32_t bytes = (uint32_t)attn_stage_bytes(d);
+  const int items = a->n_kv * nsplit;
+  for (int it = it0; it < items; it += step) {
+    int k0, k1, na;
+    if (!attn_span(pos, a->window, nsplit, it % nsplit, k0, k1, na)) continue;
+    const int x0 = (it / nsplit) * d;
+    for (int ks = k0; ks < k1; ks += kps) {
+      if (rp.wrapped && !ring_wait_free(&ring.empty[rp.st], rp.ph ^ 1u, dead, status)) return false;
+      uint64_t* bar = &ring.full[rp.st];
+      mbar_arrive_expect_tx(bar, bytes);
+      unsigned char* stage = ring.stages + (size_t)rp.st * ring.stride;
+      for (int j = 0; j < nbox; ++j) {
+        attn_tma_load(stage + j * kps * 128, &a->tmk, x0 + 64 * j, ks, bar, pol);
+        attn_tma_load(stage + (nbox + j) * kps * 128, &a->tmv, x0 + 64 * j, ks, bar, pol);
+      }
+      rp.next(ring.n);
+      if (issued) *reinterpret_cast<volatile int*>(issued) = rp.tiles;
+    }
+  }
+  return true;
 }
 
 // One work item (KV head hk, split sp) of decode attention, run by the kAttnThreads
 // threads 0..kAttnThreads-1 of the block with named barrier `bar` among them and
-// `smem` (attn_smem_bytes(G, D), 16-byte aligned) as scratch.  Every exit is taken by
-// all of these threads together.  D = head dim, G = query heads per KV head on this
-// rank; every loop has a compile-time trip count.
+// `smem` (attn_smem_bytes(G, D), 16-byte aligned) as scratch; its stages come from
+// `ring` at `rp` (`wp` advances over the stages seen complete, for a drain after a
+// failure).  Every exit is taken by all of these threads together.  D = head dim (a
+// multiple of 64), G = query heads per KV head on this rank.
 template <int D, int G>
-__device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, unsigned char* smem, int bar) {
+__device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, unsigned char* smem, int bar,
+                                          const AttnRing& ring, RingPos& rp, RingPos& wp, volatile int* dead,
+                                          int* status) {
   constexpr int PER = D / 32;                 // elements per lane of one head vector
-  constexpr int LK = D / 8 < 32 ? D / 8 : 32; // lanes per key
-  constexpr int KPW = 32 / LK;                // lane groups per warp
-  constexpr int CPL = (D / 8) / LK;           // 16-byte chunks per lane of a key row
-  constexpr int NGRP = kAttnWarps * KPW;      // lane groups per CTA
-  constexpr int KB = 4;                       // keys per lane group in flight
-  // heads kept in registers at once: at most 4, so that the item fits the step
-  // kernel's register budget next to everything else (more heads = one more pass
-  // over the keys, which then come from L2)
-  constexpr int HG = G > 4 ? 4 : G;
-  float* acc_s = reinterpret_cast<float*>(smem);                     // [G][D]
-  float* gm = acc_s + G * D;                                         // [NGRP][G]
-  float* gl = gm + 64 * G;                                           // [NGRP][G]
-  float* ml = gl + 64 * G;                                           // M[G], L[G]
-  int* flag = reinterpret_cast<int*>(ml + 2 * kAttnMaxG);
-  bf16_t* q_s = reinterpret_cast<bf16_t*>(flag + 16);                // [G][D]
-  bf16_t* kn_s = q_s + G * D;                                        // [D] new key
-  bf16_t* vn_s = kn_s + D;                                           // [D] new value
-  float* rope_s = reinterpret_cast<float*>(vn_s + D);                // [D/2] cos | [D/2] sin
-  float* mslot = rope_s + D;                                         // [warps][HG][D] (slot merge)
-  constexpr bool kSlotMerge = HG * D <= 1024;
-  static_assert(kSlotMerge == (HG * D <= 1024), "same rule as attn_slot_merge");
+  constexpr int KPS = D > 256 ? 16 : 32;      // keys per stage
+  constexpr int NMT = KPS / 16;               // 16-key MMA tiles per stage
+  constexpr int NDG = D / 16;                 // 16-dim groups
+  constexpr int NPW = NDG < kAttnWarps ? NDG : kAttnWarps;  // warps owning dim groups
+  constexpr int GPW = (NDG + kAttnWarps - 1) / kAttnWarps;  // dim groups per warp
+  constexpr int NBOX = D / 64;
+  constexpr int HS = KPS + 8;
+  static_assert(D % 64 == 0 && D <= kAttnMaxD && G >= 1 && G <= kAttnMaxG, "attention shape");
+  static_assert(D / 2 <= kAttnThreads, "one RoPE frequency per thread");
+  const AttnSmem lay = attn_smem_layout(D);
+  bf16_t* q_s = reinterpret_cast<bf16_t*>(smem + lay.q);    // [8][D]
+  bf16_t* kn_s = reinterpret_cast<bf16_t*>(smem + lay.kn);  // [D] new key
+  bf16_t* vn_s = reinterpret_cast<bf16_t*>(smem + lay.vn);  // [D] new value
+  float* rope_s = reinterpret_cast<float*>(smem + lay.rope);  // [D/2] cos | [D/2] sin
+  float* spart = reinterpret_cast<float*>(smem + lay.part);   // [2][warps][8][HS]
+  int* flag = reinterpret_cast<int*>(smem + lay.flag);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g8 = lane >> 2, c4 = lane & 3;  // fragment row / column pair of this lane
   // norm weights of this lane
   float wq[PER], wk[PER];
 #pragma unroll
@@ -119,66 +280,27 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
 #pragma unroll
     for (int i = 0; i < PER; ++i) pre[i] = bf2f(ldcg_bf(src0 + lane + 32 * i));
   }
-  const int pos = a.pos_fixed >= 0 ? a.pos_fixed : ldcg_i(a.ctrl + G4_CTRL_POS);
+  const int pos = attn_pos(&a);
   if (pos < 0 || pos >= a.max_len) {  // never index the cache out of bounds
     if (threadIdx.x == 0 && hk == 0 && sp == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_POS_OVERFLOW);
     return;
   }
-  const int start = a.window > 0 ? max(0, pos - a.window + 1) : 0;
-  const int nlive = pos - start + 1;
-  int chunk = (nlive + a.nsplit - 1) / a.nsplit;
-  if (chunk < kAttnMinKeys) chunk = kAttnMinKeys;
-  const int n_active = (nlive + chunk - 1) / chunk;
-  if (sp >= n_active) return;
-  const int k0 = start + sp * chunk;
-  const int k1 = min(pos + 1, k0 + chunk);
-  int n = k1 - k0;
-  if (n > kAttnMaxChunk) {  // host sizes nsplit so this cannot happen; stay in bounds
-    if (threadIdx.x == 0) atomicOr(a.ctrl + G4_CTRL_STATUS, G4_STATUS_MBAR_TIMEOUT);
-    n = kAttnMaxChunk;
-  }
+  int k0, k1, n_active;
+  if (!attn_span(pos, a.window, a.nsplit, sp, k0, k1, n_active)) return;
   const size_t row_stride = (size_t)a.n_kv * D;
-
-  // ---- 0. with all heads in one pass and registers to spare (G <= 4, G * CPL <= 4),
-  // the first KB keys of every lane group go in flight now, under step 1: the cached
-  // rows do not depend on it (only key `pos`, written below, does; it is patched from
-  // shared memory before use)
-  constexpr bool kEarly = G <= 4 && G * CPL <= 4;
-  const int gi_lane = lane / LK, li = lane % LK;
-  const int grp = warp * KPW + gi_lane;
-  const bf16_t* kbase = a.cache_k + (size_t)hk * D;
-  const bf16_t* vbase = a.cache_v + (size_t)hk * D;
-  const int jstart = warp * KPW;  // warp-uniform
-  uint4 kr[KB][CPL], vr[KB][CPL];
-  auto load_keys = [&](int jw) {
-#pragma unroll
-    for (int m = 0; m < KB; ++m) {
-      const int j = jw + gi_lane + m * NGRP;
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) {
-        if (j < n) {
-          kr[m][c] = ldcg_u4(kbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
-          vr[m][c] = ldcg_u4(vbase + (size_t)(k0 + j) * row_stride + (li + c * LK) * 8);
-        } else {
-          kr[m][c] = make_uint4(0, 0, 0, 0);
-          vr[m][c] = make_uint4(0, 0, 0, 0);
-        }
-      }
-    }
-  };
-  if (kEarly) load_keys(jstart);
 
   // ---- 1. RoPE table of this position (cos / sin of pos * inv_freq, rounded to bf16
   // as the reference does, model.py:76-78): one sincosf per thread, shared by every
   // vector below.  Then the q heads (and the new k/v if this split holds pos): one
   // warp per vector.
-  static_assert(D / 2 <= kAttnThreads, "one RoPE frequency per thread");
   if ((int)threadIdx.x < D / 2) {
     float sn, cs;
     sincosf((float)pos * fr, &sn, &cs);
     rope_s[threadIdx.x] = rbf(cs);
     rope_s[D / 2 + threadIdx.x] = rbf(sn);
   }
+  for (int i = threadIdx.x; i < (8 - G) * D; i += kAttnThreads) q_s[G * D + i] = 0;  // padding heads
+  if (threadIdx.x < 4) reinterpret_cast<uint32_t*>(smem + lay.zero)[threadIdx.x] = 0u;
   named_bar(bar, kAttnThreads);
   const bool has_new = (pos >= k0 && pos < k1);
   const int nvec = G + (has_new ? 2 : 0);
@@ -228,164 +350,175 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
       }
     }
   }
-  for (int i = threadIdx.x; i < G * D; i += kAttnThreads) acc_s[i] = 0.f;
-  __threadfence_block();
   named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 3);
 
-  // ---- 2. online softmax per lane group over its keys
-  const int jnew = has_new ? pos - k0 : -1;  // index of the new key in this slice
-#pragma unroll 1
-  for (int h0 = 0; h0 < G; h0 += HG) {
-    uint4 qr[HG][CPL];
+  // ---- 2. the stages of this item
+  // Q^T operand fragments of this warp's dim groups (column = head lane/4)
+  uint32_t qb[GPW][2];
+  float o[GPW][4];
 #pragma unroll
-    for (int h = 0; h < HG; ++h)
-#pragma unroll
-      for (int c = 0; c < CPL; ++c) qr[h][c] = reinterpret_cast<const uint4*>(q_s + (h0 + h) * D)[li + c * LK];
-    float m_run[HG], l_run[HG], acc[HG][CPL * 8];
-#pragma unroll
-    for (int h = 0; h < HG; ++h) {
-      m_run[h] = -INFINITY;
-      l_run[h] = 0.f;
-#pragma unroll
-      for (int e = 0; e < CPL * 8; ++e) acc[h][e] = 0.f;
-    }
-    // The loop bound is warp-uniform (jw depends on the warp only): every lane of a
-    // warp runs the same iterations, so the shuffles in group_sum always see a full
-    // warp.  Lane group gi_lane takes keys jw + gi_lane + m*NGRP.
-#pragma unroll 1
-    for (int jw = jstart; jw < n; jw += NGRP * KB) {
-      if (!kEarly || jw != jstart || h0 != 0) load_keys(jw);  // else already in flight
-      const int j0 = jw + gi_lane;
-#pragma unroll
-      for (int m = 0; m < KB; ++m) {
-        if (j0 + m * NGRP == jnew) {
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) {
-            kr[m][c] = reinterpret_cast<const uint4*>(kn_s)[li + c * LK];
-            vr[m][c] = reinterpret_cast<const uint4*>(vn_s)[li + c * LK];
-          }
-        }
-      }
-#pragma unroll
-      for (int h = 0; h < HG; ++h) {
-        float sc[KB];
-        float mx = m_run[h];
-#pragma unroll
-        for (int m = 0; m < KB; ++m) {
-          float s = 0.f;
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) s = dot8(kr[m][c], qr[h][c], s);
-          s = rbf(group_sum(s, LK));
-          sc[m] = (j0 + m * NGRP < n) ? s : -INFINITY;
-          mx = fmaxf(mx, sc[m]);
-        }
-        const float corr = mx == -INFINITY ? 1.f : expf(m_run[h] - mx);
-        m_run[h] = mx;
-        l_run[h] *= corr;
-#pragma unroll
-        for (int e = 0; e < CPL * 8; ++e) acc[h][e] *= corr;
-#pragma unroll
-        for (int m = 0; m < KB; ++m) {
-          const float p = sc[m] == -INFINITY ? 0.f : expf(sc[m] - mx);
-          l_run[h] += p;
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) {
-            const uint4 v = vr[m][c];
-            float* o = &acc[h][c * 8];
-            o[0] = fmaf(p, bf_lo(v.x), o[0]);
-            o[1] = fmaf(p, bf_hi(v.x), o[1]);
-            o[2] = fmaf(p, bf_lo(v.y), o[2]);
-            o[3] = fmaf(p, bf_hi(v.y), o[3]);
-            o[4] = fmaf(p, bf_lo(v.z), o[4]);
-            o[5] = fmaf(p, bf_hi(v.z), o[5]);
-            o[6] = fmaf(p, bf_lo(v.w), o[6]);
-            o[7] = fmaf(p, bf_hi(v.w), o[7]);
-          }
-        }
-      }
-    }
-    // ---- 3. merge lane groups: CTA max, then rescaled shared-memory sums
-    if (li == 0) {
-#pragma unroll
-      for (int h = 0; h < HG; ++h) {
-        gm[grp * G + h0 + h] = m_run[h];
-        gl[grp * G + h0 + h] = l_run[h];
-      }
-    }
-    named_bar(bar, kAttnThreads);
-    if (threadIdx.x < HG) {
-      const int h = h0 + threadIdx.x;
-      float M = -INFINITY;
-      for (int q = 0; q < NGRP; ++q) M = fmaxf(M, gm[q * G + h]);
-      float L = 0.f;
-      for (int q = 0; q < NGRP; ++q) {
-        const float mq = gm[q * G + h];
-        L += mq == -INFINITY ? 0.f : gl[q * G + h] * expf(mq - M);
-      }
-      ml[h] = M;
-      ml[kAttnMaxG + h] = L;
-    }
-    named_bar(bar, kAttnThreads);
-    // rescale to the CTA max, sum the KPW lane groups of a warp with a butterfly (every
-    // lane ends with the same bits), then add the warps into acc_s in warp order: a
-    // fixed summation order, so results do not depend on scheduling
-#pragma unroll
-    for (int h = 0; h < HG; ++h) {
-      const float f = m_run[h] == -INFINITY ? 0.f : expf(m_run[h] - ml[h0 + h]);
-#pragma unroll
-      for (int e = 0; e < CPL * 8; ++e) acc[h][e] *= f;
+  for (int i = 0; i < GPW; ++i) {
+    const int t = warp + kAttnWarps * i;
+    qb[i][0] = qb[i][1] = 0u;
+    if (t < NDG) {
+      qb[i][0] = *reinterpret_cast<const uint32_t*>(q_s + g8 * D + 16 * t + 2 * c4);
+      qb[i][1] = *reinterpret_cast<const uint32_t*>(q_s + g8 * D + 16 * t + 2 * c4 + 8);
     }
 #pragma unroll
-    for (int o = LK; o < 32; o <<= 1)
-#pragma unroll
-      for (int h = 0; h < HG; ++h)
-#pragma unroll
-        for (int e = 0; e < CPL * 8; ++e) acc[h][e] += __shfl_xor_sync(0xffffffffu, acc[h][e], o);
-    if (kSlotMerge) {
-      // every warp stores its sums in its own slot; then each thread adds the slots of
-      // its elements in warp order, from 0 -- the same additions, in the same order, as
-      // the warp-by-warp loop below, with one barrier instead of one per warp
-      if (gi_lane == 0) {
-#pragma unroll
-        for (int h = 0; h < HG; ++h)
-#pragma unroll
-          for (int c = 0; c < CPL; ++c) {
-            float4* dst = reinterpret_cast<float4*>(mslot + (warp * HG + h) * D + (li + c * LK) * 8);
-            dst[0] = make_float4(acc[h][c * 8 + 0], acc[h][c * 8 + 1], acc[h][c * 8 + 2], acc[h][c * 8 + 3]);
-            dst[1] = make_float4(acc[h][c * 8 + 4], acc[h][c * 8 + 5], acc[h][c * 8 + 6], acc[h][c * 8 + 7]);
-          }
-      }
-      named_bar(bar, kAttnThreads);
-      for (int i = threadIdx.x; i < HG * D; i += kAttnThreads) {
-        float v = 0.f;
-#pragma unroll
-        for (int q = 0; q < kAttnWarps; ++q) v += mslot[q * HG * D + i];
-        acc_s[h0 * D + i] = v;
-      }
-      named_bar(bar, kAttnThreads);
-    } else {
-#pragma unroll 1
-      for (int q = 0; q < kAttnWarps; ++q) {
-        if (warp == q && gi_lane == 0) {
-#pragma unroll
-          for (int h = 0; h < HG; ++h)
-#pragma unroll
-            for (int e = 0; e < CPL * 8; ++e) acc_s[(h0 + h) * D + (li + (e / 8) * LK) * 8 + (e & 7)] += acc[h][e];
-        }
-        named_bar(bar, kAttnThreads);
-      }
-    }
+    for (int e = 0; e < 4; ++e) o[i][e] = 0.f;
   }
-
+  float m_run = -INFINITY, l_run = 0.f;  // head g8 (l: this lane's keys only)
+  const uint32_t zero_sa = smem_addr(smem + lay.zero);
+  const uint32_t kn_sa = smem_addr(kn_s), vn_sa = smem_addr(vn_s);
+  const int r8 = lane & 7, mi = lane >> 3;  // ldmatrix: row within an 8x8 matrix, matrix index
+  const int nst = (k1 - k0 + KPS - 1) / KPS;
+#pragma unroll 1
+  for (int s = 0; s < nst; ++s) {
+    const int kbase = k0 + s * KPS;
+    const int st = rp.st;
+    bool live = (*dead == 0);
+    if (live && !mbar_wait(&ring.full[st], rp.ph, status)) {
+      *dead = 1;
+      live = false;
+    }
+    live = __all_sync(0xffffffffu, live);  // warp-uniform: the shuffles below need the whole warp
+    if (live) wp.next(ring.n);
+    const uint32_t stage_sa = smem_addr(ring.stages + (size_t)st * ring.stride);
+    float* part_s = spart + (s & 1) * kAttnWarps * 8 * HS;
+    if (live && warp < NPW) {  // S^T partial over this warp's dim groups
+#pragma unroll
+      for (int mt = 0; mt < NMT; ++mt) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int kr = 16 * mt + r8 + (mi & 1) * 8;  // A rows = keys; matrices (rows, dims) 00 10 01 11
+        const int key = kbase + kr;
+#pragma unroll
+        for (int i = 0; i < GPW; ++i) {
+          const int t = warp + kAttnWarps * i;
+          if (t < NDG) {
+            const int q = 2 * t + (mi >> 1);  // 16-byte chunk of the row
+            uint32_t addr = stage_sa + (q >> 3) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
+            if (key == pos) addr = kn_sa + q * 16;
+            else if (key >= k1) addr = zero_sa;
+            uint32_t af[4];
+            ldsm_x4(addr, af);
+            mma_16816(acc, af, qb[i][0], qb[i][1]);
+          }
+        }
+        float* w_s = part_s + warp * 8 * HS;
+        w_s[(2 * c4) * HS + 16 * mt + g8] = acc[0];
+        w_s[(2 * c4 + 1) * HS + 16 * mt + g8] = acc[1];
+        w_s[(2 * c4) * HS + 16 * mt + g8 + 8] = acc[2];
+        w_s[(2 * c4 + 1) * HS + 16 * mt + g8 + 8] = acc[3];
+      }
+    }
+    named_bar(bar, kAttnThreads);
+    if (live) {
+      // scores of head g8 at keys 16 mt + 2c, 2c+1, 2c+8, 2c+9: warp partials in order
+      float sv[NMT][4];
+#pragma unroll
+      for (int mt = 0; mt < NMT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) sv[mt][e] = 0.f;
+#pragma unroll
+      for (int w = 0; w < NPW; ++w) {
+        const float* hrow = part_s + (w * 8 + g8) * HS;
+#pragma unroll
+        for (int mt = 0; mt < NMT; ++mt) {
+          const float2 lo = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4);
+          const float2 hi = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4 + 8);
+          sv[mt][0] += lo.x;
+          sv[mt][1] += lo.y;
+          sv[mt][2] += hi.x;
+          sv[mt][3] += hi.y;
+        }
+      }
+      float mx = m_run;
+#pragma unroll
+      for (int mt = 0; mt < NMT; ++mt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int key = kbase + 16 * mt + 2 * c4 + (e & 1) + (e >> 1) * 8;
+          sv[mt][e] = key < k1 ? rbf(sv[mt][e]) : -INFINITY;
+          mx = fmaxf(mx, sv[mt][e]);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float corr = mx == -INFINITY ? 1.f : expf(m_run - mx);
+      m_run = mx;
+      uint32_t pb[NMT][2];
+      float psum = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < NMT; ++mt) {
+        float p[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          p[e] = sv[mt][e] == -INFINITY ? 0.f : expf(sv[mt][e] - mx);
+          psum += p[e];
+        }
+        pb[mt][0] = pack_bf16x2(p[0], p[1]);
+        pb[mt][1] = pack_bf16x2(p[2], p[3]);
+      }
+      l_run = l_run * corr + psum;
+      // rescale O^T: this lane's columns are heads 2c and 2c+1, held by lanes 8c and 8c+4
+      const float ca = __shfl_sync(0xffffffffu, corr, 8 * c4);
+      const float cb = __shfl_sync(0xffffffffu, corr, 8 * c4 + 4);
+#pragma unroll
+      for (int i = 0; i < GPW; ++i) {
+        o[i][0] *= ca;
+        o[i][1] *= cb;
+        o[i][2] *= ca;
+        o[i][3] *= cb;
+      }
+#pragma unroll
+      for (int mt = 0; mt < NMT; ++mt) {
+        const int kr = 16 * mt + r8 + (mi >> 1) * 8;  // A = V^T: matrices (dims, keys) 00 10 01 11
+        const int key = kbase + kr;
+#pragma unroll
+        for (int i = 0; i < GPW; ++i) {
+          const int t = warp + kAttnWarps * i;
+          if (t < NDG) {
+            const int q = 2 * t + (mi & 1);
+            uint32_t addr = stage_sa + (NBOX + (q >> 3)) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
+            if (key == pos) addr = vn_sa + q * 16;
+            else if (key >= k1) addr = zero_sa;
+            uint32_t af[4];
+            ldsm_x4_t(addr, af);
+            mma_16816(o[i], af, pb[mt][0], pb[mt][1]);
+          }
+        }
+      }
+    }
+    __syncwarp();
+    if (lane == 0 && live) mbar_arrive(&ring.empty[st]);
+    rp.next(ring.n);
+  }
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
-  // ---- 4. partials, then the last active CTA of this KV head merges them.  The
-  // acq_rel counter update (after the block barrier) publishes this CTA's partials
-  // and, for the last CTA, acquires every other CTA's.
+
+  // ---- 3. partials (m, l, O) of this item, then the last active CTA of this KV head
+  // merges them.  The acq_rel counter update (after the block barrier) publishes this
+  // CTA's partials and, for the last CTA, acquires every other CTA's.
+  float lt = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
+  lt = lt + __shfl_xor_sync(0xffffffffu, lt, 2);  // the same bits in the four lanes of a head
   float* pbase = a.part + ((size_t)hk * a.nsplit + sp) * G * (D + 2);
-  for (int i = threadIdx.x; i < G * (D + 2); i += kAttnThreads) {
-    const int h = i / (D + 2), e = i % (D + 2);
-    pbase[i] = e == 0 ? ml[h] : (e == 1 ? ml[kAttnMaxG + h] : acc_s[h * D + e - 2]);
+  if (warp == 0 && c4 == 0 && g8 < G) {
+    pbase[g8 * (D + 2)] = m_run;
+    pbase[g8 * (D + 2) + 1] = lt;
+  }
+#pragma unroll
+  for (int i = 0; i < GPW; ++i) {
+    const int t = warp + kAttnWarps * i;
+    if (t < NDG) {
+      const int dd = 2 + 16 * t + g8;
+      if (2 * c4 < G) {
+        pbase[(2 * c4) * (D + 2) + dd] = o[i][0];
+        pbase[(2 * c4) * (D + 2) + dd + 8] = o[i][2];
+      }
+      if (2 * c4 + 1 < G) {
+        pbase[(2 * c4 + 1) * (D + 2) + dd] = o[i][1];
+        pbase[(2 * c4 + 1) * (D + 2) + dd + 8] = o[i][3];
+      }
+    }
   }
   named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) {
@@ -459,15 +592,64 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   named_bar(bar, kAttnThreads);  // shared scratch free for the caller's next use
 }
 
-// Standalone launch: grid = n_kv x nsplit, one item per CTA.
+// Consumer thread 0 after a failure: wait (bounded) for the producer to stop issuing,
+// then for every issued stage past `wp`, so that no TMA load still writes into this
+// CTA's shared memory when it exits.  ints: [1] stages issued, [2] producer done.
+__device__ __forceinline__ void attn_drain(const AttnRing& ring, RingPos wp, int* ints) {
+  volatile int* v = ints;
+  const uint64_t t0 = globaltimer_ns();
+  while (!v[2] && globaltimer_ns() - t0 < kLocalTimeoutNs) __nanosleep(256);
+  __threadfence_block();
+  const int issued = v[1];
+  while (wp.tiles < issued) {
+    const uint64_t t1 = globaltimer_ns();
+    while (!mbar_try_wait(&ring.full[wp.st], wp.ph) && globaltimer_ns() - t1 < kLocalTimeoutNs) {
+    }
+    wp.next(ring.n);
+  }
+}
+
+// Standalone launch: grid = n_kv x nsplit, one item per CTA; warps 0-7 consume, warp 8
+// lane 0 produces the stages.
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnThreads) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
-  extern __shared__ __align__(16) unsigned char attn_smem[];
+__global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  extern __shared__ unsigned char attn_smem_raw[];
+  constexpr int SB = 4 * D * (D > 256 ? 16 : 32);
+  static_assert(SB % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
+  unsigned char* base =
+      reinterpret_cast<unsigned char*>((reinterpret_cast<uintptr_t>(attn_smem_raw) + 1023) & ~uintptr_t(1023));
+  unsigned char* scratch = base + kAttnStages * SB;
+  uint64_t* full = reinterpret_cast<uint64_t*>(scratch + ((attn_smem_layout(D).bytes + 15) & ~15));
+  uint64_t* empty = full + kAttnStages;
+  int* ints = reinterpret_cast<int*>(empty + kAttnStages);  // dead, stages issued, producer done
+  int* status = a.ctrl + G4_CTRL_STATUS;
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kAttnStages; ++i) {
+      mbar_init(&full[i], 1);
+      mbar_init(&empty[i], kAttnWarps);
+    }
+    ints[0] = ints[1] = ints[2] = 0;
+    mbar_init_fence();
+  }
+  __syncthreads();
   pdl_trigger();
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 0);
-  pdl_wait();
+  pdl_wait();  // the position, the cache rows and qkv come from earlier kernels
+  const AttnRing ring{full, empty, base, SB, kAttnStages};
+  volatile int* dead = ints;
+  if (threadIdx.x >= kAttnThreads) {
+    if (threadIdx.x == kAttnThreads) {
+      RingPos rp;
+      attn_produce(&a, blockIdx.x, gridDim.x, ring, rp, dead, status, ints + 1);
+      __threadfence_block();
+      reinterpret_cast<volatile int*>(ints)[2] = 1;
+    }
+    return;
+  }
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 2);
-  attn_item<D, G>(a, blockIdx.x / a.nsplit, blockIdx.x % a.nsplit, attn_smem, 1);
+  RingPos rp, wp;
+  attn_item<D, G>(a, blockIdx.x / a.nsplit, blockIdx.x % a.nsplit, scratch, 1, ring, rp, wp, dead, status);
+  if (threadIdx.x == 0 && *dead) attn_drain(ring, wp, ints);
 }
 
 }  // namespace g4

@@ -271,4 +271,22 @@ __device__ __forceinline__ float block_sum(float v, float* red, int nthreads, in
   return s;
 }
 
+// ------------------------------------------------------------------ stage rings
+// Position in a ring of shared-memory stages (full / empty mbarrier per stage),
+// advanced identically by the producer lane and the consumers of a CTA.
+struct RingPos {
+  int st = 0;         // stage index
+  uint32_t ph = 0;    // parity of the stage's current fill
+  bool wrapped = false;  // the ring has been filled once (the producer waits for `empty`)
+  int tiles = 0;      // tiles passed so far
+  __device__ __forceinline__ void next(int stages) {
+    ++tiles;
+    if (++st == stages) {
+      st = 0;
+      ph ^= 1u;
+      wrapped = true;
+    }
+  }
+};
+
 }  // namespace g4

@@ -237,23 +237,6 @@ __device__ __forceinline__ bool wait_copies(Smem& sm, int which, uint32_t parity
   return mbar_wait(&sm.pbar[which], parity, status);
 }
 
-// Position in the stage ring, advanced identically by the producer lane and the
-// consumers of a CTA.
-struct RingPos {
-  int st = 0;         // stage index
-  uint32_t ph = 0;    // parity of the stage's current fill
-  bool wrapped = false;  // the ring has been filled once (the producer waits for `empty`)
-  int tiles = 0;      // tiles passed so far
-  __device__ __forceinline__ void next(int stages) {
-    ++tiles;
-    if (++st == stages) {
-      st = 0;
-      ph ^= 1u;
-      wrapped = true;
-    }
-  }
-};
-
 // Producer lane: fill the next stage with tile (s, u0, n) of `op`.  Returns false
 // (after setting the CTA dead flag) when the stage never became free.
 template <class Op>

@@ -124,6 +124,12 @@ void g4_prefill_release(g4_model* m);
 void g4_batch_release(g4_model* m);
 // Launch one decode-attention item grid (g4_runtime.cu).
 int g4_launch_attention(const AttnArgs& a, cudaStream_t st);
+// Encode a.tmk / a.tmv from a.cache_k / a.cache_v, n_kv, d and max_len (g4_runtime.cu).
+int g4_attention_maps(AttnArgs& a);
+// A K-major bf16 matrix [rows, inner] (row stride `ld` elements) as a TMA tensor map with
+// boxes of 64 elements x box_rows rows, 128-byte swizzle (g4_prefill.cu).
+int g4_make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t ld,
+                   uint32_t box_rows);
 // model.py:54-61: fp64 inverse frequencies of the rotated pairs, zero (NoPE) tail.
 void g4_rope_inv_freq(int d, double theta, double partial, float* out);
 float g4_host_bf16_round(float f);

@@ -795,10 +795,9 @@ static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, bf16_
 // Routed MoE of the chunk's M tokens (see pf_route_count): routing tables, the gathered
 // MoE inputs, one grouped GEMM per projection (entry e = expert e: its rows, its weights),
 // the activation, and the per-token sum of the routed experts' outputs.
-static int routed_moe(g4_model* m, const LayerDev& l, int M, cudaStream_t st) {
+static int routed_moe(g4_model* m, const LayerDev& l, int M, int* status, cudaStream_t st) {
   PrefillWs& w = *m->prefill;
   const int H = m->H, E = m->E, F = m->F_local, MK = M * m->topk;
-  int* status = m->ctrl + G4_CTRL_STATUS;
   int rc;
   pf_route_count<<<E, kRowThreads, 0, st>>>(w.wfull, M, E, w.counts);
   pf_route_scan<<<1, 32, 0, st>>>(w.counts, E, w.z_rows);
@@ -928,7 +927,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
       return rc;
     pf_router<<<M, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
     if (!dense) {  // the same sum over the routed (token, expert) pairs only
-      if ((rc = routed_moe(m, l, M, st))) return rc;
+      if ((rc = routed_moe(m, l, M, status, st))) return rc;
     } else if ((rc = gemm({w.h2, (uint64_t)H, (uint64_t)M, (uint64_t)H},
                           {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H},
                           plain(M, E * 2 * F, H, w.gu, (long long)E * 2 * F, status), 1, st, sb))) {
@@ -986,6 +985,11 @@ static PfTarget model_target(g4_model* m, std::vector<bf16_t*>& ck, std::vector<
   return t;
 }
 
+int g4_make_map_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint64_t ld,
+                   uint32_t box_rows) {
+  return make_map_2d(map, base, inner, rows, ld, box_rows);
+}
+
 extern "C" int g4_gemm_bf16(const void* A, long long lda, const void* B, long long ldb, void* C, long long ldc, int M,
                             int N, int K, int c_f32, int* status, void* stream) {
   if (!A || !B || !C) return fail(G4_ERR_ARG, "g4_gemm_bf16: null pointer");
@@ -1039,6 +1043,7 @@ struct BatchWs {
   float* logits = nullptr;      // [B, V_local] fp32 softcapped logits of the last step
   bf16_t* xf = nullptr;         // [B, H]
   bf16_t* lmlog = nullptr;      // [B, V_local]
+  std::vector<CUtensorMap> mk, mv;  // [layer * B + b]: attention tensor maps of each cache
 };
 
 void g4_batch_release(g4_model* m) {
@@ -1047,6 +1052,8 @@ void g4_batch_release(g4_model* m) {
   delete m->batch;
   m->batch = nullptr;
 }
+
+static void batch_caches(const g4_model* m, int seq, std::vector<bf16_t*>& ck, std::vector<bf16_t*>& cv);
 
 extern "C" int g4_batch_reserve(g4_model* m, int batch, int ctx_len) {
   if (!m || !m->finalized) return fail(G4_ERR_STATE, "g4_batch_reserve: model not finalized");
@@ -1091,6 +1098,25 @@ extern "C" int g4_batch_reserve(g4_model* m, int batch, int ctx_len) {
   for (int b = 0; b < batch; ++b) ctrl[(size_t)b * G4_CTRL_WORDS + G4_CTRL_TIMEOUT_US] = 2000000;
   G4_CUDA(cudaMemcpy(w->ctrl, ctrl.data(), ctrl.size() * 4, cudaMemcpyHostToDevice), G4_ERR_CUDA);
   m->batch = w;
+  // tensor maps of every sequence's caches, once (the step launches copy them)
+  w->mk.resize(m->L.size() * batch);
+  w->mv.resize(m->L.size() * batch);
+  std::vector<bf16_t*> ck, cv;
+  for (int b = 0; b < batch; ++b) {
+    batch_caches(m, b, ck, cv);
+    for (size_t li = 0; li < m->L.size(); ++li) {
+      AttnArgs a = m->k2[li];
+      a.cache_k = ck[li];
+      a.cache_v = cv[li];
+      a.max_len = ctx_len;
+      if (int rc = g4_attention_maps(a)) {
+        g4_batch_release(m);
+        return rc;
+      }
+      w->mk[li * batch + b] = a.tmk;
+      w->mv[li * batch + b] = a.tmv;
+    }
+  }
   return G4_OK;
 }
 
@@ -1172,6 +1198,8 @@ extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, vo
       a.pos_fixed = -1;
       a.max_len = bw.ctx;
       a.trace_id = -1;
+      a.tmk = bw.mk[li * B + b];
+      a.tmv = bw.mv[li * B + b];
       if ((rc = g4_launch_attention(a, st))) return rc;
     }
     if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)B, (uint64_t)nq * d},
@@ -1193,7 +1221,7 @@ extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, vo
                    plain(B, E, H, w.rlog, E, status), 1, st, sb)))
       return rc;
     pf_router<<<B, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
-    if ((rc = routed_moe(m, l, B, st))) return rc;
+    if ((rc = routed_moe(m, l, B, status, st))) return rc;
     pf_combine<<<B, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
                                            l.scalar, H, eps);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);

@@ -197,7 +197,7 @@ static int prepare_attention(int d, int g) {
   cudaGetDevice(&dev);
   AttnKernel k = attn_kernel_for(d, g);
   if (!k) return fail(G4_ERR_SHAPE, "attention: head_dim %d with %d query heads per KV head", d, g);
-  const int smem = attn_smem_bytes(g, d);
+  const int smem = attn_kernel_smem_bytes(d);
   std::lock_guard<std::mutex> lock(mu);
   int& have = done[{dev, d * 16 + g}];
   if (have >= smem) return G4_OK;
@@ -230,12 +230,21 @@ static int launch_gemv(const Op& op, int grid, cudaStream_t st) {
 static int launch_attention(const AttnArgs& a, cudaStream_t st) {
   int rc = prepare_attention(a.d, a.g);
   if (rc) return rc;
-  cudaError_t e = launch_pdl(attn_kernel_for(a.d, a.g), dim3(a.n_kv * a.nsplit), dim3(kAttnThreads),
-                             attn_smem_bytes(a.g, a.d), st, a);
+  cudaError_t e = launch_pdl(attn_kernel_for(a.d, a.g), dim3(a.n_kv * a.nsplit), dim3(kAttnKernelThreads),
+                             attn_kernel_smem_bytes(a.d), st, a);
   if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "attention launch: %s", cudaGetErrorString(e));
   return G4_OK;
 }
 int g4_launch_attention(const AttnArgs& a, cudaStream_t st) { return launch_attention(a, st); }
+
+// The TMA tensor maps of a.cache_k / a.cache_v: [max_len, n_kv * d] bf16, boxes of 64
+// elements x attn_kps(d) rows, 128-byte swizzle (the attention kernels' stage layout).
+int g4_attention_maps(AttnArgs& a) {
+  const uint64_t w = (uint64_t)a.n_kv * a.d;
+  int rc = g4_make_map_2d(&a.tmk, a.cache_k, w, (uint64_t)a.max_len, w, (uint32_t)attn_kps(a.d));
+  if (!rc) rc = g4_make_map_2d(&a.tmv, a.cache_v, w, (uint64_t)a.max_len, w, (uint32_t)attn_kps(a.d));
+  return rc;
+}
 
 void g4_rope_inv_freq(int d, double theta, double partial, float* out) {
   // model.py:54-61: fp64 inverse frequencies for the rotated pairs, zero (NoPE) tail
@@ -816,6 +825,7 @@ extern "C" int g4_model_finalize(g4_model* m) {
     t.max_len = m->max_len;
     t.eps = c.rms_norm_eps;
     t.trace_id = i * 8 + 1;
+    if (int rc = g4_attention_maps(t)) return rc;
 
     OProjOp& o = m->k3[i];
     o = OProjOp{};
@@ -1378,6 +1388,7 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   a.max_len = max_len;
   a.eps = eps;
   a.trace_id = -1;
+  if (int rc = g4_attention_maps(a)) return rc;
   return launch_attention(a, st);
 }
 
@@ -1655,5 +1666,6 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   a.max_len = max_len;
   a.eps = eps;
   a.trace_id = -1;
+  if ((rc = g4_attention_maps(a))) return rc;
   return launch_attention(a, st);
 }

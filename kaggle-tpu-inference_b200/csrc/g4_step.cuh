@@ -279,7 +279,16 @@ static __device__ __noinline__ void produce_step(const StepProgram& P, Smem sm, 
     const unsigned char* slot = sm.popc + (i & 1) * kOpCopyBytes;
     const int2* rng = step_ranges(P, sm) + i * kRangeSlots;
     switch (kind) {
-      case 0: ok = produce_op(*reinterpret_cast<const QkvOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
+      case 0:
+        ok = produce_op(*reinterpret_cast<const QkvOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer);
+        // layer l's attention stages follow its qkv weights in the ring (the cache rows
+        // do not depend on qkv; the one row qkv produces is patched by the consumers)
+        if (ok) {
+          const AttnRing ring{sm.full, sm.empty, sm.stages, kStageBytes, P.stages};
+          ok = attn_produce(P.k2 + l, blockIdx.x, gridDim.x, ring, rp, sm.ints + kSmemDead, status,
+                            sm.ints + kSmemIssued);
+        }
+        break;
       case 2: ok = produce_op(*reinterpret_cast<const OProjOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
       case 3: ok = produce_op(*reinterpret_cast<const RouterMlpOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
       case 4: ok = produce_op(*reinterpret_cast<const MoeUpOp*>(slot), l, P, sm, rp, pol, seq, rng, ids_layer); break;
@@ -446,12 +455,15 @@ __device__ __forceinline__ void gemv_phase_body(const StepProgram& P, int l, int
   if (threadIdx.x == 0) G4_TRACE_EV(ob.trace_id, 6);
 }
 
-// Attention items of this CTA for one layer.
+// Attention items of this CTA for one layer; their key stages come through the ring.
 template <int D, int G>
-__device__ __forceinline__ void attn_items(const AttnArgs& a, unsigned char* scratch) {
+__device__ __forceinline__ void attn_items(const AttnArgs& a, unsigned char* scratch, Smem& sm, PhaseState& ps,
+                                           int stages, int* status) {
+  const AttnRing ring{sm.full, sm.empty, sm.stages, kStageBytes, stages};
   const int items = a.n_kv * a.nsplit;
   for (int it = blockIdx.x; it < items; it += gridDim.x)
-    attn_item<D, G>(a, it / a.nsplit, it % a.nsplit, scratch, kBarConsumers);
+    attn_item<D, G>(a, it / a.nsplit, it % a.nsplit, scratch, kBarConsumers, ring, ps.rp, ps.wp,
+                    sm.ints + kSmemDead, status);
 }
 
 // Wait (bounded) for every issued tile thread 0 did not see complete, so that no
@@ -521,8 +533,8 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
       wait_constants(P, sm, ps);  // an empty list: completes at once (keeps the parity)
       if (ps.live) {  // the auxiliary area is free during attention
         const AttnArgs& a = P.k2[l];
-        if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0);
-        else if (a.d == DF && a.g == GF) attn_items<DF, GF>(a, sm.x0);
+        if (a.d == DS && a.g == GS) attn_items<DS, GS>(a, sm.x0, sm, ps, P.stages, status);
+        else if (a.d == DF && a.g == GF) attn_items<DF, GF>(a, sm.x0, sm, ps, P.stages, status);
       }
     } else {
       gemv_phase_body<CPLM>(P, l, k, sm, ps, h);

@@ -69,3 +69,36 @@ def test_batch_decode_real_shapes():
     g = torch.Generator().manual_seed(13)
     prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (9, 40, 17, 64)]
     _batch_case(cfg, params, prompts, 3, 128, "batch4 real shapes")
+
+
+def test_batch_decode_graph_replay_matches_eager():
+    """The CUDA-graph replay of the batched step produces the eager path's tokens and
+    logits bit for bit (one eager step, then captured steps; positions advance on the
+    device), and a prefill in between forces a fresh capture."""
+    cfg = tiny_parity_config()
+    params = random_params(cfg, 0)
+    shard = rank_shard(cfg, params.__getitem__, Mesh(0, 1, 0), DEV)
+    m = DecodeModel(cfg, shard, Mesh(0, 1, 0), 128)
+    g = torch.Generator().manual_seed(21)
+    prompts = [torch.randint(0, cfg.vocab_size, (n,), generator=g).tolist() for n in (11, 30, 45, 7)]
+
+    def run(graph):
+        bd = BatchDecoder(m, len(prompts), 128)
+        for s, p in enumerate(prompts):
+            bd.prefill(s, p)
+        toks, lg = [], []
+        for i in range(8):
+            if i == 4:  # re-prefill sequence 3: the graph must be re-captured
+                bd.prefill(3, prompts[3])
+            bd.step(write_logits=True, graph=graph)
+            toks.append(bd.tokens.clone())
+            lg.append(bd.logits.clone())
+        torch.cuda.synchronize()
+        bd.check_status()
+        return torch.stack(toks).cpu(), torch.stack(lg).cpu()
+
+    t_eager, l_eager = run(False)
+    t_graph, l_graph = run(True)
+    assert torch.equal(t_eager, t_graph)
+    assert torch.equal(l_eager, l_graph)
+    m.close()
