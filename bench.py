@@ -76,6 +76,12 @@ def parse_args():
                     help="steps timed at the end of the 32K cache (all keys live); 0 skips")
     ap.add_argument("--prefill-tokens", type=int, default=4096,
                     help="benchmark config 5 prompt length for the prefill (TTFT) leg; 0 skips it")
+    ap.add_argument("--batch-size", type=int, default=8,
+                    help="benchmark config 5 batched decode: sequences (0 skips the leg)")
+    ap.add_argument("--batch-steps", type=int, default=256, help="config 5: tokens decoded per sequence")
+    ap.add_argument("--batch-ctx", type=int, default=8192, help="config 5: cache positions per sequence")
+    ap.add_argument("--batch-prompt", type=int, default=4096, help="config 5: prompt length per sequence")
+    ap.add_argument("--batch-only", action="store_true", help="profiling: run only the batched-decode leg")
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
     # profiling knobs (smaller models for ncu captures); defaults are config 4
     ap.add_argument("--layers", type=int, default=30)
@@ -313,6 +319,64 @@ def prefill_leg(eng, cfg, args, dev):
     return out
 
 
+# ----------------------------------------------------------------------------- batched decode
+def batch_step_bytes(cfg, B, pos_avg):
+    """Algorithmic HBM bytes of one batched step (world 1): every dense weight once, the
+    union of the B tokens' routed experts per layer (its expected size under uniform
+    routing, E (1 - (1 - k/E)^B): the union is data-dependent) and every sequence's live
+    keys and values."""
+    b = class_bytes(cfg, 1, pos_avg)
+    H, F, E, K = cfg.hidden_size, cfg.moe_intermediate_size, cfg.num_experts, cfg.top_k_experts
+    L = len(cfg.layer_types)
+    union = E * (1.0 - (1.0 - K / E) ** B)
+    experts_top_k = L * 2 * 3 * K * F * H
+    experts_union = L * 2 * 3 * union * F * H
+    total = sum(b.values()) - b["attention"] - experts_top_k + experts_union + B * b["attention"]
+    return total, union
+
+
+def batch_leg(eng, cfg, args, dev):
+    """Benchmark config 5's decode: --batch-size sequences (seed 4 + s), each a prompt of
+    --batch-prompt random ids through the tensor-core prefill into its own
+    --batch-ctx-position cache, then --batch-steps greedy tokens of every sequence, the
+    step replayed as one CUDA graph; device time with CUDA events over the decode steps."""
+    import torch
+
+    from gemma4_b200.runtime import BatchDecoder
+
+    B, ctx = args.batch_size, args.batch_ctx
+    P = min(args.batch_prompt, ctx - args.batch_steps - 2)
+    m = eng.model
+    bd = BatchDecoder(m, B, ctx)
+    for s in range(B):
+        g = torch.Generator().manual_seed(4 + s)
+        bd.prefill(s, torch.randint(0, cfg.vocab_size, (P,), generator=g).tolist())
+    bd.step(graph=True)  # eager (captures nothing yet)
+    bd.step(graph=True)  # captures, replays
+    bd.step(graph=True)
+    torch.cuda.synchronize(dev)
+    n = args.batch_steps - 3
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(n):
+        bd.step(graph=True)
+    e1.record()
+    torch.cuda.synchronize(dev)
+    bd.check_status()
+    ms = e0.elapsed_time(e1) / n
+    peak, peak_kind = peaks()
+    byts, union = batch_step_bytes(cfg, B, P + args.batch_steps // 2)
+    out = {"workload": f"benchmark config 5 decode: batch {B}, {P}-token prompts, {args.batch_steps} tokens each, "
+                       f"{ctx}-position caches (world 1)",
+           "tok_per_s": B / ms * 1e3, "ms_per_step": ms, "steps_timed": n,
+           "bytes_per_step": byts, "expected_experts_per_layer": union,
+           "achieved_gbs": byts / ms / 1e6, "peak_gbs": peak, "peak_kind": peak_kind,
+           "frac": byts / ms / 1e6 / peak, "graph": True}
+    m.batch_owner = None
+    del bd
+    return out
+
+
 # ----------------------------------------------------------------------------- blocks
 def block_legs(args, dev, reps=20):
     """Benchmark configs 2 and 3 through their C-ABI block entry points, world 1: the MoE
@@ -490,6 +554,11 @@ def main() -> int:
         return 0
     eng = Engine(None, max_len=args.max_len, cfg=cfg, random_seed=args.seed, mesh=mesh,
                  engine=args.engine)
+    if args.batch_only:  # profiling case: the batched-decode leg alone, one JSON line
+        line = {"metric": "batched decode tok/s", "batch": batch_leg(eng, cfg, args, dev) if world == 1 else None}
+        if rank == 0:
+            print(json.dumps(line), flush=True)
+        return 0
     if args.prefill_only:  # profiling case: the prefill leg alone, one JSON line
         line = {"metric": "prefill TTFT ms", "config": workload,
                 "prefill": prefill_leg(eng, cfg, args, dev) if world == 1 else None}
@@ -618,6 +687,7 @@ def main() -> int:
 
     prefill = prefill_leg(eng, cfg, args, dev) if args.prefill_tokens > 0 and world == 1 else None
     blocks = block_legs(args, dev) if world == 1 and not args.no_blocks else None
+    batch = batch_leg(eng, cfg, args, dev) if world == 1 and args.batch_size > 0 else None
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -638,7 +708,7 @@ def main() -> int:
             "config": workload, "clocks": clocks, "e2e": e2e, "roofline": roofline,
             "step_roofline": step_roof, "op_kernels": op_kernels, "engine": args.engine,
             "cpu_baseline": cpu, "tokens_match": tokens_match, "prefill": prefill, "blocks": blocks,
-            "long_context": long_ctx,
+            "long_context": long_ctx, "batch_decode": batch,
             "gpu_launches": args.steps * m.kernels_per_step,
             "load_s": eng.load_seconds,
         }

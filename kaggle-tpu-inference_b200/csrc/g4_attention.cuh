@@ -35,8 +35,8 @@
 //      points at the shared copy of the new key / value, and keys past the slice point
 //      at a zero row (the stage holds stale or zero-filled rows there).
 //   3. (m, l, O) of the item go to the partial buffer; the last CTA of head h (atomic
-//      counter) merges the n_active partials in split order with max-rescaling and
-//      rounds the context to bf16.
+//      counter) merges the n_active partials in split order with max-rescaling (4-element
+//      vector loads, 4 to 16 splits in flight per thread) and rounds the context to bf16.
 // Every sum has a fixed order: results are bitwise reproducible, and the step kernel
 // and the standalone kernel (same items, same stages) compute identical bits.
 #pragma once
@@ -67,7 +67,7 @@ struct AttnArgs {
   bf16_t* cache_v;         // [max_len, n_kv, d]
   const float* inv_freq;   // [d/2]
   bf16_t* ctx;             // [n_kv*g*d]
-  float* part;             // [n_kv, nsplit, g, d+2] (m, l, acc[d])
+  float* part;             // O [n_kv, nsplit, g, d] then (m, l) [n_kv, nsplit, g, 2]
   int* counters;           // [n_kv], zero at rest
   int* ctrl;               // control block (POS, STATUS)
   int pos_fixed;           // >= 0 overrides ctrl[POS]
@@ -495,28 +495,32 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   }
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
 
-  // ---- 3. partials (m, l, O) of this item, then the last active CTA of this KV head
-  // merges them.  The acq_rel counter update (after the block barrier) publishes this
-  // CTA's partials and, for the last CTA, acquires every other CTA's.
+  // ---- 3. partials of this item -- O [G][D] in the O block (16-byte aligned rows for
+  // the merge's vector loads), (m, l) [G][2] in the block after it -- then the last
+  // active CTA of this KV head merges them.  The acq_rel counter update (after the
+  // block barrier) publishes this CTA's partials and, for the last CTA, acquires every
+  // other CTA's.
   float lt = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
   lt = lt + __shfl_xor_sync(0xffffffffu, lt, 2);  // the same bits in the four lanes of a head
-  float* pbase = a.part + ((size_t)hk * a.nsplit + sp) * G * (D + 2);
+  const size_t n_items = (size_t)a.n_kv * a.nsplit;
+  float* part_o = a.part + ((size_t)hk * a.nsplit + sp) * G * D;
+  float* part_ml = a.part + n_items * G * D + ((size_t)hk * a.nsplit + sp) * G * 2;
   if (warp == 0 && c4 == 0 && g8 < G) {
-    pbase[g8 * (D + 2)] = m_run;
-    pbase[g8 * (D + 2) + 1] = lt;
+    part_ml[g8 * 2] = m_run;
+    part_ml[g8 * 2 + 1] = lt;
   }
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
     const int t = warp + kAttnWarps * i;
     if (t < NDG) {
-      const int dd = 2 + 16 * t + g8;
+      const int dd = 16 * t + g8;
       if (2 * c4 < G) {
-        pbase[(2 * c4) * (D + 2) + dd] = o[i][0];
-        pbase[(2 * c4) * (D + 2) + dd + 8] = o[i][2];
+        part_o[(2 * c4) * D + dd] = o[i][0];
+        part_o[(2 * c4) * D + dd + 8] = o[i][2];
       }
       if (2 * c4 + 1 < G) {
-        pbase[(2 * c4 + 1) * (D + 2) + dd] = o[i][1];
-        pbase[(2 * c4 + 1) * (D + 2) + dd + 8] = o[i][3];
+        part_o[(2 * c4 + 1) * D + dd] = o[i][1];
+        part_o[(2 * c4 + 1) * D + dd + 8] = o[i][3];
       }
     }
   }
@@ -530,36 +534,37 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   const bool merge = *flag != 0;
   named_bar(bar, kAttnThreads);  // every thread has read the flag before it is reused
   if (!merge) return;
-  // One pass over the partials: each thread takes elements i = tid + 256 k of the
-  // [G][D] context and, SB splits at a time (all their loads in flight together),
+  // One pass over the partials: each thread takes 4-element chunks i = tid + 256 k of
+  // the [G][D] context and, SB splits at a time (all their loads in flight together),
   // folds (m, l, acc) into a running max-rescaled sum in split order.
-  constexpr int NE = (G * D + kAttnThreads - 1) / kAttnThreads;
-  constexpr int SB = NE <= 2 ? 16 : (NE >= 32 ? 1 : 32 / NE);  // <= 96 values in flight
-  const float* hbase = a.part + (size_t)hk * a.nsplit * G * (D + 2);
-  float M[NE], L[NE], O[NE];
+  constexpr int NC = G * D / 4;                                  // chunks per head
+  constexpr int NE = (NC + kAttnThreads - 1) / kAttnThreads;     // chunks per thread
+  constexpr int SB = NE >= 4 ? 4 : 16 / NE;                      // splits per batch
+  const float4* ho = reinterpret_cast<const float4*>(a.part + (size_t)hk * a.nsplit * G * D);
+  const float2* hml = reinterpret_cast<const float2*>(a.part + n_items * G * D) + (size_t)hk * a.nsplit * G;
+  float M[NE], L[NE];
+  float4 O[NE];
 #pragma unroll
   for (int k = 0; k < NE; ++k) {
     M[k] = -INFINITY;
     L[k] = 0.f;
-    O[k] = 0.f;
+    O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
   }
 #pragma unroll 1
   for (int s0 = 0; s0 < n_active; s0 += SB) {
-    float mv[NE][SB], lv[NE][SB], av[NE][SB];
+    float2 mlv[NE][SB];
+    float4 av[NE][SB];
 #pragma unroll
     for (int k = 0; k < NE; ++k) {
       const int i = threadIdx.x + kAttnThreads * k;
-      const int h = i / D, e = i % D;
+      const int h = (4 * i) / D;
 #pragma unroll
       for (int q = 0; q < SB; ++q) {
-        mv[k][q] = -INFINITY;
-        lv[k][q] = 0.f;
-        av[k][q] = 0.f;
-        if (i < G * D && s0 + q < n_active) {
-          const float* p = hbase + ((size_t)(s0 + q) * G + h) * (D + 2);
-          mv[k][q] = ldcg_f(p);
-          lv[k][q] = ldcg_f(p + 1);
-          av[k][q] = ldcg_f(p + 2 + e);
+        mlv[k][q] = make_float2(-INFINITY, 0.f);
+        av[k][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < NC && s0 + q < n_active) {
+          mlv[k][q] = __ldcg(hml + (size_t)(s0 + q) * G + h);
+          av[k][q] = __ldcg(ho + (size_t)(s0 + q) * NC + i);
         }
       }
     }
@@ -567,15 +572,21 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     for (int k = 0; k < NE; ++k) {
       float mb = M[k];
 #pragma unroll
-      for (int q = 0; q < SB; ++q) mb = fmaxf(mb, mv[k][q]);
+      for (int q = 0; q < SB; ++q) mb = fmaxf(mb, mlv[k][q].x);
       const float cf = M[k] == -INFINITY ? 0.f : expf(M[k] - mb);
       L[k] *= cf;
-      O[k] *= cf;
+      O[k].x *= cf;
+      O[k].y *= cf;
+      O[k].z *= cf;
+      O[k].w *= cf;
 #pragma unroll
       for (int q = 0; q < SB; ++q) {
-        const float f = mv[k][q] == -INFINITY ? 0.f : expf(mv[k][q] - mb);
-        L[k] = fmaf(lv[k][q], f, L[k]);
-        O[k] = fmaf(av[k][q], f, O[k]);
+        const float f = mlv[k][q].x == -INFINITY ? 0.f : expf(mlv[k][q].x - mb);
+        L[k] = fmaf(mlv[k][q].y, f, L[k]);
+        O[k].x = fmaf(av[k][q].x, f, O[k].x);
+        O[k].y = fmaf(av[k][q].y, f, O[k].y);
+        O[k].z = fmaf(av[k][q].z, f, O[k].z);
+        O[k].w = fmaf(av[k][q].w, f, O[k].w);
       }
       M[k] = mb;
     }
@@ -583,7 +594,13 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
 #pragma unroll
   for (int k = 0; k < NE; ++k) {
     const int i = threadIdx.x + kAttnThreads * k;
-    if (i < G * D) a.ctx[((size_t)hk * G + i / D) * D + i % D] = f2bf(O[k] / L[k]);
+    if (i < NC) {
+      const int h = (4 * i) / D, e = (4 * i) % D;
+      uint2 w;
+      w.x = pack_bf16x2(O[k].x / L[k], O[k].y / L[k]);
+      w.y = pack_bf16x2(O[k].z / L[k], O[k].w / L[k]);
+      *reinterpret_cast<uint2*>(a.ctx + ((size_t)hk * G + h) * D + e) = w;
+    }
   }
   if (threadIdx.x == 0) {
     atomicExch(a.counters + hk, 0);

@@ -22,8 +22,9 @@ microseconds:
 
 Event slots per phase (trace id = 8 * layer + kind; the LM head is 8 * layers):
 0 start, 1 staged, 2 constants + barrier, 3 prologue done, 4 first tile, 5 last tile,
-6 finish.  Attention phases use 3 (q/k prologue), 4 (key loop + merge), 5 (partials
-published), 6 (merge, merging CTA only).
+6 finish.  Attention phases use 3 (q/k prologue), 4 (key stages), 5 (partials
+published), 6 (merge, merging CTA only).  ``attn-s`` / ``attn-f`` rows: sliding / full
+layers.
 """
 import argparse
 import os
@@ -33,22 +34,25 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.dirname(HERE))
 
 KINDS = ["qkv", "attn", "oproj", "rmlp", "moeup", "moedn"]
+ROWS = ["qkv", "attn-s", "attn-f", "oproj", "rmlp", "moeup", "moedn"]  # attention: sliding / full layers
 TRACE_CTAS, TRACE_EVENTS, TRACE_LAUNCHES = 160, 8, 512
 
 
-def phase_stats(buf, layers):
+def phase_stats(buf, layers, full=()):
+    """Per-phase medians over the traced CTAs, averaged over the layers of each row of
+    ROWS (``full``: indices of the full-attention layers)."""
     import numpy as np
 
     b = buf.astype(np.int64)
     ncta = int((b[0, :, 0] > 0).sum())
-    rows = [(k, b[8 * l + k][:ncta]) for l in range(layers) for k in range(6)]
-    rows.append((6, b[8 * layers][:ncta]))
-    stats = {k: [] for k in KINDS}
+    rows = [(k, b[8 * l + k][:ncta], l) for l in range(layers) for k in range(6)]
+    rows.append((6, b[8 * layers][:ncta], layers))
+    stats = {k: [] for k in ROWS}
 
     def med(x):
         return float(np.median(x)) / 1e3 if len(x) else 0.0
 
-    for i, (k, e) in enumerate(rows[:-1]):
+    for i, (k, e, layer) in enumerate(rows[:-1]):
         s0, e1, e2, e3, e4, e5, e6 = (e[:, j] for j in range(7))
         ok = (s0 > 0) & (e6 >= s0)
         if not ok.any():
@@ -59,7 +63,8 @@ def phase_stats(buf, layers):
         m4 = (e4 > 0) & m3
         m5 = (e5 > 0) & m4
         m12 = (e1 > 0) & (e2 > 0) & m3
-        stats[KINDS[k]].append((
+        name = KINDS[k] if k != 1 else ("attn-f" if layer in full else "attn-s")
+        stats[name].append((
             (s0[ok].max() - s0[ok].min()) / 1e3,
             med(e1[m12] - s0[m12]), med(e2[m12] - e1[m12]), med(e3[m12] - e2[m12]),
             med(e4[m4] - e3[m4]), med(e5[m5] - e4[m5]),
@@ -76,6 +81,8 @@ def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--layers", type=int, default=6)
     ap.add_argument("--warm", type=int, default=132, help="tokens decoded before the traced step")
+    ap.add_argument("--pos", type=int, default=0,
+                    help="trace the step at this position instead (jumps there; 0: after --warm tokens)")
     ap.add_argument("--max-len", type=int, default=32768)
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
     ap.add_argument("--lib", default=os.path.join(HERE, "libg4b200_trace.so"))
@@ -107,7 +114,11 @@ def main():
     m = eng.model
     prompt = list(range(100, 132))
     m.reset(prompt)
-    m.step(len(prompt) + args.warm)
+    if args.pos > 0:  # positions pos-2.. read tokens_out (their values do not change the time)
+        m.ctrl[0] = args.pos - 2
+        m.step(2)
+    else:
+        m.step(len(prompt) + args.warm)
     torch.cuda.synchronize()
     m.step(1)
     torch.cuda.synchronize()
@@ -119,12 +130,13 @@ def main():
         dist.destroy_process_group()
         if rank != 0:
             return 0
-    ncta, span, st = phase_stats(buf, args.layers)
+    full = [i for i, t in enumerate(cfg.layer_types) if t == "full_attention"]
+    ncta, span, st = phase_stats(buf, args.layers, full)
     print(f"engine {args.engine}, {args.layers} layers, world {world} (rank 0 shown), {ncta} CTAs traced, "
-          f"step span {span:.1f} us")
+          f"position {int(m.ctrl[0].item()) - 1}, step span {span:.1f} us")
     cols = ["start-skew", "stage", "const+bar", "compute", "first-tile", "tiles", "straggle", "gap", "span"]
     print("kind   " + " ".join(f"{c:>10s}" for c in cols))
-    for k in KINDS:
+    for k in ROWS:
         if k in st:
             print(f"{k:6s} " + " ".join(f"{x:10.1f}" for x in st[k]))
     return 0
