@@ -170,7 +170,7 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
   return r;
 }
 
-// 2-D TMA tile load with an L2 cache policy (no multicast).
+// 2-D TMA tile load into this CTA's shared memory with an L2 cache policy.
 __device__ __forceinline__ void attn_tma_load(void* dst, const CUtensorMap* map, int x, int y, uint64_t* bar,
                                               uint64_t pol) {
   asm volatile(

@@ -8,7 +8,7 @@
 // dims).  One CTA computes one BM x BN tile:
 //
 //   warp 0 lane 0   producer: TMA tiled loads (cp.async.bulk.tensor, 128-byte swizzle,
-//                   no multicast) of A [BM x 64] and B [BN x 64] per k-block into a
+//                   one destination CTA) of A [BM x 64] and B [BN x 64] per k-block into a
 //                   STAGES-deep shared-memory ring, full/empty mbarriers;
 //   warp 1          allocates BN TMEM columns; lane 0 issues tcgen05.mma (M=128,
 //                   N=BN, K=16, kind::f16, bf16 -> fp32) four per k-block from shared
