@@ -14,15 +14,18 @@
 // tiles are issued right after layer l's qkv weights, so they stream in under the qkv
 // phase.  The standalone kernel has a ring of its own (kAttnStages deep).
 //
-// Per item, the 8 consumer warps:
+// Per item, the 8 consumer warps (two groups of 4; group g takes stages g, g+2, ...,
+// keeps its own online-softmax state and releases the other group's stages once they
+// have landed; the two states are combined at the end of the item):
 //   1. q_norm RMSNorm + RoPE of the g query heads (bf16 rounding points of model.py:198
 //      and 70-78); the item whose slice holds `pos` also normalises, RoPEs and writes k
 //      (and v = rms(v_raw), or rms(k_raw) for k==v layers) into the cache
 //      (model.py:200-206) and keeps both in shared memory;
 //   2. per stage, on the tensor cores (mma.sync m16n8k16, bf16 in, fp32 accumulate):
-//        S^T [KPS keys x 8 heads] = K . Q^T: warp w contracts its own 16-dim groups
-//          (w, w+8, ...) and leaves the partial in shared memory; after one barrier every
-//          warp adds the partials in warp order (the same bits in every warp), rounds
+//        S^T [KPS keys x 8 heads] = K . Q^T: warp w of a group contracts its own 16-dim
+//          groups (w, w+4, ...) and leaves the partial in shared memory; after one group
+//          barrier every warp adds the partials in warp order (the same bits in every
+//          warp), rounds
 //          the scores to bf16 as the reference einsum does, and updates the online
 //          softmax (running max m, mass l);
 //        O^T [16 dims x 8 heads] += V^T . P^T for the warp's own dim groups, with
@@ -51,6 +54,9 @@ constexpr int kAttnThreads = 256;                      // consumer threads (8 wa
 constexpr int kAttnWarps = kAttnThreads / 32;
 constexpr int kAttnKernelThreads = kAttnThreads + 32;  // + the producer warp (standalone kernel)
 constexpr int kAttnStages = 4;                         // ring depth of the standalone kernel
+constexpr int kAttnGroups = 2;                         // warp groups taking alternate stages
+constexpr int kAttnGroupWarps = kAttnWarps / kAttnGroups;
+constexpr int kBarAttnGroup = 3;                       // named barriers 3, 4: one per warp group
 constexpr int kAttnMaxChunk = 1024;  // keys per item the host's split aims to stay under
 constexpr int kAttnMinKeys = 32;     // keys per item before another split is used
 constexpr int kAttnMaxG = 8;         // query heads per KV head: one 8-column MMA tile
@@ -85,7 +91,8 @@ __host__ __device__ __forceinline__ int attn_hs(int d) { return attn_kps(d) + 8;
 // Scratch of one item (byte offsets from a 16-byte aligned base): the normalised query
 // heads q [8][d] bf16 (rows past g zero), the new key and value [d] bf16 each, a 16-byte
 // zero row, the RoPE table [d] fp32 (cos | sin), the score partials
-// [2][8 warps][8 heads][hs] fp32 (double-buffered by stage) and a flag word.
+// [2 groups][2][4 warps][8 heads][hs] fp32 (double-buffered by the group's stages; at the
+// end of an item the same area carries group 1's state to group 0) and a flag word.
 struct AttnSmem {
   int q, kn, vn, zero, rope, part, flag, bytes;
 };
@@ -97,7 +104,8 @@ __host__ __device__ __forceinline__ AttnSmem attn_smem_layout(int d) {
   s.zero = s.vn + d * 2;
   s.rope = s.zero + 16;
   s.part = s.rope + d * 4;
-  s.flag = s.part + 2 * kAttnWarps * 8 * attn_hs(d) * 4;
+  const int spart = 2 * kAttnWarps * 8 * attn_hs(d) * 4, xchg = 32 * d + 128;
+  s.flag = s.part + (spart > xchg ? spart : xchg);
   s.bytes = s.flag + 64;
   return s;
 }
@@ -243,8 +251,9 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   constexpr int KPS = D > 256 ? 16 : 32;      // keys per stage
   constexpr int NMT = KPS / 16;               // 16-key MMA tiles per stage
   constexpr int NDG = D / 16;                 // 16-dim groups
-  constexpr int NPW = NDG < kAttnWarps ? NDG : kAttnWarps;  // warps owning dim groups
-  constexpr int GPW = (NDG + kAttnWarps - 1) / kAttnWarps;  // dim groups per warp
+  constexpr int WPG = kAttnGroupWarps;        // warps per group
+  constexpr int NPW = NDG < WPG ? NDG : WPG;  // warps of a group owning dim groups
+  constexpr int GPW = (NDG + WPG - 1) / WPG;  // dim groups per warp
   constexpr int NBOX = D / 64;
   constexpr int HS = KPS + 8;
   static_assert(D % 64 == 0 && D <= kAttnMaxD && G >= 1 && G <= kAttnMaxG, "attention shape");
@@ -353,13 +362,14 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 3);
 
-  // ---- 2. the stages of this item
+  // ---- 2. the stages of this item (group grp computes stages grp, grp + 2, ...)
+  const int grp = warp / WPG, wig = warp % WPG;
   // Q^T operand fragments of this warp's dim groups (column = head lane/4)
   uint32_t qb[GPW][2];
   float o[GPW][4];
 #pragma unroll
   for (int i = 0; i < GPW; ++i) {
-    const int t = warp + kAttnWarps * i;
+    const int t = wig + WPG * i;
     qb[i][0] = qb[i][1] = 0u;
     if (t < NDG) {
       qb[i][0] = *reinterpret_cast<const uint32_t*>(q_s + g8 * D + 16 * t + 2 * c4);
@@ -384,143 +394,175 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     }
     live = __all_sync(0xffffffffu, live);  // warp-uniform: the shuffles below need the whole warp
     if (live) wp.next(ring.n);
-    const uint32_t stage_sa = smem_addr(ring.stages + (size_t)st * ring.stride);
-    float* part_s = spart + (s & 1) * kAttnWarps * 8 * HS;
-    if (live && warp < NPW) {  // S^T partial over this warp's dim groups
-#pragma unroll
-      for (int mt = 0; mt < NMT; ++mt) {
-        float acc[4] = {0.f, 0.f, 0.f, 0.f};
-        const int kr = 16 * mt + r8 + (mi & 1) * 8;  // A rows = keys; matrices (rows, dims) 00 10 01 11
-        const int key = kbase + kr;
-#pragma unroll
-        for (int i = 0; i < GPW; ++i) {
-          const int t = warp + kAttnWarps * i;
-          if (t < NDG) {
-            const int q = 2 * t + (mi >> 1);  // 16-byte chunk of the row
-            uint32_t addr = stage_sa + (q >> 3) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
-            if (key == pos) addr = kn_sa + q * 16;
-            else if (key >= k1) addr = zero_sa;
-            uint32_t af[4];
-            ldsm_x4(addr, af);
-            mma_16816(acc, af, qb[i][0], qb[i][1]);
-          }
-        }
-        float* w_s = part_s + warp * 8 * HS;
-        w_s[(2 * c4) * HS + 16 * mt + g8] = acc[0];
-        w_s[(2 * c4 + 1) * HS + 16 * mt + g8] = acc[1];
-        w_s[(2 * c4) * HS + 16 * mt + g8 + 8] = acc[2];
-        w_s[(2 * c4 + 1) * HS + 16 * mt + g8 + 8] = acc[3];
-      }
-    }
-    named_bar(bar, kAttnThreads);
-    if (live) {
-      // scores of head g8 at keys 16 mt + 2c, 2c+1, 2c+8, 2c+9: warp partials in order
-      float sv[NMT][4];
-#pragma unroll
-      for (int mt = 0; mt < NMT; ++mt)
-#pragma unroll
-        for (int e = 0; e < 4; ++e) sv[mt][e] = 0.f;
-#pragma unroll
-      for (int w = 0; w < NPW; ++w) {
-        const float* hrow = part_s + (w * 8 + g8) * HS;
+    if ((s & 1) == grp) {  // group-uniform
+      const uint32_t stage_sa = smem_addr(ring.stages + (size_t)st * ring.stride);
+      float* part_s = spart + (grp * 2 + ((s >> 1) & 1)) * WPG * 8 * HS;
+      if (live && wig < NPW) {  // S^T partial over this warp's dim groups
 #pragma unroll
         for (int mt = 0; mt < NMT; ++mt) {
-          const float2 lo = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4);
-          const float2 hi = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4 + 8);
-          sv[mt][0] += lo.x;
-          sv[mt][1] += lo.y;
-          sv[mt][2] += hi.x;
-          sv[mt][3] += hi.y;
+          float acc[4] = {0.f, 0.f, 0.f, 0.f};
+          const int kr = 16 * mt + r8 + (mi & 1) * 8;  // A rows = keys; matrices (rows, dims) 00 10 01 11
+          const int key = kbase + kr;
+#pragma unroll
+          for (int i = 0; i < GPW; ++i) {
+            const int t = wig + WPG * i;
+            if (t < NDG) {
+              const int q = 2 * t + (mi >> 1);  // 16-byte chunk of the row
+              uint32_t addr = stage_sa + (q >> 3) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
+              if (key == pos) addr = kn_sa + q * 16;
+              else if (key >= k1) addr = zero_sa;
+              uint32_t af[4];
+              ldsm_x4(addr, af);
+              mma_16816(acc, af, qb[i][0], qb[i][1]);
+            }
+          }
+          float* w_s = part_s + wig * 8 * HS;
+          w_s[(2 * c4) * HS + 16 * mt + g8] = acc[0];
+          w_s[(2 * c4 + 1) * HS + 16 * mt + g8] = acc[1];
+          w_s[(2 * c4) * HS + 16 * mt + g8 + 8] = acc[2];
+          w_s[(2 * c4 + 1) * HS + 16 * mt + g8 + 8] = acc[3];
         }
       }
-      float mx = m_run;
+      if (grp == 0) named_bar(kBarAttnGroup, WPG * 32);  // compile-time ids
+      else named_bar(kBarAttnGroup + 1, WPG * 32);
+      if (live) {
+        // scores of head g8 at keys 16 mt + 2c, 2c+1, 2c+8, 2c+9: warp partials in order
+        float sv[NMT][4];
 #pragma unroll
-      for (int mt = 0; mt < NMT; ++mt)
+        for (int mt = 0; mt < NMT; ++mt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          const int key = kbase + 16 * mt + 2 * c4 + (e & 1) + (e >> 1) * 8;
-          sv[mt][e] = key < k1 ? rbf(sv[mt][e]) : -INFINITY;
-          mx = fmaxf(mx, sv[mt][e]);
+          for (int e = 0; e < 4; ++e) sv[mt][e] = 0.f;
+#pragma unroll
+        for (int w = 0; w < NPW; ++w) {
+          const float* hrow = part_s + (w * 8 + g8) * HS;
+#pragma unroll
+          for (int mt = 0; mt < NMT; ++mt) {
+            const float2 lo = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4);
+            const float2 hi = *reinterpret_cast<const float2*>(hrow + 16 * mt + 2 * c4 + 8);
+            sv[mt][0] += lo.x;
+            sv[mt][1] += lo.y;
+            sv[mt][2] += hi.x;
+            sv[mt][3] += hi.y;
+          }
         }
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
-      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
-      const float corr = mx == -INFINITY ? 1.f : expf(m_run - mx);
-      m_run = mx;
-      uint32_t pb[NMT][2];
-      float psum = 0.f;
+        float mx = m_run;
 #pragma unroll
-      for (int mt = 0; mt < NMT; ++mt) {
-        float p[4];
+        for (int mt = 0; mt < NMT; ++mt)
 #pragma unroll
-        for (int e = 0; e < 4; ++e) {
-          p[e] = sv[mt][e] == -INFINITY ? 0.f : expf(sv[mt][e] - mx);
-          psum += p[e];
+          for (int e = 0; e < 4; ++e) {
+            const int key = kbase + 16 * mt + 2 * c4 + (e & 1) + (e >> 1) * 8;
+            sv[mt][e] = key < k1 ? rbf(sv[mt][e]) : -INFINITY;
+            mx = fmaxf(mx, sv[mt][e]);
+          }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        const float corr = mx == -INFINITY ? 1.f : expf(m_run - mx);
+        m_run = mx;
+        uint32_t pb[NMT][2];
+        float psum = 0.f;
+#pragma unroll
+        for (int mt = 0; mt < NMT; ++mt) {
+          float p[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            p[e] = sv[mt][e] == -INFINITY ? 0.f : expf(sv[mt][e] - mx);
+            psum += p[e];
+          }
+          pb[mt][0] = pack_bf16x2(p[0], p[1]);
+          pb[mt][1] = pack_bf16x2(p[2], p[3]);
         }
-        pb[mt][0] = pack_bf16x2(p[0], p[1]);
-        pb[mt][1] = pack_bf16x2(p[2], p[3]);
-      }
-      l_run = l_run * corr + psum;
-      // rescale O^T: this lane's columns are heads 2c and 2c+1, held by lanes 8c and 8c+4
-      const float ca = __shfl_sync(0xffffffffu, corr, 8 * c4);
-      const float cb = __shfl_sync(0xffffffffu, corr, 8 * c4 + 4);
-#pragma unroll
-      for (int i = 0; i < GPW; ++i) {
-        o[i][0] *= ca;
-        o[i][1] *= cb;
-        o[i][2] *= ca;
-        o[i][3] *= cb;
-      }
-#pragma unroll
-      for (int mt = 0; mt < NMT; ++mt) {
-        const int kr = 16 * mt + r8 + (mi >> 1) * 8;  // A = V^T: matrices (dims, keys) 00 10 01 11
-        const int key = kbase + kr;
+        l_run = l_run * corr + psum;
+        // rescale O^T: this lane's columns are heads 2c and 2c+1, held by lanes 8c and 8c+4
+        const float ca = __shfl_sync(0xffffffffu, corr, 8 * c4);
+        const float cb = __shfl_sync(0xffffffffu, corr, 8 * c4 + 4);
 #pragma unroll
         for (int i = 0; i < GPW; ++i) {
-          const int t = warp + kAttnWarps * i;
-          if (t < NDG) {
-            const int q = 2 * t + (mi & 1);
-            uint32_t addr = stage_sa + (NBOX + (q >> 3)) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
-            if (key == pos) addr = vn_sa + q * 16;
-            else if (key >= k1) addr = zero_sa;
-            uint32_t af[4];
-            ldsm_x4_t(addr, af);
-            mma_16816(o[i], af, pb[mt][0], pb[mt][1]);
+          o[i][0] *= ca;
+          o[i][1] *= cb;
+          o[i][2] *= ca;
+          o[i][3] *= cb;
+        }
+#pragma unroll
+        for (int mt = 0; mt < NMT; ++mt) {
+          const int kr = 16 * mt + r8 + (mi >> 1) * 8;  // A = V^T: matrices (dims, keys) 00 10 01 11
+          const int key = kbase + kr;
+#pragma unroll
+          for (int i = 0; i < GPW; ++i) {
+            const int t = wig + WPG * i;
+            if (t < NDG) {
+              const int q = 2 * t + (mi & 1);
+              uint32_t addr = stage_sa + (NBOX + (q >> 3)) * (KPS * 128) + kr * 128 + (((q & 7) ^ r8) << 4);
+              if (key == pos) addr = vn_sa + q * 16;
+              else if (key >= k1) addr = zero_sa;
+              uint32_t af[4];
+              ldsm_x4_t(addr, af);
+              mma_16816(o[i], af, pb[mt][0], pb[mt][1]);
+            }
           }
         }
       }
     }
+    // the other group's stage is released once it has landed (its wait above), so no
+    // warp can count toward a later fill of the stage
     __syncwarp();
     if (lane == 0 && live) mbar_arrive(&ring.empty[st]);
     rp.next(ring.n);
   }
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 4);
 
-  // ---- 3. partials of this item -- O [G][D] in the O block (16-byte aligned rows for
-  // the merge's vector loads), (m, l) [G][2] in the block after it -- then the last
-  // active CTA of this KV head merges them.  The acq_rel counter update (after the
-  // block barrier) publishes this CTA's partials and, for the last CTA, acquires every
-  // other CTA's.
+  // ---- 3. the two groups' states combined in group 0 (fixed order), then the item's
+  // partials -- O [G][D] in the O block (16-byte aligned rows for the merge's vector
+  // loads), (m, l) [G][2] in the block after it -- and the last active CTA of this KV
+  // head merges them.  The acq_rel counter update (after the block barrier) publishes
+  // this CTA's partials and, for the last CTA, acquires every other CTA's.
   float lt = l_run + __shfl_xor_sync(0xffffffffu, l_run, 1);
   lt = lt + __shfl_xor_sync(0xffffffffu, lt, 2);  // the same bits in the four lanes of a head
-  const size_t n_items = (size_t)a.n_kv * a.nsplit;
-  float* part_o = a.part + ((size_t)hk * a.nsplit + sp) * G * D;
-  float* part_ml = a.part + n_items * G * D + ((size_t)hk * a.nsplit + sp) * G * 2;
-  if (warp == 0 && c4 == 0 && g8 < G) {
-    part_ml[g8 * 2] = m_run;
-    part_ml[g8 * 2 + 1] = lt;
-  }
+  named_bar(bar, kAttnThreads);  // both groups are past their last reads of the partials
+  float4* xo = reinterpret_cast<float4*>(spart);                  // [WPG][GPW][32] group 1's O
+  float2* xml = reinterpret_cast<float2*>(spart + WPG * GPW * 32 * 4);  // [2 groups][8 heads] (m, l)
+  if (wig == 0 && c4 == 0) xml[grp * 8 + g8] = make_float2(m_run, lt);
+  if (grp == 1) {
 #pragma unroll
-  for (int i = 0; i < GPW; ++i) {
-    const int t = warp + kAttnWarps * i;
-    if (t < NDG) {
-      const int dd = 16 * t + g8;
-      if (2 * c4 < G) {
-        part_o[(2 * c4) * D + dd] = o[i][0];
-        part_o[(2 * c4) * D + dd + 8] = o[i][2];
-      }
-      if (2 * c4 + 1 < G) {
-        part_o[(2 * c4 + 1) * D + dd] = o[i][1];
-        part_o[(2 * c4 + 1) * D + dd + 8] = o[i][3];
+    for (int i = 0; i < GPW; ++i) xo[(wig * GPW + i) * 32 + lane] = make_float4(o[i][0], o[i][1], o[i][2], o[i][3]);
+  }
+  named_bar(bar, kAttnThreads);
+  const size_t n_items = (size_t)a.n_kv * a.nsplit;
+  if (grp == 0) {
+    // per head: M = max(m0, m1), factors exp(m - M) (0 for a group without keys; group 0
+    // always holds the item's first stage)
+    auto fac = [](float m, float M) { return m == -INFINITY ? 0.f : expf(m - M); };
+    const float2 a0 = xml[2 * c4], a1 = xml[8 + 2 * c4], b0 = xml[2 * c4 + 1], b1 = xml[8 + 2 * c4 + 1];
+    const float Ma = fmaxf(a0.x, a1.x), Mb = fmaxf(b0.x, b1.x);
+    const float fa0 = fac(a0.x, Ma), fa1 = fac(a1.x, Ma), fb0 = fac(b0.x, Mb), fb1 = fac(b1.x, Mb);
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+      const float4 q = xo[(wig * GPW + i) * 32 + lane];
+      o[i][0] = o[i][0] * fa0 + q.x * fa1;
+      o[i][1] = o[i][1] * fb0 + q.y * fb1;
+      o[i][2] = o[i][2] * fa0 + q.z * fa1;
+      o[i][3] = o[i][3] * fb0 + q.w * fb1;
+    }
+    float* part_o = a.part + ((size_t)hk * a.nsplit + sp) * G * D;
+    float* part_ml = a.part + n_items * G * D + ((size_t)hk * a.nsplit + sp) * G * 2;
+    if (wig == 0 && c4 == 0 && g8 < G) {
+      const float2 h0 = xml[g8], h1 = xml[8 + g8];
+      const float M = fmaxf(h0.x, h1.x);
+      part_ml[g8 * 2] = M;
+      part_ml[g8 * 2 + 1] = h0.y * fac(h0.x, M) + h1.y * fac(h1.x, M);
+    }
+#pragma unroll
+    for (int i = 0; i < GPW; ++i) {
+      const int t = wig + WPG * i;
+      if (t < NDG) {
+        const int dd = 16 * t + g8;
+        if (2 * c4 < G) {
+          part_o[(2 * c4) * D + dd] = o[i][0];
+          part_o[(2 * c4) * D + dd + 8] = o[i][2];
+        }
+        if (2 * c4 + 1 < G) {
+          part_o[(2 * c4 + 1) * D + dd] = o[i][1];
+          part_o[(2 * c4 + 1) * D + dd + 8] = o[i][3];
+        }
       }
     }
   }

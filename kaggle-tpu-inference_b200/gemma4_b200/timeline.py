@@ -86,6 +86,7 @@ def main():
     ap.add_argument("--max-len", type=int, default=32768)
     ap.add_argument("--engine", choices=["step", "ops"], default="step")
     ap.add_argument("--lib", default=os.path.join(HERE, "libg4b200_trace.so"))
+    ap.add_argument("--save", default="", help="also write the raw event buffer (.npy, rank 0)")
     args = ap.parse_args()
     os.environ["G4B200_LIB"] = os.path.abspath(args.lib)
 
@@ -130,6 +131,8 @@ def main():
         dist.destroy_process_group()
         if rank != 0:
             return 0
+    if args.save:  # [launch id][CTA][event] globaltimer ns; launch id = 8 * layer + kind
+        np.save(args.save, buf)
     full = [i for i, t in enumerate(cfg.layer_types) if t == "full_attention"]
     ncta, span, st = phase_stats(buf, args.layers, full)
     print(f"engine {args.engine}, {args.layers} layers, world {world} (rank 0 shown), {ncta} CTAs traced, "
