@@ -37,9 +37,11 @@
 //      at `pos` is never read from the stage: the ldmatrix row address of that key
 //      points at the shared copy of the new key / value, and keys past the slice point
 //      at a zero row (the stage holds stale or zero-filled rows there).
-//   3. (m, l, O) of the item go to the partial buffer; the last CTA of head h (atomic
-//      counter) merges the n_active partials in split order with max-rescaling (4-element
-//      vector loads, 4 to 16 splits in flight per thread) and rounds the context to bf16.
+//   3. (m, l, O) of the item go to the partial buffer; the last CTA of each group of 8
+//      splits (atomic counter) folds the group's partials in split order with
+//      max-rescaling, and the last group of head h folds the group partials in group
+//      order and rounds the context to bf16 (4-element vector loads, 4 to 16 partials in
+//      flight per thread).
 // Every sum has a fixed order: results are bitwise reproducible, and the step kernel
 // and the standalone kernel (same items, same stages) compute identical bits.
 #pragma once
@@ -73,14 +75,31 @@ struct AttnArgs {
   bf16_t* cache_v;         // [max_len, n_kv, d]
   const float* inv_freq;   // [d/2]
   bf16_t* ctx;             // [n_kv*g*d]
-  float* part;             // O [n_kv, nsplit, g, d] then (m, l) [n_kv, nsplit, g, 2]
-  int* counters;           // [n_kv], zero at rest
+  float* part;             // attn_part_floats(n_kv, nsplit, g, d): split and group partials
+  int* counters;           // attn_counter_ints(n_kv, nsplit), zero at rest
   int* ctrl;               // control block (POS, STATUS)
   int pos_fixed;           // >= 0 overrides ctrl[POS]
   int n_kv, g, d, nsplit, window, k_eq_v, max_len;
   float eps;
   int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
+
+// Merge of the split partials: the last CTA of each group of kAttnMergeGroup splits folds
+// the group's partials into a group partial; the last such CTA of a head folds the group
+// partials into the context (one level when the live splits fit one group).
+constexpr int kAttnMergeGroup = 8;
+__host__ __device__ __forceinline__ int attn_groups(int nsplit) {
+  return (nsplit + kAttnMergeGroup - 1) / kAttnMergeGroup;
+}
+// Floats of a layer's partial buffer: split partials O [n_kv][nsplit][g][d], their (m, l)
+// [n_kv][nsplit][g][2], then the same two blocks for the group partials [n_kv][groups].
+__host__ __device__ __forceinline__ size_t attn_part_floats(int n_kv, int nsplit, int g, int d) {
+  return (size_t)n_kv * (size_t)(nsplit + attn_groups(nsplit)) * g * (d + 2);
+}
+// Ints of a layer's counters (zero at rest): one per head, then one per (head, group).
+__host__ __device__ __forceinline__ int attn_counter_ints(int n_kv, int nsplit) {
+  return n_kv * (1 + attn_groups(nsplit));
+}
 
 // Keys per stage (a multiple of 16), bytes of a stage (K boxes then V boxes, d/64 of
 // each, KPS rows of 128 bytes per box) and the head stride of the score partials.
@@ -235,6 +254,87 @@ __device__ __forceinline__ bool attn_produce(const AttnArgs* a, int it0, int ste
     }
   }
   return true;
+}
+
+// Fold n partials in order -- O rows [G][D] at po + s * G * D, (m, l) [G][2] at
+// pml + s * G * 2 -- with max-rescaling: each thread takes 4-element chunks
+// i = tid + 256 k of the [G][D] context and, SB partials at a time (their loads in flight
+// together), keeps a running max-rescaled sum.  `ctx` non-null: writes the normalised
+// context, rounded to bf16, there; else the folded partial to out_o / out_ml.  All
+// kAttnThreads threads.
+template <int D, int G>
+__device__ __forceinline__ void attn_fold(const float* po, const float* pml, int n, bf16_t* ctx, float* out_o,
+                                          float* out_ml) {
+  constexpr int NC = G * D / 4;                                  // chunks per head set
+  constexpr int NE = (NC + kAttnThreads - 1) / kAttnThreads;     // chunks per thread
+  constexpr int SB = NE >= 4 ? 4 : 16 / NE;                      // partials per batch
+  const float4* ho = reinterpret_cast<const float4*>(po);
+  const float2* hml = reinterpret_cast<const float2*>(pml);
+  float M[NE], L[NE];
+  float4 O[NE];
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    M[k] = -INFINITY;
+    L[k] = 0.f;
+    O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
+  }
+#pragma unroll 1
+  for (int s0 = 0; s0 < n; s0 += SB) {
+    float2 mlv[NE][SB];
+    float4 av[NE][SB];
+#pragma unroll
+    for (int k = 0; k < NE; ++k) {
+      const int i = threadIdx.x + kAttnThreads * k;
+      const int h = (4 * i) / D;
+#pragma unroll
+      for (int q = 0; q < SB; ++q) {
+        mlv[k][q] = make_float2(-INFINITY, 0.f);
+        av[k][q] = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (i < NC && s0 + q < n) {
+          mlv[k][q] = __ldcg(hml + (size_t)(s0 + q) * G + h);
+          av[k][q] = __ldcg(ho + (size_t)(s0 + q) * NC + i);
+        }
+      }
+    }
+#pragma unroll
+    for (int k = 0; k < NE; ++k) {
+      float mb = M[k];
+#pragma unroll
+      for (int q = 0; q < SB; ++q) mb = fmaxf(mb, mlv[k][q].x);
+      const float cf = M[k] == -INFINITY ? 0.f : expf(M[k] - mb);
+      L[k] *= cf;
+      O[k].x *= cf;
+      O[k].y *= cf;
+      O[k].z *= cf;
+      O[k].w *= cf;
+#pragma unroll
+      for (int q = 0; q < SB; ++q) {
+        const float f = mlv[k][q].x == -INFINITY ? 0.f : expf(mlv[k][q].x - mb);
+        L[k] = fmaf(mlv[k][q].y, f, L[k]);
+        O[k].x = fmaf(av[k][q].x, f, O[k].x);
+        O[k].y = fmaf(av[k][q].y, f, O[k].y);
+        O[k].z = fmaf(av[k][q].z, f, O[k].z);
+        O[k].w = fmaf(av[k][q].w, f, O[k].w);
+      }
+      M[k] = mb;
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < NE; ++k) {
+    const int i = threadIdx.x + kAttnThreads * k;
+    if (i < NC) {
+      const int h = (4 * i) / D, e = (4 * i) % D;
+      if (ctx) {
+        uint2 w;
+        w.x = pack_bf16x2(O[k].x / L[k], O[k].y / L[k]);
+        w.y = pack_bf16x2(O[k].z / L[k], O[k].w / L[k]);
+        *reinterpret_cast<uint2*>(ctx + (size_t)h * D + e) = w;
+      } else {
+        reinterpret_cast<float4*>(out_o)[i] = O[k];
+        if (e == 0) reinterpret_cast<float2*>(out_ml)[h] = make_float2(M[k], L[k]);
+      }
+    }
+  }
 }
 
 // One work item (KV head hk, split sp) of decode attention, run by the kAttnThreads
@@ -567,85 +667,53 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
     }
   }
   named_bar(bar, kAttnThreads);
+  // level 1: the last CTA of this split's group folds the group's partials
+  const int ngs = attn_groups(a.nsplit);                                     // group slots per head
+  const int ngr = (n_active + kAttnMergeGroup - 1) / kAttnMergeGroup;        // live groups
+  const int gi = sp / kAttnMergeGroup;
+  const int gsize = min(kAttnMergeGroup, n_active - gi * kAttnMergeGroup);
+  int* cnt_top = a.counters + hk;
+  int* cnt_grp = a.counters + a.n_kv + hk * ngs + gi;
   if (threadIdx.x == 0) {
-    const int old = atomic_add_acq_rel_gpu(a.counters + hk, 1);
-    *flag = (old == n_active - 1);
+    const int old = atomic_add_acq_rel_gpu(cnt_grp, 1);
+    *flag = (old == gsize - 1);
   }
   named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 5);
   const bool merge = *flag != 0;
   named_bar(bar, kAttnThreads);  // every thread has read the flag before it is reused
   if (!merge) return;
-  // One pass over the partials: each thread takes 4-element chunks i = tid + 256 k of
-  // the [G][D] context and, SB splits at a time (all their loads in flight together),
-  // folds (m, l, acc) into a running max-rescaled sum in split order.
-  constexpr int NC = G * D / 4;                                  // chunks per head
-  constexpr int NE = (NC + kAttnThreads - 1) / kAttnThreads;     // chunks per thread
-  constexpr int SB = NE >= 4 ? 4 : 16 / NE;                      // splits per batch
-  const float4* ho = reinterpret_cast<const float4*>(a.part + (size_t)hk * a.nsplit * G * D);
-  const float2* hml = reinterpret_cast<const float2*>(a.part + n_items * G * D) + (size_t)hk * a.nsplit * G;
-  float M[NE], L[NE];
-  float4 O[NE];
-#pragma unroll
-  for (int k = 0; k < NE; ++k) {
-    M[k] = -INFINITY;
-    L[k] = 0.f;
-    O[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-#pragma unroll 1
-  for (int s0 = 0; s0 < n_active; s0 += SB) {
-    float2 mlv[NE][SB];
-    float4 av[NE][SB];
-#pragma unroll
-    for (int k = 0; k < NE; ++k) {
-      const int i = threadIdx.x + kAttnThreads * k;
-      const int h = (4 * i) / D;
-#pragma unroll
-      for (int q = 0; q < SB; ++q) {
-        mlv[k][q] = make_float2(-INFINITY, 0.f);
-        av[k][q] = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (i < NC && s0 + q < n_active) {
-          mlv[k][q] = __ldcg(hml + (size_t)(s0 + q) * G + h);
-          av[k][q] = __ldcg(ho + (size_t)(s0 + q) * NC + i);
-        }
-      }
+  const size_t gbase = n_items * G * (D + 2);  // group partials after the split partials
+  float* gpo = a.part + gbase + (size_t)hk * ngs * G * D;
+  float* gpml = a.part + gbase + (size_t)a.n_kv * ngs * G * D + (size_t)hk * ngs * G * 2;
+  const size_t s0 = (size_t)hk * a.nsplit + (size_t)gi * kAttnMergeGroup;
+  bf16_t* ctx_h = a.ctx + (size_t)hk * G * D;
+  if (ngr == 1) {  // one group: its fold is the context
+    attn_fold<D, G>(a.part + s0 * G * D, a.part + n_items * G * D + s0 * G * 2, gsize, ctx_h, nullptr, nullptr);
+    if (threadIdx.x == 0) {
+      atomicExch(cnt_grp, 0);
+      G4_TRACE_EV(a.trace_id, 6);
     }
-#pragma unroll
-    for (int k = 0; k < NE; ++k) {
-      float mb = M[k];
-#pragma unroll
-      for (int q = 0; q < SB; ++q) mb = fmaxf(mb, mlv[k][q].x);
-      const float cf = M[k] == -INFINITY ? 0.f : expf(M[k] - mb);
-      L[k] *= cf;
-      O[k].x *= cf;
-      O[k].y *= cf;
-      O[k].z *= cf;
-      O[k].w *= cf;
-#pragma unroll
-      for (int q = 0; q < SB; ++q) {
-        const float f = mlv[k][q].x == -INFINITY ? 0.f : expf(mlv[k][q].x - mb);
-        L[k] = fmaf(mlv[k][q].y, f, L[k]);
-        O[k].x = fmaf(av[k][q].x, f, O[k].x);
-        O[k].y = fmaf(av[k][q].y, f, O[k].y);
-        O[k].z = fmaf(av[k][q].z, f, O[k].z);
-        O[k].w = fmaf(av[k][q].w, f, O[k].w);
-      }
-      M[k] = mb;
-    }
+    named_bar(bar, kAttnThreads);  // shared scratch free for the caller's next use
+    return;
   }
-#pragma unroll
-  for (int k = 0; k < NE; ++k) {
-    const int i = threadIdx.x + kAttnThreads * k;
-    if (i < NC) {
-      const int h = (4 * i) / D, e = (4 * i) % D;
-      uint2 w;
-      w.x = pack_bf16x2(O[k].x / L[k], O[k].y / L[k]);
-      w.y = pack_bf16x2(O[k].z / L[k], O[k].w / L[k]);
-      *reinterpret_cast<uint2*>(a.ctx + ((size_t)hk * G + h) * D + e) = w;
-    }
-  }
+  attn_fold<D, G>(a.part + s0 * G * D, a.part + n_items * G * D + s0 * G * 2, gsize, nullptr,
+                  gpo + (size_t)gi * G * D, gpml + (size_t)gi * G * 2);
+  // level 2: the last group of this head folds the group partials (acq_rel counter after
+  // the block barrier: publishes this group partial, acquires the others)
+  named_bar(bar, kAttnThreads);
   if (threadIdx.x == 0) {
-    atomicExch(a.counters + hk, 0);
+    atomicExch(cnt_grp, 0);
+    const int old = atomic_add_acq_rel_gpu(cnt_top, 1);
+    *flag = (old == ngr - 1);
+  }
+  named_bar(bar, kAttnThreads);
+  const bool merge2 = *flag != 0;
+  named_bar(bar, kAttnThreads);
+  if (!merge2) return;
+  attn_fold<D, G>(gpo, gpml, ngr, ctx_h, nullptr, nullptr);
+  if (threadIdx.x == 0) {
+    atomicExch(cnt_top, 0);
     G4_TRACE_EV(a.trace_id, 6);
   }
   named_bar(bar, kAttnThreads);  // shared scratch free for the caller's next use

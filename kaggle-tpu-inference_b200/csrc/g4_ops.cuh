@@ -47,14 +47,13 @@ constexpr int kSmemOk = 34;
 constexpr int kSmemWriteLogits = 35;
 
 // Scratch counters (int[kNumCounters] in device memory, zero at rest).
-constexpr int kCntRouter = 0, kCntLm = 1, kCntSigAttn = 2, kCntSigFfn = 3;
+constexpr int kCntRouter = 0, kCntLm = 1;
 constexpr int kNumCounters = 32;
 
 struct Common {
   int* counters;
   char* xbase[kMaxWorld];  // exchange buffer of every rank, mapped in this process
   int rank, world;
-  int nsig;                // CTAs per rank that signal each all-reduce use (its producers)
   int xpayload;            // floats per exchange slot
   int H;
   int layer, nlayers;
@@ -69,63 +68,75 @@ __device__ __forceinline__ float* xslot(const Common& c, int peer, int site, int
   return reinterpret_cast<float*>(c.xbase[peer] + kXFlagBytes) +
          (size_t)((site * 2 + parity) * kMaxWorld + src) * c.xpayload;
 }
+// LL words (attention-out and FFN-out sites): one 64-bit word per value, the fp32 bits in
+// the low half and the tag use + 1 in the high half, written with one 64-bit store (a
+// single-copy atomic access), so a reader that sees the tag sees the value: no fence, no
+// arrival counter, no flag round trip.  A slot's tags only grow (use is monotonic while
+// the communicator serves its model), so a word of an earlier use never matches.
+__device__ __forceinline__ unsigned long long* xll(const Common& c, int peer, int site, int parity, int src) {
+  return reinterpret_cast<unsigned long long*>(xslot(c, peer, site, parity, src));
+}
+__device__ __forceinline__ void ll_put(unsigned long long* p, float v, uint32_t tag) {
+  const unsigned long long w = ((unsigned long long)tag << 32) | (unsigned long long)__float_as_uint(v);
+  asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(w) : "memory");
+}
+// The values of 8 consecutive LL words (64 bytes) once all 8 tags equal `tag`.  Bounded:
+// gives up after the control block's timeout (setting PEER_TIMEOUT) or as soon as another
+// thread has recorded one.  Returns false when it gave up.
+__device__ __forceinline__ bool ll_get8(const unsigned long long* p, uint32_t tag, float* out, int* ctrl) {
+  uint32_t w[16];
+  auto load = [&]() {
+#pragma unroll
+    for (int i = 0; i < 4; ++i)
+      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                   : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
+                   : "l"(p + 2 * i)
+                   : "memory");
+  };
+  auto ready = [&]() {
+    bool r = true;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) r = r && (w[2 * i + 1] == tag);
+    return r;
+  };
+  load();
+  if (!ready()) {
+    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
+    const uint64_t limit = static_cast<uint64_t>(tmo > 0 ? tmo : 1000000) * 1000ull;
+    const uint64_t t0 = globaltimer_ns();
+    int n = 0;
+    do {
+      if ((++n & 63) == 0) {
+        if (ldcg_i(ctrl + G4_CTRL_STATUS) & G4_STATUS_PEER_TIMEOUT) return false;
+        if (globaltimer_ns() - t0 > limit) {
+          atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_PEER_TIMEOUT);
+          return false;
+        }
+      }
+      load();
+    } while (!ready());
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i) out[i] = __uint_as_float(w[2 * i]);
+  return true;
+}
+// AND of a predicate over the consumer threads (one named barrier, id kBarReduce).
+__device__ __forceinline__ bool consumers_and(bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\t"
+      "setp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, %2, %3, p;\n\t"
+      "selp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(kBarReduce), "r"(kConsumerThreads)
+      : "memory");
+  return r != 0;
+}
+
 __device__ __forceinline__ int site_use(const int* ctrl, const Common& c, int site, int layer) {
   const int step = ldcg_i(ctrl + G4_CTRL_STEP);
   return site == kSiteArgmax ? step : step * c.nlayers + layer;
-}
-
-// Arrival counter of (site, parity) in `peer`'s exchange buffer: a 64-bit word that every
-// signalling CTA of every rank increments once per use of that site and parity, so use u
-// of the site is complete when it reaches ((u >> 1) + 1) * nsig * world (monotonic: it is
-// never reset while the communicator serves its model).
-__device__ __forceinline__ unsigned long long* xcount(const Common& c, int peer, int site, int parity) {
-  return reinterpret_cast<unsigned long long*>(xflag(c, peer, site, parity, 0));
-}
-__device__ __forceinline__ unsigned long long xcount_target(const Common& c, int use) {
-  return (unsigned long long)((use >> 1) + 1) * (unsigned long long)c.nsig * (unsigned long long)c.world;
-}
-
-// All consumer threads: make this CTA's peer stores visible (system-scope fence per
-// thread), then thread 0 counts this CTA in on every rank with one release reduction
-// each -- no grid-wide counter and no last-CTA hop on the critical path.
-__device__ __forceinline__ void xchg_signal(const Common& c, int site, int use, int /*counter_id*/) {
-  __threadfence_system();
-  named_bar(kBarReduce, kConsumerThreads);
-  if (threadIdx.x == 0) {
-    for (int p = 0; p < c.world; ++p) {
-      unsigned long long* cnt = xcount(c, p, site, use & 1);
-      asm volatile("red.release.sys.global.add.u64 [%0], %1;" ::"l"(cnt), "l"(1ull) : "memory");
-    }
-  }
-}
-
-// Wait (bounded) until the local arrival counter of (site, use) reaches its target.
-__device__ __forceinline__ bool xchg_arrived(int* ctrl, const Common& c, int site, int use) {
-  const unsigned long long* cnt = xcount(c, c.rank, site, use & 1);
-  const unsigned long long target = xcount_target(c, use);
-  auto load = [cnt]() {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(cnt) : "memory");
-    return v;
-  };
-  if (load() >= target) return true;
-  const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
-  const uint64_t limit = static_cast<uint64_t>(tmo > 0 ? tmo : 1000000) * 1000ull;
-  const uint64_t t0 = globaltimer_ns();
-  while (load() < target) {
-    if (globaltimer_ns() - t0 > limit) {
-      atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_PEER_TIMEOUT);
-      return false;
-    }
-  }
-  return true;
-}
-
-// Thread 0 waits for every rank's contributions to (site, use); broadcast to consumers.
-__device__ __forceinline__ bool xchg_wait(int* ctrl, const Common& c, int site, int use, Smem& sm) {
-  if (threadIdx.x == 0) sm.ints[kSmemOk] = xchg_arrived(ctrl, c, site, use) ? 1 : 0;
-  named_bar(kBarReduce, kConsumerThreads);
-  return sm.ints[kSmemOk] != 0;
 }
 
 // ------------------------------------------------------------------ staged vectors
@@ -251,22 +262,25 @@ __device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const T
 #pragma unroll
       for (int e = 0; e < 8; ++e) a[j][e] = rbf(a[j][e]);
   } else {
+    // every rank's MLP and MoE partials, summed in rank order (LL words, polled per chunk)
     const int use = site_use(ctrl, c, kSiteFfn, t.layer);
-    ok = xchg_wait(ctrl, c, kSiteFfn, use, sm);
+    const uint32_t tag = (uint32_t)use + 1u;
+    bool got = true;
 #pragma unroll
     for (int j = 0; j < kChunks; ++j) {
 #pragma unroll
       for (int e = 0; e < 8; ++e) a[j][e] = b[j][e] = 0.f;
       if (chunk_live(j, H)) {
         for (int src = 0; src < c.world; ++src) {
-          const float* sl = xslot(c, c.rank, kSiteFfn, use & 1, src);
-          const float4* pa = reinterpret_cast<const float4*>(sl) + 2 * chunk_of(j);
-          const float4* pb = reinterpret_cast<const float4*>(sl + H) + 2 * chunk_of(j);
-          const float4 a0 = __ldcg(pa), a1 = __ldcg(pa + 1), b0 = __ldcg(pb), b1 = __ldcg(pb + 1);
-          a[j][0] += a0.x; a[j][1] += a0.y; a[j][2] += a0.z; a[j][3] += a0.w;
-          a[j][4] += a1.x; a[j][5] += a1.y; a[j][6] += a1.z; a[j][7] += a1.w;
-          b[j][0] += b0.x; b[j][1] += b0.y; b[j][2] += b0.z; b[j][3] += b0.w;
-          b[j][4] += b1.x; b[j][5] += b1.y; b[j][6] += b1.z; b[j][7] += b1.w;
+          const unsigned long long* sl = xll(c, c.rank, kSiteFfn, use & 1, src);
+          float va[8], vb[8];
+          got = ll_get8(sl + 8 * chunk_of(j), tag, va, ctrl) && got;
+          got = ll_get8(sl + H + 8 * chunk_of(j), tag, vb, ctrl) && got;
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            a[j][e] += va[e];
+            b[j][e] += vb[e];
+          }
         }
 #pragma unroll
         for (int e = 0; e < 8; ++e) {
@@ -275,6 +289,7 @@ __device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const T
         }
       }
     }
+    ok = consumers_and(got);
   }
 #pragma unroll
   for (int j = 0; j < kChunks; ++j)
@@ -411,12 +426,10 @@ struct OProjOp : OpBase {
       out[u] = v;
     } else {
       const int use = site_use(ctrl, c, kSiteAttn, c.layer);
-      for (int p = 0; p < c.world; ++p) xslot(c, p, kSiteAttn, use & 1, c.rank)[u] = v;
+      for (int p = 0; p < c.world; ++p) ll_put(xll(c, p, kSiteAttn, use & 1, c.rank) + u, v, (uint32_t)use + 1u);
     }
   }
-  __device__ __forceinline__ void finish(Smem&, bool) const {
-    if (c.world > 1) xchg_signal(c, kSiteAttn, site_use(ctrl, c, kSiteAttn, c.layer), kCntSigAttn);
-  }
+  __device__ __forceinline__ void finish(Smem&, bool) const {}
 };
 
 // ================================================================== K4: router + MLP gate|up
@@ -466,20 +479,23 @@ struct RouterMlpOp : OpBase {
       if (c.world == 1) {
         load_f32(sf(sm, o_o), H, t);
       } else {
+        // every rank's o_proj partial, summed in rank order (LL words, polled per chunk)
         const int use = site_use(ctrl, c, kSiteAttn, c.layer);
-        ok = xchg_wait(ctrl, c, kSiteAttn, use, sm) && ok;
+        const uint32_t tag = (uint32_t)use + 1u;
+        bool got = true;
 #pragma unroll
         for (int j = 0; j < kChunks; ++j) {
 #pragma unroll
           for (int e = 0; e < 8; ++e) t[j][e] = 0.f;
           if (chunk_live(j, H))
             for (int src = 0; src < c.world; ++src) {
-              const float4* p = reinterpret_cast<const float4*>(xslot(c, c.rank, kSiteAttn, use & 1, src)) + 2 * chunk_of(j);
-              const float4 a0 = __ldcg(p), a1 = __ldcg(p + 1);
-              t[j][0] += a0.x; t[j][1] += a0.y; t[j][2] += a0.z; t[j][3] += a0.w;
-              t[j][4] += a1.x; t[j][5] += a1.y; t[j][6] += a1.z; t[j][7] += a1.w;
+              float v[8];
+              got = ll_get8(xll(c, c.rank, kSiteAttn, use & 1, src) + 8 * chunk_of(j), tag, v, ctrl) && got;
+#pragma unroll
+              for (int e = 0; e < 8; ++e) t[j][e] += v[e];
             }
         }
+        ok = consumers_and(got) && ok;
       }
       float s = 0.f;
 #pragma unroll
@@ -718,16 +734,15 @@ struct MoeDownOp : OpBase {
       for (int k = 0; k < topk; ++k) sacc += res[k * n + t];
       const float mv = ldcg_f(mlp_out + u);
       const int use = site_use(ctrl, c, kSiteFfn, c.layer);
+      const uint32_t tag = (uint32_t)use + 1u;
       for (int p = 0; p < c.world; ++p) {
-        float* sl = xslot(c, p, kSiteFfn, use & 1, c.rank);
-        sl[u] = mv;
-        sl[c.H + u] = sacc;
+        unsigned long long* sl = xll(c, p, kSiteFfn, use & 1, c.rank);
+        ll_put(sl + u, mv, tag);
+        ll_put(sl + c.H + u, sacc, tag);
       }
     }
   }
-  __device__ __forceinline__ void finish(Smem&, bool) const {
-    if (c.world > 1) xchg_signal(c, kSiteFfn, site_use(ctrl, c, kSiteFfn, c.layer), kCntSigFfn);
-  }
+  __device__ __forceinline__ void finish(Smem&, bool) const {}
 };
 
 // ================================================================== LM head + argmax

@@ -53,8 +53,10 @@ extern "C" const char* g4_strerror(int code) {
 
 extern "C" const char* g4_last_error(void) { return g_last_error.c_str(); }
 
+// Flags, then [site][parity][source rank] slots of 4 * hidden floats: the FFN-out site
+// carries 2 * hidden LL words (8 bytes each).
 static size_t comm_bytes(int hidden) {
-  return (size_t)kXFlagBytes + (size_t)kSites * 2 * kMaxWorld * (2 * (size_t)hidden) * 4;
+  return (size_t)kXFlagBytes + (size_t)kSites * 2 * kMaxWorld * (4 * (size_t)hidden) * 4;
 }
 
 extern "C" int g4_comm_create(int device, int rank, int world, int hidden, g4_comm** out) {
@@ -465,8 +467,7 @@ static Common make_common(const g4_model* m, int layer) {
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = m->comm ? m->comm->peer[p] : nullptr;
   c.rank = m->rank;
   c.world = m->world;
-  c.nsig = m->nsm;  // every matrix-product launch (step kernel or per-op kernel) has nsm CTAs
-  c.xpayload = 2 * m->H;
+  c.xpayload = 4 * m->H;  // floats per slot (2 * H LL words)
   c.H = m->H;
   c.layer = layer;
   c.nlayers = (int)m->L.size();
@@ -717,12 +718,12 @@ extern "C" int g4_model_finalize(g4_model* m) {
   }
   // ---- scratch (one allocation, carved)
   const int H = m->H;
-  size_t max_rows = 0, max_ctx = 0, max_part = 0, max_nkv = 0;
+  size_t max_rows = 0, max_ctx = 0, max_part = 0, max_nkv = 0;  // max_nkv: attention counter ints
   for (const LayerDev& l : m->L) {
     max_rows = std::max(max_rows, (size_t)(l.rows_q + l.rows_k + l.rows_v));
     max_ctx = std::max(max_ctx, (size_t)l.rows_q);
-    max_part = std::max(max_part, (size_t)l.n_kv * l.nsplit * l.g * (l.d + 2));
-    max_nkv = std::max(max_nkv, (size_t)l.n_kv);
+    max_part = std::max(max_part, attn_part_floats(l.n_kv, l.nsplit, l.g, l.d));
+    max_nkv = std::max(max_nkv, (size_t)attn_counter_ints(l.n_kv, l.nsplit));
   }
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -1301,7 +1302,7 @@ std::map<int, BlockScratch> g_block_scratch;
 // head has a fixed layout so the zero-at-rest counters never move between calls of
 // different shapes: [attention counters | MoE counters | attention control | RoPE
 // table | variable-size area].
-constexpr size_t kBlockAttnCounters = 0;     // int[kBlockMaxKv]
+constexpr size_t kBlockAttnCounters = 0;     // int[kBlockMaxKv] (attn_counter_ints)
 constexpr int kBlockMaxKv = 64;
 constexpr size_t kBlockMoeCounters = 256;    // int[kNumCounters]
 constexpr size_t kBlockCtrl = 512;           // int[G4_CTRL_WORDS] (attention block only)
@@ -1355,8 +1356,9 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   const int max_live = window > 0 ? std::min(window, max_len) : max_len;
   const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
   if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
-  if (n_kv_heads > kBlockMaxKv) return fail(G4_ERR_SHAPE, "g4_attention_decode: > %d KV heads", kBlockMaxKv);
-  const size_t part = (size_t)n_kv_heads * nsplit * g * (head_dim + 2) * 4;
+  if (n_kv_heads > kBlockMaxKv || attn_counter_ints(n_kv_heads, nsplit) > kBlockMaxKv)
+    return fail(G4_ERR_SHAPE, "g4_attention_decode: %d KV heads x %d splits exceed the counters", n_kv_heads, nsplit);
+  const size_t part = attn_part_floats(n_kv_heads, nsplit, g, head_dim) * 4;
   char* s = block_scratch(kBlockPartOffset + part);
   if (!s) return fail(G4_ERR_NOMEM, "g4_attention_decode: scratch allocation failed");
   AttnArgs a{};
@@ -1397,15 +1399,19 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
 // kernel for world > 1 that plays the role of the next layer's prologue.
 __global__ void moe_block_reduce_kernel(Common c, int* ctrl, bf16_t* out) {
   pdl_wait();
-  __shared__ int ok;
   const int use = site_use(ctrl, c, kSiteFfn, c.layer);
-  if (threadIdx.x == 0) ok = xchg_arrived(ctrl, c, kSiteFfn, use) ? 1 : 0;  // every rank's down CTAs
-  __syncthreads();
-  if (!ok) return;
-  for (int h = threadIdx.x; h < c.H; h += blockDim.x) {
-    float s = 0.f;
-    for (int src = 0; src < c.world; ++src) s += ldcg_f(xslot(c, c.rank, kSiteFfn, use & 1, src) + c.H + h);
-    out[h] = f2bf(s);
+  const uint32_t tag = (uint32_t)use + 1u;
+  // every rank's MoE partial (LL words, 8 per poll), summed in rank order
+  for (int q = threadIdx.x; q < c.H / 8; q += blockDim.x) {
+    float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool got = true;
+    for (int src = 0; src < c.world && got; ++src) {
+      float v[8];
+      got = ll_get8(xll(c, c.rank, kSiteFfn, use & 1, src) + c.H + 8 * q, tag, v, ctrl);
+      for (int e = 0; e < 8; ++e) s[e] += v[e];
+    }
+    if (got)
+      for (int e = 0; e < 8; ++e) out[8 * q + e] = f2bf(s[e]);
   }
   __syncthreads();
   if (threadIdx.x == 0) atomicAdd(ctrl + G4_CTRL_STEP, 1);  // single block: no reader left
@@ -1453,8 +1459,7 @@ extern "C" int g4_moe_block(const g4_config* cfg, int rank, int world, g4_comm* 
   for (int p = 0; p < kMaxWorld; ++p) c.xbase[p] = world > 1 ? comm->peer[p] : nullptr;
   c.rank = rank;
   c.world = world;
-  c.nsig = nsm;  // the down-projection kernel's CTAs signal the all-reduce
-  c.xpayload = 2 * H;
+  c.xpayload = 4 * H;  // floats per slot (2 * H LL words)
   c.H = H;
   c.layer = 0;
   c.nlayers = 1;
@@ -1628,7 +1633,10 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   const int max_live = window > 0 ? std::min(window, max_len) : max_len;
   const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
   if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
-  const size_t part = (size_t)n_kv_heads * nsplit * g * (head_dim + 2) * 4;
+  const size_t part = attn_part_floats(n_kv_heads, nsplit, g, head_dim) * 4;
+  if (attn_counter_ints(n_kv_heads, nsplit) > kBlockMaxKv)
+    return fail(G4_ERR_SHAPE, "g4_attention_decode_noalloc: %d KV heads x %d splits exceed the %d counters",
+                n_kv_heads, nsplit, kBlockMaxKv);
   if (part > kNoAllocScratchBytes - kNoAllocPartOffset)
     return fail(G4_ERR_SHAPE,
                 "g4_attention_decode_noalloc: needs %zu bytes of split-KV partials, the fixed "
