@@ -1302,12 +1302,18 @@ std::map<int, BlockScratch> g_block_scratch;
 // head has a fixed layout so the zero-at-rest counters never move between calls of
 // different shapes: [attention counters | MoE counters | attention control | RoPE
 // table | variable-size area].
-constexpr size_t kBlockAttnCounters = 0;     // int[kBlockMaxKv] (attn_counter_ints)
+constexpr size_t kBlockAttnCounters = 0;     // int[kBlockAttnCounterInts] (attn_counter_ints)
 constexpr int kBlockMaxKv = 64;
-constexpr size_t kBlockMoeCounters = 256;    // int[kNumCounters]
-constexpr size_t kBlockCtrl = 512;           // int[G4_CTRL_WORDS] (attention block only)
-constexpr size_t kBlockInvFreq = 1024;       // float[kAttnMaxD / 2]
-constexpr size_t kBlockPartOffset = 2048;    // attention partials / MoE staging
+constexpr int kBlockAttnCounterInts = 256;
+constexpr size_t kBlockMoeCounters = 1024;   // int[kNumCounters]
+constexpr size_t kBlockCtrl = 1280;          // int[G4_CTRL_WORDS] (attention block only)
+constexpr size_t kBlockInvFreq = 2048;       // float[kAttnMaxD / 2]
+constexpr size_t kBlockPartOffset = 4096;    // attention partials / MoE staging
+static_assert(kBlockMoeCounters >= kBlockAttnCounters + kBlockAttnCounterInts * 4 &&
+                  kBlockCtrl >= kBlockMoeCounters + kNumCounters * 4 &&
+                  kBlockInvFreq >= kBlockCtrl + G4_CTRL_WORDS * 4 &&
+                  kBlockPartOffset >= kBlockInvFreq + kAttnMaxD / 2 * 4,
+              "block scratch head layout");
 
 char* block_scratch(size_t bytes) {
   int dev = 0;
@@ -1356,7 +1362,7 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   const int max_live = window > 0 ? std::min(window, max_len) : max_len;
   const int nsplit = pick_nsplit(n_kv_heads, max_live, nsm);
   if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
-  if (n_kv_heads > kBlockMaxKv || attn_counter_ints(n_kv_heads, nsplit) > kBlockMaxKv)
+  if (n_kv_heads > kBlockMaxKv || attn_counter_ints(n_kv_heads, nsplit) > kBlockAttnCounterInts)
     return fail(G4_ERR_SHAPE, "g4_attention_decode: %d KV heads x %d splits exceed the counters", n_kv_heads, nsplit);
   const size_t part = attn_part_floats(n_kv_heads, nsplit, g, head_dim) * 4;
   char* s = block_scratch(kBlockPartOffset + part);
@@ -1635,8 +1641,10 @@ extern "C" int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_no
   if ((max_live + nsplit - 1) / nsplit > kAttnMaxChunk) return fail(G4_ERR_SHAPE, "context too long");
   const size_t part = attn_part_floats(n_kv_heads, nsplit, g, head_dim) * 4;
   if (attn_counter_ints(n_kv_heads, nsplit) > kBlockMaxKv)
-    return fail(G4_ERR_SHAPE, "g4_attention_decode_noalloc: %d KV heads x %d splits exceed the %d counters",
-                n_kv_heads, nsplit, kBlockMaxKv);
+    return fail(G4_ERR_SHAPE,
+                "g4_attention_decode_noalloc: %d KV heads x %d splits need %d counters, the fixed "
+                "scratch holds %d (use g4_attention_decode)",
+                n_kv_heads, nsplit, attn_counter_ints(n_kv_heads, nsplit), kBlockMaxKv);
   if (part > kNoAllocScratchBytes - kNoAllocPartOffset)
     return fail(G4_ERR_SHAPE,
                 "g4_attention_decode_noalloc: needs %zu bytes of split-KV partials, the fixed "
