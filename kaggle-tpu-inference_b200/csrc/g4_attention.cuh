@@ -84,10 +84,12 @@ struct AttnArgs {
   int trace_id;            // launch id for the optional timeline tracer (-DG4_TRACE)
 };
 
-// Merge of the split partials: the last CTA of each group of kAttnMergeGroup splits folds
-// the group's partials into a group partial; the last such CTA of a head folds the group
-// partials into the context (one level when the live splits fit one group).
+// Merge of the split partials: up to kAttnMergeOne live splits, the last CTA of a head folds
+// them all (one counter round trip); beyond, the last CTA of each group of kAttnMergeGroup
+// splits folds the group's partials into a group partial, and the last such CTA of a head
+// folds the group partials into the context.
 constexpr int kAttnMergeGroup = 8;
+constexpr int kAttnMergeOne = 16;
 __host__ __device__ __forceinline__ int attn_groups(int nsplit) {
   return (nsplit + kAttnMergeGroup - 1) / kAttnMergeGroup;
 }
@@ -156,7 +158,7 @@ __host__ __device__ __forceinline__ bool attn_span(int pos, int window, int nspl
   const int start = window > 0 ? (pos - window + 1 > 0 ? pos - window + 1 : 0) : 0;
   const int nlive = pos - start + 1;
   int chunk = (nlive + nsplit - 1) / nsplit;
-  if (chunk < kAttnMinKeys) chunk = kAttnMinKeys;
+  chunk = (chunk + kAttnMinKeys - 1) / kAttnMinKeys * kAttnMinKeys;  // whole 32-key stages
   n_active = (nlive + chunk - 1) / chunk;
   if (sp >= n_active) return false;
   k0 = start + sp * chunk;
@@ -668,12 +670,13 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   }
   named_bar(bar, kAttnThreads);
   // level 1: the last CTA of this split's group folds the group's partials
+  const bool one = n_active <= kAttnMergeOne;                                // one level
   const int ngs = attn_groups(a.nsplit);                                     // group slots per head
-  const int ngr = (n_active + kAttnMergeGroup - 1) / kAttnMergeGroup;        // live groups
-  const int gi = sp / kAttnMergeGroup;
-  const int gsize = min(kAttnMergeGroup, n_active - gi * kAttnMergeGroup);
+  const int ngr = one ? 1 : (n_active + kAttnMergeGroup - 1) / kAttnMergeGroup;  // live groups
+  const int gi = one ? 0 : sp / kAttnMergeGroup;
+  const int gsize = one ? n_active : min(kAttnMergeGroup, n_active - gi * kAttnMergeGroup);
   int* cnt_top = a.counters + hk;
-  int* cnt_grp = a.counters + a.n_kv + hk * ngs + gi;
+  int* cnt_grp = one ? cnt_top : a.counters + a.n_kv + hk * ngs + gi;
   if (threadIdx.x == 0) {
     const int old = atomic_add_acq_rel_gpu(cnt_grp, 1);
     *flag = (old == gsize - 1);
@@ -688,7 +691,7 @@ __device__ __forceinline__ void attn_item(const AttnArgs& a, int hk, int sp, uns
   float* gpml = a.part + gbase + (size_t)a.n_kv * ngs * G * D + (size_t)hk * ngs * G * 2;
   const size_t s0 = (size_t)hk * a.nsplit + (size_t)gi * kAttnMergeGroup;
   bf16_t* ctx_h = a.ctx + (size_t)hk * G * D;
-  if (ngr == 1) {  // one group: its fold is the context
+  if (ngr == 1) {  // one level: the fold is the context
     attn_fold<D, G>(a.part + s0 * G * D, a.part + n_items * G * D + s0 * G * 2, gsize, ctx_h, nullptr, nullptr);
     if (threadIdx.x == 0) {
       atomicExch(cnt_grp, 0);

@@ -280,13 +280,17 @@ static int router_row_weight(int E, int I_local, int H, int nsm) {
   return w < 1 ? 1 : w;
 }
 
+// Splits per KV head: one item per SM over all heads, each a whole number of 32-key
+// stages (the device rounds its slice the same way), at most kAttnMaxChunk keys each.
 static int pick_nsplit(int n_kv, int max_live, int nsm) {
   int need = (max_live + kAttnMaxChunk - 1) / kAttnMaxChunk;
   int want = nsm / n_kv;
   int ns = want > need ? want : need;
   if (ns < 1) ns = 1;
   if (ns > kAttnMaxSplit) ns = kAttnMaxSplit;
-  return ns;
+  int chunk = (max_live + ns - 1) / ns;
+  chunk = (chunk + kAttnMinKeys - 1) / kAttnMinKeys * kAttnMinKeys;
+  return (max_live + chunk - 1) / chunk;
 }
 
 static bool valid_cfg(const g4_config* c) {
