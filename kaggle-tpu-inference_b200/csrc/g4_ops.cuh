@@ -42,6 +42,7 @@ constexpr int kXFlagBytes = kSites * 2 * kMaxWorld * 128;
 // Smem::ints slots
 constexpr int kSmemRouterEnd = 32;  // end of this CTA's router units (0: none)
 constexpr int kSmemRouterMine = 36; // number of this CTA's router units
+constexpr int kSmemTopk = 37;       // step kernel: this CTA selects the top-k after its arrival
 constexpr int kSmemLast = 33;
 constexpr int kSmemOk = 34;
 constexpr int kSmemWriteLogits = 35;
@@ -83,41 +84,36 @@ __device__ __forceinline__ void ll_put(unsigned long long* p, float v, uint32_t 
 // The values of 8 consecutive LL words (64 bytes) once all 8 tags equal `tag`.  Bounded:
 // gives up after the control block's timeout (setting PEER_TIMEOUT) or as soon as another
 // thread has recorded one.  Returns false when it gave up.
-__device__ __forceinline__ bool ll_get8(const unsigned long long* p, uint32_t tag, float* out, int* ctrl) {
-  uint32_t w[16];
-  auto load = [&]() {
+__device__ __forceinline__ bool ll_try8(const unsigned long long* p, uint32_t tag, float* out) {
+  bool r = true;
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
-      asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
-                   : "=r"(w[4 * i]), "=r"(w[4 * i + 1]), "=r"(w[4 * i + 2]), "=r"(w[4 * i + 3])
-                   : "l"(p + 2 * i)
-                   : "memory");
-  };
-  auto ready = [&]() {
-    bool r = true;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) r = r && (w[2 * i + 1] == tag);
-    return r;
-  };
-  load();
-  if (!ready()) {
-    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
-    const uint64_t limit = static_cast<uint64_t>(tmo > 0 ? tmo : 1000000) * 1000ull;
-    const uint64_t t0 = globaltimer_ns();
-    int n = 0;
-    do {
-      if ((++n & 63) == 0) {
-        if (ldcg_i(ctrl + G4_CTRL_STATUS) & G4_STATUS_PEER_TIMEOUT) return false;
-        if (globaltimer_ns() - t0 > limit) {
-          atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_PEER_TIMEOUT);
-          return false;
-        }
-      }
-      load();
-    } while (!ready());
+  for (int i = 0; i < 4; ++i) {  // two words per 16-byte load; only the values stay live
+    uint32_t v0, t0, v1, t1;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];"
+                 : "=r"(v0), "=r"(t0), "=r"(v1), "=r"(t1)
+                 : "l"(p + 2 * i)
+                 : "memory");
+    out[2 * i] = __uint_as_float(v0);
+    out[2 * i + 1] = __uint_as_float(v1);
+    r = r && t0 == tag && t1 == tag;
   }
-#pragma unroll
-  for (int i = 0; i < 8; ++i) out[i] = __uint_as_float(w[2 * i]);
+  return r;
+}
+__device__ __forceinline__ bool ll_get8(const unsigned long long* p, uint32_t tag, float* out, int* ctrl) {
+  if (ll_try8(p, tag, out)) return true;
+  const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
+  const uint64_t limit = static_cast<uint64_t>(tmo > 0 ? tmo : 1000000) * 1000ull;
+  const uint64_t t0 = globaltimer_ns();
+  int n = 0;
+  while (!ll_try8(p, tag, out)) {
+    if ((++n & 63) == 0) {
+      if (ldcg_i(ctrl + G4_CTRL_STATUS) & G4_STATUS_PEER_TIMEOUT) return false;
+      if (globaltimer_ns() - t0 > limit) {
+        atomicOr(ctrl + G4_CTRL_STATUS, G4_STATUS_PEER_TIMEOUT);
+        return false;
+      }
+    }
+  }
   return true;
 }
 // AND of a predicate over the consumer threads (one named barrier, id kBarReduce).
@@ -566,16 +562,24 @@ struct RouterMlpOp : OpBase {
     if (s == 0) {
       if (ok && t < n) router_logits[u0 + t] = rbf(res[t]);
       // right after this CTA's last router tile (identical test on every thread):
-      // count its rows in; the CTA completing all E logits selects the top-k now,
-      // early in the operator, so the expert weights can stream behind it
-      if (u0 + n == sm.ints[kSmemRouterEnd]) router_done(sm.ints[kSmemRouterMine], sm);
+      // count its rows in; the CTA completing all E logits selects the top-k -- here in
+      // the per-op kernel, after its grid-barrier arrival in the step kernel (whose
+      // expert tiles wait for the router flag, not for the barrier)
+      if (u0 + n == sm.ints[kSmemRouterEnd] && router_count(sm.ints[kSmemRouterMine], sm)) {
+        if (ready) {
+          if (threadIdx.x == 0) sm.ints[kSmemTopk] = 1;  // read after the phase's closing barrier
+        } else {
+          router_topk(sm, reinterpret_cast<float*>(sm.stg));
+        }
+      }
     } else if (ok && t < n) {
       const float g = rbf(res[t]), u = rbf(res[n + t]);
       mlp_act[u0 + t] = f2bf(rbf(gelu_tanh(g)) * u);
     }
   }
   __device__ __forceinline__ void finish(Smem&, bool) const {}
-  // The CTA that completes the router's E logits selects the top-k (model.py:227-232).
+  // The CTA that completes the router's E logits selects the top-k (model.py:227-232):
+  // router_count, then router_topk.
   // Ordering: the acq_rel counter update after the block barrier publishes this CTA's
   // logits and, on the last CTA, acquires the others'; the flag store after the block
   // barrier releases top_idx / top_w.
@@ -584,10 +588,9 @@ struct RouterMlpOp : OpBase {
   // as scratch: softmax max and sum by scans in expert order (identical on every
   // thread), then each probability's rank among all E (ties -> lower expert index,
   // like a stable top-k), the top-k weights summed in rank order.
-  __device__ __forceinline__ void router_done(int mine, Smem& sm) const {
-    const int t = threadIdx.x;
-    // the expert scale is a weight: its load goes out before the counter round trip
-    const float scale = t < E ? bf2f(pes[t]) : 0.f;
+  // Count this CTA's router rows in; true (on every consumer thread) on the CTA that
+  // completes all E logits.
+  __device__ __forceinline__ bool router_count(int mine, Smem& sm) const {
     named_bar(kBarReduce, kConsumerThreads);
     if (threadIdx.x == 0) {
       int last = 0;
@@ -601,9 +604,15 @@ struct RouterMlpOp : OpBase {
     named_bar(kBarReduce, kConsumerThreads);
     const bool last = sm.ints[kSmemLast] != 0;
     named_bar(kBarReduce, kConsumerThreads);  // the flag slot is reused by later code
-    if (!last) return;
-    float* pv = reinterpret_cast<float*>(sm.stg);  // [E]
-    float* top_p = pv + kConsumerThreads;           // [topk] selected probabilities, rank order
+    return last;
+  }
+  // Softmax and top-k over the E logits (all consumer threads of the counting CTA), with
+  // `scratch` (>= kConsumerThreads + kMaxTopK floats of shared memory), then the flag.
+  __device__ __forceinline__ void router_topk(Smem& sm, float* scratch) const {
+    const int t = threadIdx.x;
+    const float scale = t < E ? bf2f(pes[t]) : 0.f;
+    float* pv = scratch;                   // [E]
+    float* top_p = pv + kConsumerThreads;  // [topk] selected probabilities, rank order
     float l = -INFINITY;
     if (t < E) {
       l = ldcg_f(router_logits + t);
@@ -680,7 +689,6 @@ struct MoeUpOp : OpBase {
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     copy_vec(sbf(sm, o_h2), c.H, sm.x0);
     copy_vec(sbf(sm, o_act), I, sm.x1);
-    if ((int)threadIdx.x < topk) sm.flts[threadIdx.x] = ldcg_f(top_w + threadIdx.x);
     return true;
   }
   __device__ __forceinline__ void epilogue(int s, int u0, int n, const Res& res, Smem& sm, bool ok, int t) const {
@@ -690,8 +698,12 @@ struct MoeUpOp : OpBase {
     } else {
       const int u = u0 + t, k = u / F;
       const float g = rbf(res[t]), up = rbf(res[n + t]);
+      // the routing weight: read here, behind this expert's tiles, which the producer
+      // issued only after it saw the router flag (the step kernel selects the top-k after
+      // the phase barrier; the mbarrier wait orders this load after that flag)
+      const float w = ldcg_f(top_w + k);
       // gelu(g) * u * w, left to right in bf16 (model.py:271)
-      moe_act[u] = f2bf(rbf(rbf(gelu_tanh(g)) * up) * rbf(sm.flts[k]));
+      moe_act[u] = f2bf(rbf(rbf(gelu_tanh(g)) * up) * rbf(w));
     }
   }
   __device__ __forceinline__ void finish(Smem&, bool) const {}

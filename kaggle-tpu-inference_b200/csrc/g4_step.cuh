@@ -14,10 +14,10 @@
 // of every operator in program order, so while the consumers wait at a barrier, run
 // a prologue or compute attention, the ring already holds the next operator's
 // weights.  Weight addresses never depend on activations except the expert tiles,
-// for which the producer waits on the layer's router flag; the router's top-k is
-// published as soon as the router rows are done (they come first in their
-// operator), so the expert weights stream in while the dense MLP rows are still
-// being consumed.
+// for which the producer waits on the layer's router flag.  The CTA that completes the
+// router logits arrives at the grid barrier first and then selects the top-k and
+// publishes the flag, so the next operator starts on its dense MLP-down rows while the
+// selection runs and the expert weights stream in behind it.
 //
 // Warp specialisation with register reallocation: 12 warps, launched at 168
 // registers per thread.  The 4 warps of the producer warpgroup drop to 56
@@ -493,6 +493,7 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     sm.ints[kSmemIssued] = 0;
     sm.ints[kSmemProdExit] = 0;
     sm.ints[kSmemRangesGiven] = 1;
+    sm.ints[kSmemTopk] = 0;
     mbar_init(&sm.pbar[0], 1);
     mbar_init(&sm.pbar[1], 1);
     mbar_init_fence();
@@ -541,6 +542,14 @@ __global__ void __launch_bounds__(kStepThreads, 1) step_kernel(const __grid_cons
     }
     if (p < 6 * L)
       phase_end(P, sm, ps, op_base(P, (p + 1) / 6, (p + 1) == 6 * L ? kKindLm : (p + 1) % 6));
+    if (k == kKindRouterMlp && sm.ints[kSmemTopk]) {
+      // this CTA completed the router logits: it selects the top-k after its arrival, so
+      // the next phase's barrier does not wait for the selection (its expert tiles wait for
+      // the router flag); the per-tile result buffers are free until that phase's tiles
+      named_bar(kBarConsumers, kConsumerThreads);  // every thread has read the slot
+      if (threadIdx.x == 0) sm.ints[kSmemTopk] = 0;
+      if (ps.live) reinterpret_cast<const RouterMlpOp*>(sm.opc)->router_topk(sm, sm.res);
+    }
   }
   named_bar(kBarConsumers, kConsumerThreads);
   if (threadIdx.x == 0) {

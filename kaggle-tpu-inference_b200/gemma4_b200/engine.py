@@ -221,6 +221,14 @@ class Engine:
 
         self._all(first)
         self._all(lambda m: m.capture())
+        if self.use_prefill and len(self.models) == 1:
+            # one prefill of the largest chunk this engine uses: the tensor-core prefill
+            # allocates its workspace and configures its kernels here, not in a request's TTFT
+            m = self.model
+            n = min(self.max_len - 1, self.prefill_chunk or 4096)
+            m.reset([0] * n)
+            m.prefill(n, self.prefill_chunk)
+            m.check_status()
         self._sync()
         out["prefill_compile_s"] = time.perf_counter() - t0
         t0 = time.perf_counter()
