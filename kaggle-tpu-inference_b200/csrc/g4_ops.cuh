@@ -566,7 +566,7 @@ struct RouterMlpOp : OpBase {
       // the per-op kernel, after its grid-barrier arrival in the step kernel (whose
       // expert tiles wait for the router flag, not for the barrier)
       if (u0 + n == sm.ints[kSmemRouterEnd] && router_count(sm.ints[kSmemRouterMine], sm)) {
-        if (ready) {
+        if (sm.ints[kSmemRangesGiven]) {  // the step kernel (the per-op kernel sets 0)
           if (threadIdx.x == 0) sm.ints[kSmemTopk] = 1;  // read after the phase's closing barrier
         } else {
           router_topk(sm, reinterpret_cast<float*>(sm.stg));
