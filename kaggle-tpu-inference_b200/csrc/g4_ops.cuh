@@ -242,7 +242,8 @@ struct Tail {
   int o_mlp, o_moe, o_res;  // staged activations (world 1)
 };
 
-__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, Smem& sm, Vec& x) {
+__device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const Tail& t, Smem& sm, Vec& x,
+                                             int trace_id) {
   const int H = c.H;
   bool ok = true;
   // the layer scalar is a global load: issued first, it lands under the reductions
@@ -286,6 +287,7 @@ __device__ __forceinline__ bool layer_output(int* ctrl, const Common& c, const T
       }
     }
     ok = consumers_and(got);
+    if (threadIdx.x == 0) G4_TRACE_EV(trace_id, 7);  // peer partials in (timeline: exchange wait)
   }
 #pragma unroll
   for (int j = 0; j < kChunks; ++j)
@@ -384,7 +386,7 @@ struct QkvOp : OpBase {
 #pragma unroll
         for (int e = 0; e < 8; ++e) x[j][e] = rbf(x[j][e] * embed_scale);
     } else {
-      ok = layer_output(ctrl, c, tail, sm, x);
+      ok = layer_output(ctrl, c, tail, sm, x, trace_id);
     }
     if (blockIdx.x == 0) store_bf16(xres, H, x);
     norm_into(c, x, sbf(sm, o_win), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
@@ -492,6 +494,7 @@ struct RouterMlpOp : OpBase {
             }
         }
         ok = consumers_and(got) && ok;
+        if (threadIdx.x == 0) G4_TRACE_EV(trace_id, 7);  // peer partials in (timeline: exchange wait)
       }
       float s = 0.f;
 #pragma unroll
@@ -780,7 +783,7 @@ struct LmHeadOp : OpBase {
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     Vec x;
-    const bool ok = layer_output(ctrl, c, tail, sm, x);
+    const bool ok = layer_output(ctrl, c, tail, sm, x, trace_id);
     norm_into(c, x, sbf(sm, o_wn), reinterpret_cast<bf16_t*>(sm.x0), sm, 3);
     float* bv = reinterpret_cast<float*>(sm.x1);
     int* bi = reinterpret_cast<int*>(sm.x1) + kConsumerThreads;

@@ -22,8 +22,9 @@ microseconds:
 
 Event slots per phase (trace id = 8 * layer + kind; the LM head is 8 * layers):
 0 start, 1 staged, 2 constants + barrier, 3 prologue done, 4 first tile, 5 last tile,
-6 finish.  Attention phases use 3 (q/k prologue), 4 (key stages), 5 (partials
-published), 6 (merge, merging CTA only).  ``attn-s`` / ``attn-f`` rows: sliding / full
+6 finish, 7 the peer partials of an all-reduce received (world > 1: the prologues of
+router+MLP and of qkv / the LM head; ``xchg-wait`` = 7 - 2).  Attention phases use 3 (q/k
+prologue), 4 (key stages), 5 (partials published), 6 (merge, merging CTA only).  ``attn-s`` / ``attn-f`` rows: sliding / full
 layers.
 """
 import argparse
@@ -53,7 +54,7 @@ def phase_stats(buf, layers, full=()):
         return float(np.median(x)) / 1e3 if len(x) else 0.0
 
     for i, (k, e, layer) in enumerate(rows[:-1]):
-        s0, e1, e2, e3, e4, e5, e6 = (e[:, j] for j in range(7))
+        s0, e1, e2, e3, e4, e5, e6, e7 = (e[:, j] for j in range(8))
         ok = (s0 > 0) & (e6 >= s0)
         if not ok.any():
             continue
@@ -71,6 +72,7 @@ def phase_stats(buf, layers, full=()):
             (e6[ok].max() - np.median(e6[ok])) / 1e3,
             (nstart - e6[ok].max()) / 1e3,
             (nstart - s0[ok].min()) / 1e3,
+            med(e7[m12 & (e7 >= e2)] - e2[m12 & (e7 >= e2)]),  # exchange wait (world > 1)
         ))
     t0 = b[b > 0].min()
     span = (b[8 * layers][:ncta, 6].max() - t0) / 1e3
@@ -137,11 +139,19 @@ def main():
     ncta, span, st = phase_stats(buf, args.layers, full)
     print(f"engine {args.engine}, {args.layers} layers, world {world} (rank 0 shown), {ncta} CTAs traced, "
           f"position {int(m.ctrl[0].item()) - 1}, step span {span:.1f} us")
-    cols = ["start-skew", "stage", "const+bar", "compute", "first-tile", "tiles", "straggle", "gap", "span"]
+    cols = ["start-skew", "stage", "const+bar", "compute", "first-tile", "tiles", "straggle", "gap", "span",
+            "xchg-wait"]
     print("kind   " + " ".join(f"{c:>10s}" for c in cols))
     for k in ROWS:
         if k in st:
             print(f"{k:6s} " + " ".join(f"{x:10.1f}" for x in st[k]))
+    if world > 1:  # the two all-reduces' waits, inside the consumers' prologues
+        nl = {k: (len(full) if k == "attn-f" else args.layers - len(full) if k == "attn-s" else args.layers)
+              for k in st}
+        wait = sum(st[k][9] * nl[k] for k in st)
+        total = sum(st[k][8] * nl[k] for k in st)
+        print(f"exchange wait (median CTA) {wait:.1f} us per step = {100 * wait / total:.1f}% of the "
+              f"summed phase spans ({total:.1f} us)")
     return 0
 
 
