@@ -614,10 +614,22 @@ static int upload_step_program(g4_model* m) {
                          : r == 2      ? static_cast<const OpBase*>(&m->k4[l])
                          : r == 3      ? static_cast<const OpBase*>(&m->k5[l])
                                        : static_cast<const OpBase*>(&m->k6[l]);
+      // MLP-down + experts-up: every CTA takes its share of EACH segment, so it streams
+      // dense MLP-down rows (which need no routing) while the router's top-k is selected
+      // after the phase barrier, then its expert rows; elsewhere the CTA's slice of the
+      // byte-weighted concatenation.  Results do not depend on the split (each row is one
+      // warp's dot product), so the per-op kernels' own split gives the same bits.
+      const bool per_segment = (i != nops - 1 && r == 3);
       for (int cta = 0; cta < m->nsm; ++cta)
         for (int sg = 0; sg < op->nseg; ++sg) {
           int ub, ue;
-          cta_unit_range(op->seg, op->nseg, sg, cta, m->nsm, ub, ue);
+          if (per_segment) {
+            const long long u = op->seg[sg].units;
+            ub = (int)(u * cta / m->nsm);
+            ue = (int)(u * (cta + 1) / m->nsm);
+          } else {
+            cta_unit_range(op->seg, op->nseg, sg, cta, m->nsm, ub, ue);
+          }
           tab[((size_t)cta * nops + i) * kRangeSlots + sg] = make_int2(ub, ue);
         }
     }
