@@ -1171,7 +1171,7 @@ extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, vo
   PrefillWs& w = *m->prefill;
   const SplitBuf sb{w.split, w.split_elems};
   const g4_config& c = m->cfg;
-  const int H = m->H, E = m->E, F = m->F_local, I = m->I_local, K = m->topk;
+  const int H = m->H, E = m->E, I = m->I_local, K = m->topk;
   const float eps = c.rms_norm_eps;
   int* status = bw.ctrl + G4_CTRL_STATUS;  // sequence 0's status word collects GEMM timeouts
   cudaStream_t st = static_cast<cudaStream_t>(stream);

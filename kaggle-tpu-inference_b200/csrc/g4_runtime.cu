@@ -1220,7 +1220,7 @@ extern "C" int g4_graph_capture(g4_model* m, void* stream) {
   if (!m) return fail(G4_ERR_ARG, "g4_graph_capture: null model");
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_graph_capture before g4_model_finalize");
   G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  (void)stream;  // the graph is launched on the caller's stream by g4_graph_launch
   if (m->gexec) {
     cudaGraphExecDestroy(m->gexec);
     m->gexec = nullptr;
@@ -1235,7 +1235,6 @@ extern "C" int g4_graph_capture(g4_model* m, void* stream) {
   // Capture on a private stream: the caller's stream may be the legacy default stream,
   // which cannot be captured; capturing executes nothing, and the graph is launched
   // on the caller's stream by g4_graph_launch.
-  (void)st;
   cudaStream_t cap = nullptr;
   G4_CUDA(cudaStreamCreateWithFlags(&cap, cudaStreamNonBlocking), G4_ERR_CUDA);
   cudaError_t e0 = cudaStreamBeginCapture(cap, cudaStreamCaptureModeThreadLocal);

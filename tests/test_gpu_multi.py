@@ -42,10 +42,11 @@ def _run(world, case, engine="step", timeout=900):
     assert r.stdout.count(f"{case} ok") == world, r.stdout[-3000:]
 
 
-@pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("engine", ["step", "ops"])
-def test_tiny_tensor_parallel(world, engine):
-    _run(world, "tiny", engine)
+def test_tiny_tensor_parallel(engine):
+    """Config 1 has 2 KV heads (and 4 query heads), so it shards over at most 2 ranks,
+    as the reference's mesh requires (model.py:84-156); the real shapes run at 2, 4, 8."""
+    _run(2, "tiny", engine)
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
@@ -67,14 +68,16 @@ def test_single_process_engine_owns_all_devices(world):
     is reproducible."""
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs, {torch.cuda.device_count()} visible")
-    from gemma4_b200.config import tiny_parity_config
+    from gemma4_b200.config import FULL, SLIDING, make_config, tiny_parity_config
     from gemma4_b200.engine import Engine
     from gemma4_b200.model import Mesh
     from gemma4_b200.weights import random_params
     from oracle.reference_model import Oracle
     from test_gpu_decode import decided_mask
 
-    cfg = tiny_parity_config()
+    # config 1 shards over at most 2 ranks (2 KV heads); beyond, the real per-layer shapes
+    cfg = tiny_parity_config() if world <= 2 else make_config(
+        num_hidden_layers=2, layer_types=(SLIDING, FULL), num_experts=16, vocab_size=16384)
     params = random_params(cfg, 0)
     eng = Engine(None, max_len=96, cfg=cfg, params=params, devices=list(range(world)))
     assert eng.n_devices == world and len(eng.models) == world
