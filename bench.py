@@ -51,7 +51,7 @@ FALLBACK_HBM_GBS = 6650.0
 # this bench, one metric pass) on the build named beside it; re-captured when the kernel
 # changes.  None where no capture exists (reported as null).
 NCU_STEP_TRAFFIC_BYTES_PER_LAUNCH: dict = {
-    (1, 30): (7.41e9 + 18.04e6, "step kernel of commit 4c55f17, config 4, launch at position 36"),
+    (1, 30): (7.41e9 + 20.12e6, "step kernel of commit 680ec0c, config 4, launch at position 36"),
 }
 
 
