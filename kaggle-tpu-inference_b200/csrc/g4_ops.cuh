@@ -410,7 +410,17 @@ struct OProjOp : OpBase {
   __device__ __forceinline__ void load_dependent(Smem&) const {}
   template <class Fn>
   __device__ __forceinline__ void copies(int, int u0, int n, const int*, Fn&& f) const {
-    f(w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), 0u);
+    const int ns = seg[0].nsub;
+    if (ns == 1) {
+      f(w + (size_t)u0 * Kc, (uint32_t)(n * Kc * 2), 0u);
+      return;
+    }
+    // rows split into ns sub-rows (each with its slice of the context): the stage holds
+    // sub-row j of every row of the tile after the tile's sub-rows j - 1
+    const int ks = Kc / ns;
+    for (int r = 0; r < n; ++r)
+      for (int j = 0; j < ns; ++j)
+        f(w + (size_t)(u0 + r) * Kc + (size_t)j * ks, (uint32_t)(ks * 2), (uint32_t)((j * n + r) * ks * 2));
   }
   __device__ __forceinline__ bool prologue(Smem& sm) const {
     copy_vec(sbf(sm, o_ctx), Kc, sm.x0);
@@ -419,7 +429,8 @@ struct OProjOp : OpBase {
   __device__ __forceinline__ void epilogue(int, int u0, int n, const Res& res, Smem&, bool ok, int t) const {
     if (!ok || t >= n) return;
     const int u = u0 + t;
-    const float v = res[t];
+    float v = res[t];
+    for (int j = 1; j < seg[0].nsub; ++j) v += res[j * n + t];  // sub-rows in order
     if (c.world == 1) {
       out[u] = v;
     } else {

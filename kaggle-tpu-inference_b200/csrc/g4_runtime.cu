@@ -282,6 +282,14 @@ static int router_row_weight(int E, int I_local, int H, int nsm) {
 
 // Splits per KV head: one item per SM over all heads, each a whole number of 32-key
 // stages (the device rounds its slice the same way), at most kAttnMaxChunk keys each.
+// Sub-rows of an o_proj row of `k` elements: the fewest (1, 2 or 4) of at most 4,096
+// elements each, a multiple of 8 each; 0 when none fits.
+static int o_proj_subrows(int k) {
+  for (int ns = 1; ns <= 4; ns *= 2)
+    if (k % ns == 0 && k / ns <= 4096 && (k / ns) % 8 == 0) return ns;
+  return 0;
+}
+
 static int pick_nsplit(int n_kv, int max_live, int nsm) {
   int need = (max_live + kAttnMaxChunk - 1) / kAttnMaxChunk;
   int want = nsm / n_kv;
@@ -366,9 +374,9 @@ extern "C" int g4_model_create(const g4_config* cfg, const unsigned char* layer_
     }
   }
   for (const LayerDev& l : m->L)
-    if (l.rows_q > 4096 || c.hidden_size > 4096 || m->I_local > 4096) {
+    if (!o_proj_subrows(l.rows_q) || c.hidden_size > 4096 || m->I_local > 4096) {
       delete m;
-      return fail(G4_ERR_SHAPE, "a matrix row is longer than 4096 elements on this rank "
+      return fail(G4_ERR_SHAPE, "a matrix row is longer than the decode engine takes on this rank "
                                 "(o_proj of %d heads x %d at world %d)", l.n_kv * l.g, l.d, world);
     }
   *out = m;
@@ -850,7 +858,11 @@ extern "C" int g4_model_finalize(g4_model* m) {
     o.ctrl = m->ctrl;
     o.nseg = 1;
     o.trace_id = i * 8 + 2;
-    o.seg[0] = SegDesc{H, 1, l.rows_q, 0};
+    // a row longer than the engine's 4,096-element dot (d 512 x 16 query heads at world
+    // 1) runs as nsub sub-rows, each dotted with its slice of the context, summed in order
+    const int onsub = o_proj_subrows(l.rows_q);
+    o.seg[0] = SegDesc{H, onsub, l.rows_q / onsub, 0};
+    o.xsub[0] = onsub > 1 ? l.rows_q / onsub : 0;
     o.xbytes[0] = l.rows_q * 2;
     {
       Stager sg(&o);

@@ -161,6 +161,27 @@ def test_real_layer_shapes_two_layers():
     assert bool(agree[decided].all())
 
 
+@pytest.mark.parametrize("engine", ["step", "ops"])
+def test_global_head_dim_512_on_one_gpu(engine):
+    """The real checkpoint's global layers (README.md:214-218 of the reference: head_dim 512,
+    16 query heads over 2 KV heads, partial RoPE 0.25) on one GPU: their 8192-element o_proj
+    rows run as two sub-rows of the decode engine's 4096-element dot; 2 layers [sliding,
+    full], 16 experts, 16K vocab, decoded past the prompt against the oracle, and the two
+    engines bit-identical."""
+    cfg = make_config(num_hidden_layers=2, layer_types=(SLIDING, FULL), num_experts=16,
+                      vocab_size=16384, global_head_dim=512)
+    assert cfg.num_attention_heads * 512 == 8192
+    params = random_params(cfg, 7)
+    prompt = [int(t) for t in torch.randint(0, cfg.vocab_size, (7,), generator=torch.Generator().manual_seed(7))]
+    worst, agree, decided, ids, _ = _compare(cfg, params, prompt, 5, 64, engine=engine, name=f"global_d512_{engine}")
+    assert worst >= 0.9999, worst
+    assert bool(agree[decided].all())
+    if engine == "ops":
+        a = _run_gpu(cfg, params, prompt, 5, 64, engine="step")
+        b = _run_gpu(cfg, params, prompt, 5, 64, engine="ops")
+        assert torch.equal(a[0], b[0]) and a[1] == b[1]
+
+
 def test_engine_generate_protocol():
     cfg = tiny_parity_config()
     params = random_params(cfg, 0)
