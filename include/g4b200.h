@@ -270,6 +270,16 @@ int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_norm, const v
                                 float theta, float partial_rotary, float eps, void* ctx,
                                 void* stream);
 
+/* g4_selftest_peer_timeout: failure-detection check of the bounded cross-GPU wait, on one
+   GPU (the current device), touching no peer memory.  Runs the all-reduce consumers' poll
+   of tagged exchange words (the wait of every decode step at world > 1) on a zeroed local
+   exchange slot that no producer writes, with a timeout of `timeout_us`; the wait gives
+   up, sets G4_STATUS_PEER_TIMEOUT in a control block and the kernel returns.  Synchronises
+   and writes that control block's status word to *status_out.  Returns G4_OK when the
+   wait ran out as designed (the status bit set), G4_ERR_TIMEOUT otherwise.  No reference
+   counterpart (the reference has no device-side waits). */
+int g4_selftest_peer_timeout(int timeout_us, int* status_out);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1427,6 +1427,37 @@ extern "C" int g4_attention_decode(const void* qkv_raw, const void* q_norm, cons
   return launch_attention(a, st);
 }
 
+// The all-reduce consumers' bounded poll (ll_get8) on a local slot nobody writes: every
+// lane waits for 8 words tagged 1 (the slot holds zeros), gives up after the control
+// block's timeout and records PEER_TIMEOUT.
+__global__ void selftest_peer_wait_kernel(const unsigned long long* slot, int* ctrl) {
+  float v[8];
+  (void)ll_get8(slot + 8 * threadIdx.x, 1u, v, ctrl);
+}
+
+extern "C" int g4_selftest_peer_timeout(int timeout_us, int* status_out) {
+  if (timeout_us <= 0 || timeout_us > 10000000 || !status_out)
+    return fail(G4_ERR_ARG, "g4_selftest_peer_timeout: timeout %d us (1..10^7), status pointer", timeout_us);
+  char* s = block_scratch(kBlockPartOffset + 32 * 8 * 8);
+  if (!s) return fail(G4_ERR_NOMEM, "g4_selftest_peer_timeout: scratch allocation failed");
+  int* ctrl = reinterpret_cast<int*>(s + kBlockCtrl);
+  int words[G4_CTRL_WORDS] = {};
+  words[G4_CTRL_TIMEOUT_US] = timeout_us;
+  G4_CUDA(cudaMemcpy(ctrl, words, sizeof(words), cudaMemcpyHostToDevice), G4_ERR_CUDA);
+  G4_CUDA(cudaMemset(s + kBlockPartOffset, 0, 32 * 8 * 8), G4_ERR_CUDA);
+  selftest_peer_wait_kernel<<<1, 32>>>(reinterpret_cast<const unsigned long long*>(s + kBlockPartOffset), ctrl);
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  G4_CUDA(cudaDeviceSynchronize(), G4_ERR_CUDA);
+  G4_CUDA(cudaMemcpy(words, ctrl, sizeof(words), cudaMemcpyDeviceToHost), G4_ERR_CUDA);
+  *status_out = words[G4_CTRL_STATUS];
+  int zero[G4_CTRL_WORDS] = {};
+  G4_CUDA(cudaMemcpy(ctrl, zero, sizeof(zero), cudaMemcpyHostToDevice), G4_ERR_CUDA);
+  if (!(words[G4_CTRL_STATUS] & G4_STATUS_PEER_TIMEOUT))
+    return fail(G4_ERR_TIMEOUT, "g4_selftest_peer_timeout: the wait did not report a timeout (status 0x%x)",
+                words[G4_CTRL_STATUS]);
+  return G4_OK;
+}
+
 // A standalone MoE block reuses the layer kernels K4 (router only, block mode), K5
 // (experts gate|up only) and K6 (down + fused all-reduce push), plus a small reduce
 // kernel for world > 1 that plays the role of the next layer's prologue.

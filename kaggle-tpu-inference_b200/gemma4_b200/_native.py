@@ -42,6 +42,7 @@ EXPORTS = (
     "g4_moe_block", "g4_attention_decode", "g4_trace_read", "g4_attention_decode_noalloc",
     "g4_model_set_engine", "g4_prefill", "g4_gemm_bf16", "g4_comm_open_local",
     "g4_batch_reserve", "g4_batch_prefill", "g4_batch_step", "g4_batch_status",
+    "g4_selftest_peer_timeout",
 )
 
 ENGINE_STEP_KERNEL = 0  # one persistent kernel per decode step (default)
@@ -119,6 +120,7 @@ def lib() -> ctypes.CDLL:
     L.g4_batch_prefill.argtypes = [c_void_p, c_int, c_int, c_void_p, c_void_p]
     L.g4_batch_step.argtypes = [c_void_p, c_void_p, c_void_p, c_void_p]
     L.g4_batch_status.argtypes = [c_void_p, c_void_p, POINTER(c_int)]
+    L.g4_selftest_peer_timeout.argtypes = [c_int, POINTER(c_int)]
     L.g4_gemm_bf16.argtypes = [c_void_p, c_longlong, c_void_p, c_longlong, c_void_p, c_longlong, c_int, c_int,
                                c_int, c_int, c_void_p, c_void_p]
     L.g4_model_host_tokens.argtypes = [c_void_p, POINTER(POINTER(c_int))]
