@@ -260,8 +260,8 @@ int g4_attention_decode(const void* qkv_raw, const void* q_norm, const void* k_n
  * G4_ERR_SHAPE.  It calls no cudaMalloc/cudaFree: each call enqueues one small set-up
  * kernel (zeroes the merge counters and status word, writes the RoPE table, passed by
  * value) and the attention kernel on `stream`.  The first call on a device looks the
- * array's address up (cudaGetSymbolAddress) with that device current; make that first
- * call before any stream capture.  Every call shares the one array: calls that overlap
+ * array's address up (cudaGetSymbolAddress) with that device current.  Every call shares
+ * the one array: calls that overlap
  * on the GPU (different streams, no ordering) race.  Kernel-side status bits are not
  * reported (the return code covers argument checks and launches only). */
 int g4_attention_decode_noalloc(const void* qkv_raw, const void* q_norm, const void* k_norm,
