@@ -739,10 +739,10 @@ __device__ __forceinline__ void attn_drain(const AttnRing& ring, RingPos wp, int
   }
 }
 
-// Standalone launch: grid = n_kv x nsplit, one item per CTA; warps 0-7 consume, warp 8
-// lane 0 produces the stages.
+// One item per CTA (standalone launches): item `it` of the items (0, step) of args `a`;
+// warps 0-7 consume, warp 8 lane 0 produces the stages into a ring of its own.
 template <int D, int G>
-__global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+__device__ __forceinline__ void attn_cta(const AttnArgs& a, int it, int step) {
   extern __shared__ unsigned char attn_smem_raw[];
   constexpr int SB = 4 * D * (D > 256 ? 16 : 32);
   static_assert(SB % 1024 == 0, "stages stay 1024-byte aligned (128-byte swizzle)");
@@ -770,7 +770,7 @@ __global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_kernel(cons
   if (threadIdx.x >= kAttnThreads) {
     if (threadIdx.x == kAttnThreads) {
       RingPos rp;
-      attn_produce(&a, blockIdx.x, gridDim.x, ring, rp, dead, status, ints + 1);
+      attn_produce(&a, it, step, ring, rp, dead, status, ints + 1);
       __threadfence_block();
       reinterpret_cast<volatile int*>(ints)[2] = 1;
     }
@@ -778,8 +778,23 @@ __global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_kernel(cons
   }
   if (threadIdx.x == 0) G4_TRACE_EV(a.trace_id, 2);
   RingPos rp, wp;
-  attn_item<D, G>(a, blockIdx.x / a.nsplit, blockIdx.x % a.nsplit, scratch, 1, ring, rp, wp, dead, status);
+  attn_item<D, G>(a, it / a.nsplit, it % a.nsplit, scratch, 1, ring, rp, wp, dead, status);
   if (threadIdx.x == 0 && *dead) attn_drain(ring, wp, ints);
+}
+
+// Standalone launch: grid = n_kv x nsplit, one item per CTA.
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_kernel(const __grid_constant__ AttnArgs a) {
+  attn_cta<D, G>(a, blockIdx.x, gridDim.x);
+}
+
+// Batched launch (several sequences' caches, one layer): grid = sequences x items, CTA b
+// takes item b % items of sequence b / items, whose args (tensor maps included) live in
+// the device array `args`.
+template <int D, int G>
+__global__ void __launch_bounds__(kAttnKernelThreads, 1) attn_decode_batch_kernel(const AttnArgs* __restrict__ args,
+                                                                                   int items) {
+  attn_cta<D, G>(args[blockIdx.x / items], blockIdx.x % items, items);
 }
 
 }  // namespace g4

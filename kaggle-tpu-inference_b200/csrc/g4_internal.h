@@ -124,6 +124,11 @@ void g4_prefill_release(g4_model* m);
 void g4_batch_release(g4_model* m);
 // Launch one decode-attention item grid (g4_runtime.cu).
 int g4_launch_attention(const AttnArgs& a, cudaStream_t st);
+// One decode-attention launch over several sequences: grid = seqs x items, the sequences'
+// args in the device array `dargs` (g4_runtime.cu).
+int g4_launch_attention_batch(const AttnArgs* dargs, int d, int g, int seqs, int items, cudaStream_t st);
+// Splits per KV head of a decode-attention layer for `nsm` SMs (g4_runtime.cu).
+int g4_pick_nsplit(int n_kv, int max_live, int nsm);
 // Encode a.tmk / a.tmv from a.cache_k / a.cache_v, n_kv, d and max_len (g4_runtime.cu).
 int g4_attention_maps(AttnArgs& a);
 // A K-major bf16 matrix [rows, inner] (row stride `ld` elements) as a TMA tensor map with

@@ -1044,6 +1044,17 @@ struct BatchWs {
   bf16_t* xf = nullptr;         // [B, H]
   bf16_t* lmlog = nullptr;      // [B, V_local]
   std::vector<CUtensorMap> mk, mv;  // [layer * B + b]: attention tensor maps of each cache
+  // attention of all sequences in one launch per layer: the sequences' args in device
+  // memory (rebuilt when the prefill workspace they point into moves), splits sized for
+  // the whole batch, and each sequence's own partials and merge counters
+  AttnArgs* dargs = nullptr;       // [layer][B]
+  const bf16_t* dargs_qkv = nullptr;  // the workspace's qkv and ctx rows dargs point at
+  const bf16_t* dargs_ctx = nullptr;
+  std::vector<int> nsplit;         // per layer
+  float* part = nullptr;           // [B][part_floats]
+  int* cnt = nullptr;              // [B][cnt_ints], zero at rest
+  size_t part_floats = 0;
+  int cnt_ints = 0;
 };
 
 void g4_batch_release(g4_model* m) {
@@ -1077,6 +1088,21 @@ extern "C" int g4_batch_reserve(g4_model* m, int batch, int ctx_len) {
   const size_t o_ctrl = take((size_t)batch * G4_CTRL_WORDS * 4), o_tok = take((size_t)batch * 4),
                o_lg = take((size_t)batch * m->V_local * 4), o_xf = take((size_t)batch * m->H * 2),
                o_lm = take((size_t)batch * m->V_local * 2);
+  // batched attention: one item per SM over all sequences' heads
+  std::vector<int> nsplit;
+  size_t part_floats = 0;
+  int cnt_ints = 0;
+  for (const LayerDev& l : m->L) {
+    const int max_live = l.full ? ctx_len : std::min(ctx_len, m->cfg.sliding_window);
+    const int ns = g4_pick_nsplit(l.n_kv, max_live, std::max(1, m->nsm / batch));
+    nsplit.push_back(ns);
+    part_floats = std::max(part_floats, attn_part_floats(l.n_kv, ns, l.g, l.d));
+    cnt_ints = std::max(cnt_ints, attn_counter_ints(l.n_kv, ns));
+  }
+  part_floats = (part_floats + 63) / 64 * 64;
+  cnt_ints = (cnt_ints + 63) / 64 * 64;
+  const size_t o_part = take((size_t)batch * part_floats * 4), o_cnt = take((size_t)batch * cnt_ints * 4),
+               o_args = take(m->L.size() * (size_t)batch * sizeof(AttnArgs));
   BatchWs* w = new BatchWs();
   if (cudaMalloc(&w->mem, off) != cudaSuccess) {
     delete w;
@@ -1094,6 +1120,12 @@ extern "C" int g4_batch_reserve(g4_model* m, int batch, int ctx_len) {
   w->logits = reinterpret_cast<float*>(w->mem + o_lg);
   w->xf = reinterpret_cast<bf16_t*>(w->mem + o_xf);
   w->lmlog = reinterpret_cast<bf16_t*>(w->mem + o_lm);
+  w->nsplit = nsplit;
+  w->part_floats = part_floats;
+  w->cnt_ints = cnt_ints;
+  w->part = reinterpret_cast<float*>(w->mem + o_part);
+  w->cnt = reinterpret_cast<int*>(w->mem + o_cnt);
+  w->dargs = reinterpret_cast<AttnArgs*>(w->mem + o_args);
   std::vector<int> ctrl((size_t)batch * G4_CTRL_WORDS, 0);
   for (int b = 0; b < batch; ++b) ctrl[(size_t)b * G4_CTRL_WORDS + G4_CTRL_TIMEOUT_US] = 2000000;
   G4_CUDA(cudaMemcpy(w->ctrl, ctrl.data(), ctrl.size() * 4, cudaMemcpyHostToDevice), G4_ERR_CUDA);
@@ -1179,7 +1211,38 @@ extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, vo
                               bw.ctrl);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   const float hinv = g4_host_bf16_round(std::pow((float)H, -0.5f));
-  std::vector<bf16_t*> ck, cv;
+  if (bw.dargs_qkv != w.qkv || bw.dargs_ctx != w.ctx) {  // the args point into the workspace
+    cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+    G4_CUDA(cudaStreamIsCapturing(st, &cs), G4_ERR_CUDA);
+    if (cs != cudaStreamCaptureStatusNone)
+      return fail(G4_ERR_STATE, "g4_batch_step: capture a step only after an eager step since the last prefill");
+    std::vector<bf16_t*> ck, cv;
+    std::vector<AttnArgs> host(m->L.size() * (size_t)B);
+    for (int b = 0; b < B; ++b) {
+      batch_caches(m, b, ck, cv);
+      for (size_t li = 0; li < m->L.size(); ++li) {
+        const LayerDev& l = m->L[li];
+        AttnArgs a = m->k2[li];
+        a.qkv = w.qkv + (size_t)b * (l.rows_q + l.rows_k + l.rows_v);
+        a.cache_k = ck[li];
+        a.cache_v = cv[li];
+        a.ctx = w.ctx + (size_t)b * l.n_kv * l.g * l.d;
+        a.ctrl = bw.ctrl + (size_t)b * G4_CTRL_WORDS;
+        a.part = bw.part + (size_t)b * bw.part_floats;
+        a.counters = bw.cnt + (size_t)b * bw.cnt_ints;
+        a.nsplit = bw.nsplit[li];
+        a.pos_fixed = -1;
+        a.max_len = bw.ctx;
+        a.trace_id = -1;
+        a.tmk = bw.mk[li * B + b];
+        a.tmv = bw.mv[li * B + b];
+        host[li * B + b] = a;
+      }
+    }
+    G4_CUDA(cudaMemcpy(bw.dargs, host.data(), host.size() * sizeof(AttnArgs), cudaMemcpyHostToDevice), G4_ERR_CUDA);
+    bw.dargs_qkv = w.qkv;
+    bw.dargs_ctx = w.ctx;
+  }
   for (size_t li = 0; li < m->L.size(); ++li) {
     const LayerDev& l = m->L[li];
     const int nq = l.n_kv * l.g, d = l.d, R = l.rows_q + l.rows_k + l.rows_v;
@@ -1187,21 +1250,8 @@ extern "C" int g4_batch_step(g4_model* m, int* tokens_out, float* logits_out, vo
     if ((rc = gemm({w.xn, (uint64_t)H, (uint64_t)B, (uint64_t)H}, {l.qkv, (uint64_t)H, (uint64_t)R, (uint64_t)H},
                    plain(B, R, H, w.qkv, R, status), 1, st, sb)))
       return rc;
-    for (int b = 0; b < B; ++b) {  // q/k norm, RoPE, cache write and attention of sequence b
-      batch_caches(m, b, ck, cv);
-      AttnArgs a = m->k2[li];
-      a.qkv = w.qkv + (size_t)b * R;
-      a.cache_k = ck[li];
-      a.cache_v = cv[li];
-      a.ctx = w.ctx + (size_t)b * nq * d;
-      a.ctrl = bw.ctrl + (size_t)b * G4_CTRL_WORDS;
-      a.pos_fixed = -1;
-      a.max_len = bw.ctx;
-      a.trace_id = -1;
-      a.tmk = bw.mk[li * B + b];
-      a.tmv = bw.mv[li * B + b];
-      if ((rc = g4_launch_attention(a, st))) return rc;
-    }
+    // q/k norm, RoPE, cache write and attention of every sequence: one launch
+    if ((rc = g4_launch_attention_batch(bw.dargs + li * B, d, l.g, B, l.n_kv * bw.nsplit[li], st))) return rc;
     if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)B, (uint64_t)nq * d},
                    {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(B, H, nq * d, w.o, H, status), 1,
                    st, sb)))

@@ -239,6 +239,49 @@ static int launch_attention(const AttnArgs& a, cudaStream_t st) {
 }
 int g4_launch_attention(const AttnArgs& a, cudaStream_t st) { return launch_attention(a, st); }
 
+// The batched attention kernel for (head dim, query heads per KV head).
+typedef void (*AttnBatchKernel)(const AttnArgs*, int);
+template <int D>
+static AttnBatchKernel attn_batch_kernel_for_g(int g) {
+  switch (g) {
+    case 1: return attn_decode_batch_kernel<D, 1>;
+    case 2: return attn_decode_batch_kernel<D, 2>;
+    case 4: return attn_decode_batch_kernel<D, 4>;
+    case 8: return attn_decode_batch_kernel<D, 8>;
+    default: return nullptr;
+  }
+}
+static AttnBatchKernel attn_batch_kernel_for(int d, int g) {
+  switch (d) {
+    case 64: return attn_batch_kernel_for_g<64>(g);
+    case 128: return attn_batch_kernel_for_g<128>(g);
+    case 256: return attn_batch_kernel_for_g<256>(g);
+    case 512: return attn_batch_kernel_for_g<512>(g);
+    default: return nullptr;
+  }
+}
+
+int g4_launch_attention_batch(const AttnArgs* dargs, int d, int g, int seqs, int items, cudaStream_t st) {
+  AttnBatchKernel k = attn_batch_kernel_for(d, g);
+  if (!k) return fail(G4_ERR_SHAPE, "batched attention: head_dim %d with %d query heads per KV head", d, g);
+  const int smem = attn_kernel_smem_bytes(d);
+  {
+    static std::mutex mu;
+    static std::map<std::pair<int, int>, int> done;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    std::lock_guard<std::mutex> lock(mu);
+    int& have = done[{dev, d * 16 + g}];
+    if (have < smem) {
+      G4_CUDA(cudaFuncSetAttribute(k, cudaFuncAttributeMaxDynamicSharedMemorySize, smem), G4_ERR_LAUNCH);
+      have = smem;
+    }
+  }
+  cudaError_t e = launch_pdl(k, dim3(seqs * items), dim3(kAttnKernelThreads), smem, st, dargs, items);
+  if (e != cudaSuccess) return fail(G4_ERR_LAUNCH, "batched attention launch: %s", cudaGetErrorString(e));
+  return G4_OK;
+}
+
 // The TMA tensor maps of a.cache_k / a.cache_v: [max_len, n_kv * d] bf16, boxes of 64
 // elements x attn_kps(d) rows, 128-byte swizzle (the attention kernels' stage layout).
 int g4_attention_maps(AttnArgs& a) {
@@ -300,6 +343,7 @@ static int pick_nsplit(int n_kv, int max_live, int nsm) {
   chunk = (chunk + kAttnMinKeys - 1) / kAttnMinKeys * kAttnMinKeys;
   return (max_live + chunk - 1) / chunk;
 }
+int g4_pick_nsplit(int n_kv, int max_live, int nsm) { return pick_nsplit(n_kv, max_live, nsm); }
 
 static bool valid_cfg(const g4_config* c) {
   return c && c->hidden_size > 0 && c->num_hidden_layers > 0 && c->num_attention_heads > 0 &&
