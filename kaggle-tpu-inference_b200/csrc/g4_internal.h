@@ -37,7 +37,13 @@ struct g4_comm {
   char* peer[kMaxWorld] = {};
   bool mapped[kMaxWorld] = {};
   bool open = false;
+  int pf_seq = 0;  // tensor-parallel prefill exchanges done (the same count on every rank)
 };
+
+// Tensor-parallel prefill exchange: the end of every communicator buffer holds kMaxWorld
+// arrival flags (128 bytes apart) and two parity slots of kPfXRows x 2 * hidden fp32.
+constexpr int kPfXRows = 512;  // prompt rows per chunk under tensor parallelism
+size_t g4_comm_pf_offset(int hidden);  // byte offset of that region (g4_runtime.cu)
 
 // ------------------------------------------------------------------ launch helper
 template <class Kernel, class... Args>

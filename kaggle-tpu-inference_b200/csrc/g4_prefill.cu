@@ -398,7 +398,8 @@ __global__ void pf_routed_act(const bf16_t* gug, const float* gather_w, const in
 }
 
 // moe[t] = bf16(sum over t's experts in increasing order of the fp32 down outputs).
-__global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, int H, bf16_t* moe) {
+__global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, int H, bf16_t* moe,
+                                  float* f32_out = nullptr, int ld = 0) {
   __shared__ int rows[kMaxTopK * 2];
   __shared__ int nrows;
   const int t = blockIdx.x;
@@ -414,8 +415,92 @@ __global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, i
   for (int h = threadIdx.x; h < H; h += blockDim.x) {
     float acc = 0.f;
     for (int i = 0; i < nrows; ++i) acc += outg[(size_t)rows[i] * H + h];
-    moe[(size_t)t * H + h] = f2bf(acc);
+    if (f32_out) f32_out[(size_t)t * ld + h] = acc;  // a rank's partial (tensor parallel)
+    else moe[(size_t)t * H + h] = f2bf(acc);
   }
+}
+
+// ------------------------------------------------------------------ tensor-parallel exchange
+// Every rank's communicator buffer ends with kMaxWorld arrival flags (128 bytes apart:
+// rank src has written its partial of exchange `seq` when flag[src] >= seq) and two parity
+// slots of kPfXRows x 2H fp32.  A rank writes its partial into its OWN slot (earlier
+// kernels of the stream), then raises its flag on every rank; each rank waits (bounded)
+// for every flag and sums all ranks' slots (peer loads over NVLink) in rank order, so every
+// rank gets the same bits.  A slot is reused two exchanges later: by then every rank has
+// passed the wait of the exchange between, which its peers enter only after their reads.
+struct PfX {
+  char* base[kMaxWorld];  // communicator buffer of every rank, mapped here
+  size_t off;             // byte offset of the exchange region
+  size_t slot_floats;     // floats per parity slot
+  int rank, world;
+};
+__host__ __device__ __forceinline__ float* pfx_slot(const PfX& x, int r, int parity) {
+  return reinterpret_cast<float*>(x.base[r] + x.off + (size_t)kMaxWorld * 128) + (size_t)parity * x.slot_floats;
+}
+__device__ __forceinline__ int* pfx_flag(const PfX& x, int r, int src) {
+  return reinterpret_cast<int*>(x.base[r] + x.off + (size_t)src * 128);
+}
+// CTA 0 raises this rank's flag on every rank; thread 0 of every CTA waits for all ranks'.
+__device__ __forceinline__ bool pfx_arrive_wait(const PfX& x, int seq, int* ctrl) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) {
+    if (blockIdx.x == 0) {
+      __threadfence_system();
+      for (int p = 0; p < x.world; ++p) st_release_sys(pfx_flag(x, p, x.rank), seq);
+    }
+    const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
+    bool good = true;
+    for (int src = 0; src < x.world && good; ++src)
+      good = wait_flag_geq(pfx_flag(x, x.rank, src), seq, tmo, ctrl + G4_CTRL_STATUS);
+    ok = good;
+  }
+  __syncthreads();
+  return ok != 0;
+}
+// out0 / out1 [rows, H] = bf16(sum over ranks of the slots' columns [0, H) / [H, 2H)).
+__global__ void pf_xsum(PfX x, int seq, int parity, int rows, int cols, int H, bf16_t* out0, bf16_t* out1,
+                        int* ctrl) {
+  if (!pfx_arrive_wait(x, seq, ctrl)) return;
+  const size_t n4 = (size_t)rows * cols / 4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int src = 0; src < x.world; ++src) {
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(pfx_slot(x, src, parity)) + i);
+      s.x += v.x;
+      s.y += v.y;
+      s.z += v.z;
+      s.w += v.w;
+    }
+    const size_t r = (4 * i) / cols, c = (4 * i) % cols;
+    bf16_t* dst = c < (size_t)H ? out0 + r * H + c : out1 + r * H + (c - H);
+    uint2 w;
+    w.x = (uint32_t)f2bf(s.x) | ((uint32_t)f2bf(s.y) << 16);
+    w.y = (uint32_t)f2bf(s.z) | ((uint32_t)f2bf(s.w) << 16);
+    *reinterpret_cast<uint2*>(dst) = w;
+  }
+}
+// The prompt's first token: the best (value, index) pair over the ranks' vocab slices
+// (ties: lower index), then the position and the step counter, as a decode step leaves them.
+__global__ void pf_xargmax(PfX x, int seq, int parity, int* tok_out, int out_index, int* tokens_host, int* ctrl,
+                           int n) {
+  if (!pfx_arrive_wait(x, seq, ctrl)) return;
+  if (threadIdx.x != 0) return;
+  float best = -INFINITY;
+  int bidx = 0x7fffffff;
+  for (int src = 0; src < x.world; ++src) {
+    const float* pr = pfx_slot(x, src, parity);
+    const float v = __ldcg(pr);
+    const int idx = __float_as_int(__ldcg(pr + 1));
+    if (v > best || (v == best && idx < bidx)) {
+      best = v;
+      bidx = idx;
+    }
+  }
+  const int token = bidx == 0x7fffffff ? 0 : bidx;
+  tok_out[out_index] = token;
+  if (tokens_host) tokens_host[out_index] = token;
+  ctrl[G4_CTRL_POS] = n;
+  ctrl[G4_CTRL_STEP] = ldcg_i(ctrl + G4_CTRL_STEP) + 1;  // the sampler's and later steps' exchange uses
 }
 
 // Layer output (model.py:312-322, one row per CTA): h1 = rms(mlp)*pf1, h2 = rms(moe)*pf2,
@@ -448,7 +533,7 @@ __global__ void pf_combine(const bf16_t* mlp, const bf16_t* moe, bf16_t* x, cons
 // logits + r * V, tok_out[out_index + r] and ctrl + r * ctrl_stride (n + r * n_stride).
 __global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegin, float softcap, int* tok_out,
                                int out_index, int* tokens_host, int* ctrl, int n, int ctrl_stride = 0,
-                               int n_stride = 0) {
+                               int n_stride = 0, float* xpair = nullptr) {
   __shared__ float bv[32];
   __shared__ int bi[32];
   const int row = blockIdx.x;
@@ -489,6 +574,11 @@ __global__ void pf_lm_epilogue(const bf16_t* lg, float* logits, int V, int vbegi
       bidx = bi[w];
     }
   const int token = bidx == 0x7fffffff ? 0 : vbegin + bidx;
+  if (xpair) {  // tensor parallel: this rank's best of its vocab slice, for pf_xargmax
+    xpair[0] = best;
+    xpair[1] = __int_as_float(token);
+    return;
+  }
   tok_out[out_index] = token;
   if (tokens_host) tokens_host[out_index] = token;
   ctrl[G4_CTRL_POS] = n >= 0 ? n : ctrl[G4_CTRL_POS] + 1;  // n < 0: a decode step advances
@@ -797,7 +887,10 @@ static int launch_qk_rope(const LayerDev& l, const bf16_t* qkv, bf16_t* q, bf16_
 // Routed MoE of the chunk's M tokens (see pf_route_count): routing tables, the gathered
 // MoE inputs, one grouped GEMM per projection (entry e = expert e: its rows, its weights),
 // the activation, and the per-token sum of the routed experts' outputs.
-static int routed_moe(g4_model* m, const LayerDev& l, int M, int* status, cudaStream_t st) {
+// `f32_out` (tensor parallel): the per-token sums go there as this rank's fp32 partial
+// (row stride `ld`) instead of to moe_out.
+static int routed_moe(g4_model* m, const LayerDev& l, int M, int* status, cudaStream_t st,
+                      float* f32_out = nullptr, int ld = 0) {
   PrefillWs& w = *m->prefill;
   const int H = m->H, E = m->E, F = m->F_local, MK = M * m->topk;
   int rc;
@@ -825,7 +918,7 @@ static int routed_moe(g4_model* m, const LayerDev& l, int M, int* status, cudaSt
                    {l.exp_down, (uint64_t)F, (uint64_t)E * H, (uint64_t)F}, g, E, st)))
       return rc;
   }
-  pf_routed_combine<<<M, 256, 0, st>>>(w.outg, w.rowmap, E, H, w.moe_out);
+  pf_routed_combine<<<M, 256, 0, st>>>(w.outg, w.rowmap, E, H, w.moe_out, f32_out, ld);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   return G4_OK;
 }
@@ -855,6 +948,22 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
   const float eps = c.rms_norm_eps;
   int* status = tg.ctrl + G4_CTRL_STATUS;
   int rc;
+  // tensor parallel: the two all-reduces of every layer and the LM head's argmax go through
+  // the communicators' prefill exchange (this rank's partial into its own slot)
+  const bool tp = m->world > 1;
+  PfX px{};
+  if (tp) {
+    for (int p = 0; p < kMaxWorld; ++p) px.base[p] = m->comm->peer[p];
+    px.off = g4_comm_pf_offset(m->comm->hidden);
+    px.slot_floats = (size_t)kPfXRows * 2 * m->comm->hidden;
+    px.rank = m->rank;
+    px.world = m->world;
+  }
+  auto xnext = [&](int& seq, int& par) {
+    seq = ++m->comm->pf_seq;
+    par = seq & 1;
+  };
+  const int xgrid = std::min(4 * m->nsm, (int)(((size_t)M * 2 * H / 4 + 255) / 256));
   pf_embed<<<M, 256, 0, st>>>(tg.tokens + c0, m->embed, w.x, H, c.vocab_size,
                               g4_host_bf16_round(std::sqrt((float)H)), tg.ctrl);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
@@ -905,10 +1014,22 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
                      {w.vt, (uint64_t)span, (uint64_t)l.n_kv * d, (uint64_t)w.ks}, g, nq, st)))
         return rc;
     }
-    if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
-                   {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(M, H, nq * d, w.o, H, status), 1,
-                   st, sb)))
-      return rc;
+    if (!tp) {
+      if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
+                     {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, plain(M, H, nq * d, w.o, H, status), 1,
+                     st, sb)))
+        return rc;
+    } else {  // this rank's heads' o_proj partial (fp32), summed over the ranks into w.o
+      int seq, par;
+      xnext(seq, par);
+      GemmArgs g = plain(M, H, nq * d, pfx_slot(px, px.rank, par), H, status);
+      g.c_f32 = 1;
+      if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
+                     {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, g, 1, st, sb)))
+        return rc;
+      pf_xsum<<<std::max(1, xgrid / 2), 256, 0, st>>>(px, seq, par, M, H, H, w.o, nullptr, tg.ctrl);
+      G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    }
     pf_post_attn<<<M, kRowThreads, 0, st>>>(w.o, w.x, l.n_post_attn, l.n_pre_ff, l.n_pre_ff2, l.router_scale,
                                              w.mlp_in, w.h2, w.rin, H, eps, hinv);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
@@ -920,16 +1041,28 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
                    plain(M, I, H, w.up, I, status), 1, st, sb)))
       return rc;
     pf_gelu_mul<<<std::min(4096, (M * I + 255) / 256), 256, 0, st>>>(w.gate, w.up, w.act, (size_t)M * I);
-    if ((rc = gemm({w.act, (uint64_t)I, (uint64_t)M, (uint64_t)I}, {l.down, (uint64_t)I, (uint64_t)H, (uint64_t)I},
-                   plain(M, H, I, w.mlp_out, H, status), 1, st, sb)))
-      return rc;
+    // tensor parallel: this rank's MLP partial and (below) MoE partial share one exchange
+    int fseq = 0, fpar = 0;
+    float* fslot = nullptr;
+    if (tp) {
+      xnext(fseq, fpar);
+      fslot = pfx_slot(px, px.rank, fpar);
+    }
+    {
+      GemmArgs g = plain(M, H, I, tp ? static_cast<void*>(fslot) : static_cast<void*>(w.mlp_out), tp ? 2 * H : H,
+                         status);
+      g.c_f32 = tp ? 1 : 0;
+      if ((rc = gemm({w.act, (uint64_t)I, (uint64_t)M, (uint64_t)I}, {l.down, (uint64_t)I, (uint64_t)H, (uint64_t)I},
+                     g, 1, st, sb)))
+        return rc;
+    }
     // ---- router + dense MoE over all experts (model.py:224-250)
     if ((rc = gemm({w.rin, (uint64_t)H, (uint64_t)M, (uint64_t)H}, {l.router, (uint64_t)H, (uint64_t)E, (uint64_t)H},
                    plain(M, E, H, w.rlog, E, status), 1, st, sb)))
       return rc;
     pf_router<<<M, 256, 0, st>>>(w.rlog, l.pes, w.wfull, E, K);
     if (!dense) {  // the same sum over the routed (token, expert) pairs only
-      if ((rc = routed_moe(m, l, M, status, st))) return rc;
+      if ((rc = routed_moe(m, l, M, status, st, fslot ? fslot + H : nullptr, 2 * H))) return rc;
     } else if ((rc = gemm({w.h2, (uint64_t)H, (uint64_t)M, (uint64_t)H},
                           {l.exp_gu, (uint64_t)H, (uint64_t)E * 2 * F, (uint64_t)H},
                           plain(M, E * 2 * F, H, w.gu, (long long)E * 2 * F, status), 1, st, sb))) {
@@ -949,9 +1082,28 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
       B.slabs = E;
       if ((rc = gemm({w.mact, (uint64_t)E * F, (uint64_t)M, (uint64_t)E * F}, B, g, 1, st, sb))) return rc;
     }
+    if (tp) {
+      pf_xsum<<<xgrid, 256, 0, st>>>(px, fseq, fpar, M, 2 * H, H, w.mlp_out, w.moe_out, tg.ctrl);
+      G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    }
     pf_combine<<<M, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
                                            l.scalar, H, eps);
     G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  }
+  if (last && tp) {  // tensor parallel: the LM head's argmax over every rank's vocab slice
+    pf_rmsnorm<<<1, kRowThreads, 0, st>>>(w.x + (size_t)(M - 1) * H, m->final_norm, w.xf, H, eps);
+    if ((rc = gemm({w.xf, (uint64_t)H, 1, (uint64_t)H},
+                   {m->embed + (size_t)m->vbegin * H, (uint64_t)H, (uint64_t)m->V_local, (uint64_t)H},
+                   plain(1, m->V_local, H, w.lmlog, m->V_local, status), 1, st, sb)))
+      return rc;
+    int seq, par;
+    xnext(seq, par);
+    pf_lm_epilogue<<<1, 1024, 0, st>>>(w.lmlog, tg.logits, m->V_local, m->vbegin, c.final_logit_softcapping,
+                                       tg.tok_out, tg.out_index, tg.tok_host, tg.ctrl, n_total, 0, 0,
+                                       pfx_slot(px, px.rank, par));
+    pf_xargmax<<<1, 32, 0, st>>>(px, seq, par, tg.tok_out, tg.out_index, tg.tok_host, tg.ctrl, n_total);
+    G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+    return G4_OK;
   }
   if (last) {  // final norm, LM head of the last prompt position (last_index, model.py:372-385)
     pf_rmsnorm<<<1, kRowThreads, 0, st>>>(w.x + (size_t)(M - 1) * H, m->final_norm, w.xf, H, eps);
@@ -1007,10 +1159,16 @@ extern "C" int g4_prefill(g4_model* m, int n_tokens, int chunk, int flags, void*
   if (!m) return fail(G4_ERR_ARG, "g4_prefill: null model");
   if (flags & ~G4_PREFILL_DENSE_MOE) return fail(G4_ERR_ARG, "g4_prefill: unknown flags 0x%x", flags);
   if (!m->finalized) return fail(G4_ERR_STATE, "g4_prefill before g4_model_finalize");
-  if (m->world != 1) return fail(G4_ERR_SHAPE, "g4_prefill: tensor-parallel prefill is not built (world %d)", m->world);
+  if (m->world > 1 && (flags & G4_PREFILL_DENSE_MOE))
+    return fail(G4_ERR_ARG, "g4_prefill: the dense all-expert MoE runs at world 1 (routed pairs under tensor parallelism)");
+  if (m->world > 1 && (!m->comm || !m->comm->open))
+    return fail(G4_ERR_STATE, "g4_prefill: world %d needs an open communicator", m->world);
+  if (m->world > 1 && m->comm->hidden < m->H)
+    return fail(G4_ERR_SHAPE, "g4_prefill: communicator hidden %d < model hidden %d", m->comm->hidden, m->H);
   if (n_tokens < 1 || n_tokens > m->max_len)
     return fail(G4_ERR_ARG, "g4_prefill: %d tokens outside [1, %d]", n_tokens, m->max_len);
   if (chunk <= 0) chunk = 4096;
+  if (m->world > 1) chunk = std::min(chunk, kPfXRows);  // the exchange slots' rows
   chunk = std::min(chunk, n_tokens);
   chunk = (chunk + kGemmBM - 1) / kGemmBM * kGemmBM;
   G4_CUDA(cudaSetDevice(m->device), G4_ERR_CUDA);

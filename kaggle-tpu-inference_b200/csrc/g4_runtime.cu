@@ -53,10 +53,14 @@ extern "C" const char* g4_strerror(int code) {
 
 extern "C" const char* g4_last_error(void) { return g_last_error.c_str(); }
 
-// Flags, then [site][parity][source rank] slots of 4 * hidden floats: the FFN-out site
-// carries 2 * hidden LL words (8 bytes each).
-static size_t comm_bytes(int hidden) {
+// Flags, then [site][parity][source rank] slots of 4 * hidden floats (the FFN-out site
+// carries 2 * hidden LL words of 8 bytes), then the tensor-parallel prefill exchange:
+// kMaxWorld flags of 128 bytes and two parity slots of kPfXRows x 2 * hidden fp32.
+size_t g4_comm_pf_offset(int hidden) {
   return (size_t)kXFlagBytes + (size_t)kSites * 2 * kMaxWorld * (4 * (size_t)hidden) * 4;
+}
+static size_t comm_bytes(int hidden) {
+  return g4_comm_pf_offset(hidden) + (size_t)kMaxWorld * 128 + 2 * (size_t)kPfXRows * 2 * hidden * 4;
 }
 
 extern "C" int g4_comm_create(int device, int rank, int world, int hidden, g4_comm** out) {

@@ -17,8 +17,8 @@ explicit ``mesh`` (one rank) or ``devices`` list overrides both.
 
 What changes underneath: the decode step is one captured CUDA graph of the C-ABI
 kernels per device, replayed per token; a prompt goes through the tensor-core prefill
-(``g4_prefill``, engine.py:57-69) on one device, or through forced decode steps under
-tensor parallelism; tokens never leave the device between steps and the host reads
+(``g4_prefill``, engine.py:57-69) on every rank, the ranks exchanging their partials
+per layer under tensor parallelism; tokens never leave the device between steps and the host reads
 token i from rank 0's mapped pinned mirror once step i's event has completed,
 ``lookahead`` steps behind the dispatch, like the reference's lookahead-3 loop
 (engine.py:192-221).  ``temperature > 0`` samples on the device (model.py:414-424).
@@ -27,6 +27,7 @@ token i from rank 0's mapped pinned mirror once step i's event has completed,
 from __future__ import annotations
 
 import os
+import threading
 import time
 from collections import deque
 from typing import Iterator
@@ -195,10 +196,36 @@ class Engine:
         return self._step_fn(None)
 
     # ---------------------------------------------------------------- helpers
+    def _all_threads(self, fn):
+        """fn(model) on every rank this process owns, one host thread per rank when it owns
+        several: a rank's launches that wait on its peers' exchange flags must not fill
+        its device's launch queue (blocking the host) before the peers' launches exist."""
+        if len(self.models) == 1:
+            return self._all(fn)
+        errors = []
+
+        def run(m):
+            try:
+                with torch.cuda.device(m.device):
+                    fn(m)
+            except BaseException as e:  # re-raised on the calling thread
+                errors.append(e)
+
+        threads = [threading.Thread(target=run, args=(m,)) for m in self.models]
+        for t in threads:
+            t.start()
+        for t in threads:
+            t.join()
+        if errors:
+            raise errors[0]
+
     def _consume_prompt(self, n: int):
-        """The prompt through the model: one tensor-core prefill (engine.py:57-69) when
-        the library has it for this model (world 1), else ``n`` decode steps."""
-        if not (self.use_prefill and len(self.models) == 1 and self.model.prefill(n, self.prefill_chunk)):
+        """The prompt through the model: one tensor-core prefill (engine.py:57-69) on every
+        rank (under tensor parallelism the ranks exchange their partials per layer), or
+        ``n`` forced decode steps when the engine was built with ``prefill=False``."""
+        if self.use_prefill:
+            self._all_threads(lambda m: m.prefill(n, self.prefill_chunk))
+        else:
             self._all(lambda m: m.step(n))
 
     def reset_cache(self):
@@ -221,15 +248,17 @@ class Engine:
 
         self._all(first)
         self._all(lambda m: m.capture())
-        if self.use_prefill and len(self.models) == 1:
+        if self.use_prefill:
             # one prefill of the largest chunk this engine uses: the tensor-core prefill
             # allocates its workspace and configures its kernels here, not in a request's TTFT
-            m = self.model
             n = min(self.max_len - 1, self.prefill_chunk or 4096)
-            m.reset([0] * n)
-            m.prefill(n, self.prefill_chunk)
-            m.check_status()
-            m.reset([0, 0, 0, 0])  # the warm-up decode steps below start near the cache start
+            if self.mesh.world > 1:
+                n = min(n, 512)  # the tensor-parallel chunk
+            self._all(lambda m: m.reset([0] * n))
+            self._all_threads(lambda m: m.prefill(n, self.prefill_chunk))
+            self._sync()
+            self._check()
+            self._all(lambda m: m.reset([0, 0, 0, 0]))  # the warm-up decode steps start near the cache start
         self._sync()
         out["prefill_compile_s"] = time.perf_counter() - t0
         t0 = time.perf_counter()

@@ -180,11 +180,10 @@ class DecodeModel:
         """Consume the first ``n_tokens`` forced tokens in one tensor-core pass per chunk
         (``g4_prefill``): cache rows [0, n), tokens_out[n] and POS = n, like ``n`` steps.
         ``dense_moe`` runs the reference's all-expert MoE as written instead of the routed
-        pairs (same result up to fp32 summation order).  Returns False (nothing enqueued)
-        where the library has no prefill for this model (tensor parallel), so the caller
-        consumes the prompt with decode steps."""
-        if self.mesh.world > 1:
-            return False
+        pairs (same result up to fp32 summation order; world 1 only).  Under tensor
+        parallelism every rank must make the same call: the layers' two all-reduces and
+        the LM head's argmax run through the communicators' prefill exchange, in chunks of
+        at most 512 prompt rows.  Returns True (enqueued)."""
         flags = N.PREFILL_DENSE_MOE if dense_moe else 0
         self.workspace_epoch += 1
         with torch.cuda.device(self.device):

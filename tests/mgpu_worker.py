@@ -8,6 +8,8 @@ all-reduced so that every rank exits with the same status):
   tiny      -- the tiny parity model (config 1 shapes), tensor parallel over W ranks
   real2     -- two layers [sliding, full] at the 26B-A4B per-layer shapes, 16 experts,
                vocab 16384
+  prefill   -- the tensor-parallel prefill (g4_prefill over W ranks) at the real2 shapes,
+               300 prompt tokens in 128-row chunks, then 3 decode steps
   moe_block -- the standalone MoE block (config 2: hidden 2816, 128 experts top-8,
                moe_intermediate 704 split 704/W per rank) with its fused all-reduce
 
@@ -148,6 +150,91 @@ def case_real2(engine):
     return case_decode(cfg, 3, [7, 300, 9000, 15000, 42, 1], 4, 64, engine)
 
 
+def prefill_run(cfg, params_dev, mesh, prompt, chunk, n_dec, max_len, comm=None):
+    """(logits of this rank's vocab slice [1 + n_dec, V/W], token ring) of one tensor-core
+    prefill of ``prompt`` followed by ``n_dec`` decode steps."""
+    from gemma4_b200.runtime import DecodeModel
+    from gemma4_b200.weights import rank_shard
+
+    dev = torch.device("cuda", mesh.device)
+    m = DecodeModel(cfg, rank_shard(cfg, params_dev.__getitem__, mesh, dev), mesh, max_len, comm)
+    p = len(prompt)
+    m.reset(prompt, write_logits=True)
+    assert m.prefill(p, chunk)
+    torch.cuda.synchronize(dev)
+    m.check_status()
+    assert int(m.ctrl[0]) == p, int(m.ctrl[0])
+    out = [m.logits.clone()]
+    for _ in range(n_dec):
+        m.step(1)
+        out.append(m.logits.clone())
+    torch.cuda.synchronize(dev)
+    m.check_status()
+    ring = m.tokens_out.clone()
+    m.close()
+    return torch.stack(out), ring
+
+
+def case_prefill(_engine):
+    """Tensor-parallel prefill: 300 prompt tokens in 128-row chunks (3 chunks, so the
+    exchange slots are reused and later chunks attend to earlier chunks' cache rows) at
+    the 26B-A4B per-layer shapes, then 3 decode steps from the prefilled caches."""
+    from gemma4_b200.config import FULL, SLIDING, make_config
+    from gemma4_b200.model import Mesh
+    from gemma4_b200.runtime import Comm
+    from gemma4_b200.weights import random_params
+
+    rank, world = dist.get_rank(), dist.get_world_size()
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    dev = torch.device("cuda", local)
+    cfg = make_config(num_hidden_layers=2, layer_types=(SLIDING, FULL), num_experts=16, vocab_size=16384)
+    params_dev = random_params(cfg, 3, device=dev)
+    prompt = torch.randint(0, cfg.vocab_size, (300,), generator=torch.Generator().manual_seed(12)).tolist()
+    n_dec, max_len, p = 3, 640, len(prompt)
+    mesh = Mesh(rank, world, local)
+    comm = Comm(mesh, cfg.hidden_size)
+    logits, ring = prefill_run(cfg, params_dev, mesh, prompt, 128, n_dec, max_len, comm)
+    comm.close()
+    rings = [torch.empty_like(ring) for _ in range(world)]
+    dist.all_gather(rings, ring)
+    parts = [torch.empty_like(logits) for _ in range(world)]
+    dist.all_gather(parts, logits)
+    if rank != 0:
+        return None
+    for r in range(1, world):
+        assert torch.equal(rings[r], rings[0]), f"rank {r} token ring differs from rank 0"
+    full = torch.cat(parts, dim=-1).cpu()
+    ids = rings[0][p:p + n_dec + 1].cpu().tolist()
+    assert ids == full.argmax(-1).tolist(), "written tokens are not the argmax of the gathered logits"
+    one, _ = prefill_run(cfg, params_dev, Mesh(0, 1, local), prompt, 128, n_dec, max_len)
+    one = one.cpu()
+    from oracle.reference_model import Oracle
+
+    params = {k: v.cpu() for k, v in params_dev.items()}
+    o = Oracle(cfg, params, mode="bf16")
+    cache = o.new_cache(1, max_len)
+    ref_all, cache = o.prefill(cache, prompt, p, dense_moe=True)
+    refs = [ref_all[p - 1]]
+    for j in range(n_dec):  # teacher-forced with the world-W tokens
+        lg, cache = o.decode(cache, ids[j], p + j, max_len)
+        refs.append(lg)
+    ref = torch.stack(refs)
+    dec = decided_mask(ref)
+    worst = min(corr(full[i], ref[i]) for i in range(len(ref)))
+    w1 = min(corr(full[i], one[i]) for i in range(len(ref)))
+    max_abs = float((full - ref).abs().max())
+    max_rel = max_abs / float(ref.abs().max())
+    assert worst >= 0.9999, worst
+    agree = full.argmax(-1) == ref.argmax(-1)
+    assert bool(agree[dec].all()), (full.argmax(-1), ref.argmax(-1))
+    agree1 = full.argmax(-1) == one.argmax(-1)
+    assert bool(agree1[dec].all()), (full.argmax(-1), one.argmax(-1))
+    return (f"PARITY prefill world{world} T={p} chunk=128, last prompt position + {n_dec} decode steps: "
+            f"worst corr vs oracle {worst:.7f}, vs world 1 {w1:.7f}, max_abs {max_abs:.3e}, "
+            f"max_rel {max_rel:.3e}, argmax = oracle where decided ({int(dec.sum())}/{len(ref)}), "
+            f"token rings identical on {world} ranks")
+
+
 def case_moe_block(_engine):
     import ctypes
 
@@ -220,7 +307,8 @@ def main():
     failed = 0
     msg = None
     try:
-        msg = {"tiny": case_tiny, "real2": case_real2, "moe_block": case_moe_block}[case](engine)
+        msg = {"tiny": case_tiny, "real2": case_real2, "moe_block": case_moe_block,
+               "prefill": case_prefill}[case](engine)
     except Exception:
         traceback.print_exc()
         failed = 1

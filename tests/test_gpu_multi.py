@@ -55,6 +55,14 @@ def test_real_shapes_tensor_parallel(world):
 
 
 @pytest.mark.parametrize("world", [2, 4, 8])
+def test_tensor_parallel_prefill(world):
+    """g4_prefill on every rank: per-layer partials exchanged through the communicators'
+    prefill slots, the LM head's argmax over all vocab slices; the gathered logits of the
+    last prompt position and of the decode steps that follow against the oracle."""
+    _run(world, "prefill")
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
 def test_moe_block_sharded(world):
     _run(world, "moe_block")
 
