@@ -277,44 +277,54 @@ def prefill_flops(cfg, T, dense):
     return tot + 2.0 * H * cfg.vocab_size
 
 
-def prefill_leg(eng, cfg, args, dev):
+def prefill_leg(eng, cfg, args, dev, world=1):
     """Benchmark config 5's prefill: a prompt of --prefill-tokens random ids (seed 4)
     through g4_prefill (tcgen05 GEMMs), timed with CUDA events (best of 2 after one
-    warm-up) in both MoE modes; TTFT ms and tensor-core throughput against the measured
-    bf16 peak.  Weights are the bench model's (values do not change the timing)."""
+    warm-up) in both MoE modes (routed only under tensor parallelism, where every rank
+    prefills its shard and the time is the max over ranks); TTFT ms and tensor-core
+    throughput of the whole job against the measured bf16 peak x ranks.  Weights are the
+    bench model's (values do not change the timing)."""
     import torch
+    import torch.distributed as dist
 
     T = min(args.prefill_tokens, args.max_len - 1)
     g = torch.Generator().manual_seed(4)
     prompt = torch.randint(0, cfg.vocab_size, (T,), generator=g).tolist()
     m = eng.model
-    out = {"tokens": T, "workload": "benchmark config 5 prefill (one prompt, world 1)"}
+    out = {"tokens": T, "workload": f"benchmark config 5 prefill (one prompt, tp{world})"}
     try:
         with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
             peak = float(json.load(f)["bf16_tflops"])
         peak_kind = "measured"
     except (OSError, KeyError, ValueError):
         peak, peak_kind = 1590.0, "fallback"
-    for dense in (False, True):
+    for dense in ((False, True) if world == 1 else (False,)):
         times = []
         for rep in range(3):
             m.reset(prompt)
             torch.cuda.synchronize(dev)
+            if world > 1:
+                dist.barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
             m.prefill(T, 0, dense_moe=dense)
             e1.record()
             torch.cuda.synchronize(dev)
+            t = e0.elapsed_time(e1)
+            if world > 1:
+                tt = torch.tensor([t], device=dev, dtype=torch.float64)
+                dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+                t = float(tt.item())
             if rep:
-                times.append(e0.elapsed_time(e1))
+                times.append(t)
         m.check_status()
         ms = min(times)
         key = "dense_moe" if dense else "routed_moe"
         fl = prefill_flops(cfg, T, dense)
         out[key] = {"ttft_ms": ms, "tflops_as_run": fl / ms / 1e9, "flops_as_run": fl,
                     "useful_tflops": prefill_flops(cfg, T, False) / ms / 1e9,
-                    "frac_of_bf16_peak": fl / ms / 1e9 / peak}
-    out["bf16_peak_tflops"] = peak
+                    "frac_of_bf16_peak": fl / ms / 1e9 / (peak * world)}
+    out["bf16_peak_tflops"] = peak * world
     out["peak_kind"] = peak_kind
     return out
 
@@ -561,7 +571,7 @@ def main() -> int:
         return 0
     if args.prefill_only:  # profiling case: the prefill leg alone, one JSON line
         line = {"metric": "prefill TTFT ms", "config": workload,
-                "prefill": prefill_leg(eng, cfg, args, dev) if world == 1 else None}
+                "prefill": prefill_leg(eng, cfg, args, dev, world)}
         if rank == 0:
             print(json.dumps(line), flush=True)
         return 0
@@ -685,7 +695,7 @@ def main() -> int:
                "d2h_bytes_per_step": 4, "ttft_ms": 1000 * evs[0]["ttft"], "tokens": len(evs),
                "path": "Engine.generate (temperature 0), wall clock call -> last token"}
 
-    prefill = prefill_leg(eng, cfg, args, dev) if args.prefill_tokens > 0 and world == 1 else None
+    prefill = prefill_leg(eng, cfg, args, dev, world) if args.prefill_tokens > 0 else None
     blocks = block_legs(args, dev) if world == 1 and not args.no_blocks else None
     batch = batch_leg(eng, cfg, args, dev) if world == 1 and args.batch_size > 0 else None
 

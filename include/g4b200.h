@@ -169,8 +169,13 @@ int g4_model_set_engine(g4_model* model, int engine);
  * sample when control[TEMPERATURE] > 0) and sets control[POS] = n_tokens, so the next
  * g4_step continues the sequence.  The caller sets control[FORCED_LEN] = n_tokens (the
  * prompt).  Allocates a workspace on first use (grown for a larger chunk; freed by
- * g4_model_destroy).  world > 1: G4_ERR_SHAPE (tensor-parallel prefill is not built;
- * consume the prompt with g4_step instead).
+ * g4_model_destroy).  world > 1 (tensor parallel, the reference's sharded prefill over
+ * its mesh, model.py:84-156): every rank makes the same call on its own stream; each
+ * layer's o_proj and MLP + MoE outputs are this rank's fp32 partials, summed over the
+ * ranks in rank order through the open communicator (bounded waits: a peer that never
+ * arrives sets G4_STATUS_PEER_TIMEOUT), and the first token is the argmax over every
+ * rank's vocab slice; chunks are capped at 4096 rows; G4_PREFILL_DENSE_MOE is rejected
+ * (G4_ERR_ARG) and a closed communicator is G4_ERR_STATE.
  * flags: 0 computes the MoE over the routed (token, expert) pairs only, as grouped GEMMs:
  * an expert off a token's top-k has routing weight 0 in the reference's dense einsum
  * (model.py:241-250), so its terms are exactly zero and the result is the dense one up to

@@ -42,7 +42,7 @@ struct g4_comm {
 
 // Tensor-parallel prefill exchange: the end of every communicator buffer holds kMaxWorld
 // arrival flags (128 bytes apart) and two parity slots of kPfXRows x 2 * hidden fp32.
-constexpr int kPfXRows = 512;  // prompt rows per chunk under tensor parallelism
+constexpr int kPfXRows = 4096;  // prompt rows per chunk under tensor parallelism
 size_t g4_comm_pf_offset(int hidden);  // byte offset of that region (g4_runtime.cu)
 
 // ------------------------------------------------------------------ launch helper

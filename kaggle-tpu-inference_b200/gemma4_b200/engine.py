@@ -252,8 +252,6 @@ class Engine:
             # one prefill of the largest chunk this engine uses: the tensor-core prefill
             # allocates its workspace and configures its kernels here, not in a request's TTFT
             n = min(self.max_len - 1, self.prefill_chunk or 4096)
-            if self.mesh.world > 1:
-                n = min(n, 512)  # the tensor-parallel chunk
             self._all(lambda m: m.reset([0] * n))
             self._all_threads(lambda m: m.prefill(n, self.prefill_chunk))
             self._sync()

@@ -183,7 +183,7 @@ class DecodeModel:
         pairs (same result up to fp32 summation order; world 1 only).  Under tensor
         parallelism every rank must make the same call: the layers' two all-reduces and
         the LM head's argmax run through the communicators' prefill exchange, in chunks of
-        at most 512 prompt rows.  Returns True (enqueued)."""
+        at most 4096 prompt rows.  Returns True (enqueued)."""
         flags = N.PREFILL_DENSE_MOE if dense_moe else 0
         self.workspace_epoch += 1
         with torch.cuda.device(self.device):
