@@ -421,13 +421,21 @@ __global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, i
 }
 
 // ------------------------------------------------------------------ tensor-parallel exchange
-// Every rank's communicator buffer ends with kMaxWorld arrival flags (128 bytes apart:
-// rank src has written its partial of exchange `seq` when flag[src] >= seq) and two parity
-// slots of kPfXRows x 2H fp32.  A rank writes its partial into its OWN slot (earlier
-// kernels of the stream), then raises its flag on every rank; each rank waits (bounded)
-// for every flag and sums all ranks' slots (peer loads over NVLink) in rank order, so every
-// rank gets the same bits.  A slot is reused two exchanges later: by then every rank has
-// passed the wait of the exchange between, which its peers enter only after their reads.
+// Every rank's communicator buffer ends with kMaxWorld 128-byte flag blocks (block src holds
+// rank src's phase-1 flag at byte 0 and its phase-2 flag at byte 64: src has finished phase
+// p of exchange `seq` when that flag >= seq) and two parity slots of kPfXRows x 2H fp32.
+// A rank writes its partial into its OWN slot (earlier kernels of the stream); then
+//   phase 1 (pf_xsum_rs, a reduce-scatter): it raises its phase-1 flag on every rank, waits
+//     (bounded) for every rank's, and sums its share of the rows -- rows [q M / W, (q+1) M / W)
+//     for rank q -- over all ranks' slots in rank order (peer loads over NVLink), writing
+//     the fp32 sums back over those rows of its own slot;
+//   phase 2 (pf_xsum_ag, an all-gather): it raises its phase-2 flag, waits for every rank's,
+//     and reads each share's sums from its owner's slot, rounding them to bf16.
+// Every rank gets the same bits, the sum order of a single all-ranks pass, and each rank
+// moves ~2 (W-1)/W slots over NVLink instead of W-1.  Only the owner writes a share's rows,
+// and no other rank reads them before the owner's phase-2 flag.  A slot is rewritten two
+// exchanges later: by then every rank has passed the phase-1 wait of the exchange between,
+// which its peers enter only after their phase-2 reads.
 struct PfX {
   char* base[kMaxWorld];  // communicator buffer of every rank, mapped here
   size_t off;             // byte offset of the exchange region
@@ -437,32 +445,37 @@ struct PfX {
 __host__ __device__ __forceinline__ float* pfx_slot(const PfX& x, int r, int parity) {
   return reinterpret_cast<float*>(x.base[r] + x.off + (size_t)kMaxWorld * 128) + (size_t)parity * x.slot_floats;
 }
-__device__ __forceinline__ int* pfx_flag(const PfX& x, int r, int src) {
-  return reinterpret_cast<int*>(x.base[r] + x.off + (size_t)src * 128);
+__device__ __forceinline__ int* pfx_flag(const PfX& x, int r, int src, int phase) {
+  return reinterpret_cast<int*>(x.base[r] + x.off + (size_t)src * 128 + (size_t)phase * 64);
 }
-// CTA 0 raises this rank's flag on every rank; thread 0 of every CTA waits for all ranks'.
-__device__ __forceinline__ bool pfx_arrive_wait(const PfX& x, int seq, int* ctrl) {
+// CTA 0 raises this rank's flag of `phase` on every rank; thread 0 of every CTA waits for
+// all ranks'.
+__device__ __forceinline__ bool pfx_arrive_wait(const PfX& x, int seq, int phase, int* ctrl) {
   __shared__ int ok;
   if (threadIdx.x == 0) {
     if (blockIdx.x == 0) {
       __threadfence_system();
-      for (int p = 0; p < x.world; ++p) st_release_sys(pfx_flag(x, p, x.rank), seq);
+      for (int p = 0; p < x.world; ++p) st_release_sys(pfx_flag(x, p, x.rank, phase), seq);
     }
     const int tmo = ldcg_i(ctrl + G4_CTRL_TIMEOUT_US);
     bool good = true;
     for (int src = 0; src < x.world && good; ++src)
-      good = wait_flag_geq(pfx_flag(x, x.rank, src), seq, tmo, ctrl + G4_CTRL_STATUS);
+      good = wait_flag_geq(pfx_flag(x, x.rank, src, phase), seq, tmo, ctrl + G4_CTRL_STATUS);
     ok = good;
   }
   __syncthreads();
   return ok != 0;
 }
-// out0 / out1 [rows, H] = bf16(sum over ranks of the slots' columns [0, H) / [H, 2H)).
-__global__ void pf_xsum(PfX x, int seq, int parity, int rows, int cols, int H, bf16_t* out0, bf16_t* out1,
-                        int* ctrl) {
-  if (!pfx_arrive_wait(x, seq, ctrl)) return;
-  const size_t n4 = (size_t)rows * cols / 4;
-  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+__host__ __device__ __forceinline__ int pfx_share_row(int q, int rows, int world) {
+  return (int)((long long)q * rows / world);
+}
+// Phase 1: this rank's share of the rows ([rows, cols] fp32 slots) summed over the ranks.
+__global__ void pf_xsum_rs(PfX x, int seq, int parity, int rows, int cols, int* ctrl) {
+  if (!pfx_arrive_wait(x, seq, 0, ctrl)) return;
+  const size_t i0 = (size_t)pfx_share_row(x.rank, rows, x.world) * cols / 4;
+  const size_t i1 = (size_t)pfx_share_row(x.rank + 1, rows, x.world) * cols / 4;
+  float4* own = reinterpret_cast<float4*>(pfx_slot(x, x.rank, parity));
+  for (size_t i = i0 + (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < i1; i += (size_t)gridDim.x * blockDim.x) {
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int src = 0; src < x.world; ++src) {
       const float4 v = __ldcg(reinterpret_cast<const float4*>(pfx_slot(x, src, parity)) + i);
@@ -471,6 +484,40 @@ __global__ void pf_xsum(PfX x, int seq, int parity, int rows, int cols, int H, b
       s.z += v.z;
       s.w += v.w;
     }
+    own[i] = s;
+  }
+}
+// Phase 2: out0 / out1 [rows, H] = bf16 of the summed columns [0, H) / [H, 2H), each row
+// read from the slot of the rank whose share it is.
+__global__ void pf_xsum_ag(PfX x, int seq, int parity, int rows, int cols, int H, bf16_t* out0, bf16_t* out1,
+                           int* ctrl) {
+  if (!pfx_arrive_wait(x, seq, 1, ctrl)) return;
+  const size_t n4 = (size_t)rows * cols / 4;
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const size_t r = (4 * i) / cols, c = (4 * i) % cols;
+    int q = (int)((long long)r * x.world / rows);  // the share holding row r
+    while (q + 1 < x.world && pfx_share_row(q + 1, rows, x.world) <= (int)r) ++q;
+    while (q > 0 && pfx_share_row(q, rows, x.world) > (int)r) --q;
+    const float4 s = __ldcg(reinterpret_cast<const float4*>(pfx_slot(x, q, parity)) + i);
+    bf16_t* dst = c < (size_t)H ? out0 + r * H + c : out1 + r * H + (c - H);
+    uint2 w;
+    w.x = (uint32_t)f2bf(s.x) | ((uint32_t)f2bf(s.y) << 16);
+    w.y = (uint32_t)f2bf(s.z) | ((uint32_t)f2bf(s.w) << 16);
+    *reinterpret_cast<uint2*>(dst) = w;
+  }
+}
+// Two ranks: one pass (phase-1 flags only) in which each rank sums every row of both slots
+// -- the same bytes over NVLink as the two phases, one wait fewer.
+__global__ void pf_xsum_pair(PfX x, int seq, int parity, int rows, int cols, int H, bf16_t* out0, bf16_t* out1,
+                             int* ctrl) {
+  if (!pfx_arrive_wait(x, seq, 0, ctrl)) return;
+  const size_t n4 = (size_t)rows * cols / 4;
+  const float4* s0 = reinterpret_cast<const float4*>(pfx_slot(x, 0, parity));
+  const float4* s1 = reinterpret_cast<const float4*>(pfx_slot(x, 1, parity));
+  for (size_t i = (size_t)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (size_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldcg(s0 + i), b = __ldcg(s1 + i);
+    // 0 + a + b: the order of the two-phase sum
+    const float4 s = make_float4((0.f + a.x) + b.x, (0.f + a.y) + b.y, (0.f + a.z) + b.z, (0.f + a.w) + b.w);
     const size_t r = (4 * i) / cols, c = (4 * i) % cols;
     bf16_t* dst = c < (size_t)H ? out0 + r * H + c : out1 + r * H + (c - H);
     uint2 w;
@@ -479,11 +526,24 @@ __global__ void pf_xsum(PfX x, int seq, int parity, int rows, int cols, int H, b
     *reinterpret_cast<uint2*>(dst) = w;
   }
 }
+// The exchange of one [rows, cols] partial into out0 / out1: one pass at two ranks, else
+// phase 1 then phase 2.
+static int pf_xsum(const PfX& x, int seq, int parity, int rows, int cols, int H, bf16_t* out0, bf16_t* out1,
+                   int* ctrl, int grid, cudaStream_t st) {
+  if (x.world == 2) {
+    pf_xsum_pair<<<std::max(1, grid), 256, 0, st>>>(x, seq, parity, rows, cols, H, out0, out1, ctrl);
+  } else {
+    pf_xsum_rs<<<std::max(1, grid / x.world), 256, 0, st>>>(x, seq, parity, rows, cols, ctrl);
+    pf_xsum_ag<<<std::max(1, grid), 256, 0, st>>>(x, seq, parity, rows, cols, H, out0, out1, ctrl);
+  }
+  G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+  return G4_OK;
+}
 // The prompt's first token: the best (value, index) pair over the ranks' vocab slices
 // (ties: lower index), then the position and the step counter, as a decode step leaves them.
 __global__ void pf_xargmax(PfX x, int seq, int parity, int* tok_out, int out_index, int* tokens_host, int* ctrl,
                            int n) {
-  if (!pfx_arrive_wait(x, seq, ctrl)) return;
+  if (!pfx_arrive_wait(x, seq, 0, ctrl)) return;
   if (threadIdx.x != 0) return;
   float best = -INFINITY;
   int bidx = 0x7fffffff;
@@ -1027,8 +1087,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
       if ((rc = gemm({w.ctx, (uint64_t)nq * d, (uint64_t)M, (uint64_t)nq * d},
                      {l.o, (uint64_t)nq * d, (uint64_t)H, (uint64_t)nq * d}, g, 1, st, sb)))
         return rc;
-      pf_xsum<<<std::max(1, xgrid / 2), 256, 0, st>>>(px, seq, par, M, H, H, w.o, nullptr, tg.ctrl);
-      G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+      if ((rc = pf_xsum(px, seq, par, M, H, H, w.o, nullptr, tg.ctrl, xgrid / 2, st))) return rc;
     }
     pf_post_attn<<<M, kRowThreads, 0, st>>>(w.o, w.x, l.n_post_attn, l.n_pre_ff, l.n_pre_ff2, l.router_scale,
                                              w.mlp_in, w.h2, w.rin, H, eps, hinv);
@@ -1083,8 +1142,7 @@ static int prefill_chunk(g4_model* m, int c0, int M, bool last, int n_total, boo
       if ((rc = gemm({w.mact, (uint64_t)E * F, (uint64_t)M, (uint64_t)E * F}, B, g, 1, st, sb))) return rc;
     }
     if (tp) {
-      pf_xsum<<<xgrid, 256, 0, st>>>(px, fseq, fpar, M, 2 * H, H, w.mlp_out, w.moe_out, tg.ctrl);
-      G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
+      if ((rc = pf_xsum(px, fseq, fpar, M, 2 * H, H, w.mlp_out, w.moe_out, tg.ctrl, xgrid, st))) return rc;
     }
     pf_combine<<<M, kRowThreads, 0, st>>>(w.mlp_out, w.moe_out, w.x, l.n_post_ff1, l.n_post_ff2, l.n_post_ff,
                                            l.scalar, H, eps);
