@@ -400,19 +400,29 @@ __global__ void pf_routed_act(const bf16_t* gug, const float* gather_w, const in
 // moe[t] = bf16(sum over t's experts in increasing order of the fp32 down outputs).
 __global__ void pf_routed_combine(const float* outg, const int* rowmap, int E, int H, bf16_t* moe,
                                   float* f32_out = nullptr, int ld = 0) {
+  // launched with blockDim.x >= E (<= 1024): thread e reads expert e's row index, and the
+  // token's routed rows are compacted in expert order (warp ballots, prefix over warps)
   __shared__ int rows[kMaxTopK * 2];
+  __shared__ int wcount[32];
   __shared__ int nrows;
-  const int t = blockIdx.x;
+  const int t = blockIdx.x, lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int r = (int)threadIdx.x < E ? rowmap[(size_t)t * E + threadIdx.x] : -1;
+  const unsigned b = __ballot_sync(0xffffffffu, r >= 0);
+  if (lane == 0) wcount[warp] = __popc(b);
+  __syncthreads();
+  if (r >= 0) {
+    int pos = __popc(b & ((1u << lane) - 1u));
+    for (int w = 0; w < warp; ++w) pos += wcount[w];
+    if (pos < kMaxTopK * 2) rows[pos] = r;
+  }
   if (threadIdx.x == 0) {
     int n = 0;
-    for (int e = 0; e < E && n < kMaxTopK * 2; ++e) {
-      const int r = rowmap[(size_t)t * E + e];
-      if (r >= 0) rows[n++] = r;
-    }
-    nrows = n;
+    for (int w = 0; w < (int)(blockDim.x >> 5); ++w) n += wcount[w];
+    nrows = min(n, kMaxTopK * 2);
   }
   __syncthreads();
-  for (int h = threadIdx.x; h < H; h += blockDim.x) {
+  // columns split over gridDim.y blocks (short prompts: more blocks than tokens)
+  for (int h = blockIdx.y * blockDim.x + threadIdx.x; h < H; h += gridDim.y * blockDim.x) {
     float acc = 0.f;
     for (int i = 0; i < nrows; ++i) acc += outg[(size_t)rows[i] * H + h];
     if (f32_out) f32_out[(size_t)t * ld + h] = acc;  // a rank's partial (tensor parallel)
@@ -978,7 +988,9 @@ static int routed_moe(g4_model* m, const LayerDev& l, int M, int* status, cudaSt
                    {l.exp_down, (uint64_t)F, (uint64_t)E * H, (uint64_t)F}, g, E, st)))
       return rc;
   }
-  pf_routed_combine<<<M, 256, 0, st>>>(w.outg, w.rowmap, E, H, w.moe_out, f32_out, ld);
+  if (E > 256) return fail(G4_ERR_SHAPE, "prefill: %d experts (at most 256)", E);
+  pf_routed_combine<<<dim3(M, M < 512 ? (H + 255) / 256 : 1), 256, 0, st>>>(w.outg, w.rowmap, E, H, w.moe_out,
+                                                                           f32_out, ld);
   G4_CUDA(cudaGetLastError(), G4_ERR_LAUNCH);
   return G4_OK;
 }
